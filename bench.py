@@ -1,0 +1,398 @@
+"""Benchmark of the hot path on B200 (driver contract: one JSON line on rank 0).
+
+Workload (the configuration the headline metric is quoted
+on): Y = GELU_tanh(X W + b), X [8192, 4096] bf16, W [4096, 4096] bf16,
+b [4096] bf16, Y bf16, f32 accumulation -- one call of the Family A operator
+(the tcgen05 kernel) per step.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--scaling weak|strong]
+
+Multi-GPU (torchrun, one process per GPU): the M rows are sharded with no
+collective on the data path. Default "weak": every rank owns 8192 rows of a
+global X of 8192*N rows (per-GPU work fixed); "strong": the 8192 rows are
+split N ways. value = FLOPs of all ranks / max-over-ranks device time.
+
+`--impl reference` times the reference's CPU arithmetic for the same workload
+(the oracle restatement, since the reference itself cannot be built here) on
+the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "TFLOP/s per GPU and % of dense tensor peak (GEMM, fused MSM) at 1/2/4/8 B200"
+UNIT = "TFLOP/s"
+M_FULL, N_DIM, K_DIM = 8192, 4096, 4096
+L2_BYTES = 126 * 1024 * 1024
+ROTATE = 4  # input/output sets cycled between steps (working set > L2)
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"bf16_tflops": d.get("bf16_tflops", 1590.0),
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", 1400.0),
+                "hbm_gbs": d.get("hbm_gbs", 6650.0), "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0,
+            "source": "fallback"}
+
+
+def _profiled_traffic(kernel_key: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    p = os.path.join(ROOT, "profiles", "gemm_tc_bf16_config2.md")
+    if not os.path.exists(p):
+        return None
+    m = re.search(rf"{kernel_key}_dram_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """NVML clocks and throttle reasons sampled in a thread while running."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.01):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._period = period_s
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _sample(self):
+        n = self._nvml
+        self.samples.append(n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM))
+        try:
+            mask = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        except Exception:
+            mask = n.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+        for name, bit in self.REASONS.items():
+            if mask & bit and name != "gpu_idle":
+                self.reasons.add(name)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self._nvml:
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._nvml:
+            self._t.join()
+            if not self.samples:
+                try:
+                    self._sample()
+                except Exception:
+                    pass
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _init_pg(world, backend):
+    import datetime
+
+    import torch.distributed as dist
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+
+
+def _max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_baseline(target_seconds: float = 10.0, rows: int = 256):
+    """The oracle's fp32 OpenMP GEMM + bias + GELU on a bounded row sample."""
+    import oracle
+    oracle.build()
+    rng = np.random.default_rng(10)
+    x = rng.standard_normal((rows, K_DIM), dtype=np.float32)
+    w = rng.standard_normal((K_DIM, N_DIM), dtype=np.float32) * np.float32(1 / 64)
+    b = rng.standard_normal(N_DIM, dtype=np.float32) * np.float32(0.02)
+    xf = oracle.bf16_to_f32(oracle.bf16_from_f32(x))
+    wf = oracle.bf16_to_f32(oracle.bf16_from_f32(w))
+    bf = oracle.bf16_to_f32(oracle.bf16_from_f32(b))
+    threads = oracle.max_threads()
+    oracle.baseline_gemm_bias_gelu(xf[:8], wf, bf, threads)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        oracle.baseline_gemm_bias_gelu(xf, wf, bf, threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= target_seconds:
+            break
+    flops = 2.0 * rows * K_DIM * N_DIM * reps
+    return {"value": flops / el / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{reps} x {rows} of {M_FULL} rows of config 2 (fp32 oracle GEMM+bias+GELU, "
+                      f"bf16 inputs widened), {el:.1f} s"}
+
+
+def run_reference(args):
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    import oracle
+    oracle.build()
+    threads = oracle.max_threads()
+    rng = np.random.default_rng(10)
+    w = rng.standard_normal((K_DIM, N_DIM), dtype=np.float32) * np.float32(1 / 64)
+    wf = oracle.bf16_to_f32(oracle.bf16_from_f32(w))
+    bf = oracle.bf16_to_f32(oracle.bf16_from_f32(
+        rng.standard_normal(N_DIM, dtype=np.float32) * np.float32(0.02)))
+    # Size each step so the whole run stays within ~2 minutes.
+    calib = oracle.bf16_to_f32(oracle.bf16_from_f32(rng.standard_normal((16, K_DIM), dtype=np.float32)))
+    t0 = time.perf_counter()
+    oracle.baseline_gemm_bias_gelu(calib, wf, bf, threads)
+    per_row = (time.perf_counter() - t0) / 16
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    rows = int(max(4, min(M_FULL, budget / max(per_row, 1e-9))))
+    x = oracle.bf16_to_f32(oracle.bf16_from_f32(rng.standard_normal((rows, K_DIM), dtype=np.float32)))
+    for _ in range(args.warmup):
+        oracle.baseline_gemm_bias_gelu(x, wf, bf, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.baseline_gemm_bias_gelu(x, wf, bf, threads)
+    el = time.perf_counter() - t0
+    value = 2.0 * rows * K_DIM * N_DIM * args.steps / el / 1e12
+    sample = (f"{rows} of {M_FULL} rows of config 2 per step (fp32 oracle port of the reference "
+              f"Family A arithmetic, GEMM+bias+GELU_tanh)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": args.scaling,
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config2 GELU_tanh(X W + b) 8192x4096x4096", "rows_per_step": rows,
+                   "parallelism": "cpu (rank 0 only)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    world, rank, local = _dist()
+    if world > 1:
+        torch.cuda.set_device(local)
+        _init_pg(world, "nccl")
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    import matcoredsl_b200 as mcb
+    from matcoredsl_b200 import _abi
+    lib = mcb.load()
+
+    m = M_FULL if args.scaling == "weak" else M_FULL // world
+    flops_step = 2.0 * m * N_DIM * K_DIM
+    g = torch.Generator(device=dev)
+    g.manual_seed(10 + 1000 * rank)
+    sets = []
+    for _ in range(ROTATE):
+        x = torch.randn(m, K_DIM, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.randn(K_DIM, N_DIM, generator=g, device=dev) / 64.0).to(torch.bfloat16)
+        b = (torch.randn(N_DIM, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        y = torch.empty(m, N_DIM, dtype=torch.bfloat16, device=dev)
+        sets.append((x, w, b, y))
+    working_set = sum(t.numel() * t.element_size() for s in sets for t in s)
+    stream = torch.cuda.current_stream(dev)
+    ep = _abi.make_epilogue("row", "add", "gelu_tanh")
+    ex = _abi.make_exec(device=dev.index, stream=stream.cuda_stream)
+
+    def descs(s, device=True):
+        x, w, b, y = s
+        mk = lambda t: _abi.make_tensor(t.data_ptr(), "bf16", t.shape, t.stride(), device)  # noqa
+        return [mk(y), mk(x), mk(w), mk(b)]
+
+    dsets = [descs(s) for s in sets]
+    calls = [tuple(ctypes.byref(d) for d in ds) for ds in dsets]
+
+    def step(i):
+        c = calls[i % ROTATE]
+        code = lib.mcb_gemm_epilogue_v1(c[0], c[1], c[2], c[3], ctypes.byref(ep), 0,
+                                        ctypes.byref(ex))
+        if code:
+            raise _abi.McbError(code, "mcb_gemm_epilogue_v1")
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    # route check (one synchronous reported call, outside the timed region)
+    rep = _abi.make_report()
+    ex_chk = _abi.make_exec(device=dev.index, stream=stream.cuda_stream, flags=_abi.EXEC_SYNC,
+                            report=rep)
+    c = calls[0]
+    _abi.check(lib.mcb_gemm_epilogue_v1(c[0], c[1], c[2], c[3], ctypes.byref(ep), 0,
+                                        ctypes.byref(ex_chk)), "route check")
+    route = rep.route.decode()
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clk:
+        t_start.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            step(i)
+            ev[i][1].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    _barrier(world)
+    t_ms = t_start.elapsed_time(t_end)
+    launch_ms = statistics.mean(s.elapsed_time(e) for s, e in ev)
+    t_ms_max = _max_over_ranks(t_ms, world, dev)
+    launch_ms_max = _max_over_ranks(launch_ms, world, dev)
+    value = world * flops_step * args.steps / (t_ms_max / 1e3) / 1e12
+
+    # ---- end to end through the public API with host buffers -------------------------
+    e2e_steps = max(3, min(args.steps, 10))
+    xh = torch.empty(m, K_DIM, dtype=torch.bfloat16, pin_memory=True)
+    wh = torch.empty(K_DIM, N_DIM, dtype=torch.bfloat16, pin_memory=True)
+    bh = torch.empty(N_DIM, dtype=torch.bfloat16, pin_memory=True)
+    yh = torch.empty(m, N_DIM, dtype=torch.bfloat16, pin_memory=True)
+    xh.copy_(sets[0][0])
+    wh.copy_(sets[0][1])
+    bh.copy_(sets[0][2])
+    hd = descs((xh, wh, bh, yh), device=False)
+    rep_e2e = _abi.make_report()
+    ex_h = _abi.make_exec(device=dev.index, stream=stream.cuda_stream, report=rep_e2e)
+    hcall = tuple(ctypes.byref(d) for d in hd)
+
+    def e2e_step():
+        code = lib.mcb_gemm_epilogue_v1(hcall[0], hcall[1], hcall[2], hcall[3],
+                                        ctypes.byref(ep), 0, ctypes.byref(ex_h))
+        if code:
+            raise _abi.McbError(code, "e2e")
+
+    for _ in range(2):
+        e2e_step()
+    _barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    _barrier(world)
+    e2e_s_max = _max_over_ranks(e2e_s, world, dev)
+    e2e_value = world * flops_step * e2e_steps / e2e_s_max / 1e12
+
+    peaks = _peaks()
+    achieved = flops_step / (launch_ms_max / 1e3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_ms_max / args.steps,
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": "config2: Y = GELU_tanh(X W + b), X [M,4096] bf16, W [4096,4096] "
+                            "bf16 (row-major, consumed MN-major), b [4096] bf16, Y bf16, f32 "
+                            "accumulate",
+                "m_per_gpu": m, "n": N_DIM, "k": K_DIM, "global_m": m * world,
+                "parallelism": f"dp{world} (M rows sharded, no collective)",
+                "l2": f"{ROTATE} rotating X/W/b/Y sets, {working_set / 2**20:.0f} MiB working "
+                      f"set > 126 MB L2",
+                "route": route,
+            },
+            "pct_of_peak": value / world / peaks["bf16_tflops"],
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                         "unit": UNIT, "frac": achieved / peaks["bf16_tflops"],
+                         "traffic": _profiled_traffic("gemm_tc_bf16"),
+                         "peak_source": f"{peaks['source']} bf16 burst (cuBLAS)",
+                         "kernel": "gemm_tc_bf16_kernel",
+                         "algorithmic_flops_per_launch": flops_step},
+            "clocks": clk.summary(),
+            "e2e": {"value": e2e_value, "unit": UNIT, "steps": e2e_steps,
+                    "h2d_bytes_per_step": int(rep_e2e.h2d_bytes),
+                    "d2h_bytes_per_step": int(rep_e2e.d2h_bytes),
+                    "path": "mcb_gemm_epilogue_v1 with pinned host operands (staged by the library)"},
+            "gpu_launches": args.steps,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

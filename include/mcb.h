@@ -1,0 +1,275 @@
+/*
+ * mcb.h -- C ABI of the B200 (sm_100a) implementation of MatcoreDSL's
+ * data-parallel hot path: strict f32 GEMM and fused GEMM pair, bf16 GEMM with
+ * a fused epilogue (Family A), matmul-softmax-matmul (Family C), the FP8
+ * block-scaled GEMM, and the attention-residual block region.
+ *
+ * Every entry point is extern "C", noexcept, takes plain pointers and sizes,
+ * and reports failure only through its return code. Each declaration names
+ * the MatcoreDSL interface (path:line in the MatcoreDSL repository) it
+ * replaces; the adapters a maintainer adds on the reference side are shown in
+ * INTEGRATION.md.
+ *
+ * Conventions
+ *  - Ownership: the caller owns every buffer. Operands may live in host
+ *    memory (MCB_MEMORY_HOST: the library stages them through device buffers
+ *    on the caller's stream and synchronises before returning) or in device
+ *    memory (MCB_MEMORY_CUDA_DEVICE: the call is asynchronous on the stream
+ *    unless MCB_EXEC_SYNC is set). All operands of one call must live in the
+ *    same memory space.
+ *  - Layout: dims and strides are in elements, row-major, innermost stride 1.
+ *  - Errors: all failures return a status; nothing throws across this
+ *    boundary. Device-side pipeline stalls are bounded: a kernel that waits
+ *    too long records a bit in the per-device status word and exits, and a
+ *    synchronous call then returns MCB_STATUS_DEVICE_TIMEOUT.
+ *  - Threading: calls on distinct streams are independent; the only global
+ *    state is a lazily created per-device context guarded by a mutex.
+ */
+#ifndef MCB_H
+#define MCB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__cplusplus)
+#define MCB_NOEXCEPT noexcept
+extern "C" {
+#else
+#define MCB_NOEXCEPT
+#endif
+
+#if defined(_WIN32)
+#define MCB_API
+#else
+#define MCB_API __attribute__((visibility("default")))
+#endif
+
+#define MCB_ABI_VERSION_V1 UINT32_C(1)
+#define MCB_MAX_RANK 4
+
+/* Status codes. 0-26 keep the numbering of MatcoreDSL's runtime C ABI
+ * (compiler/include/matcore/runtime_c.h:77-104); 40+ are device-side codes
+ * that mirror closed_host_v1::Code (compiler/include/matcore/detail/
+ * region_storage.h:16-21) where the meaning matches. */
+typedef int32_t mcb_status;
+enum {
+  MCB_STATUS_OK = 0,
+  MCB_STATUS_INVALID_ARGUMENT = 1,
+  MCB_STATUS_ABI_MISMATCH = 2,
+  MCB_STATUS_UNSUPPORTED_DTYPE = 3,
+  MCB_STATUS_UNSUPPORTED_RANK = 4,
+  MCB_STATUS_INVALID_SHAPE = 5,
+  MCB_STATUS_UNSUPPORTED_LAYOUT = 6,
+  MCB_STATUS_UNSUPPORTED_MEMORY_SPACE = 7,
+  MCB_STATUS_MIXED_MEMORY_SPACES = 8,
+  MCB_STATUS_OUTPUT_NOT_MUTABLE = 9,
+  MCB_STATUS_SHAPE_MISMATCH = 11,
+  MCB_STATUS_ALIAS_VIOLATION = 12,
+  MCB_STATUS_ARITHMETIC_OVERFLOW = 15,
+  MCB_STATUS_INVALID_ALIGNMENT = 16,
+  MCB_STATUS_INSUFFICIENT_WORKSPACE = 17,
+  MCB_STATUS_UNAVAILABLE_VARIANT = 18,
+  MCB_STATUS_ALLOCATION_FAILURE = 40,   /* Code::allocation_failure */
+  MCB_STATUS_CANDIDATE_FAILURE = 41,    /* Code::candidate_failure (CUDA error) */
+  MCB_STATUS_CANDIDATE_UNAVAILABLE = 42,/* Code::candidate_unavailable (no sm_100 GPU) */
+  MCB_STATUS_DEVICE_TIMEOUT = 43,       /* a bounded device-side wait expired */
+  MCB_STATUS_STALE_HANDLE = 44          /* device buffer handle freed or unknown */
+};
+
+/* Element types; 1-5 keep runtime_c.h:38-46 numbering. */
+typedef uint32_t mcb_dtype;
+enum {
+  MCB_DTYPE_INVALID = 0,
+  MCB_DTYPE_F32 = 1,
+  MCB_DTYPE_F64 = 2,
+  MCB_DTYPE_BF16 = 3,
+  MCB_DTYPE_I8 = 4,
+  MCB_DTYPE_I32 = 5,
+  MCB_DTYPE_F16 = 6,
+  MCB_DTYPE_E4M3 = 7, /* OCP float8 e4m3 ("fn": no Inf, max 448) */
+  MCB_DTYPE_E5M2 = 8  /* OCP float8 e5m2 (IEEE-style Inf/NaN, max 57344) */
+};
+
+typedef uint32_t mcb_memory_space;
+enum { MCB_MEMORY_INVALID = 0, MCB_MEMORY_HOST = 1, MCB_MEMORY_CUDA_DEVICE = 2 };
+
+/* Tensor descriptor; mirrors matcore_tensor_desc_v0
+ * (compiler/include/matcore/runtime_c.h:107-118) and RuntimeTensorView
+ * (include/matcore/kernel_ir.h:274-283). Set abi_version = MCB_ABI_VERSION_V1
+ * and struct_size = sizeof(mcb_tensor). */
+typedef struct mcb_tensor {
+  uint32_t abi_version;
+  uint32_t struct_size;
+  void *data;
+  mcb_dtype dtype;
+  uint32_t rank;
+  int64_t dims[MCB_MAX_RANK];
+  int64_t strides[MCB_MAX_RANK];
+  mcb_memory_space memory_space;
+  uint32_t reserved0;
+  uint64_t reserved[2];
+} mcb_tensor;
+
+/* Per-call report: which kernel ran and what it moved. Mirrors the roles of
+ * CompilationStats (include/matcore/jit_runner.h:13-21) and CandidateReport
+ * (compiler/lib/runtime/closed_host_v1.h:29-44). */
+typedef struct mcb_report {
+  uint32_t abi_version;
+  uint32_t struct_size;
+  char route[48];          /* e.g. "tcgen05_bf16_gemm_epilogue" */
+  int32_t kernel_launches; /* launches this call issued */
+  int32_t tile_m, tile_n, tile_k, stages, ctas;
+  float kernel_ms;         /* device time of the compute kernels (MCB_EXEC_TIME) */
+  float h2d_ms, d2h_ms;    /* staging copies (MCB_EXEC_TIME, host operands) */
+  uint64_t h2d_bytes, d2h_bytes;
+  uint32_t device_status;  /* device status word after a synchronous call */
+  uint32_t reserved0;
+} mcb_report;
+
+/* Execution context: device, stream and options for one call. */
+enum {
+  MCB_EXEC_SYNC = 1u << 0, /* synchronise the stream before returning */
+  MCB_EXEC_TIME = 1u << 1  /* fill report->kernel_ms / h2d_ms / d2h_ms (implies SYNC) */
+};
+typedef struct mcb_exec {
+  uint32_t abi_version;
+  uint32_t struct_size;
+  int32_t device;          /* CUDA ordinal, -1 = the calling thread's current device */
+  uint32_t flags;
+  void *stream;            /* cudaStream_t, NULL = the legacy default stream */
+  void *workspace;         /* optional device scratch supplied by the caller */
+  uint64_t workspace_bytes;
+  mcb_report *report;      /* optional */
+  uint64_t reserved[2];
+} mcb_exec;
+
+/* ---- library ------------------------------------------------------------ */
+MCB_API uint32_t mcb_abi_version(void) MCB_NOEXCEPT;
+MCB_API const char *mcb_status_message(mcb_status code) MCB_NOEXCEPT;
+/* Reads (and with clear != 0 resets) the device status word of `device`. */
+MCB_API mcb_status mcb_device_status(int32_t device, uint32_t *word, int32_t clear) MCB_NOEXCEPT;
+/* Ok when `device` is an sm_100 GPU this build can run on; replaces
+ * detail::cudaCandidateAvailable (compiler/lib/runtime/closed_cuda_candidate_v1.h:13). */
+MCB_API mcb_status mcb_candidate_available(int32_t device) MCB_NOEXCEPT;
+
+/* ---- strict f32 (bit-exact with the reference's strict leaf) ------------- */
+/* C = A*B with a separate binary32 multiply and add per step, increasing k,
+ * +0 seed (compiler/lib/runtime/closed_host_v1.cpp:401-415). Replaces
+ * detail::cudaGemmCandidate (compiler/lib/runtime/closed_cuda_candidate_v1.h:14). */
+MCB_API mcb_status mcb_strict_gemm_f32_v1(const mcb_tensor *c, const mcb_tensor *a,
+                                          const mcb_tensor *b, const mcb_exec *exec) MCB_NOEXCEPT;
+/* E = (A*B)*D with the intermediate rounded to binary32 and never written to
+ * the caller (compiler/lib/mlir/MatcoreCpuFusedGemmCandidate.h:19-31).
+ * Replaces detail::cudaFusedPairCandidate
+ * (compiler/lib/runtime/closed_cuda_candidate_v1.h:19-20). K may be 0 (E =
+ * +0*D, so Inf/NaN in D propagate); N = 0 gives E = +0. */
+MCB_API mcb_status mcb_strict_fused_pair_f32_v1(const mcb_tensor *e, const mcb_tensor *a,
+                                                const mcb_tensor *b, const mcb_tensor *d,
+                                                const mcb_exec *exec) MCB_NOEXCEPT;
+
+/* ---- Family A: GEMM + fused epilogue ------------------------------------ */
+enum { MCB_BIAS_NONE = 0, MCB_BIAS_ROW = 1 /* b[N] broadcast over rows */,
+       MCB_BIAS_FULL = 2 /* boundary [M,N] */ };
+enum { MCB_BIAS_ADD = 0 /* acc + b */, MCB_BIAS_RSUB = 1 /* b - acc */ };
+enum { MCB_ACT_NONE = 0, MCB_ACT_RELU = 1, MCB_ACT_GELU_TANH = 2, MCB_ACT_EXP = 3,
+       MCB_ACT_SIGMOID = 4, MCB_ACT_TANH = 5 };
+typedef struct mcb_epilogue {
+  uint32_t abi_version;
+  uint32_t struct_size;
+  uint32_t bias_mode;
+  uint32_t bias_op;
+  uint32_t activation;   /* applied after the bias */
+  uint32_t reserved0;
+  uint64_t reserved[2];
+} mcb_epilogue;
+/* Y = act(X*W (+|r-) bias). X [M,K], W [K,N] (row-major, "MN-major" B) or,
+ * with w given as [N,K] and rank-2 dims {N,K} plus MCB_GEMM_W_TRANSPOSED in
+ * flags, W^T. bf16 X/W run on tcgen05 tensor cores with an f32 TMEM
+ * accumulator; f32 X/W run on CUDA cores with f32 FMA accumulation. Output
+ * bf16 or f32. GELU is the tanh form of src/fusion_emitter_common.cpp:86-108.
+ * Replaces the Family A leaf emitted by FusionMlirEmitter::emitFamilyA
+ * (src/fusion_emitter_family_a.cpp:12-244) and reached through compileAndRun
+ * (include/matcore/jit_runner.h:23-26). */
+enum { MCB_GEMM_W_TRANSPOSED = 1u << 0 };
+MCB_API mcb_status mcb_gemm_epilogue_v1(const mcb_tensor *y, const mcb_tensor *x,
+                                        const mcb_tensor *w, const mcb_tensor *bias,
+                                        const mcb_epilogue *epilogue, uint32_t gemm_flags,
+                                        const mcb_exec *exec) MCB_NOEXCEPT;
+
+/* ---- Family C: matmul-softmax-matmul -------------------------------------- */
+/* O = softmax(scale * Q*K^T) * V per leading index. Q [.., M, Dqk],
+ * K [.., N, Dqk], V [.., N, Dv], O [.., M, Dv] with up to two leading
+ * (batch, head) dims. scale = 1 gives the reference's unscaled softmax
+ * (tests/test_family_c.py:102-113). bf16 with Dqk = Dv = 128 runs the tcgen05
+ * kernel (S and O in TMEM, online softmax, S never in HBM); other shapes and
+ * f32 run a CUDA-core online-softmax kernel. Replaces the kernel emitted by
+ * FusionMlirEmitter::emitFamilyC (src/fusion_emitter_family_c.cpp:13-596). */
+MCB_API mcb_status mcb_msm_v1(const mcb_tensor *o, const mcb_tensor *q, const mcb_tensor *k,
+                              const mcb_tensor *v, double scale,
+                              const mcb_exec *exec) MCB_NOEXCEPT;
+
+/* ---- FP8 block-scaled GEMM ------------------------------------------------ */
+/* Per-(block x block) absmax quantisation of an f32 or bf16 matrix:
+ * s = absmax/fmt_max (1 for an all-zero block), q = sat_RNE(x/s). scales is
+ * f32 [ceil(rows/block), ceil(cols/block)]. */
+MCB_API mcb_status mcb_fp8_quantize_blockwise_v1(const mcb_tensor *q, const mcb_tensor *scales,
+                                                 const mcb_tensor *x, int64_t block,
+                                                 const mcb_exec *exec) MCB_NOEXCEPT;
+/* C = (sa.A) * (sb.B)^T... precisely C[m,n] = sum_k sa[m/b,k/b] A[m,k] *
+ * sbt[n/b,k/b] Bt[n,k]: A [M,K] and Bt [N,K] are e4m3/e5m2 codes (K-major),
+ * fp32 accumulation, C bf16 or f32. Replaces the throwing
+ * runFp8WgmmaPreflight (src/lowering_pipeline.cpp:2531-2572). */
+MCB_API mcb_status mcb_gemm_fp8_blockscaled_v1(const mcb_tensor *c, const mcb_tensor *a,
+                                               const mcb_tensor *sa, const mcb_tensor *bt,
+                                               const mcb_tensor *sbt, int64_t block,
+                                               const mcb_exec *exec) MCB_NOEXCEPT;
+/* Tile policy of getFp8WgmmaTileConfig / isLegalFp8WgmmaShape
+ * (src/fp8_wgmma.cpp:10-24,61-109), kept for callers that query it. */
+typedef struct mcb_fp8_tile_config {
+  int32_t m_tile, n_tile, k_tile, use_tma;
+} mcb_fp8_tile_config;
+MCB_API int32_t mcb_fp8_is_legal_shape_v1(int64_t m, int64_t n, int64_t k) MCB_NOEXCEPT;
+MCB_API mcb_fp8_tile_config mcb_fp8_tile_config_v1(int64_t m, int64_t n,
+                                                   int64_t k) MCB_NOEXCEPT;
+
+/* ---- attention-residual block region ------------------------------------------- */
+/* Y = RMSNorm(X + Wo * MSM(X Wq, X Wk, X Wv)) with unit gain; X [B,S,D] bf16,
+ * W* [D,D] bf16, `heads` heads of D/heads, softmax scale (D/heads)^-0.5.
+ * Composed from the kernels above with device-resident intermediates in the
+ * caller's workspace (mcb_attn_block_workspace_bytes_v1). Named after the
+ * region path of RegionMlirEmitter (src/region_emitter_block_attn_res.cpp:38-432). */
+MCB_API uint64_t mcb_attn_block_workspace_bytes_v1(int64_t batch, int64_t seq,
+                                                   int64_t d_model) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_attn_block_region_v1(const mcb_tensor *y, const mcb_tensor *x,
+                                            const mcb_tensor *wq, const mcb_tensor *wk,
+                                            const mcb_tensor *wv, const mcb_tensor *wo,
+                                            int64_t heads, float eps,
+                                            const mcb_exec *exec) MCB_NOEXCEPT;
+
+/* ---- device buffers ------------------------------------------------------- */
+/* Ownership-tracked device memory; mirrors DeviceBufferHandle and the
+ * matcore_device_* functions (include/matcore/device_buffer.h:11-53): a
+ * monotonic alloc_id detects stale handles after free and reuse. */
+typedef struct mcb_buffer {
+  uint64_t ptr;
+  uint64_t size_bytes;
+  uint64_t alloc_id;
+  int32_t device;
+  uint32_t reserved0;
+} mcb_buffer;
+MCB_API mcb_status mcb_device_alloc(int32_t device, uint64_t size_bytes,
+                                    mcb_buffer *out) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_device_free(mcb_buffer handle) MCB_NOEXCEPT;
+MCB_API int32_t mcb_device_is_valid(mcb_buffer handle) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_device_upload(mcb_buffer dst, const void *host_src,
+                                     uint64_t size_bytes) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_device_download(void *host_dst, mcb_buffer src,
+                                       uint64_t size_bytes) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_device_zero(mcb_buffer handle) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_device_zero_raw_on_stream(void *device_ptr, uint64_t size_bytes,
+                                                 void *stream) MCB_NOEXCEPT;
+
+#if defined(__cplusplus)
+}
+#endif
+#endif /* MCB_H */

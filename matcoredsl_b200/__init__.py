@@ -1,0 +1,16 @@
+"""B200-native (sm_100a) implementation of MatcoreDSL's data-parallel hot path.
+
+The product is ``libmcb.so`` (hand-written CUDA kernels + C ABI, declared in
+``include/mcb.h``); this package builds it (``build.py``), mirrors its ABI in
+ctypes (``_abi.py``) and offers the reference's operator shapes on top
+(``api.py``). Importing the package loads the library and fails loudly when it
+is missing -- there is no CPU fallback.
+"""
+from . import _abi
+from ._abi import McbError, load
+from .api import (device_status, gemm_epilogue, msm, strict_fused_pair, strict_gemm)
+
+__all__ = ["McbError", "load", "strict_gemm", "strict_fused_pair", "gemm_epilogue", "msm",
+           "device_status"]
+
+load()

@@ -1,0 +1,174 @@
+"""Host-side mirror of MatcoreDSL's hot-path operators, over the C ABI.
+
+Each function takes numpy arrays (host memory: the library stages them on the
+GPU and returns when the result is back) or torch CUDA tensors (device
+memory: the call is queued on torch's current stream), builds the C
+descriptors of include/mcb.h and calls libmcb. There is no CPU compute here
+and no fallback: a missing library or a non-sm_100 device raises.
+
+Operator meanings follow the reference:
+  strict_gemm / strict_fused_pair  Session::gemm / Session::gemmStrictFusedPair
+                                   (compiler/lib/runtime/closed_host_v1.cpp)
+  gemm_epilogue                    @mc.fused Family A, act(A @ B (+|-) bias)
+                                   (src/fusion_emitter_family_a.cpp)
+  msm                              @mc.fused Family C, softmax(Q @ K.T) @ V
+                                   (src/fusion_emitter_family_c.cpp)
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _abi
+
+try:  # bf16 / fp8 numpy dtypes (optional for host-memory callers)
+    import ml_dtypes as _mld
+except ImportError:  # pragma: no cover
+    _mld = None
+
+_NP_DTYPE = {np.dtype(np.float32): "f32", np.dtype(np.float64): "f64",
+             np.dtype(np.int8): "i8", np.dtype(np.int32): "i32"}
+if _mld is not None:
+    _NP_DTYPE[np.dtype(_mld.bfloat16)] = "bf16"
+    _NP_DTYPE[np.dtype(_mld.float8_e4m3fn)] = "e4m3"
+    _NP_DTYPE[np.dtype(_mld.float8_e5m2)] = "e5m2"
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def _is_torch(x) -> bool:
+    return type(x).__module__.startswith("torch")
+
+
+def _desc(x, what: str):
+    """(Tensor descriptor, is_device) for a numpy array or a torch tensor."""
+    if _is_torch(x):
+        torch = _torch()
+        tmap = {torch.float32: "f32", torch.bfloat16: "bf16", torch.float16: "f16",
+                torch.int8: "i8", torch.int32: "i32", torch.float64: "f64",
+                torch.float8_e4m3fn: "e4m3", torch.float8_e5m2: "e5m2"}
+        if x.dtype not in tmap:
+            raise TypeError(f"{what}: unsupported torch dtype {x.dtype}")
+        return _abi.make_tensor(x.data_ptr(), tmap[x.dtype], x.shape, x.stride(), x.is_cuda), x.is_cuda
+    if isinstance(x, np.ndarray):
+        dt = _NP_DTYPE.get(x.dtype)
+        if dt is None:
+            raise TypeError(f"{what}: unsupported numpy dtype {x.dtype}")
+        strides = [s // x.itemsize for s in x.strides]
+        return _abi.make_tensor(x.ctypes.data, dt, x.shape, strides, False), False
+    raise TypeError(f"{what}: expected a numpy array or torch tensor, got {type(x)}")
+
+
+def _exec(device_call: bool, device: int, flags: int, report):
+    stream = 0
+    if device_call:
+        torch = _torch()
+        stream = torch.cuda.current_stream().cuda_stream
+        if device < 0:
+            device = torch.cuda.current_device()
+    return _abi.make_exec(device=device, stream=stream, flags=flags, report=report)
+
+
+def _empty_like_out(ref, shape, dtype_name):
+    if _is_torch(ref):
+        torch = _torch()
+        td = {"f32": torch.float32, "bf16": torch.bfloat16}[dtype_name]
+        return torch.empty(shape, dtype=td, device=ref.device)
+    nd = {"f32": np.float32, "bf16": (_mld.bfloat16 if _mld else None)}[dtype_name]
+    return np.empty(shape, dtype=nd)
+
+
+class Result:
+    """Route/launch report of the last call (mirrors get_compilation_stats)."""
+
+    def __init__(self, rep: _abi.Report):
+        self.route = rep.route.decode()
+        self.kernel_launches = rep.kernel_launches
+        self.tile = (rep.tile_m, rep.tile_n, rep.tile_k)
+        self.stages = rep.stages
+        self.ctas = rep.ctas
+        self.kernel_ms = rep.kernel_ms
+        self.h2d_ms, self.d2h_ms = rep.h2d_ms, rep.d2h_ms
+        self.h2d_bytes, self.d2h_bytes = rep.h2d_bytes, rep.d2h_bytes
+        self.device_status = rep.device_status
+
+
+last_result: Result | None = None
+
+
+def _call(fn_name, tensors, extra_args, device=-1, flags=0):
+    global last_result
+    lib = _abi.load()
+    descs, spaces = [], set()
+    for name, t in tensors:
+        if t is None:
+            descs.append(None)
+            continue
+        d, dev = _desc(t, name)
+        descs.append(d)
+        spaces.add(dev)
+    device_call = True in spaces
+    rep = _abi.make_report()
+    ex = _exec(device_call, device, flags, rep)
+    ptrs = [ctypes.byref(d) if d is not None else None for d in descs]
+    # Every entry point is fn(tensor..., extra..., exec).
+    code = getattr(lib, fn_name)(*ptrs, *extra_args, ctypes.byref(ex))
+    last_result = Result(rep)
+    _abi.check(code, fn_name)
+    return last_result
+
+
+def strict_gemm(a, b, out=None, *, device=-1, flags=0):
+    """C = A @ B with the reference's strict f32 arithmetic (bit-exact)."""
+    if out is None:
+        out = _empty_like_out(a, (a.shape[0], b.shape[1]), "f32")
+    _call("mcb_strict_gemm_f32_v1", [("c", out), ("a", a), ("b", b)], [], device, flags)
+    return out
+
+
+def strict_fused_pair(a, b, d, out=None, *, device=-1, flags=0, workspace=None):
+    """E = (A @ B) @ D, strict f32, intermediate rounded to f32 (bit-exact)."""
+    if out is None:
+        out = _empty_like_out(a, (a.shape[0], d.shape[1]), "f32")
+    _call("mcb_strict_fused_pair_f32_v1", [("e", out), ("a", a), ("b", b), ("d", d)], [],
+          device, flags)
+    return out
+
+
+def gemm_epilogue(x, w, bias=None, *, bias_mode=None, bias_op="add", act="none", out=None,
+                  out_dtype=None, w_transposed=False, device=-1, flags=0):
+    """Y = act(X @ W (+|r-) bias) (Family A). bias [N] broadcasts over rows;
+    bias [M,N] is the reference's exact-shape boundary."""
+    if bias_mode is None:
+        bias_mode = "none" if bias is None else ("full" if len(bias.shape) == 2 else "row")
+    n = w.shape[0] if w_transposed else w.shape[1]
+    if out is None:
+        if out_dtype is None:
+            out_dtype = "bf16" if str(getattr(x, "dtype", "")).endswith("bfloat16") else "f32"
+        out = _empty_like_out(x, (x.shape[0], n), out_dtype)
+    ep = _abi.make_epilogue(bias_mode, bias_op, act)
+    gflags = _abi.GEMM_W_TRANSPOSED if w_transposed else 0
+    _call("mcb_gemm_epilogue_v1", [("y", out), ("x", x), ("w", w), ("bias", bias)],
+          [ctypes.byref(ep), gflags], device, flags)
+    return out
+
+
+def msm(q, k, v, scale=1.0, out=None, *, device=-1, flags=0):
+    """O = softmax(scale * Q @ K^T) @ V over the last two dims (Family C)."""
+    if out is None:
+        shape = tuple(q.shape[:-1]) + (v.shape[-1],)
+        dt = "bf16" if str(q.dtype).endswith("bfloat16") else "f32"
+        out = _empty_like_out(q, shape, dt)
+    _call("mcb_msm_v1", [("o", out), ("q", q), ("k", k), ("v", v)], [float(scale)], device, flags)
+    return out
+
+
+def device_status(device=0, clear=False) -> int:
+    w = ctypes.c_uint32(0)
+    _abi.check(_abi.load().mcb_device_status(device, ctypes.byref(w), 1 if clear else 0),
+               "mcb_device_status")
+    return int(w.value)

@@ -1,0 +1,872 @@
+// C-ABI implementation of include/mcb.h: argument validation, per-device
+// context, staging of host-resident operands, dispatch to the kernels, and
+// the ownership-tracked device-buffer registry.
+//
+// Nothing in this file computes results on the CPU: when no sm_100 GPU is
+// usable every compute entry point returns MCB_STATUS_CANDIDATE_UNAVAILABLE.
+#include "mcb.h"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <unordered_map>
+#include <vector>
+
+#include "internal.h"
+
+namespace mcb {
+
+// ---- tensor maps --------------------------------------------------------------
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+std::once_flag g_encode_once;
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  std::call_once(g_encode_once, [] {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode_tiled;
+}
+}  // namespace
+
+bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base,
+                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                    uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  auto fn = encoder();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool encode_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base, uint64_t d0,
+                    uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes,
+                    uint32_t box0, uint32_t box1, uint32_t box2, CUtensorMapSwizzle swizzle) {
+  auto fn = encoder();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {box0, box1, box2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace mcb
+
+namespace {
+
+using mcb::LaunchInfo;
+
+constexpr int kMaxDevices = 64;
+constexpr int kStageSlots = 8;
+
+// Lazily created per-device state: SM count, the device status word and the
+// grow-only staging buffers used for host-resident operands.
+struct DeviceCtx {
+  std::mutex mu;
+  bool ready = false;
+  bool usable = false;  // an sm_100 part
+  int sms = 0;
+  int smem_optin = 0;
+  uint32_t *status = nullptr;
+  void *stage[kStageSlots] = {};
+  size_t stage_cap[kStageSlots] = {};
+};
+DeviceCtx g_dev[kMaxDevices];
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  bool switched = false;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) {
+      switched = cudaSetDevice(dev) == cudaSuccess;
+    }
+  }
+  ~DeviceGuard() {
+    if (switched) cudaSetDevice(prev);
+  }
+};
+
+mcb_status init_ctx(int dev, DeviceCtx **out) {
+  if (dev < 0 || dev >= kMaxDevices) return MCB_STATUS_INVALID_ARGUMENT;
+  DeviceCtx &c = g_dev[dev];
+  std::lock_guard<std::mutex> lock(c.mu);
+  if (!c.ready) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
+    c.usable = prop.major == 10 && prop.minor == 0;
+    c.sms = prop.multiProcessorCount;
+    c.smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+    if (c.usable) {
+      DeviceGuard g(dev);
+      if (cudaMalloc(&c.status, sizeof(uint32_t)) != cudaSuccess) return MCB_STATUS_ALLOCATION_FAILURE;
+      if (cudaMemset(c.status, 0, sizeof(uint32_t)) != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
+    }
+    c.ready = true;
+  }
+  if (!c.usable) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
+  *out = &c;
+  return MCB_STATUS_OK;
+}
+
+mcb_status resolve_device(const mcb_exec *exec, int *dev) {
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    return MCB_STATUS_CANDIDATE_UNAVAILABLE;
+  }
+  int d = exec ? exec->device : -1;
+  if (d < 0 && cudaGetDevice(&d) != cudaSuccess) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
+  if (d >= count) return MCB_STATUS_INVALID_ARGUMENT;
+  *dev = d;
+  return MCB_STATUS_OK;
+}
+
+size_t dtype_size(mcb_dtype t) {
+  switch (t) {
+    case MCB_DTYPE_F32: case MCB_DTYPE_I32: return 4;
+    case MCB_DTYPE_F64: return 8;
+    case MCB_DTYPE_BF16: case MCB_DTYPE_F16: return 2;
+    case MCB_DTYPE_I8: case MCB_DTYPE_E4M3: case MCB_DTYPE_E5M2: return 1;
+    default: return 0;
+  }
+}
+
+// Structural checks common to every tensor argument.
+mcb_status check_tensor(const mcb_tensor *t, uint32_t min_rank, uint32_t max_rank) {
+  if (!t) return MCB_STATUS_INVALID_ARGUMENT;
+  if (t->abi_version != MCB_ABI_VERSION_V1 || t->struct_size < sizeof(mcb_tensor))
+    return MCB_STATUS_ABI_MISMATCH;
+  if (t->rank < min_rank || t->rank > max_rank) return MCB_STATUS_UNSUPPORTED_RANK;
+  if (dtype_size(t->dtype) == 0) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  if (t->memory_space != MCB_MEMORY_HOST && t->memory_space != MCB_MEMORY_CUDA_DEVICE)
+    return MCB_STATUS_UNSUPPORTED_MEMORY_SPACE;
+  int64_t elems = 1;
+  for (uint32_t i = 0; i < t->rank; ++i) {
+    if (t->dims[i] < 0) return MCB_STATUS_INVALID_SHAPE;
+    if (t->dims[i] != 0 && elems > INT64_MAX / t->dims[i]) return MCB_STATUS_ARITHMETIC_OVERFLOW;
+    elems *= t->dims[i];
+  }
+  if (elems > 0) {
+    if (!t->data) return MCB_STATUS_INVALID_ARGUMENT;
+    if (t->strides[t->rank - 1] != 1) return MCB_STATUS_UNSUPPORTED_LAYOUT;
+    // Outer strides must step over a whole inner slice (row-major, no
+    // self-overlap); a dimension of extent 1 may carry any stride.
+    for (int i = static_cast<int>(t->rank) - 2; i >= 0; --i)
+      if (t->dims[i] > 1 && t->strides[i] < t->dims[i + 1] * t->strides[i + 1])
+        return MCB_STATUS_UNSUPPORTED_LAYOUT;
+    if (reinterpret_cast<uintptr_t>(t->data) % dtype_size(t->dtype) != 0)
+      return MCB_STATUS_INVALID_ALIGNMENT;
+  }
+  return MCB_STATUS_OK;
+}
+
+int64_t numel(const mcb_tensor *t) {
+  int64_t e = 1;
+  for (uint32_t i = 0; i < t->rank; ++i) e *= t->dims[i];
+  return e;
+}
+
+// Bytes spanned by a (possibly strided) tensor, from its base pointer.
+uint64_t span_bytes(const mcb_tensor *t) {
+  if (numel(t) == 0) return 0;
+  int64_t last = 0;
+  for (uint32_t i = 0; i < t->rank; ++i) last += (t->dims[i] - 1) * t->strides[i];
+  return static_cast<uint64_t>(last + 1) * dtype_size(t->dtype);
+}
+
+bool overlaps(const mcb_tensor *a, const mcb_tensor *b) {
+  if (!a || !b || numel(a) == 0 || numel(b) == 0) return false;
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(a->data), a1 = a0 + span_bytes(a);
+  const uintptr_t b0 = reinterpret_cast<uintptr_t>(b->data), b1 = b0 + span_bytes(b);
+  return a0 < b1 && b0 < a1;
+}
+
+mcb_status check_exec(const mcb_exec *exec) {
+  if (!exec) return MCB_STATUS_OK;
+  if (exec->abi_version != MCB_ABI_VERSION_V1 || exec->struct_size < sizeof(mcb_exec))
+    return MCB_STATUS_ABI_MISMATCH;
+  if (exec->report && (exec->report->abi_version != MCB_ABI_VERSION_V1 ||
+                       exec->report->struct_size < sizeof(mcb_report)))
+    return MCB_STATUS_ABI_MISMATCH;
+  return MCB_STATUS_OK;
+}
+
+mcb_status from_cuda(cudaError_t e) {
+  if (e == cudaSuccess) return MCB_STATUS_OK;
+  if (e == cudaErrorMemoryAllocation) return MCB_STATUS_ALLOCATION_FAILURE;
+  if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver ||
+      e == cudaErrorNoKernelImageForDevice)
+    return MCB_STATUS_CANDIDATE_UNAVAILABLE;
+  return MCB_STATUS_CANDIDATE_FAILURE;
+}
+
+// One call: resolves the device, owns the staging of host operands and the
+// optional timing, and finishes with the synchronisation/status checks.
+class Call {
+ public:
+  explicit Call(const mcb_exec *exec) : exec_(exec) {}
+  ~Call() {
+    for (auto &e : events_)
+      if (e) cudaEventDestroy(e);
+    if (lock_.owns_lock()) lock_.unlock();
+    delete guard_;
+  }
+
+  mcb_status begin(bool host_operands) {
+    mcb_status s = check_exec(exec_);
+    if (s) return s;
+    s = resolve_device(exec_, &dev_);
+    if (s) return s;
+    guard_ = new (std::nothrow) DeviceGuard(dev_);
+    if (!guard_) return MCB_STATUS_ALLOCATION_FAILURE;
+    s = init_ctx(dev_, &ctx_);
+    if (s) return s;
+    stream_ = exec_ ? static_cast<cudaStream_t>(exec_->stream) : nullptr;
+    host_ = host_operands;
+    timed_ = exec_ && (exec_->flags & MCB_EXEC_TIME);
+    sync_ = host_ || timed_ || (exec_ && (exec_->flags & MCB_EXEC_SYNC));
+    if (host_) lock_ = std::unique_lock<std::mutex>(ctx_->mu);  // staging slots are per device
+    if (timed_) {
+      for (auto &e : events_)
+        if (cudaEventCreate(&e) != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
+      cudaEventRecord(events_[0], stream_);
+    }
+    return MCB_STATUS_OK;
+  }
+
+  // Device pointer for an operand: itself when device-resident, else a
+  // staging buffer (uploaded when `upload`).
+  mcb_status device_ptr(const mcb_tensor *t, bool upload, void **out) {
+    if (!t || numel(t) == 0) {
+      *out = t ? t->data : nullptr;
+      return MCB_STATUS_OK;
+    }
+    if (t->memory_space == MCB_MEMORY_CUDA_DEVICE) {
+      *out = t->data;
+      return MCB_STATUS_OK;
+    }
+    if (slot_ >= kStageSlots) return MCB_STATUS_INSUFFICIENT_WORKSPACE;
+    const size_t bytes = span_bytes(t);
+    const int s = slot_++;
+    if (ctx_->stage_cap[s] < bytes) {
+      if (ctx_->stage[s]) {
+        cudaStreamSynchronize(stream_);
+        cudaFree(ctx_->stage[s]);
+        ctx_->stage[s] = nullptr;
+        ctx_->stage_cap[s] = 0;
+      }
+      const size_t cap = std::max<size_t>(bytes, 1 << 20);
+      if (cudaMalloc(&ctx_->stage[s], cap) != cudaSuccess) return MCB_STATUS_ALLOCATION_FAILURE;
+      ctx_->stage_cap[s] = cap;
+    }
+    *out = ctx_->stage[s];
+    if (upload) {
+      if (cudaMemcpyAsync(*out, t->data, bytes, cudaMemcpyHostToDevice, stream_) != cudaSuccess)
+        return MCB_STATUS_CANDIDATE_FAILURE;
+      h2d_bytes_ += bytes;
+    }
+    return MCB_STATUS_OK;
+  }
+
+  // Device scratch for a kernel: the caller's workspace when it is large
+  // enough, else a staging slot. A staging slot is shared by later calls on
+  // this device, so using one forces this call to synchronise before return.
+  mcb_status scratch(uint64_t bytes, void **out) {
+    if (exec_ && exec_->workspace && exec_->workspace_bytes >= bytes) {
+      *out = exec_->workspace;
+      return MCB_STATUS_OK;
+    }
+    if (!lock_.owns_lock()) lock_ = std::unique_lock<std::mutex>(ctx_->mu);
+    sync_ = true;
+    mcb_tensor tmp{};
+    tmp.abi_version = MCB_ABI_VERSION_V1;
+    tmp.struct_size = sizeof(mcb_tensor);
+    tmp.data = reinterpret_cast<void *>(16);
+    tmp.dtype = MCB_DTYPE_I8;
+    tmp.rank = 1;
+    tmp.dims[0] = static_cast<int64_t>(bytes);
+    tmp.strides[0] = 1;
+    tmp.memory_space = MCB_MEMORY_HOST;
+    return device_ptr(&tmp, false, out);
+  }
+
+  void mark_compute_start() {
+    if (timed_) cudaEventRecord(events_[1], stream_);
+  }
+  void mark_compute_end() {
+    if (timed_) cudaEventRecord(events_[2], stream_);
+  }
+
+  // Copies a staged output back, synchronises and checks the status word.
+  mcb_status finish(const mcb_tensor *out, void *dev_out, const LaunchInfo &info,
+                    cudaError_t launch_err) {
+    if (launch_err != cudaSuccess) return from_cuda(launch_err);
+    if (out && host_ && numel(out) > 0) {
+      const size_t bytes = span_bytes(out);
+      if (cudaMemcpyAsync(out->data, dev_out, bytes, cudaMemcpyDeviceToHost, stream_) !=
+          cudaSuccess)
+        return MCB_STATUS_CANDIDATE_FAILURE;
+      d2h_bytes_ += bytes;
+    }
+    if (timed_) cudaEventRecord(events_[3], stream_);
+    uint32_t word = 0;
+    if (sync_) {
+      cudaError_t e = cudaStreamSynchronize(stream_);
+      if (e != cudaSuccess) return from_cuda(e);
+      if (cudaMemcpy(&word, ctx_->status, sizeof(word), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return MCB_STATUS_CANDIDATE_FAILURE;
+    }
+    if (exec_ && exec_->report) {
+      mcb_report *r = exec_->report;
+      std::memcpy(r->route, info.route, sizeof(r->route));
+      r->kernel_launches = info.launches;
+      r->tile_m = info.tile_m;
+      r->tile_n = info.tile_n;
+      r->tile_k = info.tile_k;
+      r->stages = info.stages;
+      r->ctas = info.ctas;
+      r->h2d_bytes = h2d_bytes_;
+      r->d2h_bytes = d2h_bytes_;
+      r->device_status = word;
+      r->kernel_ms = r->h2d_ms = r->d2h_ms = 0.0f;
+      if (timed_) {
+        cudaEventElapsedTime(&r->h2d_ms, events_[0], events_[1]);
+        cudaEventElapsedTime(&r->kernel_ms, events_[1], events_[2]);
+        cudaEventElapsedTime(&r->d2h_ms, events_[2], events_[3]);
+      }
+    }
+    if (word != 0) return MCB_STATUS_DEVICE_TIMEOUT;
+    return MCB_STATUS_OK;
+  }
+
+  DeviceCtx *ctx() const { return ctx_; }
+  cudaStream_t stream() const { return stream_; }
+  int sms() const { return ctx_->sms; }
+  const mcb_exec *exec() const { return exec_; }
+
+ private:
+  const mcb_exec *exec_;
+  int dev_ = -1;
+  DeviceGuard *guard_ = nullptr;
+  DeviceCtx *ctx_ = nullptr;
+  cudaStream_t stream_ = nullptr;
+  bool host_ = false, timed_ = false, sync_ = false;
+  std::unique_lock<std::mutex> lock_;
+  cudaEvent_t events_[4] = {};
+  int slot_ = 0;
+  uint64_t h2d_bytes_ = 0, d2h_bytes_ = 0;
+};
+
+// All operands of one call must share one memory space.
+mcb_status same_space(std::initializer_list<const mcb_tensor *> ts, bool *host) {
+  int space = 0;
+  for (const mcb_tensor *t : ts) {
+    if (!t) continue;
+    if (space == 0) space = static_cast<int>(t->memory_space);
+    else if (space != static_cast<int>(t->memory_space)) return MCB_STATUS_MIXED_MEMORY_SPACES;
+  }
+  *host = space == MCB_MEMORY_HOST;
+  return MCB_STATUS_OK;
+}
+
+mcb_status guarded(mcb_status (*fn)(void *), void *arg) noexcept {
+  try {
+    return fn(arg);
+  } catch (const std::bad_alloc &) {
+    return MCB_STATUS_ALLOCATION_FAILURE;
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+// ---- strict ---------------------------------------------------------------------
+mcb_status strict_gemm_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_tensor *b,
+                            const mcb_exec *exec) {
+  mcb_status s;
+  if ((s = check_tensor(a, 2, 2)) || (s = check_tensor(b, 2, 2)) || (s = check_tensor(c, 2, 2)))
+    return s;
+  if (a->dtype != MCB_DTYPE_F32 || b->dtype != MCB_DTYPE_F32 || c->dtype != MCB_DTYPE_F32)
+    return MCB_STATUS_UNSUPPORTED_DTYPE;
+  const int64_t m = a->dims[0], k = a->dims[1], n = b->dims[1];
+  if (b->dims[0] != k || c->dims[0] != m || c->dims[1] != n) return MCB_STATUS_SHAPE_MISMATCH;
+  if (overlaps(c, a) || overlaps(c, b)) return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({a, b, c}, &host))) return s;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  void *da, *db, *dc;
+  if ((s = call.device_ptr(a, true, &da)) || (s = call.device_ptr(b, true, &db)) ||
+      (s = call.device_ptr(c, false, &dc)))
+    return s;
+  LaunchInfo info;
+  call.mark_compute_start();
+  cudaError_t e = mcb::launch_strict_gemm(
+      static_cast<const float *>(da), static_cast<const float *>(db), static_cast<float *>(dc), m,
+      k, n, a->strides[0], b->strides[0], c->strides[0], call.sms(), call.stream(), &info);
+  call.mark_compute_end();
+  return call.finish(c, dc, info, e);
+}
+
+mcb_status strict_pair_impl(const mcb_tensor *e, const mcb_tensor *a, const mcb_tensor *b,
+                            const mcb_tensor *d, const mcb_exec *exec) {
+  mcb_status s;
+  if ((s = check_tensor(a, 2, 2)) || (s = check_tensor(b, 2, 2)) || (s = check_tensor(d, 2, 2)) ||
+      (s = check_tensor(e, 2, 2)))
+    return s;
+  if (a->dtype != MCB_DTYPE_F32 || b->dtype != MCB_DTYPE_F32 || d->dtype != MCB_DTYPE_F32 ||
+      e->dtype != MCB_DTYPE_F32)
+    return MCB_STATUS_UNSUPPORTED_DTYPE;
+  const int64_t m = a->dims[0], k = a->dims[1], n = b->dims[1], p = d->dims[1];
+  if (b->dims[0] != k || d->dims[0] != n || e->dims[0] != m || e->dims[1] != p)
+    return MCB_STATUS_SHAPE_MISMATCH;
+  if (overlaps(e, a) || overlaps(e, b) || overlaps(e, d)) return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({a, b, d, e}, &host))) return s;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  void *da, *db, *dd, *de;
+  if ((s = call.device_ptr(a, true, &da)) || (s = call.device_ptr(b, true, &db)) ||
+      (s = call.device_ptr(d, true, &dd)) || (s = call.device_ptr(e, false, &de)))
+    return s;
+  // The intermediate panel lives in shared memory when it fits; otherwise it
+  // needs scratch, taken from the caller's workspace or a staging slot.
+  const int smem_limit = call.ctx()->smem_optin;
+  const int64_t scratch_floats = mcb::strict_pair_scratch_floats(m, n, call.sms(), smem_limit);
+  void *scratch = nullptr;
+  if (scratch_floats > 0 &&
+      (s = call.scratch(static_cast<uint64_t>(scratch_floats) * 4, &scratch)))
+    return s;
+  LaunchInfo info;
+  call.mark_compute_start();
+  cudaError_t err = mcb::launch_strict_pair(
+      static_cast<const float *>(da), static_cast<const float *>(db),
+      static_cast<const float *>(dd), static_cast<float *>(de), static_cast<float *>(scratch), m,
+      k, n, p, k ? a->strides[0] : 0, n ? b->strides[0] : 0, p ? d->strides[0] : 0,
+      e->strides[0], call.sms(), smem_limit, call.stream(), &info);
+  call.mark_compute_end();
+  return call.finish(e, de, info, err);
+}
+
+// ---- Family A -------------------------------------------------------------------------
+mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mcb_tensor *w,
+                              const mcb_tensor *bias, const mcb_epilogue *epi,
+                              uint32_t gemm_flags, const mcb_exec *exec) {
+  mcb_status s;
+  if ((s = check_tensor(x, 2, 2)) || (s = check_tensor(w, 2, 2)) || (s = check_tensor(y, 2, 2)))
+    return s;
+  mcb::Epilogue ep;
+  if (epi) {
+    if (epi->abi_version != MCB_ABI_VERSION_V1 || epi->struct_size < sizeof(mcb_epilogue))
+      return MCB_STATUS_ABI_MISMATCH;
+    if (epi->bias_mode > MCB_BIAS_FULL || epi->bias_op > MCB_BIAS_RSUB ||
+        epi->activation > MCB_ACT_TANH)
+      return MCB_STATUS_INVALID_ARGUMENT;
+    ep.bias_mode = static_cast<int>(epi->bias_mode);
+    ep.bias_op = static_cast<int>(epi->bias_op);
+    ep.act = static_cast<int>(epi->activation);
+  }
+  const bool wt = (gemm_flags & MCB_GEMM_W_TRANSPOSED) != 0;
+  const int64_t m = x->dims[0], k = x->dims[1];
+  const int64_t n = wt ? w->dims[0] : w->dims[1];
+  if ((wt ? w->dims[1] : w->dims[0]) != k || y->dims[0] != m || y->dims[1] != n)
+    return MCB_STATUS_SHAPE_MISMATCH;
+  const bool in_bf16 = x->dtype == MCB_DTYPE_BF16 && w->dtype == MCB_DTYPE_BF16;
+  const bool in_f32 = x->dtype == MCB_DTYPE_F32 && w->dtype == MCB_DTYPE_F32;
+  if (!in_bf16 && !in_f32) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  if (y->dtype != MCB_DTYPE_BF16 && y->dtype != MCB_DTYPE_F32) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  if (ep.bias_mode != MCB_BIAS_NONE) {
+    if ((s = check_tensor(bias, 1, 2))) return s;
+    if (bias->dtype != MCB_DTYPE_BF16 && bias->dtype != MCB_DTYPE_F32)
+      return MCB_STATUS_UNSUPPORTED_DTYPE;
+    if (ep.bias_mode == MCB_BIAS_ROW &&
+        !(numel(bias) == n && (bias->rank == 1 || bias->dims[0] == 1)))
+      return MCB_STATUS_SHAPE_MISMATCH;
+    if (ep.bias_mode == MCB_BIAS_FULL &&
+        !(bias->rank == 2 && bias->dims[0] == m && bias->dims[1] == n))
+      return MCB_STATUS_SHAPE_MISMATCH;
+    ep.bias_bf16 = bias->dtype == MCB_DTYPE_BF16;
+    ep.ld_bias = bias->rank == 2 ? bias->strides[0] : n;
+  }
+  if (overlaps(y, x) || overlaps(y, w) || (ep.bias_mode && overlaps(y, bias)))
+    return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({x, w, y, ep.bias_mode ? bias : nullptr}, &host))) return s;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  void *dx, *dw, *dy, *db = nullptr;
+  if ((s = call.device_ptr(x, true, &dx)) || (s = call.device_ptr(w, true, &dw)) ||
+      (s = call.device_ptr(y, false, &dy)))
+    return s;
+  if (ep.bias_mode && (s = call.device_ptr(bias, true, &db))) return s;
+  ep.bias = db;
+  ep.bias_aligned16 = (reinterpret_cast<uintptr_t>(db) & 15u) == 0;
+  LaunchInfo info;
+  cudaError_t err;
+  const int64_t ld_x = x->strides[0], ld_w = w->strides[0], ld_y = y->strides[0];
+  // Tensor-core eligibility: TMA wants 16-byte aligned bases and row strides.
+  const bool tma_ok = in_bf16 && k > 0 && (k % 8 == 0) && (ld_x % 8 == 0) && (ld_w % 8 == 0) &&
+                      (wt || n % 8 == 0) && (reinterpret_cast<uintptr_t>(dx) % 16 == 0) &&
+                      (reinterpret_cast<uintptr_t>(dw) % 16 == 0) &&
+                      (reinterpret_cast<uintptr_t>(dy) % 16 == 0) &&
+                      (ld_y % (y->dtype == MCB_DTYPE_BF16 ? 8 : 4) == 0);
+  call.mark_compute_start();
+  if (tma_ok) {
+    err = mcb::launch_gemm_tc_bf16(dx, dw, dy, m, n, k, ld_x, ld_w, ld_y, wt ? 1 : 0,
+                                   y->dtype == MCB_DTYPE_BF16 ? 1 : 0, ep, call.ctx()->status,
+                                   call.sms(), call.stream(), &info);
+  } else {
+    err = mcb::launch_gemm_simt(dx, static_cast<int>(x->dtype), dw, static_cast<int>(w->dtype),
+                                dy, static_cast<int>(y->dtype), m, n, k, ld_x, ld_w, ld_y,
+                                wt ? 1 : 0, ep, call.stream(), &info);
+  }
+  call.mark_compute_end();
+  return call.finish(y, dy, info, err);
+}
+
+// ---- Family C -----------------------------------------------------------------------------
+constexpr bool kHaveMsmTc = false;
+
+mcb_status msm_impl(const mcb_tensor *o, const mcb_tensor *q, const mcb_tensor *k,
+                    const mcb_tensor *v, double scale, const mcb_exec *exec) {
+  mcb_status s;
+  if ((s = check_tensor(q, 2, 4)) || (s = check_tensor(k, 2, 4)) || (s = check_tensor(v, 2, 4)) ||
+      (s = check_tensor(o, 2, 4)))
+    return s;
+  const uint32_t r = q->rank;
+  if (k->rank != r || v->rank != r || o->rank != r) return MCB_STATUS_SHAPE_MISMATCH;
+  if (q->dtype != k->dtype || q->dtype != v->dtype || q->dtype != o->dtype)
+    return MCB_STATUS_UNSUPPORTED_DTYPE;
+  if (q->dtype != MCB_DTYPE_BF16 && q->dtype != MCB_DTYPE_F32) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  mcb::MsmShape sh;
+  sh.m = q->dims[r - 2];
+  sh.dqk = q->dims[r - 1];
+  sh.n = k->dims[r - 2];
+  sh.dv = v->dims[r - 1];
+  if (k->dims[r - 1] != sh.dqk || v->dims[r - 2] != sh.n || o->dims[r - 2] != sh.m ||
+      o->dims[r - 1] != sh.dv)
+    return MCB_STATUS_SHAPE_MISMATCH;
+  for (uint32_t i = 0; i + 2 < r; ++i)
+    if (k->dims[i] != q->dims[i] || v->dims[i] != q->dims[i] || o->dims[i] != q->dims[i])
+      return MCB_STATUS_SHAPE_MISMATCH;
+  sh.batch = r == 4 ? q->dims[0] : 1;
+  sh.heads = r >= 3 ? q->dims[r - 3] : 1;
+  auto fill = [&](const mcb_tensor *t, int64_t *st) {
+    st[0] = r == 4 ? t->strides[0] : 0;
+    st[1] = r >= 3 ? t->strides[r - 3] : 0;
+    st[2] = t->strides[r - 2];
+  };
+  fill(q, sh.q_s);
+  fill(k, sh.k_s);
+  fill(v, sh.v_s);
+  fill(o, sh.o_s);
+  if (sh.n == 0) return MCB_STATUS_INVALID_SHAPE;  // softmax over zero keys is undefined
+  if (!std::isfinite(scale)) return MCB_STATUS_INVALID_ARGUMENT;
+  if (overlaps(o, q) || overlaps(o, k) || overlaps(o, v)) return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({q, k, v, o}, &host))) return s;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  void *dq, *dk, *dv, *dout;
+  if ((s = call.device_ptr(q, true, &dq)) || (s = call.device_ptr(k, true, &dk)) ||
+      (s = call.device_ptr(v, true, &dv)) || (s = call.device_ptr(o, false, &dout)))
+    return s;
+  LaunchInfo info;
+  cudaError_t err;
+  call.mark_compute_start();
+  const bool tc_ok = kHaveMsmTc && q->dtype == MCB_DTYPE_BF16 && sh.dqk == 128 && sh.dv == 128 &&
+                     sh.m % 128 == 0 && sh.n % 128 == 0 &&
+                     sh.q_s[2] % 8 == 0 && sh.k_s[2] % 8 == 0 && sh.v_s[2] % 8 == 0 &&
+                     sh.o_s[2] % 8 == 0 && sh.q_s[0] % 8 == 0 && sh.q_s[1] % 8 == 0 &&
+                     sh.k_s[0] % 8 == 0 && sh.k_s[1] % 8 == 0 && sh.v_s[0] % 8 == 0 &&
+                     sh.v_s[1] % 8 == 0 && (reinterpret_cast<uintptr_t>(dq) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(dk) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(dv) % 16 == 0) &&
+                     (reinterpret_cast<uintptr_t>(dout) % 16 == 0);
+  if (tc_ok) {
+    err = mcb::launch_msm_tc_bf16(dq, dk, dv, dout, sh, static_cast<float>(scale),
+                                  call.ctx()->status, call.sms(), call.stream(), &info);
+  } else {
+    if (sh.dqk > 256 || sh.dv > 256) return MCB_STATUS_UNAVAILABLE_VARIANT;
+    err = mcb::launch_msm_simt(dq, dk, dv, dout, static_cast<int>(q->dtype), sh,
+                               static_cast<float>(scale), call.stream(), &info);
+  }
+  call.mark_compute_end();
+  return call.finish(o, dout, info, err);
+}
+
+// ---- device buffers ------------------------------------------------------------------------
+std::mutex g_buf_mu;
+std::unordered_map<uint64_t, mcb_buffer> g_bufs;  // ptr -> live handle
+std::atomic<uint64_t> g_next_alloc_id{1};
+
+bool live(const mcb_buffer &h) {
+  auto it = g_bufs.find(h.ptr);
+  return it != g_bufs.end() && it->second.alloc_id == h.alloc_id &&
+         it->second.size_bytes == h.size_bytes && it->second.device == h.device;
+}
+
+}  // namespace
+
+// =====================================================================================
+extern "C" {
+
+MCB_API uint32_t mcb_abi_version(void) noexcept { return MCB_ABI_VERSION_V1; }
+
+MCB_API const char *mcb_status_message(mcb_status code) noexcept {
+  switch (code) {
+    case MCB_STATUS_OK: return "ok";
+    case MCB_STATUS_INVALID_ARGUMENT: return "invalid argument";
+    case MCB_STATUS_ABI_MISMATCH: return "ABI version or struct size mismatch";
+    case MCB_STATUS_UNSUPPORTED_DTYPE: return "unsupported dtype";
+    case MCB_STATUS_UNSUPPORTED_RANK: return "unsupported rank";
+    case MCB_STATUS_INVALID_SHAPE: return "invalid shape";
+    case MCB_STATUS_UNSUPPORTED_LAYOUT: return "unsupported layout (innermost stride must be 1)";
+    case MCB_STATUS_UNSUPPORTED_MEMORY_SPACE: return "unsupported memory space";
+    case MCB_STATUS_MIXED_MEMORY_SPACES: return "operands live in different memory spaces";
+    case MCB_STATUS_OUTPUT_NOT_MUTABLE: return "output not mutable";
+    case MCB_STATUS_SHAPE_MISMATCH: return "shape mismatch";
+    case MCB_STATUS_ALIAS_VIOLATION: return "output overlaps an input";
+    case MCB_STATUS_ARITHMETIC_OVERFLOW: return "extent overflow";
+    case MCB_STATUS_INVALID_ALIGNMENT: return "invalid alignment";
+    case MCB_STATUS_INSUFFICIENT_WORKSPACE: return "insufficient workspace";
+    case MCB_STATUS_UNAVAILABLE_VARIANT: return "no kernel variant for this shape/dtype";
+    case MCB_STATUS_ALLOCATION_FAILURE: return "device allocation failed";
+    case MCB_STATUS_CANDIDATE_FAILURE: return "CUDA error during execution";
+    case MCB_STATUS_CANDIDATE_UNAVAILABLE: return "no usable sm_100 GPU";
+    case MCB_STATUS_DEVICE_TIMEOUT: return "a device-side wait timed out (see mcb_device_status)";
+    case MCB_STATUS_STALE_HANDLE: return "stale or unknown device buffer handle";
+    default: return "unknown status";
+  }
+}
+
+MCB_API mcb_status mcb_device_status(int32_t device, uint32_t *word, int32_t clear) noexcept {
+  if (!word) return MCB_STATUS_INVALID_ARGUMENT;
+  mcb_exec ex{};
+  ex.abi_version = MCB_ABI_VERSION_V1;
+  ex.struct_size = sizeof(ex);
+  ex.device = device;
+  int dev;
+  mcb_status s = resolve_device(&ex, &dev);
+  if (s) return s;
+  DeviceGuard g(dev);
+  DeviceCtx *c;
+  if ((s = init_ctx(dev, &c))) return s;
+  if (cudaMemcpy(word, c->status, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  if (clear && cudaMemset(c->status, 0, 4) != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
+  return MCB_STATUS_OK;
+}
+
+MCB_API mcb_status mcb_candidate_available(int32_t device) noexcept {
+  mcb_exec ex{};
+  ex.abi_version = MCB_ABI_VERSION_V1;
+  ex.struct_size = sizeof(ex);
+  ex.device = device;
+  int dev;
+  mcb_status s = resolve_device(&ex, &dev);
+  if (s) return s;
+  DeviceCtx *c;
+  return init_ctx(dev, &c);
+}
+
+MCB_API mcb_status mcb_strict_gemm_f32_v1(const mcb_tensor *c, const mcb_tensor *a,
+                                          const mcb_tensor *b, const mcb_exec *exec) noexcept {
+  try {
+    return strict_gemm_impl(c, a, b, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API mcb_status mcb_strict_fused_pair_f32_v1(const mcb_tensor *e, const mcb_tensor *a,
+                                                const mcb_tensor *b, const mcb_tensor *d,
+                                                const mcb_exec *exec) noexcept {
+  try {
+    return strict_pair_impl(e, a, b, d, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API mcb_status mcb_gemm_epilogue_v1(const mcb_tensor *y, const mcb_tensor *x,
+                                        const mcb_tensor *w, const mcb_tensor *bias,
+                                        const mcb_epilogue *epilogue, uint32_t gemm_flags,
+                                        const mcb_exec *exec) noexcept {
+  try {
+    return gemm_epilogue_impl(y, x, w, bias, epilogue, gemm_flags, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API mcb_status mcb_msm_v1(const mcb_tensor *o, const mcb_tensor *q, const mcb_tensor *k,
+                              const mcb_tensor *v, double scale, const mcb_exec *exec) noexcept {
+  try {
+    return msm_impl(o, q, k, v, scale, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API int32_t mcb_fp8_is_legal_shape_v1(int64_t m, int64_t n, int64_t k) noexcept {
+  // Shape rule of isLegalFp8WgmmaShapeImpl (src/fp8_wgmma.cpp:10-24).
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  if (m % 64 != 0 || k % 32 != 0) return 0;
+  if (n < 8 || n > 256 || n % 8 != 0) return 0;
+  return 1;
+}
+
+MCB_API mcb_fp8_tile_config mcb_fp8_tile_config_v1(int64_t m, int64_t n, int64_t k) noexcept {
+  // Tile policy of getFp8WgmmaTileConfig (src/fp8_wgmma.cpp:30-57,85-109).
+  mcb_fp8_tile_config c{64, 128, 32, 0};
+  if (m <= 0 || n <= 0 || k <= 0) return c;
+  c.m_tile = (m >= 128 && m % 128 == 0) ? 128 : 64;
+  if (n >= 128 && n % 128 == 0) {
+    c.n_tile = 128;
+  } else {
+    int best = 0;
+    for (int cand = 8; cand <= 256 && cand <= n; cand += 8)
+      if (n % cand == 0) best = cand;
+    if (best > 0) {
+      c.n_tile = best;
+    } else {
+      const int64_t clamped = std::min<int64_t>(256, std::max<int64_t>(8, n));
+      c.n_tile = static_cast<int32_t>((clamped + 7) / 8 * 8);
+    }
+  }
+  c.k_tile = 32;
+  c.use_tma = mcb_fp8_is_legal_shape_v1(m, n, k) && m * n * k >= int64_t{64} * 64 * 32;
+  return c;
+}
+
+MCB_API mcb_status mcb_fp8_quantize_blockwise_v1(const mcb_tensor *, const mcb_tensor *,
+                                                 const mcb_tensor *, int64_t,
+                                                 const mcb_exec *) noexcept {
+  return MCB_STATUS_UNAVAILABLE_VARIANT;
+}
+
+MCB_API mcb_status mcb_gemm_fp8_blockscaled_v1(const mcb_tensor *, const mcb_tensor *,
+                                               const mcb_tensor *, const mcb_tensor *,
+                                               const mcb_tensor *, int64_t,
+                                               const mcb_exec *) noexcept {
+  return MCB_STATUS_UNAVAILABLE_VARIANT;
+}
+
+MCB_API uint64_t mcb_attn_block_workspace_bytes_v1(int64_t, int64_t, int64_t) noexcept {
+  return 0;
+}
+
+MCB_API mcb_status mcb_attn_block_region_v1(const mcb_tensor *, const mcb_tensor *,
+                                            const mcb_tensor *, const mcb_tensor *,
+                                            const mcb_tensor *, const mcb_tensor *, int64_t,
+                                            float, const mcb_exec *) noexcept {
+  return MCB_STATUS_UNAVAILABLE_VARIANT;
+}
+
+MCB_API mcb_status mcb_device_alloc(int32_t device, uint64_t size_bytes, mcb_buffer *out) noexcept {
+  if (!out) return MCB_STATUS_INVALID_ARGUMENT;
+  mcb_exec ex{};
+  ex.abi_version = MCB_ABI_VERSION_V1;
+  ex.struct_size = sizeof(ex);
+  ex.device = device;
+  int dev;
+  mcb_status s = resolve_device(&ex, &dev);
+  if (s) return s;
+  DeviceGuard g(dev);
+  void *p = nullptr;
+  if (cudaMalloc(&p, size_bytes ? size_bytes : 1) != cudaSuccess) {
+    cudaGetLastError();
+    return MCB_STATUS_ALLOCATION_FAILURE;
+  }
+  mcb_buffer h{};
+  h.ptr = reinterpret_cast<uint64_t>(p);
+  h.size_bytes = size_bytes;
+  h.alloc_id = g_next_alloc_id.fetch_add(1);
+  h.device = dev;
+  try {
+    std::lock_guard<std::mutex> lock(g_buf_mu);
+    g_bufs[h.ptr] = h;
+  } catch (...) {
+    cudaFree(p);
+    return MCB_STATUS_ALLOCATION_FAILURE;
+  }
+  *out = h;
+  return MCB_STATUS_OK;
+}
+
+MCB_API mcb_status mcb_device_free(mcb_buffer handle) noexcept {
+  std::lock_guard<std::mutex> lock(g_buf_mu);
+  if (!live(handle)) return MCB_STATUS_STALE_HANDLE;
+  DeviceGuard g(handle.device);
+  g_bufs.erase(handle.ptr);
+  return from_cuda(cudaFree(reinterpret_cast<void *>(handle.ptr)));
+}
+
+MCB_API int32_t mcb_device_is_valid(mcb_buffer handle) noexcept {
+  std::lock_guard<std::mutex> lock(g_buf_mu);
+  return live(handle) ? 1 : 0;
+}
+
+MCB_API mcb_status mcb_device_upload(mcb_buffer dst, const void *host_src,
+                                     uint64_t size_bytes) noexcept {
+  {
+    std::lock_guard<std::mutex> lock(g_buf_mu);
+    if (!live(dst)) return MCB_STATUS_STALE_HANDLE;
+  }
+  if (size_bytes > dst.size_bytes) return MCB_STATUS_ARITHMETIC_OVERFLOW;
+  if (size_bytes && !host_src) return MCB_STATUS_INVALID_ARGUMENT;
+  DeviceGuard g(dst.device);
+  return from_cuda(cudaMemcpy(reinterpret_cast<void *>(dst.ptr), host_src, size_bytes,
+                              cudaMemcpyHostToDevice));
+}
+
+MCB_API mcb_status mcb_device_download(void *host_dst, mcb_buffer src,
+                                       uint64_t size_bytes) noexcept {
+  {
+    std::lock_guard<std::mutex> lock(g_buf_mu);
+    if (!live(src)) return MCB_STATUS_STALE_HANDLE;
+  }
+  if (size_bytes > src.size_bytes) return MCB_STATUS_ARITHMETIC_OVERFLOW;
+  if (size_bytes && !host_dst) return MCB_STATUS_INVALID_ARGUMENT;
+  DeviceGuard g(src.device);
+  return from_cuda(cudaMemcpy(host_dst, reinterpret_cast<void *>(src.ptr), size_bytes,
+                              cudaMemcpyDeviceToHost));
+}
+
+MCB_API mcb_status mcb_device_zero(mcb_buffer handle) noexcept {
+  {
+    std::lock_guard<std::mutex> lock(g_buf_mu);
+    if (!live(handle)) return MCB_STATUS_STALE_HANDLE;
+  }
+  DeviceGuard g(handle.device);
+  return from_cuda(cudaMemset(reinterpret_cast<void *>(handle.ptr), 0, handle.size_bytes));
+}
+
+MCB_API mcb_status mcb_device_zero_raw_on_stream(void *device_ptr, uint64_t size_bytes,
+                                                 void *stream) noexcept {
+  if (size_bytes && !device_ptr) return MCB_STATUS_INVALID_ARGUMENT;
+  return from_cuda(
+      cudaMemsetAsync(device_ptr, 0, size_bytes, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

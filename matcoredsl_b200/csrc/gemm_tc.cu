@@ -1,0 +1,338 @@
+// bf16 GEMM with a fused epilogue on the B200's 5th-generation tensor cores.
+//
+//   Y[M,N] = act(X[M,K] * W (+|r-) bias)      (Family A, src/fusion_emitter_family_a.cpp)
+//
+// Design (one persistent CTA per SM, 192 threads, warp-specialised):
+//   warp 0      TMA producer: streams 128x64 tiles of X and 64x256 (or 256x64
+//               for W^T) tiles of W into a 4-stage shared-memory ring
+//               (128-byte swizzle), signalling `full[s]` by transaction bytes.
+//   warp 1      allocates 512 TMEM columns (two 128x256 f32 accumulators);
+//               one thread issues tcgen05.mma (M=128, N=256, K=16, bf16 in,
+//               f32 accumulate), releases each stage with tcgen05.commit on
+//               `empty[s]`, and hands a finished accumulator to the epilogue
+//               with a commit on `acc_full[a]`.
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time from the TMEM lanes
+//               their warp may access (warp % 4), add the bias, apply the
+//               activation, round to bf16/f32 and store, then release the
+//               accumulator on `acc_empty[a]` so the MMA of the next tile
+//               overlaps this tile's epilogue.
+// X is K-major; W [K,N] row-major is consumed MN-major straight from HBM
+// (no transpose pass); W^T [N,K] is consumed K-major.
+//
+// Roofline (config 2, 8192x4096x4096): 2*M*N*K = 274.9 GFLOP against the
+// bf16 dense tensor peak; ideal HBM traffic X + W + Y = 160 MiB.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "epilogue.cuh"
+#include "internal.h"
+
+namespace mcb {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KiB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KiB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int BAR_BYTES = 256;
+constexpr size_t SMEM_BYTES = static_cast<size_t>(STAGES) * STAGE_BYTES + BAR_BYTES + 1024;
+
+struct Params {
+  int64_t m, n, k, ld_y;
+  int n_tiles, num_tiles, num_kb;
+  int w_transposed, y_bf16;
+  void *y;
+  uint32_t *status;
+  Epilogue epi;
+};
+
+// Epilogue of one 32-column chunk held by one thread (one output row).
+__device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (&r)[32],
+                                               int64_t row, int64_t col0) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  const Epilogue &e = p.epi;
+  const bool full_chunk = col0 + 32 <= p.n;
+  if (e.bias_mode == 1 && e.bias_bf16 && e.bias_aligned16 && full_chunk) {
+    // Row-broadcast bf16 bias: every lane reads the same 64 bytes.
+    const uint4 *bp = reinterpret_cast<const uint4 *>(
+        reinterpret_cast<const __nv_bfloat16 *>(e.bias) + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 w4 = __ldg(bp + q);
+      const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float b0 = __uint_as_float(ws[h] << 16);
+        const float b1 = __uint_as_float(ws[h] & 0xffff0000u);
+        float &x0 = v[q * 8 + h * 2], &x1 = v[q * 8 + h * 2 + 1];
+        x0 = e.bias_op == 1 ? b0 - x0 : x0 + b0;
+        x1 = e.bias_op == 1 ? b1 - x1 : x1 + b1;
+      }
+    }
+  } else if (e.bias_mode != 0) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (col0 + i < p.n) {
+        const float b = load_bias(e, row, col0 + i);
+        v[i] = e.bias_op == 1 ? b - v[i] : v[i] + b;
+      }
+    }
+  }
+  switch (e.act) {
+    case 0: break;
+    case 2:
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = apply_act<true>(v[i], 2);
+      break;
+    default:
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = apply_act<true>(v[i], e.act);
+      break;
+  }
+  if (row >= p.m) return;
+  if (p.y_bf16) {
+    __nv_bfloat16 *yr = reinterpret_cast<__nv_bfloat16 *>(p.y) + row * p.ld_y + col0;
+    if (full_chunk) {
+      uint4 *dst = reinterpret_cast<uint4 *>(yr);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 o;
+        o.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+        o.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+        o.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+        o.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+        dst[q] = o;
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < p.n) yr[i] = __float2bfloat16_rn(v[i]);
+    }
+  } else {
+    float *yr = reinterpret_cast<float *>(p.y) + row * p.ld_y + col0;
+    if (full_chunk) {
+      float4 *dst = reinterpret_cast<float4 *>(yr);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        dst[q] = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < p.n) yr[i] = v[i];
+    }
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                        const __grid_constant__ CUtensorMap tmap_w, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *sa = smem;
+  uint8_t *sb = smem + STAGES * A_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + STAGES;
+  uint64_t *acc_full = bars + 2 * STAGES;
+  uint64_t *acc_empty = acc_full + 2;
+  uint64_t *drain = acc_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_x);
+    tma_prefetch_desc(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+        const int m0 = (tile / p.n_tiles) * BM;
+        const int n0 = (tile % p.n_tiles) * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kErrTimeoutEmpty))
+            goto producer_done;
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_2d(sa + stage * A_BYTES, &tmap_x, &full[stage], kb * BK, m0);
+          if (p.w_transposed) {
+            tma_load_2d(sb + stage * B_BYTES, &tmap_w, &full[stage], kb * BK, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + stage * B_BYTES + j * (64 * BK * 2), &tmap_w, &full[stage],
+                          n0 + j * 64, kb * BK);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(1, 1, 0, p.w_transposed ? 0u : 1u, BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.status, kErrTimeoutAccum))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sa + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sb + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // K-major SW128: advancing K by 16 bf16 = 32 bytes inside the row.
+            const uint64_t adesc = make_sdesc_sw128(a_addr + kk * 32, 16, 1024);
+            // W^T is K-major like X. W itself is MN-major: 64-column chunks
+            // are LBO = 64*BK*2 bytes apart, 8-row K groups SBO = 1024 apart,
+            // and K advances by 16 rows = 2048 bytes.
+            const uint64_t bdesc = p.w_transposed
+                                       ? make_sdesc_sw128(b_addr + kk * 32, 16, 1024)
+                                       : make_sdesc_sw128(b_addr + kk * 2048, 64 * BK * 2, 1024);
+            mma_f16_ss(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // Drain: every MMA this thread issued must finish before TMEM is freed.
+      mma_commit(drain);
+      if (!mbar_wait(drain, 0, nullptr, p.status, kErrTimeoutDrain)) *abort_flag = 1;
+    }
+  } else {
+    const int sub = warp & 3;  // TMEM lanes [32*sub, 32*sub+32)
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BM;
+      const int64_t n0 = static_cast<int64_t>(tile % p.n_tiles) * BN;
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, kErrTimeoutAccum)) break;
+      tc_fence_after();
+      const int64_t row = m0 + sub * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        if (n0 + c >= p.n) break;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c, r);
+        tmem_ld_wait();
+        epilogue_chunk(p, r, row, n0 + c);
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m, int64_t n,
+                                int64_t k, int64_t ld_x, int64_t ld_w, int64_t ld_y,
+                                int w_transposed, int y_bf16, const Epilogue &epi,
+                                uint32_t *status, int sms, cudaStream_t stream,
+                                LaunchInfo *info) {
+  if (m == 0 || n == 0) return cudaSuccess;
+  CUtensorMap tx, tw;
+  if (!encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m, ld_x * 2, BK, BM,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  const bool ok_w =
+      w_transposed
+          ? encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, k, n, ld_w * 2, BK, BN,
+                           CU_TENSOR_MAP_SWIZZLE_128B)
+          : encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, n, k, ld_w * 2, 64, BK,
+                           CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!ok_w) return cudaErrorInvalidValue;
+  Params p;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.ld_y = ld_y;
+  p.n_tiles = static_cast<int>((n + BN - 1) / BN);
+  const int64_t tiles = ((m + BM - 1) / BM) * p.n_tiles;
+  if (tiles > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  p.num_tiles = static_cast<int>(tiles);
+  p.num_kb = static_cast<int>((k + BK - 1) / BK);
+  p.w_transposed = w_transposed;
+  p.y_bf16 = y_bf16;
+  p.y = y;
+  p.status = status;
+  p.epi = epi;
+  // Per-device function attribute; cheap, so set on every launch.
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_bf16_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(SMEM_BYTES));
+  if (e != cudaSuccess) return e;
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  gemm_tc_bf16_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tx, tw, p);
+  if (info) {
+    info->launches = 1;
+    info->tile_m = BM;
+    info->tile_n = BN;
+    info->tile_k = BK;
+    info->stages = STAGES;
+    info->ctas = grid;
+    info->set_route("tcgen05_bf16_gemm_epilogue");
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace mcb

@@ -1,0 +1,103 @@
+// Internal launcher interface between the C-ABI layer (api.cpp) and the
+// kernel translation units. Nothing here is exported from libmcb.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+namespace mcb {
+
+struct LaunchInfo {
+  int launches = 0;
+  int tile_m = 0, tile_n = 0, tile_k = 0, stages = 0, ctas = 0;
+  char route[48] = {0};
+  void set_route(const char *r) {
+    strncpy(route, r, sizeof(route) - 1);
+    route[sizeof(route) - 1] = 0;
+  }
+};
+
+// ---- strict.cu ----------------------------------------------------------------
+cudaError_t launch_strict_gemm(const float *a, const float *b, float *c, int64_t m, int64_t k,
+                               int64_t n, int64_t lda, int64_t ldb, int64_t ldc, int sms,
+                               cudaStream_t stream, LaunchInfo *info);
+// Floats of global scratch the fused pair needs (0 when the panel fits in
+// shared memory).
+int64_t strict_pair_scratch_floats(int64_t m, int64_t n, int sms, int smem_limit_bytes);
+cudaError_t launch_strict_pair(const float *a, const float *b, const float *d, float *e,
+                               float *scratch, int64_t m, int64_t k, int64_t n, int64_t p,
+                               int64_t lda, int64_t ldb, int64_t ldd, int64_t lde, int sms,
+                               int smem_limit_bytes, cudaStream_t stream, LaunchInfo *info);
+
+// ---- epilogue description shared by the GEMM kernels ----------------------------
+struct Epilogue {
+  int bias_mode = 0;  // 0 none, 1 row-broadcast [N], 2 full [M,N]
+  int bias_op = 0;    // 0 add, 1 reverse subtract
+  int act = 0;        // 0 none, 1 relu, 2 gelu_tanh, 3 exp, 4 sigmoid, 5 tanh
+  int bias_bf16 = 0;  // bias element type (1 bf16, 0 f32)
+  int bias_aligned16 = 0;  // bias base is 16-byte aligned (vector loads allowed)
+  const void *bias = nullptr;
+  int64_t ld_bias = 0;
+};
+
+// ---- gemm_tc.cu: tcgen05 bf16 GEMM + epilogue -------------------------------------
+// X [M,K] bf16 (ld_x), W [K,N] bf16 (ld_w, w_transposed=0) or W^T [N,K]
+// (w_transposed=1), Y [M,N] bf16 or f32 (y_bf16). Requires K, N, ld_x, ld_w
+// multiples of 8 and 16-byte aligned bases (TMA); the caller checks.
+cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m, int64_t n,
+                                int64_t k, int64_t ld_x, int64_t ld_w, int64_t ld_y,
+                                int w_transposed, int y_bf16, const Epilogue &epi,
+                                uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info);
+
+// ---- simt.cu: CUDA-core fallbacks for shapes/dtypes the tensor-core kernels do not take
+// dtype codes: 1 f32, 3 bf16 (as in mcb.h)
+cudaError_t launch_gemm_simt(const void *x, int x_dtype, const void *w, int w_dtype, void *y,
+                             int y_dtype, int64_t m, int64_t n, int64_t k, int64_t ld_x,
+                             int64_t ld_w, int64_t ld_y, int w_transposed, const Epilogue &epi,
+                             cudaStream_t stream, LaunchInfo *info);
+
+// Batched rank-2 MSM on CUDA cores (online softmax), any Dqk/Dv <= 256.
+struct MsmShape {
+  int64_t batch = 1, heads = 1, m = 0, n = 0, dqk = 0, dv = 0;
+  // element strides: [batch, head, row] for each tensor (innermost is 1)
+  int64_t q_s[3], k_s[3], v_s[3], o_s[3];
+};
+cudaError_t launch_msm_simt(const void *q, const void *k, const void *v, void *o, int dtype,
+                            const MsmShape &s, float scale, cudaStream_t stream,
+                            LaunchInfo *info);
+
+// ---- msm_tc.cu: tcgen05 MSM, bf16, Dqk = Dv = 128 ----------------------------------------
+cudaError_t launch_msm_tc_bf16(const void *q, const void *k, const void *v, void *o,
+                               const MsmShape &s, float scale, uint32_t *status, int sms,
+                               cudaStream_t stream, LaunchInfo *info);
+
+// ---- fp8.cu -------------------------------------------------------------------------------
+cudaError_t launch_fp8_quantize(const void *x, int x_dtype, uint8_t *q, float *scales,
+                                int64_t rows, int64_t cols, int64_t ld_x, int64_t block,
+                                int fmt_e5m2, cudaStream_t stream, LaunchInfo *info);
+cudaError_t launch_gemm_fp8_tc(const uint8_t *a, int a_e5m2, const float *sa, const uint8_t *bt,
+                               int b_e5m2, const float *sbt, void *c, int c_bf16, int64_t m,
+                               int64_t n, int64_t k, int64_t block, uint32_t *status, int sms,
+                               cudaStream_t stream, LaunchInfo *info);
+cudaError_t launch_gemm_fp8_simt(const uint8_t *a, int a_e5m2, const float *sa,
+                                 const uint8_t *bt, int b_e5m2, const float *sbt, void *c,
+                                 int c_bf16, int64_t m, int64_t n, int64_t k, int64_t block,
+                                 cudaStream_t stream, LaunchInfo *info);
+
+// ---- rmsnorm (attention block) -------------------------------------------------------------
+cudaError_t launch_residual_rmsnorm(const void *x, const void *attn_proj, void *y, int64_t rows,
+                                    int64_t cols, float eps, cudaStream_t stream,
+                                    LaunchInfo *info);
+
+// Tensor-map encoder (driver entry point fetched once through the runtime).
+bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base,
+                    uint64_t inner, uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner,
+                    uint32_t box_outer, CUtensorMapSwizzle swizzle);
+bool encode_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base,
+                    uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes,
+                    uint64_t stride2_bytes, uint32_t box0, uint32_t box1, uint32_t box2,
+                    CUtensorMapSwizzle swizzle);
+
+}  // namespace mcb

@@ -1,0 +1,194 @@
+// Strict f32 kernels on CUDA cores, bit-exact with MatcoreDSL's strict leaf.
+//
+// Arithmetic contract (compiler/lib/runtime/closed_host_v1.cpp:401-415 and
+// compiler/lib/mlir/MatcoreCpuFusedGemmCandidate.h:19-31): every output is a
+// reduction in increasing index order from a +0 seed, each step one binary32
+// multiply rounded on its own followed by one binary32 add. __fmul_rn and
+// __fadd_rn are never contracted into an FMA, and this file is also compiled
+// with -fmad=false and without flush-to-zero, so subnormals survive exactly
+// as on the CPU. For the fused pair the intermediate C is rounded to binary32
+// (it lives in shared memory or in a scratch panel) before the second GEMM.
+//
+// Work decomposition (B200: 148 SMs): one CTA owns a panel of R rows; its
+// threads stride over output columns so global loads of B/D are coalesced
+// and every thread carries R independent reduction chains to hide the
+// dependent-add latency.
+#include "common.cuh"
+#include "internal.h"
+
+namespace mcb {
+namespace {
+
+template <int R>
+__global__ void __launch_bounds__(256) strict_gemm_kernel(const float *__restrict__ a,
+                                                          const float *__restrict__ b,
+                                                          float *__restrict__ c, int64_t m,
+                                                          int64_t k, int64_t n, int64_t lda,
+                                                          int64_t ldb, int64_t ldc) {
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * R;
+  const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (j >= n) return;
+  float acc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+  const int rows = static_cast<int>(m - r0 < R ? m - r0 : R);
+  for (int64_t h = 0; h < k; ++h) {
+    const float bv = __ldg(b + h * ldb + j);
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (r < rows) acc[r] = __fadd_rn(acc[r], __fmul_rn(__ldg(a + (r0 + r) * lda + h), bv));
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+    if (r < rows) c[(r0 + r) * ldc + j] = acc[r];
+}
+
+// One CTA per panel of R rows. Phase 1 writes the panel C[R, N] (binary32) to
+// `panel` (shared memory when it fits, else this CTA's slice of a global
+// scratch buffer); phase 2 reduces it against D.
+template <int R, bool kSmemPanel>
+__global__ void __launch_bounds__(256) strict_pair_kernel(
+    const float *__restrict__ a, const float *__restrict__ b, const float *__restrict__ d,
+    float *__restrict__ e, float *__restrict__ scratch, int64_t m, int64_t k, int64_t n,
+    int64_t p, int64_t lda, int64_t ldb, int64_t ldd, int64_t lde) {
+  extern __shared__ float smem_panel[];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * R;
+  if (r0 >= m) return;
+  const int rows = static_cast<int>(m - r0 < R ? m - r0 : R);
+  float *panel = kSmemPanel ? smem_panel : scratch + static_cast<int64_t>(blockIdx.x) * R * n;
+
+  // Phase 1: C[r, j] = sum_h A[r0+r, h] * B[h, j]
+  for (int64_t j = threadIdx.x; j < n; j += blockDim.x) {
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+    for (int64_t h = 0; h < k; ++h) {
+      const float bv = __ldg(b + h * ldb + j);
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        if (r < rows) acc[r] = __fadd_rn(acc[r], __fmul_rn(__ldg(a + (r0 + r) * lda + h), bv));
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (r < rows) panel[r * n + j] = acc[r];
+  }
+  __syncthreads();
+  // Phase 2: E[r0+r, q] = sum_j C[r, j] * D[j, q]
+  for (int64_t q = threadIdx.x; q < p; q += blockDim.x) {
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+    for (int64_t j = 0; j < n; ++j) {
+      const float dv = __ldg(d + j * ldd + q);
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        if (r < rows) acc[r] = __fadd_rn(acc[r], __fmul_rn(panel[r * n + j], dv));
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (r < rows) e[(r0 + r) * lde + q] = acc[r];
+  }
+}
+
+__global__ void fill_zero_kernel(float *__restrict__ y, int64_t rows, int64_t cols, int64_t ld) {
+  const int64_t total = rows * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    y[(i / cols) * ld + (i % cols)] = 0.0f;
+}
+
+// Rows per CTA: the largest R in {4, 2, 1} that still gives at least two CTAs
+// per SM, so small problems are spread over the whole GPU.
+int pick_rows(int64_t m, int sms) {
+  if ((m + 3) / 4 >= 2 * sms) return 4;
+  if ((m + 1) / 2 >= 2 * sms) return 2;
+  if ((m + 3) / 4 >= sms) return 4;
+  return (m + 1) / 2 >= sms ? 2 : 1;
+}
+
+}  // namespace
+
+cudaError_t launch_strict_gemm(const float *a, const float *b, float *c, int64_t m, int64_t k,
+                               int64_t n, int64_t lda, int64_t ldb, int64_t ldc, int sms,
+                               cudaStream_t stream, LaunchInfo *info) {
+  if (m == 0 || n == 0) return cudaSuccess;
+  const int R = pick_rows(m, sms);
+  const int threads = n >= 256 ? 256 : 128;
+  dim3 grid(static_cast<unsigned>((n + threads - 1) / threads),
+            static_cast<unsigned>((m + R - 1) / R));
+  if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
+  switch (R) {
+    case 4: strict_gemm_kernel<4><<<grid, threads, 0, stream>>>(a, b, c, m, k, n, lda, ldb, ldc); break;
+    case 2: strict_gemm_kernel<2><<<grid, threads, 0, stream>>>(a, b, c, m, k, n, lda, ldb, ldc); break;
+    default: strict_gemm_kernel<1><<<grid, threads, 0, stream>>>(a, b, c, m, k, n, lda, ldb, ldc); break;
+  }
+  if (info) {
+    info->launches = 1;
+    info->tile_m = R;
+    info->tile_n = threads;
+    info->ctas = static_cast<int>(grid.x * grid.y);
+    info->set_route("strict_f32_simt_gemm");
+  }
+  return cudaGetLastError();
+}
+
+int64_t strict_pair_scratch_floats(int64_t m, int64_t n, int sms, int smem_limit_bytes) {
+  const int R = pick_rows(m, sms);
+  if (static_cast<int64_t>(R) * n * 4 <= smem_limit_bytes) return 0;
+  return ((m + R - 1) / R) * R * n;
+}
+
+cudaError_t launch_strict_pair(const float *a, const float *b, const float *d, float *e,
+                               float *scratch, int64_t m, int64_t k, int64_t n, int64_t p,
+                               int64_t lda, int64_t ldb, int64_t ldd, int64_t lde, int sms,
+                               int smem_limit_bytes, cudaStream_t stream, LaunchInfo *info) {
+  if (m == 0 || p == 0) return cudaSuccess;
+  if (info) info->launches = 0;
+  if (n == 0) {  // empty consumer reduction: E = +0
+    fill_zero_kernel<<<sms, 256, 0, stream>>>(e, m, p, lde);
+    if (info) {
+      info->launches = 1;
+      info->set_route("strict_f32_zero_reduction");
+    }
+    return cudaGetLastError();
+  }
+  const int R = pick_rows(m, sms);
+  const int64_t panel_bytes = static_cast<int64_t>(R) * n * 4;
+  const bool in_smem = panel_bytes <= smem_limit_bytes;
+  if (!in_smem && scratch == nullptr) return cudaErrorInvalidValue;
+  const int64_t ctas = (m + R - 1) / R;
+  if (ctas > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  const int threads = (n >= 256 || p >= 256) ? 256 : 128;
+  const size_t smem = in_smem ? static_cast<size_t>(panel_bytes) : 0;
+#define MCB_PAIR_CASE(RR)                                                                    \
+  case RR:                                                                                   \
+    if (in_smem) {                                                                           \
+      if (smem > 48 * 1024)                                                                  \
+        cudaFuncSetAttribute(strict_pair_kernel<RR, true>,                                   \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);        \
+      strict_pair_kernel<RR, true><<<(unsigned)ctas, threads, smem, stream>>>(              \
+          a, b, d, e, scratch, m, k, n, p, lda, ldb, ldd, lde);                              \
+    } else {                                                                                 \
+      strict_pair_kernel<RR, false><<<(unsigned)ctas, threads, 0, stream>>>(                \
+          a, b, d, e, scratch, m, k, n, p, lda, ldb, ldd, lde);                              \
+    }                                                                                        \
+    break;
+  switch (R) {
+    MCB_PAIR_CASE(4)
+    MCB_PAIR_CASE(2)
+    default:
+      MCB_PAIR_CASE(1)
+  }
+#undef MCB_PAIR_CASE
+  if (info) {
+    info->launches = 1;
+    info->tile_m = R;
+    info->tile_n = threads;
+    info->ctas = static_cast<int>(ctas);
+    info->set_route(in_smem ? "strict_f32_simt_pair_smem_panel"
+                            : "strict_f32_simt_pair_scratch_panel");
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace mcb

@@ -1,0 +1,257 @@
+"""CPU oracle for the MatcoreDSL hot path -- TEST INFRASTRUCTURE ONLY.
+
+This package is the checker the CUDA path is compared against. It is loaded
+only by ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline legs of
+``bench.py``; the product library (``matcoredsl_b200``) never imports it.
+
+The arithmetic lives in C++ (``oracle/*.cpp``, built by ``oracle/Makefile``
+into ``oracle/_build/liboracle.so``); this module is a thin ctypes wrapper
+over it plus numpy helpers for seeded synthetic inputs. Each C++ function
+cites the MatcoreDSL source it restates.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "liboracle.so")
+_REF_PATH = os.path.join(_HERE, "_ref", "libmcref.so")
+_lib = None
+_ref = None
+
+ACT = {"none": 0, "relu": 1, "gelu_tanh": 2, "exp": 3, "sigmoid": 4, "tanh": 5}
+BIAS_MODE = {"none": 0, "row": 1, "full": 2}
+BIAS_OP = {"add": 0, "rsub": 1}
+FP8 = {"e4m3": 0, "e5m2": 1}
+FP8_MAX = {"e4m3": 448.0, "e5m2": 57344.0}
+
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(dtype=np.int8, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_i64 = ctypes.c_int64
+
+
+def build(ref: bool = False) -> None:
+    """Compile the oracle (and, when asked, the reference's numeric file)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    if ref:
+        subprocess.run(["make", "-s", "-C", _HERE, "ref"], check=True)
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        sig = {
+            "orc_strict_gemm_f32": [_f32p, _f32p, _f32p, _i64, _i64, _i64],
+            "orc_strict_fused_pair_f32": [_f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64],
+            "orc_strict_fused_pair_f32_mt": [_f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64, ctypes.c_int],
+            "orc_bf16_from_f32": [_f32p, _u16p, _i64],
+            "orc_bf16_to_f32": [_u16p, _f32p, _i64],
+            "orc_gemm_bf16_f32_fma": [_u16p, _u16p, _f32p, _i64, _i64, _i64],
+            "orc_gemm_i8_i32": [_i8p, _i8p, _i32p, _i64, _i64, _i64],
+            "orc_gemm_epilogue_f64": [_f32p, _f32p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_int, _f64p, _i64, _i64, _i64, ctypes.c_void_p, _i64],
+            "orc_msm_f64": [_f32p, _f32p, _f32p, _f64p, _i64, _i64, _i64, _i64, ctypes.c_double],
+            "orc_fp8_encode": [_f32p, _u8p, _i64, ctypes.c_int],
+            "orc_fp8_decode": [_u8p, _f32p, _i64, ctypes.c_int],
+            "orc_fp8_quantize_blockwise": [_f32p, _i64, _i64, _i64, ctypes.c_int, _u8p, _f32p],
+            "orc_gemm_fp8_blockscaled_f64": [_u8p, ctypes.c_int, _f32p, _u8p, ctypes.c_int, _f32p,
+                                             _f64p, _i64, _i64, _i64, _i64, ctypes.c_void_p, _i64],
+            "orc_baseline_gemm_bias_gelu_f32_full": [_f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64,
+                                                     ctypes.c_int],
+        }
+        for name, argtypes in sig.items():
+            fn = getattr(L, name)
+            fn.argtypes = argtypes
+            fn.restype = None
+        L.orc_max_threads.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def ref_lib() -> ctypes.CDLL | None:
+    """The reference's own cpu_numeric_reference.cpp, when it was compiled here."""
+    global _ref
+    if _ref is None and os.path.exists(_REF_PATH):
+        R = ctypes.CDLL(_REF_PATH)
+        R.ref_bf16_from_f32.argtypes = [_f32p, _u16p, _i64]
+        R.ref_bf16_to_f32.argtypes = [_u16p, _f32p, _i64]
+        R.ref_gemm_bf16_f32.argtypes = [_u16p, _u16p, _f32p, _i64, _i64, _i64]
+        R.ref_gemm_bf16_f32.restype = ctypes.c_int
+        R.ref_gemm_i8_i32.argtypes = [_i8p, _i8p, _i32p, _i64, _i64, _i64]
+        R.ref_gemm_i8_i32.restype = ctypes.c_int
+        _ref = R
+    return _ref
+
+
+def _c(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+# ---- strict f32 -----------------------------------------------------------
+def strict_gemm(a, b):
+    a, b = _c(a, np.float32), _c(b, np.float32)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.empty((m, n), np.float32)
+    lib().orc_strict_gemm_f32(a, b, c, m, k, n)
+    return c
+
+
+def strict_fused_pair(a, b, d, threads: int = 1):
+    a, b, d = _c(a, np.float32), _c(b, np.float32), _c(d, np.float32)
+    m, k = a.shape
+    n, p = d.shape
+    e = np.empty((m, p), np.float32)
+    if threads > 1:
+        lib().orc_strict_fused_pair_f32_mt(a.reshape(-1) if a.size else np.zeros(1, np.float32),
+                                           b.reshape(-1) if b.size else np.zeros(1, np.float32),
+                                           d.reshape(-1) if d.size else np.zeros(1, np.float32),
+                                           e.reshape(-1) if e.size else np.zeros(1, np.float32),
+                                           m, k, n, p, threads)
+    else:
+        lib().orc_strict_fused_pair_f32(a.reshape(-1) if a.size else np.zeros(1, np.float32),
+                                        b.reshape(-1) if b.size else np.zeros(1, np.float32),
+                                        d.reshape(-1) if d.size else np.zeros(1, np.float32),
+                                        e.reshape(-1) if e.size else np.zeros(1, np.float32),
+                                        m, k, n, p)
+    return e
+
+
+# ---- bf16 ------------------------------------------------------------------
+def bf16_from_f32(x):
+    x = _c(x, np.float32)
+    y = np.empty(x.shape, np.uint16)
+    lib().orc_bf16_from_f32(x.reshape(-1), y.reshape(-1), x.size)
+    return y
+
+
+def bf16_to_f32(h):
+    h = _c(h, np.uint16)
+    y = np.empty(h.shape, np.float32)
+    lib().orc_bf16_to_f32(h.reshape(-1), y.reshape(-1), h.size)
+    return y
+
+
+def gemm_bf16_f32_fma(a, b):
+    a, b = _c(a, np.uint16), _c(b, np.uint16)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.empty((m, n), np.float32)
+    lib().orc_gemm_bf16_f32_fma(a, b, c, m, k, n)
+    return c
+
+
+def gemm_i8_i32(a, b):
+    a, b = _c(a, np.int8), _c(b, np.int8)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.empty((m, n), np.int32)
+    lib().orc_gemm_i8_i32(a, b, c, m, k, n)
+    return c
+
+
+# ---- Family A / C (fp64) -----------------------------------------------------
+def gemm_epilogue(x, w, bias=None, bias_mode="none", bias_op="add", act="none", rows=None):
+    """fp64 y = act(x w (+|r-) bias) for `rows` (all rows when None)."""
+    x, w = _c(x, np.float32), _c(w, np.float32)
+    m, k = x.shape
+    n = w.shape[1]
+    bptr = None
+    if bias_mode != "none":
+        bias = _c(bias, np.float32)
+        bptr = bias.ctypes.data
+    if rows is None:
+        y = np.empty((m, n), np.float64)
+        rptr, nr = None, m
+    else:
+        rows = _c(rows, np.int64)
+        y = np.empty((rows.size, n), np.float64)
+        rptr, nr = rows.ctypes.data, rows.size
+    lib().orc_gemm_epilogue_f64(x, w, bptr, BIAS_MODE[bias_mode], BIAS_OP[bias_op], ACT[act],
+                                y, m, k, n, rptr, nr)
+    return y
+
+
+def msm(q, k, v, scale=1.0):
+    """fp64 softmax(scale * q k^T) v for rank-2 q [m,d], k [n,d], v [n,dv]."""
+    q, k, v = _c(q, np.float32), _c(k, np.float32), _c(v, np.float32)
+    m, dqk = q.shape
+    n, dv = v.shape
+    o = np.empty((m, dv), np.float64)
+    lib().orc_msm_f64(q, k, v, o, m, n, dqk, dv, float(scale))
+    return o
+
+
+# ---- FP8 -------------------------------------------------------------------
+def fp8_encode(x, fmt="e4m3"):
+    x = _c(x, np.float32)
+    q = np.empty(x.shape, np.uint8)
+    lib().orc_fp8_encode(x.reshape(-1), q.reshape(-1), x.size, FP8[fmt])
+    return q
+
+
+def fp8_decode(q, fmt="e4m3"):
+    q = _c(q, np.uint8)
+    x = np.empty(q.shape, np.float32)
+    lib().orc_fp8_decode(q.reshape(-1), x.reshape(-1), q.size, FP8[fmt])
+    return x
+
+
+def fp8_quantize_blockwise(x, block=128, fmt="e4m3"):
+    x = _c(x, np.float32)
+    r, c = x.shape
+    q = np.empty((r, c), np.uint8)
+    s = np.empty(((r + block - 1) // block, (c + block - 1) // block), np.float32)
+    lib().orc_fp8_quantize_blockwise(x, r, c, block, FP8[fmt], q, s)
+    return q, s
+
+
+def gemm_fp8_blockscaled(a, sa, bt, sbt, a_fmt="e4m3", b_fmt="e4m3", block=128, rows=None):
+    a, bt = _c(a, np.uint8), _c(bt, np.uint8)
+    sa, sbt = _c(sa, np.float32), _c(sbt, np.float32)
+    m, k = a.shape
+    n = bt.shape[0]
+    if rows is None:
+        c = np.empty((m, n), np.float64)
+        rptr, nr = None, m
+    else:
+        rows = _c(rows, np.int64)
+        c = np.empty((rows.size, n), np.float64)
+        rptr, nr = rows.ctypes.data, rows.size
+    lib().orc_gemm_fp8_blockscaled_f64(a, FP8[a_fmt], sa, bt, FP8[b_fmt], sbt, c, m, k, n,
+                                       block, rptr, nr)
+    return c
+
+
+# ---- CPU baseline -------------------------------------------------------------
+def baseline_gemm_bias_gelu(x32, w32, b32, threads=None):
+    x32, w32, b32 = _c(x32, np.float32), _c(w32, np.float32), _c(b32, np.float32)
+    m, k = x32.shape
+    n = w32.shape[1]
+    y = np.empty((m, n), np.float32)
+    lib().orc_baseline_gemm_bias_gelu_f32_full(x32, w32, b32, y, m, k, n,
+                                               int(threads or max_threads()))
+    return y
+
+
+def max_threads() -> int:
+    return int(lib().orc_max_threads())
+
+
+# ---- seeded synthetic inputs ----------------------------------------------------
+def rel_frobenius(x, ref) -> float:
+    x = np.asarray(x, np.float64)
+    ref = np.asarray(ref, np.float64)
+    den = np.linalg.norm(ref)
+    return float(np.linalg.norm(x - ref) / (den if den > 0 else 1.0))

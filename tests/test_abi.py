@@ -1,0 +1,139 @@
+"""CPU: the C-ABI library loads, exports every declared entry point, and its
+host-only logic behaves; no kernel is launched here."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared_symbols():
+    text = open(os.path.join(ROOT, "include", "mcb.h")).read()
+    return sorted(set(re.findall(r"MCB_API\s+[\w\s\*]+?\b(mcb_\w+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = _declared_symbols()
+    for required in ("mcb_strict_fused_pair_f32_v1", "mcb_strict_gemm_f32_v1",
+                     "mcb_gemm_epilogue_v1", "mcb_msm_v1", "mcb_gemm_fp8_blockscaled_v1",
+                     "mcb_attn_block_region_v1", "mcb_device_alloc"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol(mcb):
+    from matcoredsl_b200 import _abi
+    lib = ctypes.CDLL(_abi.LIB_PATH)
+    missing = [n for n in _declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+    # and the ctypes mirror declares exactly the header's set
+    assert sorted(_abi.SIGNATURES) == _declared_symbols()
+
+
+def test_abi_struct_layouts_match_c_compiler(mcb, tmp_path):
+    """The ctypes mirror and a C compiler agree on every struct's size and offsets."""
+    import shutil
+    import subprocess
+    from matcoredsl_b200 import _abi
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    structs = {"mcb_tensor": _abi.Tensor, "mcb_exec": _abi.Exec, "mcb_report": _abi.Report,
+               "mcb_epilogue": _abi.Epilogue, "mcb_buffer": _abi.Buffer,
+               "mcb_fp8_tile_config": _abi.Fp8TileConfig}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "mcb.h"', "int main(void){"]
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
+        for f, _ in py._fields_:
+            lines.append(f'printf("{cname}.{f} %zu\\n", offsetof({cname}, {f}));')
+    lines.append("return 0;}")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    out = dict(l.split() for l in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                 check=True).stdout.splitlines())
+    for cname, py in structs.items():
+        assert int(out[cname]) == ctypes.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert int(out[f"{cname}.{f}"]) == getattr(py, f).offset, (cname, f)
+
+
+def test_status_messages(mcb):
+    lib = mcb.load()
+    assert lib.mcb_status_message(0) == b"ok"
+    assert b"sm_100" in lib.mcb_status_message(42)
+    assert lib.mcb_status_message(9999) == b"unknown status"
+
+
+def test_fp8_tile_policy_matches_reference_table(mcb):
+    """Restates src/fp8_wgmma.cpp:10-24,61-109 expectations for a set of shapes."""
+    lib = mcb.load()
+    legal = lib.mcb_fp8_is_legal_shape_v1
+    assert legal(64, 8, 32) == 1 and legal(128, 256, 64) == 1
+    assert legal(64, 264, 32) == 0 and legal(63, 8, 32) == 0 and legal(64, 8, 31) == 0
+    assert legal(0, 8, 32) == 0 and legal(64, 12, 32) == 0
+    cfg = lib.mcb_fp8_tile_config_v1
+    c = cfg(256, 384, 128)
+    assert (c.m_tile, c.n_tile, c.k_tile, c.use_tma) == (128, 128, 32, 0)  # N>256: illegal shape
+    c = cfg(128, 256, 64)
+    assert (c.m_tile, c.n_tile, c.k_tile, c.use_tma) == (128, 128, 32, 1)
+    c = cfg(64, 96, 32)
+    assert (c.m_tile, c.n_tile, c.use_tma) == (64, 96, 1)
+    c = cfg(64, 100, 32)  # largest legal divisor of 100 that is a multiple of 8: none -> 104
+    assert c.n_tile == 104
+    c = cfg(64, 40, 32)
+    assert c.n_tile == 40
+    c = cfg(0, 40, 32)
+    assert (c.m_tile, c.n_tile, c.k_tile, c.use_tma) == (64, 128, 32, 0)
+    c = cfg(32, 8, 32)  # M not a multiple of 64: tiles chosen, TMA off
+    assert (c.m_tile, c.n_tile, c.use_tma) == (64, 8, 0)
+
+
+def test_invalid_descriptors_rejected_without_gpu(mcb):
+    from matcoredsl_b200 import _abi
+    lib = mcb.load()
+    a = np.zeros((2, 3), np.float32)
+    t = _abi.make_tensor(a.ctypes.data, "f32", a.shape, [3, 1], False)
+    bad = _abi.make_tensor(a.ctypes.data, "f32", a.shape, [3, 1], False)
+    bad.abi_version = 7
+    ex = _abi.make_exec()
+    assert lib.mcb_strict_gemm_f32_v1(ctypes.byref(t), ctypes.byref(bad), ctypes.byref(t),
+                                      ctypes.byref(ex)) == _abi.STATUS_CODE["ABI_MISMATCH"]
+    col = _abi.make_tensor(a.ctypes.data, "f32", a.shape, [1, 2], False)  # column-major
+    assert lib.mcb_strict_gemm_f32_v1(ctypes.byref(t), ctypes.byref(col), ctypes.byref(t),
+                                      ctypes.byref(ex)) == _abi.STATUS_CODE["UNSUPPORTED_LAYOUT"]
+    b = np.zeros((4, 2), np.float32)
+    tb = _abi.make_tensor(b.ctypes.data, "f32", b.shape, [2, 1], False)
+    c = np.zeros((2, 2), np.float32)
+    tc = _abi.make_tensor(c.ctypes.data, "f32", c.shape, [2, 1], False)
+    assert lib.mcb_strict_gemm_f32_v1(ctypes.byref(tc), ctypes.byref(t), ctypes.byref(tb),
+                                      ctypes.byref(ex)) == _abi.STATUS_CODE["SHAPE_MISMATCH"]
+    # the output may not overlap an input
+    assert lib.mcb_strict_gemm_f32_v1(ctypes.byref(t), ctypes.byref(t), ctypes.byref(tb),
+                                      ctypes.byref(ex)) in (_abi.STATUS_CODE["ALIAS_VIOLATION"],
+                                                            _abi.STATUS_CODE["SHAPE_MISMATCH"])
+
+
+def test_compute_without_gpu_fails_loudly(mcb):
+    """With no sm_100 device every compute entry point refuses; none computes on the CPU."""
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present")
+    except ImportError:
+        pass
+    with pytest.raises(mcb.McbError) as e:
+        mcb.strict_gemm(np.ones((2, 2), np.float32), np.ones((2, 2), np.float32))
+    assert e.value.name == "CANDIDATE_UNAVAILABLE"
+
+
+def test_stale_buffer_handle_rejected(mcb):
+    from matcoredsl_b200 import _abi
+    lib = mcb.load()
+    h = _abi.Buffer()
+    h.ptr, h.size_bytes, h.alloc_id, h.device = 0x1000, 16, 12345, 0
+    assert lib.mcb_device_is_valid(h) == 0
+    assert lib.mcb_device_free(h) == _abi.STATUS_CODE["STALE_HANDLE"]

@@ -1,0 +1,93 @@
+"""GPU: the strict f32 GEMM and fused pair are bit-exact with the oracle.
+
+Cases are the reference's own strict test suites regenerated from the same
+mt19937 draws (tests/reference_cases.py), the stated known answers, and
+BASELINE config 1 at full size. All calls go through the C ABI.
+"""
+import numpy as np
+import pytest
+
+from tests import reference_cases as rc
+
+pytestmark = pytest.mark.gpu
+
+
+def _check_pair(mcb, orc, name, a, b, d):
+    got = mcb.strict_fused_pair(a, b, d)
+    exp = orc.strict_fused_pair(a, b, d)
+    assert rc.same_bits(got, exp), name
+
+
+def test_known_answers(mcb, orc):
+    for name, a, b, d, expected in rc.known_answers():
+        got = mcb.strict_fused_pair(a, b, d)
+        assert rc.same_bits(got, expected), (name, got, expected)
+
+
+def test_two_gemm_example(mcb):
+    a, b, d, c_exp, e_exp = rc.two_gemm_example()
+    c = mcb.strict_gemm(a, b)
+    assert rc.same_bits(c, c_exp)
+    assert rc.same_bits(mcb.strict_gemm(d, c), e_exp)
+
+
+def test_physical_suite_bit_exact(mcb, orc):
+    for name, a, b, d in rc.physical_cases():
+        if a.shape[0] == 0 or d.shape[1] == 0:
+            continue  # empty E: nothing to launch, nothing to compare
+        _check_pair(mcb, orc, name, a, b, d)
+
+
+def test_execution_suite_bit_exact(mcb, orc):
+    for name, a, b, d in rc.execution_cases():
+        if a.shape[0] == 0 or d.shape[1] == 0:
+            continue
+        _check_pair(mcb, orc, name, a, b, d)
+
+
+def test_scratch_panel_route(mcb, orc):
+    """N large enough that the intermediate panel spills to global scratch."""
+    rng = np.random.default_rng(11)
+    a = rng.uniform(-1, 1, (37, 5)).astype(np.float32)
+    b = rng.uniform(-1, 1, (5, 70001)).astype(np.float32)
+    d = rng.uniform(-1, 1, (70001, 3)).astype(np.float32)
+    got = mcb.strict_fused_pair(a, b, d)
+    assert "scratch" in mcb.api.last_result.route
+    assert rc.same_bits(got, orc.strict_fused_pair(a, b, d))
+
+
+def test_strict_gemm_bit_exact(mcb, orc):
+    rng = np.random.default_rng(12)
+    for m, k, n in [(1, 1, 1), (7, 0, 5), (33, 65, 129), (300, 257, 513)]:
+        a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+        b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+        assert rc.same_bits(mcb.strict_gemm(a, b), orc.strict_gemm(a, b)), (m, k, n)
+
+
+def _config1():
+    a = np.random.default_rng(0).uniform(-1, 1, (512, 256)).astype(np.float32)
+    b = np.random.default_rng(1).uniform(-1, 1, (256, 384)).astype(np.float32)
+    d = np.random.default_rng(2).uniform(-1, 1, (384, 128)).astype(np.float32)
+    return a, b, d
+
+
+def test_config1_bit_exact_host_and_device(mcb, orc):
+    import torch
+    a, b, d = _config1()
+    exp = orc.strict_fused_pair(a, b, d)
+    assert rc.same_bits(mcb.strict_fused_pair(a, b, d), exp)
+    ta, tb, td = (torch.from_numpy(x).cuda() for x in (a, b, d))
+    te = mcb.strict_fused_pair(ta, tb, td)
+    torch.cuda.synchronize()
+    assert rc.same_bits(te.cpu().numpy(), exp)
+
+
+def test_strided_device_operands(mcb, orc):
+    import torch
+    a, b, d = _config1()
+    big = torch.zeros(512, 300, device="cuda")
+    big[:, 10:266] = torch.from_numpy(a).cuda()
+    ta = big[:, 10:266]  # row stride 300, offset base
+    te = mcb.strict_fused_pair(ta, torch.from_numpy(b).cuda(), torch.from_numpy(d).cuda())
+    torch.cuda.synchronize()
+    assert rc.same_bits(te.cpu().numpy(), orc.strict_fused_pair(a, b, d))
