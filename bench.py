@@ -303,6 +303,16 @@ def run_ours(args):
     value = world * flops_step * args.steps / (t_ms_max / 1e3) / 1e12
 
     # ---- end to end through the public API with host buffers -------------------------
+    e2e = None
+    if not args.no_e2e:
+        e2e = _run_e2e(args, lib, ep, sets, descs, dev, stream, world, flops_step, m)
+    _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, working_set, route,
+            clk, e2e)
+
+
+def _run_e2e(args, lib, ep, sets, descs, dev, stream, world, flops_step, m):
+    import torch
+    from matcoredsl_b200 import _abi
     e2e_steps = max(3, min(args.steps, 10))
     xh = torch.empty(m, K_DIM, dtype=torch.bfloat16, pin_memory=True)
     wh = torch.empty(K_DIM, N_DIM, dtype=torch.bfloat16, pin_memory=True)
@@ -334,7 +344,14 @@ def run_ours(args):
     _barrier(world)
     e2e_s_max = _max_over_ranks(e2e_s, world, dev)
     e2e_value = world * flops_step * e2e_steps / e2e_s_max / 1e12
+    return {"value": e2e_value, "unit": UNIT, "steps": e2e_steps,
+            "h2d_bytes_per_step": int(rep_e2e.h2d_bytes),
+            "d2h_bytes_per_step": int(rep_e2e.d2h_bytes),
+            "path": "mcb_gemm_epilogue_v1 with pinned host operands (staged by the library)"}
 
+
+def _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, working_set, route,
+            clk, e2e):
     peaks = _peaks()
     achieved = flops_step / (launch_ms_max / 1e3) / 1e12
     cpu = None
@@ -364,10 +381,7 @@ def run_ours(args):
                          "kernel": "gemm_tc_bf16_kernel",
                          "algorithmic_flops_per_launch": flops_step},
             "clocks": clk.summary(),
-            "e2e": {"value": e2e_value, "unit": UNIT, "steps": e2e_steps,
-                    "h2d_bytes_per_step": int(rep_e2e.h2d_bytes),
-                    "d2h_bytes_per_step": int(rep_e2e.d2h_bytes),
-                    "path": "mcb_gemm_epilogue_v1 with pinned host operands (staged by the library)"},
+            "e2e": e2e,
             "gpu_launches": args.steps,
             "cpu_baseline": cpu,
         }
@@ -385,6 +399,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the host-buffer end-to-end leg (used for short profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
