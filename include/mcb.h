@@ -167,6 +167,24 @@ MCB_API mcb_status mcb_strict_fused_pair_f32_v1(const mcb_tensor *e, const mcb_t
                                                 const mcb_tensor *b, const mcb_tensor *d,
                                                 const mcb_exec *exec) MCB_NOEXCEPT;
 
+/* Allocation-free variant of mcb_strict_fused_pair_f32_v1, for callers that
+ * cannot call cudaMalloc: a host framework that owns every byte of device
+ * memory through its own pool, a latency-critical path that must not trigger
+ * cudaMalloc's implicit device-wide synchronisation, or code that must not
+ * fail for lack of memory midway through a run. It has no counterpart in the
+ * reference. Same bit-exact result; the intermediate panel lives in a fixed
+ * 8 MiB array (2^21 floats) compiled into the library and held on every GPU
+ * that loads it until exit. Limits: all operands device-resident
+ * (MCB_STATUS_UNSUPPORTED_MEMORY_SPACE otherwise), N <= 2^21
+ * (MCB_STATUS_INSUFFICIENT_WORKSPACE otherwise), MCB_EXEC_TIME not accepted.
+ * The first call on each device performs a one-time set-up (it looks up the
+ * array's device address) and should come before any stream capture. All
+ * calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller. */
+MCB_API mcb_status mcb_strict_fused_pair_f32_noalloc_v1(const mcb_tensor *e, const mcb_tensor *a,
+                                                        const mcb_tensor *b, const mcb_tensor *d,
+                                                        const mcb_exec *exec) MCB_NOEXCEPT;
+
 /* ---- Family A: GEMM + fused epilogue ------------------------------------ */
 enum { MCB_BIAS_NONE = 0, MCB_BIAS_ROW = 1 /* b[N] broadcast over rows */,
        MCB_BIAS_FULL = 2 /* boundary [M,N] */ };

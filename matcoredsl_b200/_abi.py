@@ -99,6 +99,7 @@ SIGNATURES = {
     "mcb_candidate_available": (ctypes.c_int32, [ctypes.c_int32]),
     "mcb_strict_gemm_f32_v1": (ctypes.c_int32, [_T, _T, _T, _E]),
     "mcb_strict_fused_pair_f32_v1": (ctypes.c_int32, [_T, _T, _T, _T, _E]),
+    "mcb_strict_fused_pair_f32_noalloc_v1": (ctypes.c_int32, [_T, _T, _T, _T, _E]),
     "mcb_gemm_epilogue_v1": (ctypes.c_int32, [_T, _T, _T, _T, _P(Epilogue), ctypes.c_uint32, _E]),
     "mcb_msm_v1": (ctypes.c_int32, [_T, _T, _T, _T, ctypes.c_double, _E]),
     "mcb_fp8_quantize_blockwise_v1": (ctypes.c_int32, [_T, _T, _T, ctypes.c_int64, _E]),

@@ -34,6 +34,7 @@ SOURCES = {
     "strict.cu": STRICT,
     "gemm_tc.cu": [],
     "simt.cu": [],
+    "noalloc.cu": [],
 }
 HEADERS = ["common.cuh", "internal.h", "epilogue.cuh"]
 

@@ -31,6 +31,14 @@ cudaError_t launch_strict_pair(const float *a, const float *b, const float *d, f
                                int64_t lda, int64_t ldb, int64_t ldd, int64_t lde, int sms,
                                int smem_limit_bytes, cudaStream_t stream, LaunchInfo *info);
 
+// The fused pair with its intermediate panel in a fixed scratch array of
+// `scratch_floats` floats (used by the allocation-free entry point).
+cudaError_t launch_strict_pair_fixed_scratch(const float *a, const float *b, const float *d,
+                                             float *e, float *scratch, int64_t scratch_floats,
+                                             int64_t m, int64_t k, int64_t n, int64_t p,
+                                             int64_t lda, int64_t ldb, int64_t ldd, int64_t lde,
+                                             int sms, cudaStream_t stream, LaunchInfo *info);
+
 // ---- epilogue description shared by the GEMM kernels ----------------------------
 struct Epilogue {
   int bias_mode = 0;  // 0 none, 1 row-broadcast [N], 2 full [M,N]

@@ -191,4 +191,64 @@ cudaError_t launch_strict_pair(const float *a, const float *b, const float *d, f
   return cudaGetLastError();
 }
 
+// The fused pair with the intermediate panel always in a caller-supplied
+// fixed-size scratch array of `scratch_floats` floats. Rows are processed in
+// as many back-to-back launches (same stream) as the array needs, so only one
+// panel of R x N floats has to fit. Returns cudaErrorInvalidValue when even a
+// single-row panel (N floats) does not fit.
+cudaError_t launch_strict_pair_fixed_scratch(const float *a, const float *b, const float *d,
+                                             float *e, float *scratch, int64_t scratch_floats,
+                                             int64_t m, int64_t k, int64_t n, int64_t p,
+                                             int64_t lda, int64_t ldb, int64_t ldd, int64_t lde,
+                                             int sms, cudaStream_t stream, LaunchInfo *info) {
+  if (info) info->launches = 0;
+  if (m == 0 || p == 0) return cudaSuccess;
+  if (n == 0) {  // empty consumer reduction: E = +0, no panel
+    fill_zero_kernel<<<sms, 256, 0, stream>>>(e, m, p, lde);
+    if (info) {
+      info->launches = 1;
+      info->set_route("strict_f32_zero_reduction");
+    }
+    return cudaGetLastError();
+  }
+  int R = pick_rows(m, sms);
+  while (R > 1 && static_cast<int64_t>(R) * n > scratch_floats) R /= 2;
+  if (static_cast<int64_t>(R) * n > scratch_floats) return cudaErrorInvalidValue;
+  const int64_t rows_per_launch = (scratch_floats / (static_cast<int64_t>(R) * n)) * R;
+  const int threads = (n >= 256 || p >= 256) ? 256 : 128;
+  int launches = 0;
+  for (int64_t r0 = 0; r0 < m; r0 += rows_per_launch) {
+    const int64_t mc = m - r0 < rows_per_launch ? m - r0 : rows_per_launch;
+    const int64_t ctas = (mc + R - 1) / R;
+    if (ctas > 0x7fffffff) return cudaErrorInvalidConfiguration;
+    const float *ac = k ? a + r0 * lda : a;
+    float *ec = e + r0 * lde;
+    switch (R) {
+      case 4:
+        strict_pair_kernel<4, false><<<(unsigned)ctas, threads, 0, stream>>>(
+            ac, b, d, ec, scratch, mc, k, n, p, lda, ldb, ldd, lde);
+        break;
+      case 2:
+        strict_pair_kernel<2, false><<<(unsigned)ctas, threads, 0, stream>>>(
+            ac, b, d, ec, scratch, mc, k, n, p, lda, ldb, ldd, lde);
+        break;
+      default:
+        strict_pair_kernel<1, false><<<(unsigned)ctas, threads, 0, stream>>>(
+            ac, b, d, ec, scratch, mc, k, n, p, lda, ldb, ldd, lde);
+        break;
+    }
+    ++launches;
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+  }
+  if (info) {
+    info->launches = launches;
+    info->tile_m = R;
+    info->tile_n = threads;
+    info->ctas = static_cast<int>((rows_per_launch + R - 1) / R);
+    info->set_route("strict_f32_simt_pair_fixed_scratch");
+  }
+  return cudaSuccess;
+}
+
 }  // namespace mcb
