@@ -35,6 +35,7 @@ SOURCES = {
     "gemm_tc.cu": [],
     "simt.cu": [],
     "noalloc.cu": [],
+    "msm_tc.cu": [],
 }
 HEADERS = ["common.cuh", "internal.h", "epilogue.cuh"]
 

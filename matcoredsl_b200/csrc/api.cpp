@@ -69,6 +69,21 @@ bool encode_tmap_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *bas
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 4D bf16 map {d0 (innermost), d1, d2, d3} with byte strides s1..s3, box
+// {64, 128, 1, 1} and 128-byte swizzle (the MSM Q/K/V tiles).
+bool encode_tmap_4d_bf16(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1,
+                         uint64_t d2, uint64_t d3, uint64_t s1, uint64_t s2, uint64_t s3) {
+  auto fn = encoder();
+  if (!fn) return false;
+  cuuint64_t dims[4] = {d0, d1, d2, d3};
+  cuuint64_t strides[3] = {s1, s2, s3};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides,
+            box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace mcb
 
 namespace {
@@ -169,11 +184,23 @@ mcb_status check_tensor(const mcb_tensor *t, uint32_t min_rank, uint32_t max_ran
   if (elems > 0) {
     if (!t->data) return MCB_STATUS_INVALID_ARGUMENT;
     if (t->strides[t->rank - 1] != 1) return MCB_STATUS_UNSUPPORTED_LAYOUT;
-    // Outer strides must step over a whole inner slice (row-major, no
-    // self-overlap); a dimension of extent 1 may carry any stride.
-    for (int i = static_cast<int>(t->rank) - 2; i >= 0; --i)
-      if (t->dims[i] > 1 && t->strides[i] < t->dims[i + 1] * t->strides[i + 1])
-        return MCB_STATUS_UNSUPPORTED_LAYOUT;
+    // Any positive strides describe a valid view (e.g. heads interleaved in
+    // a packed QKV row). The element sets of different indices must not
+    // collide: ordering the dimensions by stride, each stride must step over
+    // the whole block spanned by the smaller ones. Extent-1 dims are free.
+    int order[MCB_MAX_RANK];
+    int nd = 0;
+    for (uint32_t i = 0; i < t->rank; ++i) {
+      if (t->dims[i] <= 1) continue;
+      if (t->strides[i] <= 0) return MCB_STATUS_UNSUPPORTED_LAYOUT;
+      order[nd++] = static_cast<int>(i);
+    }
+    std::sort(order, order + nd, [t](int x, int y) { return t->strides[x] < t->strides[y]; });
+    int64_t block = 1;
+    for (int j = 0; j < nd; ++j) {
+      if (t->strides[order[j]] < block) return MCB_STATUS_UNSUPPORTED_LAYOUT;
+      block = t->strides[order[j]] * t->dims[order[j]];
+    }
     if (reinterpret_cast<uintptr_t>(t->data) % dtype_size(t->dtype) != 0)
       return MCB_STATUS_INVALID_ALIGNMENT;
   }
@@ -544,7 +571,7 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
 }
 
 // ---- Family C -----------------------------------------------------------------------------
-constexpr bool kHaveMsmTc = false;
+constexpr bool kHaveMsmTc = true;
 
 mcb_status msm_impl(const mcb_tensor *o, const mcb_tensor *q, const mcb_tensor *k,
                     const mcb_tensor *v, double scale, const mcb_exec *exec) {
@@ -602,10 +629,11 @@ mcb_status msm_impl(const mcb_tensor *o, const mcb_tensor *q, const mcb_tensor *
                      (reinterpret_cast<uintptr_t>(dk) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(dv) % 16 == 0) &&
                      (reinterpret_cast<uintptr_t>(dout) % 16 == 0);
-  if (tc_ok) {
+  err = cudaErrorNotSupported;
+  if (tc_ok)
     err = mcb::launch_msm_tc_bf16(dq, dk, dv, dout, sh, static_cast<float>(scale),
                                   call.ctx()->status, call.sms(), call.stream(), &info);
-  } else {
+  if (err == cudaErrorNotSupported) {
     if (sh.dqk > 256 || sh.dv > 256) return MCB_STATUS_UNAVAILABLE_VARIANT;
     err = mcb::launch_msm_simt(dq, dk, dv, dout, static_cast<int>(q->dtype), sh,
                                static_cast<float>(scale), call.stream(), &info);

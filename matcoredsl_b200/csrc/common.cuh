@@ -78,6 +78,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   }
 }
 
+// Warp-uniform wait: every lane waits and the warp agrees on the outcome, so
+// the warp-collective tcgen05 instructions that follow run with all 32 lanes
+// or with none (a lane that timed out never leaves the others stranded).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                               uint32_t *status, uint32_t err_bit) {
+  const bool ok = mbar_wait(bar, parity, abort, status, err_bit);
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
 // ---- TMA ---------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -198,6 +207,26 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 }
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// tcgen05.ld writes its destination registers asynchronously. After the
+// wait, pass the registers through an empty asm so that no use of them can
+// be scheduled above the wait.
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                 "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                 "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+// Load 32 columns and wait for them.
+__device__ __forceinline__ void tmem_ld32_sync(uint32_t taddr, uint32_t (&r)[32]) {
+  tmem_ld_32x32b_x32(taddr, r);
+  tmem_ld_wait();
+  reg_fence(r);
 }
 // 32 lanes x 16 columns store (thread i writes lane base+i).
 __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {

@@ -254,7 +254,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BM;
       const int64_t n0 = static_cast<int64_t>(tile % p.n_tiles) * BN;
-      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.status, kErrTimeoutAccum)) break;
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.status, kErrTimeoutAccum))
+        break;
       tc_fence_after();
       const int64_t row = m0 + sub * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
@@ -263,8 +264,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int c = 0; c < BN; c += 32) {
         if (n0 + c >= p.n) break;
         uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c, r);
-        tmem_ld_wait();
+        tmem_ld32_sync(t_row + c, r);
         epilogue_chunk(p, r, row, n0 + c);
       }
       tc_fence_before();

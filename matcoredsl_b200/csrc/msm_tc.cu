@@ -1,0 +1,438 @@
+// Matmul-softmax-matmul (Family C) on tcgen05 tensor cores, bf16, D = 128.
+//
+//   O[b,h] = softmax(scale * Q[b,h] K[b,h]^T) V[b,h]      (src/fusion_emitter_family_c.cpp)
+//
+// One work unit = (b, h, 128-row query block). Persistent CTAs (one per SM,
+// 224 threads) loop over units; consecutive units share (b, h) so K/V stay
+// in L2 for the CTAs running at the same time.
+//
+//   warp 0      TMA producer: Q (once per unit), K tiles into a 3-stage ring,
+//               V tiles into a 2-stage ring (128 keys x 128 dims, 128B swizzle).
+//   warp 1      TMEM owner (512 columns: S0 | S1 | O) and single-thread MMA
+//               issuer: S_t = Q K_t^T (M=128, N=128, K=128) into S[t%2], then
+//               O += P_{t-1} V_{t-1} with P from shared memory and V consumed
+//               MN-major. S_{t+1} is issued before PV_t so the tensor core
+//               works on the next score tile while the softmax runs.
+//   warps 2-5   softmax: thread r owns query row r (its TMEM lane). It loads
+//               the 128 scores of its row, takes the row max in registers (no
+//               shuffles), computes p = 2^(s*c - m*c) with c = scale*log2(e),
+//               accumulates the row sum, writes P (bf16) in the 128B-swizzled
+//               K-major layout the MMA reads, and signals the MMA warp.
+//               The running max is lazy: O and l are rescaled (in TMEM, by
+//               the owning thread) only when a tile's max exceeds the
+//               reference max by more than 2^8 in probability, which keeps
+//               every p <= 256 and makes rescales rare. At the end of a unit
+//               the same threads read O, divide by l and store bf16.
+// S and P never touch HBM.
+//
+// Roofline (config 3, [8,32,4096,128]): 4*B*H*S^2*D = 2.199 TFLOP (exp
+// excluded) against the bf16 dense tensor peak; the exponentials
+// (B*H*S^2 = 4.3e9 ex2 on the 16/clk/SM special-function units) are a
+// co-bound of the same order.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace mcb {
+namespace {
+
+constexpr int D = 128;        // head dim (QK and V)
+constexpr int BQ = 128;       // query rows per unit
+constexpr int BKV = 128;      // keys per tile
+constexpr int KSTAGES = 3, VSTAGES = 2;
+constexpr int TILE_BYTES = BKV * D * 2;  // 32 KiB (also Q and P)
+constexpr int CHUNK_BYTES = 128 * 128;   // one 64-column half of a tile
+constexpr int THREADS = 192;  // 6 warps: producer, MMA, 4 softmax (one per TMEM lane quarter)
+constexpr int TMEM_COLS = 512;
+constexpr uint32_t S_COL0 = 0, O_COL = 256;
+
+struct Smem {
+  uint8_t q[TILE_BYTES];
+  uint8_t k[KSTAGES][TILE_BYTES];
+  uint8_t v[VSTAGES][TILE_BYTES];
+  uint8_t p[TILE_BYTES];
+  uint64_t q_full, q_empty;
+  uint64_t k_full[KSTAGES], k_empty[KSTAGES];
+  uint64_t v_full[VSTAGES], v_empty[VSTAGES];
+  uint64_t s_full[2], s_free[2];
+  uint64_t p_full, p_free;
+  uint64_t o_full, o_empty;
+  uint64_t drain;
+  uint32_t tmem_slot;
+  int abort_flag;
+};
+constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
+
+struct Params {
+  int64_t heads, qblocks, nkv_tiles, units;
+  int64_t o_s[3];  // output element strides [batch, head, row]
+  float c;         // scale * log2(e)
+  __nv_bfloat16 *o;
+  uint32_t *status;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// K-major SW128 descriptor for the K=16 slice `kk` (0..7) of a 128x128 bf16
+// tile stored as two 64-column halves of 16 KiB.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk) {
+  return make_sdesc_sw128(base + (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32, 16, 1024);
+}
+// MN-major SW128 descriptor (V as the B operand): K = keys advance 16 rows of
+// 128 bytes; the two 64-column halves are LBO = 16 KiB apart.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int kk) {
+  return make_sdesc_sw128(base + kk * 2048, CHUNK_BYTES, 1024);
+}
+
+__device__ __forceinline__ void tma_load_4d(void *dst, const void *tmap, uint64_t *bar, int32_t x,
+                                            int32_t y, int32_t z, int32_t w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
+__device__ __forceinline__ void unit_coords(const Params &p, int64_t u, int32_t &b, int32_t &h,
+                                            int32_t &q0) {
+  const int64_t qb = u % p.qblocks;
+  const int64_t bh = u / p.qblocks;
+  h = static_cast<int32_t>(bh % p.heads);
+  b = static_cast<int32_t>(bh / p.heads);
+  q0 = static_cast<int32_t>(qb * BQ);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    msm_tc_bf16_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                       const __grid_constant__ CUtensorMap tv, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem &sm = *reinterpret_cast<Smem *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  volatile int *abort_flag = &sm.abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.q_empty, 1);
+    for (int s = 0; s < KSTAGES; ++s) {
+      mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+    }
+    for (int s = 0; s < VSTAGES; ++s) {
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.s_full[s], 1);
+      mbar_init(&sm.s_free[s], 128);
+    }
+    mbar_init(&sm.p_full, 128);
+    mbar_init(&sm.p_free, 1);
+    mbar_init(&sm.o_full, 1);
+    mbar_init(&sm.o_empty, 128);
+    mbar_init(&sm.drain, 1);
+    sm.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_slot;
+  const int64_t nkv = p.nkv_tiles;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      uint32_t kt = 0, vt = 0, uc = 0;
+      for (int64_t u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
+        int32_t b, h, q0;
+        unit_coords(p, u, b, h, q0);
+        if (!mbar_wait(&sm.q_empty, (uc & 1) ^ 1, abort_flag, p.status, kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&sm.q_full, TILE_BYTES);
+        tma_load_4d(sm.q, &tq, &sm.q_full, 0, q0, h, b);
+        tma_load_4d(sm.q + CHUNK_BYTES, &tq, &sm.q_full, 64, q0, h, b);
+        bool ok = true;
+        for (int64_t t = 0; t < nkv && ok; ++t, ++kt, ++vt) {
+          const int ks = kt % KSTAGES, vs = vt % VSTAGES;
+          const int32_t key0 = static_cast<int32_t>(t * BKV);
+          ok = mbar_wait(&sm.k_empty[ks], ((kt / KSTAGES) & 1) ^ 1, abort_flag, p.status,
+                         kErrTimeoutEmpty);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&sm.k_full[ks], TILE_BYTES);
+          tma_load_4d(sm.k[ks], &tk, &sm.k_full[ks], 0, key0, h, b);
+          tma_load_4d(sm.k[ks] + CHUNK_BYTES, &tk, &sm.k_full[ks], 64, key0, h, b);
+          ok = mbar_wait(&sm.v_empty[vs], ((vt / VSTAGES) & 1) ^ 1, abort_flag, p.status,
+                         kErrTimeoutEmpty);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&sm.v_full[vs], TILE_BYTES);
+          tma_load_4d(sm.v[vs], &tv, &sm.v_full[vs], 0, key0, h, b);
+          tma_load_4d(sm.v[vs] + CHUNK_BYTES, &tv, &sm.v_full[vs], 64, key0, h, b);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc_s = make_idesc(1, 1, 0, 0, BQ, BKV);
+      const uint32_t idesc_o = make_idesc(1, 1, 0, 1, BQ, D);
+      const uint32_t q_addr = smem_u32(sm.q), p_addr = smem_u32(sm.p);
+      uint32_t st = 0, pt = 0, uc = 0;
+      bool ok = true;
+      auto issue_s = [&]() -> bool {
+        const int sb = st & 1, ks = st % KSTAGES;
+        if (!mbar_wait(&sm.s_free[sb], ((st >> 1) & 1) ^ 1, abort_flag, p.status, kErrTimeoutAccum))
+          return false;
+        if (!mbar_wait(&sm.k_full[ks], (st / KSTAGES) & 1, abort_flag, p.status, kErrTimeoutFull))
+          return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sm.k[ks]);
+        const uint32_t d_tmem = tmem + S_COL0 + sb * BKV;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          mma_f16_ss(d_tmem, kmajor_desc(q_addr, kk), kmajor_desc(k_addr, kk), idesc_s,
+                     kk ? 1u : 0u);
+        mma_commit(&sm.k_empty[ks]);
+        mma_commit(&sm.s_full[sb]);
+        ++st;
+        return true;
+      };
+      for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uc) {
+        if (!mbar_wait(&sm.q_full, uc & 1, abort_flag, p.status, kErrTimeoutFull)) break;
+        tc_fence_after();
+        if (!(ok = issue_s())) break;
+        for (int64_t t = 0; t < nkv; ++t) {
+          if (t + 1 < nkv) {
+            if (!(ok = issue_s())) break;
+          } else {
+            mma_commit(&sm.q_empty);  // every S MMA of this unit has been issued
+          }
+          if (t == 0 &&
+              !(ok = mbar_wait(&sm.o_empty, (uc & 1) ^ 1, abort_flag, p.status, kErrTimeoutAccum)))
+            break;
+          const int vs = pt % VSTAGES;
+          if (!(ok = mbar_wait(&sm.v_full[vs], (pt / VSTAGES) & 1, abort_flag, p.status,
+                               kErrTimeoutFull)))
+            break;
+          if (!(ok = mbar_wait(&sm.p_full, pt & 1, abort_flag, p.status, kErrTimeoutAccum))) break;
+          tc_fence_after();
+          const uint32_t v_addr = smem_u32(sm.v[vs]);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk)
+            mma_f16_ss(tmem + O_COL, kmajor_desc(p_addr, kk), mnmajor_desc(v_addr, kk), idesc_o,
+                       (t | kk) ? 1u : 0u);
+          mma_commit(&sm.v_empty[vs]);
+          mma_commit(&sm.p_free);
+          ++pt;
+        }
+        if (!ok) break;
+        mma_commit(&sm.o_full);
+      }
+      mma_commit(&sm.drain);
+      if (!mbar_wait(&sm.drain, 0, nullptr, p.status, kErrTimeoutDrain)) *abort_flag = 1;
+    }
+  } else {
+    // ---------------- softmax + output ----------------
+    const int sub = warp & 3;
+    const int row = sub * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(sub * 32) << 16);
+    uint8_t *p_row = sm.p + row * 128;
+    const int rsw = row & 7;
+    uint32_t s_cnt = 0, p_cnt = 0, uc = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uc) {
+      int32_t b, h, q0;
+      unit_coords(p, u, b, h, q0);
+      float m_ref = -INFINITY, l = 0.0f;
+      for (int64_t t = 0; t < nkv; ++t) {
+        const int sb = s_cnt & 1;
+        if (!(ok = mbar_wait_warp(&sm.s_full[sb], (s_cnt >> 1) & 1, abort_flag, p.status,
+                             kErrTimeoutAccum)))
+          break;
+        tc_fence_after();
+        uint32_t s[128];
+        {
+          uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
+          uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
+          uint32_t (&s2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[64]);
+          uint32_t (&s3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[96]);
+          const uint32_t a = lane_base + S_COL0 + sb * BKV;
+          tmem_ld_32x32b_x32(a, s0);
+          tmem_ld_32x32b_x32(a + 32, s1);
+          tmem_ld_32x32b_x32(a + 64, s2);
+          tmem_ld_32x32b_x32(a + 96, s3);
+          tmem_ld_wait();
+          reg_fence(s0);
+          reg_fence(s1);
+          reg_fence(s2);
+          reg_fence(s3);
+        }
+        tc_fence_before();
+        mbar_arrive(&sm.s_free[sb]);
+        ++s_cnt;
+        float mx = __uint_as_float(s[0]);
+#pragma unroll
+        for (int i = 1; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(s[i]));
+        bool need = false;
+        if (t == 0) {
+          m_ref = mx;
+        } else if ((mx - m_ref) * p.c > 8.0f) {
+          need = true;
+        }
+        if (__any_sync(0xffffffffu, need)) {
+          // Rescale O and l for the rows whose max grew: O must be complete
+          // up to PV_{t-1} and PV_t cannot start before this thread signals.
+          if (!(ok = mbar_wait_warp(&sm.p_free, (p_cnt - 1) & 1, abort_flag, p.status,
+                               kErrTimeoutAccum)))
+            break;
+          tc_fence_after();
+          const float f = need ? ex2((m_ref - mx) * p.c) : 1.0f;
+          // Load / scale / store the 128 O columns of this row in 4 chunks.
+#pragma unroll 1
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t o[32];
+            tmem_ld32_sync(lane_base + O_COL + c0, o);
+            uint32_t lo[16], hi[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              lo[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+              hi[i] = __float_as_uint(__uint_as_float(o[16 + i]) * f);
+            }
+            tmem_st_32x32b_x16(lane_base + O_COL + c0, lo);
+            tmem_st_32x32b_x16(lane_base + O_COL + c0 + 16, hi);
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          if (need) {
+            l *= f;
+            m_ref = mx;
+          }
+        }
+        const float mc = m_ref * p.c;
+        uint32_t pk[64];
+        float psum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float e0 = ex2(fmaf(__uint_as_float(s[2 * i]), p.c, -mc));
+          const float e1 = ex2(fmaf(__uint_as_float(s[2 * i + 1]), p.c, -mc));
+          psum += e0 + e1;
+          pk[i] = pack_bf16x2(e0, e1);
+        }
+        l += psum;
+        // P buffer is free once PV of the previous tile has completed.
+        if (!(ok = mbar_wait_warp(&sm.p_free, (p_cnt & 1) ^ 1, abort_flag, p.status,
+                             kErrTimeoutAccum)))
+          break;
+#pragma unroll
+        for (int u16 = 0; u16 < 16; ++u16) {
+          const int chunk = u16 >> 3, j = u16 & 7;
+          uint4 v4 = make_uint4(pk[u16 * 4], pk[u16 * 4 + 1], pk[u16 * 4 + 2], pk[u16 * 4 + 3]);
+          *reinterpret_cast<uint4 *>(p_row + chunk * CHUNK_BYTES + ((j ^ rsw) << 4)) = v4;
+        }
+        fence_async_smem();
+        mbar_arrive(&sm.p_full);
+        ++p_cnt;
+      }
+      if (!ok) break;
+      // ---- output: O / l -> bf16 ----
+      if (!(ok = mbar_wait_warp(&sm.o_full, uc & 1, abort_flag, p.status, kErrTimeoutAccum)))
+        break;
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      __nv_bfloat16 *orow =
+          p.o + b * p.o_s[0] + h * p.o_s[1] + static_cast<int64_t>(q0 + row) * p.o_s[2];
+#pragma unroll 1
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t o[32];
+        tmem_ld32_sync(lane_base + O_COL + c0, o);
+        uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(o[q * 8 + 0]) * inv, __uint_as_float(o[q * 8 + 1]) * inv);
+          w.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv, __uint_as_float(o[q * 8 + 3]) * inv);
+          w.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv, __uint_as_float(o[q * 8 + 5]) * inv);
+          w.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv, __uint_as_float(o[q * 8 + 7]) * inv);
+          dst[q] = w;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sm.o_empty);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+bool encode_tmap_4d_bf16(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
+                         uint64_t d3, uint64_t s1, uint64_t s2, uint64_t s3);
+
+cudaError_t launch_msm_tc_bf16(const void *q, const void *k, const void *v, void *o,
+                               const MsmShape &s, float scale, uint32_t *status, int sms,
+                               cudaStream_t stream, LaunchInfo *info) {
+  if (s.m % BQ || s.n % BKV || s.dqk != D || s.dv != D) return cudaErrorNotSupported;
+  CUtensorMap tq, tk, tv;
+  auto enc = [&](CUtensorMap *map, const void *base, int64_t rows, const int64_t *st) {
+    // dims {D, rows, heads, batch}; byte strides of rows/heads/batch. A unit
+    // dimension gets a harmless stride (TMA only needs it 16-byte aligned).
+    const uint64_t srow = static_cast<uint64_t>(st[2]) * 2;
+    const uint64_t sh = s.heads > 1 ? static_cast<uint64_t>(st[1]) * 2 : srow * rows;
+    const uint64_t sb = s.batch > 1 ? static_cast<uint64_t>(st[0]) * 2 : sh * s.heads;
+    return encode_tmap_4d_bf16(map, base, D, rows, s.heads, s.batch, srow, sh, sb);
+  };
+  // cudaErrorNotSupported (nothing launched) lets the caller take another kernel.
+  if (!enc(&tq, q, s.m, s.q_s) || !enc(&tk, k, s.n, s.k_s) || !enc(&tv, v, s.n, s.v_s))
+    return cudaErrorNotSupported;
+  Params p;
+  p.heads = s.heads;
+  p.qblocks = s.m / BQ;
+  p.nkv_tiles = s.n / BKV;
+  p.units = s.batch * s.heads * p.qblocks;
+  for (int i = 0; i < 3; ++i) p.o_s[i] = s.o_s[i];
+  p.c = scale * 1.4426950408889634f;
+  p.o = static_cast<__nv_bfloat16 *>(o);
+  p.status = status;
+  cudaError_t e = cudaFuncSetAttribute(msm_tc_bf16_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(SMEM_BYTES));
+  if (e != cudaSuccess) return e;
+  const int grid = static_cast<int>(p.units < sms ? p.units : sms);
+  msm_tc_bf16_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  if (info) {
+    info->launches = 1;
+    info->tile_m = BQ;
+    info->tile_n = BKV;
+    info->tile_k = D;
+    info->stages = KSTAGES;
+    info->ctas = grid;
+    info->set_route("tcgen05_bf16_msm");
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace mcb

@@ -42,20 +42,85 @@ def test_family_c_reference_cases(mcb, orc, case):
         assert np.max(np.abs(ref - orc.msm(q, k, v, 1 / np.sqrt(dqk)))) > 5e-2
 
 
-@pytest.mark.parametrize("shape", [(1, 2, 256, 128), (2, 3, 384, 128), (1, 1, 200, 128),
-                                   (2, 2, 128, 64)])
-def test_bf16_batched(mcb, orc, shape):
-    import torch
+def _bf16_case(shape, seed, kv_len=None, k_growth=0.0):
     b, h, s, d = shape
-    rng = np.random.default_rng(sum(shape))
-    qh, qf = gu.bf16_pair(rng.standard_normal(shape, dtype=np.float32))
-    kh, kf = gu.bf16_pair(rng.standard_normal(shape, dtype=np.float32))
-    vh, vf = gu.bf16_pair(rng.standard_normal(shape, dtype=np.float32))
-    scale = d ** -0.5
+    n = kv_len or s
+    rng = np.random.default_rng(seed)
+    q = rng.standard_normal((b, h, s, d), dtype=np.float32)
+    k = rng.standard_normal((b, h, n, d), dtype=np.float32)
+    v = rng.standard_normal((b, h, n, d), dtype=np.float32)
+    if k_growth:  # later key tiles score higher: forces the running max to grow
+        k *= (1.0 + k_growth * (np.arange(n) // 128))[None, None, :, None].astype(np.float32)
+    return [gu.bf16_pair(x) for x in (q, k, v)]
+
+
+def _check_msm(mcb, orc, pairs, scale, route, pairs_to_check=None):
+    import torch
+    (qh, qf), (kh, kf), (vh, vf) = pairs
     o = mcb.msm(gu.to_dev_bf16(qh), gu.to_dev_bf16(kh), gu.to_dev_bf16(vh), scale)
+    assert mcb.api.last_result.route == route
     assert o.dtype == torch.bfloat16
+    got = gu.from_dev(o)
+    b, h = qh.shape[:2]
+    todo = pairs_to_check or [(bi, hi) for bi in range(b) for hi in range(h)]
+    for bi, hi in todo:
+        ref = orc.msm(qf[bi, hi], kf[bi, hi], vf[bi, hi], scale)
+        assert orc.rel_frobenius(got[bi, hi], ref) < 1e-2, (bi, hi)
+
+
+@pytest.mark.parametrize("shape,route", [
+    ((1, 2, 256, 128), "tcgen05_bf16_msm"),
+    ((2, 3, 384, 128), "tcgen05_bf16_msm"),
+    ((1, 1, 128, 128), "tcgen05_bf16_msm"),
+    ((1, 1, 200, 128), "simt_online_softmax_msm"),
+    ((2, 2, 128, 64), "simt_online_softmax_msm"),
+])
+def test_bf16_batched(mcb, orc, shape, route):
+    _check_msm(mcb, orc, _bf16_case(shape, sum(shape)), shape[-1] ** -0.5, route)
+
+
+def test_tcgen05_rescale_path(mcb, orc):
+    """Key tiles with growing scores make the running max jump several times."""
+    _check_msm(mcb, orc, _bf16_case((1, 2, 256, 128), 5, kv_len=1024, k_growth=0.6),
+               128 ** -0.5, "tcgen05_bf16_msm")
+
+
+def test_tcgen05_unscaled_reference_semantics(mcb, orc):
+    """scale = 1 (the reference's mc.softmax(Q @ K.T)): scores of std ~11."""
+    _check_msm(mcb, orc, _bf16_case((1, 1, 256, 128), 6, kv_len=640), 1.0, "tcgen05_bf16_msm")
+
+
+def test_tcgen05_rectangular_and_strided(mcb, orc):
+    """M != N, and Q/K/V as strided views of a packed [B, S, 3, H, D] tensor."""
+    import torch
+    b, s, h, d, n = 2, 256, 2, 128, 384
+    rng = np.random.default_rng(9)
+    packed = rng.standard_normal((b, n, 3, h, d), dtype=np.float32)
+    ph, pf = gu.bf16_pair(packed)
+    t = gu.to_dev_bf16(ph)
+    q = t[:, :s, 0].permute(0, 2, 1, 3)   # [B, H, S, D] with row stride 3*H*D
+    k = t[:, :, 1].permute(0, 2, 1, 3)
+    v = t[:, :, 2].permute(0, 2, 1, 3)
+    o = mcb.msm(q, k, v, d ** -0.5)
+    assert mcb.api.last_result.route == "tcgen05_bf16_msm"
     got = gu.from_dev(o)
     for bi in range(b):
         for hi in range(h):
-            ref = orc.msm(qf[bi, hi], kf[bi, hi], vf[bi, hi], scale)
-            assert orc.rel_frobenius(got[bi, hi], ref) < 1e-2, (bi, hi)
+            ref = orc.msm(pf[bi, :s, 0, hi], pf[bi, :, 1, hi], pf[bi, :, 2, hi], d ** -0.5)
+            assert orc.rel_frobenius(got[bi, hi], ref) < 1e-2
+
+
+def config3_pairs(bh_subset):
+    """Q, K, V [8,32,4096,128] ~ N(0,1), seed 20, drawn Q, K, V."""
+    rng = np.random.default_rng(20)
+    shape = (8, 32, 4096, 128)
+    return [rng.standard_normal(shape, dtype=np.float32) for _ in range(3)]
+
+
+def test_config3_full_size_sampled(mcb, orc):
+    q, k, v = config3_pairs(None)
+    pairs = [gu.bf16_pair(x) for x in (q, k, v)]
+    del q, k, v
+    sample = [(0, 0), (3, 17), (5, 31), (7, 9)]
+    _check_msm(mcb, orc, pairs, 128 ** -0.5, "tcgen05_bf16_msm", sample)
+    assert mcb.device_status(0) == 0
