@@ -167,6 +167,36 @@ def msm(q, k, v, scale=1.0, out=None, *, device=-1, flags=0):
     return out
 
 
+def fp8_quantize_blockwise(x, block=128, fmt="e4m3", *, device=-1, flags=0):
+    """(q, scales): per-(block x block) absmax scaling s = absmax/fmt_max,
+    q = sat_RNE(x / s) as e4m3 or e5m2 codes."""
+    rows, cols = x.shape
+    sshape = ((rows + block - 1) // block, (cols + block - 1) // block)
+    if _is_torch(x):
+        torch = _torch()
+        qd = torch.float8_e4m3fn if fmt == "e4m3" else torch.float8_e5m2
+        q = torch.empty(rows, cols, dtype=qd, device=x.device)
+        s = torch.empty(sshape, dtype=torch.float32, device=x.device)
+    else:
+        qd = _mld.float8_e4m3fn if fmt == "e4m3" else _mld.float8_e5m2
+        q = np.empty((rows, cols), dtype=qd)
+        s = np.empty(sshape, dtype=np.float32)
+    _call("mcb_fp8_quantize_blockwise_v1", [("q", q), ("scales", s), ("x", x)], [int(block)],
+          device, flags)
+    return q, s
+
+
+def gemm_fp8_blockscaled(a, sa, bt, sbt, *, block=128, out=None, out_dtype="bf16", device=-1,
+                         flags=0):
+    """C = (sa.A) (sbt.Bt)^T with fp8 A [M,K], Bt [N,K] and per-block f32 scales."""
+    if out is None:
+        out = _empty_like_out(a, (a.shape[0], bt.shape[0]), out_dtype)
+    _call("mcb_gemm_fp8_blockscaled_v1",
+          [("c", out), ("a", a), ("sa", sa), ("bt", bt), ("sbt", sbt)], [int(block)],
+          device, flags)
+    return out
+
+
 def device_status(device=0, clear=False) -> int:
     w = ctypes.c_uint32(0)
     _abi.check(_abi.load().mcb_device_status(device, ctypes.byref(w), 1 if clear else 0),

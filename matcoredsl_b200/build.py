@@ -36,6 +36,7 @@ SOURCES = {
     "simt.cu": [],
     "noalloc.cu": [],
     "msm_tc.cu": [],
+    "fp8.cu": [],
 }
 HEADERS = ["common.cuh", "internal.h", "epilogue.cuh"]
 

@@ -642,6 +642,104 @@ mcb_status msm_impl(const mcb_tensor *o, const mcb_tensor *q, const mcb_tensor *
   return call.finish(o, dout, info, err);
 }
 
+// ---- FP8 ---------------------------------------------------------------------------------
+bool is_fp8(mcb_dtype t) { return t == MCB_DTYPE_E4M3 || t == MCB_DTYPE_E5M2; }
+
+// Dense row-major rank-2 tensor of the given shape.
+bool dense2(const mcb_tensor *t, int64_t rows, int64_t cols) {
+  return t->rank == 2 && t->dims[0] == rows && t->dims[1] == cols &&
+         (rows <= 1 || t->strides[0] == cols) && t->strides[1] == 1;
+}
+
+mcb_status fp8_quantize_impl(const mcb_tensor *q, const mcb_tensor *scales, const mcb_tensor *x,
+                             int64_t block, const mcb_exec *exec) {
+  mcb_status s;
+  if ((s = check_tensor(x, 2, 2)) || (s = check_tensor(q, 2, 2)) ||
+      (s = check_tensor(scales, 2, 2)))
+    return s;
+  if (block <= 0) return MCB_STATUS_INVALID_ARGUMENT;
+  if (x->dtype != MCB_DTYPE_F32 && x->dtype != MCB_DTYPE_BF16) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  if (!is_fp8(q->dtype) || scales->dtype != MCB_DTYPE_F32) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  const int64_t rows = x->dims[0], cols = x->dims[1];
+  if (!dense2(q, rows, cols)) return MCB_STATUS_SHAPE_MISMATCH;
+  if (!dense2(scales, (rows + block - 1) / block, (cols + block - 1) / block))
+    return MCB_STATUS_SHAPE_MISMATCH;
+  if (overlaps(q, x) || overlaps(scales, x) || overlaps(q, scales))
+    return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({x, q, scales}, &host))) return s;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  void *dx, *dq, *ds;
+  if ((s = call.device_ptr(x, true, &dx)) || (s = call.device_ptr(q, false, &dq)) ||
+      (s = call.device_ptr(scales, false, &ds)))
+    return s;
+  LaunchInfo info;
+  call.mark_compute_start();
+  cudaError_t err = mcb::launch_fp8_quantize(
+      dx, static_cast<int>(x->dtype), static_cast<uint8_t *>(dq), static_cast<float *>(ds), rows,
+      cols, x->strides[0], block, q->dtype == MCB_DTYPE_E5M2, call.stream(), &info);
+  call.mark_compute_end();
+  if (err != cudaSuccess) return from_cuda(err);
+  // Both outputs come back for host callers.
+  if (host && numel(scales) > 0) {
+    if (cudaMemcpyAsync(scales->data, ds, span_bytes(scales), cudaMemcpyDeviceToHost,
+                        call.stream()) != cudaSuccess)
+      return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+  return call.finish(q, dq, info, cudaSuccess);
+}
+
+mcb_status gemm_fp8_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_tensor *sa,
+                         const mcb_tensor *bt, const mcb_tensor *sbt, int64_t block,
+                         const mcb_exec *exec) {
+  mcb_status s;
+  if ((s = check_tensor(a, 2, 2)) || (s = check_tensor(bt, 2, 2)) || (s = check_tensor(sa, 2, 2)) ||
+      (s = check_tensor(sbt, 2, 2)) || (s = check_tensor(c, 2, 2)))
+    return s;
+  if (block <= 0) return MCB_STATUS_INVALID_ARGUMENT;
+  if (!is_fp8(a->dtype) || !is_fp8(bt->dtype)) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  if (sa->dtype != MCB_DTYPE_F32 || sbt->dtype != MCB_DTYPE_F32) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  if (c->dtype != MCB_DTYPE_BF16 && c->dtype != MCB_DTYPE_F32) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  const int64_t m = a->dims[0], k = a->dims[1], n = bt->dims[0];
+  const int64_t kbs = (k + block - 1) / block;
+  if (!dense2(a, m, k) || !dense2(bt, n, k) || !dense2(c, m, n) ||
+      !dense2(sa, (m + block - 1) / block, kbs) || !dense2(sbt, (n + block - 1) / block, kbs))
+    return MCB_STATUS_SHAPE_MISMATCH;
+  if (overlaps(c, a) || overlaps(c, bt) || overlaps(c, sa) || overlaps(c, sbt))
+    return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({a, bt, sa, sbt, c}, &host))) return s;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  void *da, *db, *dsa, *dsb, *dc;
+  if ((s = call.device_ptr(a, true, &da)) || (s = call.device_ptr(bt, true, &db)) ||
+      (s = call.device_ptr(sa, true, &dsa)) || (s = call.device_ptr(sbt, true, &dsb)) ||
+      (s = call.device_ptr(c, false, &dc)))
+    return s;
+  LaunchInfo info;
+  call.mark_compute_start();
+  const int ae5 = a->dtype == MCB_DTYPE_E5M2, be5 = bt->dtype == MCB_DTYPE_E5M2;
+  const int cbf = c->dtype == MCB_DTYPE_BF16;
+  cudaError_t err = cudaErrorNotSupported;
+  const bool aligned = (reinterpret_cast<uintptr_t>(da) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(db) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(dc) % 16 == 0) && (n % 8 == 0);
+  if (aligned && k > 0)
+    err = mcb::launch_gemm_fp8_tc(static_cast<const uint8_t *>(da), ae5,
+                                  static_cast<const float *>(dsa), static_cast<const uint8_t *>(db),
+                                  be5, static_cast<const float *>(dsb), dc, cbf, m, n, k, block,
+                                  call.ctx()->status, call.sms(), call.stream(), &info);
+  if (err == cudaErrorNotSupported)
+    err = mcb::launch_gemm_fp8_simt(static_cast<const uint8_t *>(da), ae5,
+                                    static_cast<const float *>(dsa),
+                                    static_cast<const uint8_t *>(db), be5,
+                                    static_cast<const float *>(dsb), dc, cbf, m, n, k, block,
+                                    call.stream(), &info);
+  call.mark_compute_end();
+  return call.finish(c, dc, info, err);
+}
+
 // ---- device buffers ------------------------------------------------------------------------
 std::mutex g_buf_mu;
 std::unordered_map<uint64_t, mcb_buffer> g_bufs;  // ptr -> live handle
@@ -787,17 +885,25 @@ MCB_API mcb_fp8_tile_config mcb_fp8_tile_config_v1(int64_t m, int64_t n, int64_t
   return c;
 }
 
-MCB_API mcb_status mcb_fp8_quantize_blockwise_v1(const mcb_tensor *, const mcb_tensor *,
-                                                 const mcb_tensor *, int64_t,
-                                                 const mcb_exec *) noexcept {
-  return MCB_STATUS_UNAVAILABLE_VARIANT;
+MCB_API mcb_status mcb_fp8_quantize_blockwise_v1(const mcb_tensor *q, const mcb_tensor *scales,
+                                                 const mcb_tensor *x, int64_t block,
+                                                 const mcb_exec *exec) noexcept {
+  try {
+    return fp8_quantize_impl(q, scales, x, block, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
 }
 
-MCB_API mcb_status mcb_gemm_fp8_blockscaled_v1(const mcb_tensor *, const mcb_tensor *,
-                                               const mcb_tensor *, const mcb_tensor *,
-                                               const mcb_tensor *, int64_t,
-                                               const mcb_exec *) noexcept {
-  return MCB_STATUS_UNAVAILABLE_VARIANT;
+MCB_API mcb_status mcb_gemm_fp8_blockscaled_v1(const mcb_tensor *c, const mcb_tensor *a,
+                                               const mcb_tensor *sa, const mcb_tensor *bt,
+                                               const mcb_tensor *sbt, int64_t block,
+                                               const mcb_exec *exec) noexcept {
+  try {
+    return gemm_fp8_impl(c, a, sa, bt, sbt, block, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
 }
 
 MCB_API uint64_t mcb_attn_block_workspace_bytes_v1(int64_t, int64_t, int64_t) noexcept {
