@@ -8,10 +8,10 @@ is missing -- there is no CPU fallback.
 """
 from . import _abi
 from ._abi import McbError, load
-from .api import (device_status, fp8_quantize_blockwise, gemm_epilogue, gemm_fp8_blockscaled, msm,
-                  strict_fused_pair, strict_gemm)
+from .api import (attn_block, device_status, fp8_quantize_blockwise, gemm_epilogue,
+                  gemm_fp8_blockscaled, msm, strict_fused_pair, strict_gemm)
 
 __all__ = ["McbError", "load", "strict_gemm", "strict_fused_pair", "gemm_epilogue", "msm",
-           "device_status"]
+           "fp8_quantize_blockwise", "gemm_fp8_blockscaled", "attn_block", "device_status"]
 
 load()

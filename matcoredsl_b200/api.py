@@ -197,6 +197,17 @@ def gemm_fp8_blockscaled(a, sa, bt, sbt, *, block=128, out=None, out_dtype="bf16
     return out
 
 
+def attn_block(x, wq, wk, wv, wo, heads, eps=1e-6, out=None, *, device=-1, flags=0):
+    """Y = RMSNorm(X + MSM(X Wq, X Wk, X Wv) Wo), unit gain, softmax scale
+    (D/heads)^-0.5; X [B, S, D] bf16, W* [D, D] bf16."""
+    if out is None:
+        out = _empty_like_out(x, tuple(x.shape), "bf16")
+    _call("mcb_attn_block_region_v1",
+          [("y", out), ("x", x), ("wq", wq), ("wk", wk), ("wv", wv), ("wo", wo)],
+          [int(heads), float(eps)], device, flags)
+    return out
+
+
 def device_status(device=0, clear=False) -> int:
     w = ctypes.c_uint32(0)
     _abi.check(_abi.load().mcb_device_status(device, ctypes.byref(w), 1 if clear else 0),

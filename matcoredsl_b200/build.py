@@ -37,6 +37,7 @@ SOURCES = {
     "noalloc.cu": [],
     "msm_tc.cu": [],
     "fp8.cu": [],
+    "region.cu": [],
 }
 HEADERS = ["common.cuh", "internal.h", "epilogue.cuh"]
 

@@ -740,6 +740,111 @@ mcb_status gemm_fp8_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_ten
   return call.finish(c, dc, info, err);
 }
 
+// ---- attention-residual block region ------------------------------------------------------
+uint64_t attn_workspace_bytes(int64_t batch, int64_t seq, int64_t d) {
+  // Q, K, V, O and the output projection: five [B*S, D] bf16 buffers.
+  const uint64_t one = static_cast<uint64_t>(batch) * seq * d * 2;
+  return 5 * ((one + 255) / 256 * 256);
+}
+
+mcb_status attn_block_impl(const mcb_tensor *y, const mcb_tensor *x, const mcb_tensor *wq,
+                           const mcb_tensor *wk, const mcb_tensor *wv, const mcb_tensor *wo,
+                           int64_t heads, float eps, const mcb_exec *exec) {
+  mcb_status s;
+  if ((s = check_tensor(x, 3, 3)) || (s = check_tensor(y, 3, 3)) || (s = check_tensor(wq, 2, 2)) ||
+      (s = check_tensor(wk, 2, 2)) || (s = check_tensor(wv, 2, 2)) || (s = check_tensor(wo, 2, 2)))
+    return s;
+  for (const mcb_tensor *t : {x, y, wq, wk, wv, wo})
+    if (t->dtype != MCB_DTYPE_BF16) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  const int64_t B = x->dims[0], S = x->dims[1], D = x->dims[2];
+  if (heads <= 0 || D % heads != 0) return MCB_STATUS_INVALID_ARGUMENT;
+  if (!(eps >= 0.0f)) return MCB_STATUS_INVALID_ARGUMENT;
+  const int64_t hd = D / heads, M = B * S;
+  auto dense3 = [&](const mcb_tensor *t) {
+    return t->dims[0] == B && t->dims[1] == S && t->dims[2] == D && t->strides[2] == 1 &&
+           (S <= 1 || t->strides[1] == D) && (B <= 1 || t->strides[0] == S * D);
+  };
+  if (!dense3(x) || !dense3(y)) return MCB_STATUS_SHAPE_MISMATCH;
+  for (const mcb_tensor *w : {wq, wk, wv, wo})
+    if (!dense2(w, D, D)) return MCB_STATUS_SHAPE_MISMATCH;
+  if (S == 0) return MCB_STATUS_INVALID_SHAPE;
+  for (const mcb_tensor *t : {x, wq, wk, wv, wo})
+    if (overlaps(y, t)) return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({x, y, wq, wk, wv, wo}, &host))) return s;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  void *dx, *dq, *dk, *dv, *dwo, *dy;
+  if ((s = call.device_ptr(x, true, &dx)) || (s = call.device_ptr(wq, true, &dq)) ||
+      (s = call.device_ptr(wk, true, &dk)) || (s = call.device_ptr(wv, true, &dv)) ||
+      (s = call.device_ptr(wo, true, &dwo)) || (s = call.device_ptr(y, false, &dy)))
+    return s;
+  void *ws = nullptr;
+  const uint64_t ws_bytes = attn_workspace_bytes(B, S, D);
+  if ((s = call.scratch(ws_bytes, &ws))) return s;
+  const uint64_t one = ws_bytes / 5;
+  uint8_t *base = static_cast<uint8_t *>(ws);
+  void *Q = base, *K = base + one, *V = base + 2 * one, *O = base + 3 * one, *P = base + 4 * one;
+
+  LaunchInfo info, step;
+  cudaError_t err = cudaSuccess;
+  mcb::Epilogue none;
+  const bool tc_gemm = D % 8 == 0 && (reinterpret_cast<uintptr_t>(dx) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(ws) % 16 == 0);
+  auto gemm = [&](const void *a, const void *w, void *out) {
+    if (tc_gemm && (reinterpret_cast<uintptr_t>(w) % 16 == 0))
+      return mcb::launch_gemm_tc_bf16(a, w, out, M, D, D, D, D, D, 0, 1, none, call.ctx()->status,
+                                      call.sms(), call.stream(), &step);
+    return mcb::launch_gemm_simt(a, MCB_DTYPE_BF16, w, MCB_DTYPE_BF16, out, MCB_DTYPE_BF16, M, D,
+                                 D, D, D, D, 0, none, call.stream(), &step);
+  };
+  call.mark_compute_start();
+  int launches = 0;
+  for (auto [w, out] : {std::pair<void *, void *>{dq, Q}, {dk, K}, {dv, V}}) {
+    if ((err = gemm(dx, w, out)) != cudaSuccess) break;
+    launches += step.launches;
+  }
+  if (err == cudaSuccess) {
+    // Q/K/V/O are [B, S, D] = [B, S, H, hd]; the MSM reads them as the
+    // strided head-major view [B, H, S, hd] (no transpose pass).
+    mcb::MsmShape sh;
+    sh.batch = B;
+    sh.heads = heads;
+    sh.m = sh.n = S;
+    sh.dqk = sh.dv = hd;
+    const int64_t st[3] = {S * D, hd, D};
+    for (int i = 0; i < 3; ++i) sh.q_s[i] = sh.k_s[i] = sh.v_s[i] = sh.o_s[i] = st[i];
+    const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+    err = cudaErrorNotSupported;
+    if (hd == 128 && S % 128 == 0 && D % 8 == 0)
+      err = mcb::launch_msm_tc_bf16(Q, K, V, O, sh, scale, call.ctx()->status, call.sms(),
+                                    call.stream(), &step);
+    if (err == cudaErrorNotSupported) {
+      err = hd <= 256 ? mcb::launch_msm_simt(Q, K, V, O, MCB_DTYPE_BF16, sh, scale, call.stream(),
+                                             &step)
+                      : cudaErrorNotSupported;
+    }
+    launches += step.launches;
+  }
+  if (err == cudaSuccess) {
+    err = gemm(O, dwo, P);
+    launches += step.launches;
+  }
+  if (err == cudaSuccess) {
+    step.launches = 0;
+    err = mcb::launch_residual_rmsnorm(dx, P, dy, M, D, eps, call.stream(), &step);
+    launches += step.launches;
+  }
+  call.mark_compute_end();
+  if (err == cudaErrorNotSupported) return MCB_STATUS_UNAVAILABLE_VARIANT;
+  info.launches = launches;
+  info.tile_m = 128;
+  info.tile_n = 256;
+  info.ctas = call.sms();
+  info.set_route("attn_block_region");
+  return call.finish(y, dy, info, err);
+}
+
 // ---- device buffers ------------------------------------------------------------------------
 std::mutex g_buf_mu;
 std::unordered_map<uint64_t, mcb_buffer> g_bufs;  // ptr -> live handle
@@ -906,15 +1011,22 @@ MCB_API mcb_status mcb_gemm_fp8_blockscaled_v1(const mcb_tensor *c, const mcb_te
   }
 }
 
-MCB_API uint64_t mcb_attn_block_workspace_bytes_v1(int64_t, int64_t, int64_t) noexcept {
-  return 0;
+MCB_API uint64_t mcb_attn_block_workspace_bytes_v1(int64_t batch, int64_t seq,
+                                                   int64_t d_model) noexcept {
+  if (batch < 0 || seq < 0 || d_model < 0) return 0;
+  return attn_workspace_bytes(batch, seq, d_model);
 }
 
-MCB_API mcb_status mcb_attn_block_region_v1(const mcb_tensor *, const mcb_tensor *,
-                                            const mcb_tensor *, const mcb_tensor *,
-                                            const mcb_tensor *, const mcb_tensor *, int64_t,
-                                            float, const mcb_exec *) noexcept {
-  return MCB_STATUS_UNAVAILABLE_VARIANT;
+MCB_API mcb_status mcb_attn_block_region_v1(const mcb_tensor *y, const mcb_tensor *x,
+                                            const mcb_tensor *wq, const mcb_tensor *wk,
+                                            const mcb_tensor *wv, const mcb_tensor *wo,
+                                            int64_t heads, float eps,
+                                            const mcb_exec *exec) noexcept {
+  try {
+    return attn_block_impl(y, x, wq, wk, wv, wo, heads, eps, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
 }
 
 MCB_API mcb_status mcb_device_alloc(int32_t device, uint64_t size_bytes, mcb_buffer *out) noexcept {

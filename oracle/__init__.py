@@ -234,6 +234,37 @@ def gemm_fp8_blockscaled(a, sa, bt, sbt, a_fmt="e4m3", b_fmt="e4m3", block=128, 
     return c
 
 
+# ---- attention-residual block (fp64, numpy) -------------------------------------
+def attn_block(x, wq, wk, wv, wo, heads, eps=1e-6, batch=0, tokens=None):
+    """fp64 Y[b, t] = RMSNorm(X + MSM(X Wq, X Wk, X Wv) Wo) for batch element
+    `batch` and the listed tokens (all when None), unit gain, scale hd^-0.5.
+
+    The block is not a reference operator (the reference's region op is the
+    depth-attention block_attn_res); this restates BASELINE config 5 from its
+    definition, composing the Family A/C semantics above. parity unpinned
+    against the reference. K and V are needed for every token of the batch
+    element; Q, attention, projection and norm only for the sampled tokens.
+    """
+    xb = np.asarray(x[batch], np.float64)
+    s, d = xb.shape
+    hd = d // heads
+    t = np.arange(s) if tokens is None else np.asarray(tokens)
+    wq, wk, wv, wo = (np.asarray(w, np.float64) for w in (wq, wk, wv, wo))
+    q = xb[t] @ wq
+    k = xb @ wk
+    v = xb @ wv
+    attn = np.empty((t.size, d))
+    for h in range(heads):
+        sl = slice(h * hd, (h + 1) * hd)
+        sc = (q[:, sl] @ k[:, sl].T) * (hd ** -0.5)
+        sc -= sc.max(axis=1, keepdims=True)
+        p = np.exp(sc)
+        p /= p.sum(axis=1, keepdims=True)
+        attn[:, sl] = p @ v[:, sl]
+    r = xb[t] + attn @ wo
+    return r / np.sqrt(np.mean(r * r, axis=1, keepdims=True) + eps)
+
+
 # ---- CPU baseline -------------------------------------------------------------
 def baseline_gemm_bias_gelu(x32, w32, b32, threads=None):
     x32, w32, b32 = _c(x32, np.float32), _c(w32, np.float32), _c(b32, np.float32)
