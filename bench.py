@@ -183,6 +183,102 @@ def cpu_baseline(target_seconds: float = 10.0, rows: int = 256):
                       f"bf16 inputs widened), {el:.1f} s"}
 
 
+def _time_steps(fn, steps, stream, flush=None):
+    """Mean device ms of `fn` over `steps` launches (CUDA events on `stream`);
+    `flush` (if given) runs between steps, outside the timed events."""
+    import torch
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for i in range(steps):
+        if flush is not None:
+            flush()
+        evs[i][0].record(stream)
+        fn()
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    return statistics.mean(s.elapsed_time(e) for s, e in evs)
+
+
+def run_other_configs(dev, steps: int = 10):
+    """Configs 1, 3, 4 and 5 on this GPU (device-resident inputs, one call of
+    the public operator per step). Config 1 flushes L2 between steps; the
+    others' working sets exceed L2."""
+    import torch
+    import matcoredsl_b200 as mcb
+    peaks = _peaks()
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator(device=dev)
+    out = {}
+
+    # config 1: strict fused pair, 512x256 . 256x384 . 384x128, U(-1,1) seeds 0/1/2
+    a, b, d = (torch.from_numpy(np.random.default_rng(s).uniform(-1, 1, sh).astype(np.float32))
+               .to(dev) for s, sh in ((0, (512, 256)), (1, (256, 384)), (2, (384, 128))))
+    e = torch.empty(512, 128, device=dev)
+    flush_buf = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        mcb.strict_fused_pair(a, b, d, out=e)
+    ms = _time_steps(lambda: mcb.strict_fused_pair(a, b, d, out=e), 50, stream,
+                     flush=lambda: flush_buf.fill_(1))
+    fl = 2.0 * 512 * 256 * 384 + 2.0 * 512 * 384 * 128
+    out["config1_strict_pair"] = {"ms": ms, "gflops": fl / ms / 1e6,
+                                  "route": mcb.api.last_result.route,
+                                  "note": "latency-bound; L2 flushed between steps"}
+    del a, b, d, e, flush_buf
+
+    # config 3: MSM [8,32,4096,128] bf16, scale 128^-0.5, seed 20
+    g.manual_seed(20)
+    q, k, v = (torch.randn(8, 32, 4096, 128, generator=g, device=dev).to(torch.bfloat16)
+               for _ in range(3))
+    o = torch.empty_like(q)
+    for _ in range(2):
+        mcb.msm(q, k, v, 128 ** -0.5, out=o)
+    ms = _time_steps(lambda: mcb.msm(q, k, v, 128 ** -0.5, out=o), steps, stream)
+    fl = 4.0 * 8 * 32 * 4096 * 4096 * 128
+    out["config3_msm"] = {"ms": ms, "tflops": fl / ms / 1e9,
+                          "frac_of_bf16_peak": fl / ms / 1e9 / peaks["bf16_tflops"],
+                          "route": mcb.api.last_result.route}
+    del q, k, v, o
+
+    # config 4: FP8 block-scaled 16384^3, e4m3, seed 30, bf16 out
+    g.manual_seed(30)
+    n = 16384
+    x = torch.randn(n, n, generator=g, device=dev)
+    qa, sa = mcb.fp8_quantize_blockwise(x, 128, "e4m3")
+    x.normal_(generator=g)
+    qb, sb = mcb.fp8_quantize_blockwise(x, 128, "e4m3")
+    del x
+    c = torch.empty(n, n, dtype=torch.bfloat16, device=dev)
+    for _ in range(2):
+        mcb.gemm_fp8_blockscaled(qa, sa, qb, sb, out=c)
+    ms = _time_steps(lambda: mcb.gemm_fp8_blockscaled(qa, sa, qb, sb, out=c), steps, stream)
+    fl = 2.0 * n ** 3
+    fp8_peak = 2 * peaks["bf16_tflops"]
+    out["config4_fp8_gemm"] = {"ms": ms, "tflops": fl / ms / 1e9,
+                               "frac_of_fp8_peak": fl / ms / 1e9 / fp8_peak,
+                               "fp8_peak": fp8_peak,
+                               "fp8_peak_source": "2x measured bf16 burst (no fp8 peak measured)",
+                               "route": mcb.api.last_result.route}
+    del qa, sa, qb, sb, c
+
+    # config 5: attention-residual block, B4 S2048 D4096 H32, seed 40
+    g.manual_seed(40)
+    xb = torch.randn(4, 2048, 4096, generator=g, device=dev).to(torch.bfloat16)
+    ws = [(torch.randn(4096, 4096, generator=g, device=dev) / 64).to(torch.bfloat16)
+          for _ in range(4)]
+    yb = torch.empty_like(xb)
+    for _ in range(2):
+        mcb.attn_block(xb, *ws, 32, 1e-6, out=yb)
+    ms = _time_steps(lambda: mcb.attn_block(xb, *ws, 32, 1e-6, out=yb), steps, stream)
+    fl = 4.0 * 2 * 8192 * 4096 * 4096 + 4.0 * 4 * 32 * 2048 * 2048 * 128
+    out["config5_attn_block"] = {"ms": ms, "tflops": fl / ms / 1e9,
+                                 "frac_of_bf16_peak": fl / ms / 1e9 / peaks["bf16_tflops"],
+                                 "launches_per_step": mcb.api.last_result.kernel_launches,
+                                 "route": mcb.api.last_result.route}
+    del xb, ws, yb
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_reference(args):
     world, rank, _ = _dist()
     if rank != 0:
@@ -239,7 +335,10 @@ def run_ours(args):
     from matcoredsl_b200 import _abi
     lib = mcb.load()
 
-    m = M_FULL if args.scaling == "weak" else M_FULL // world
+    # This rank's rows of the global X (mcb_shard_plan_v1, 128-row aligned):
+    # weak scaling owns 8192 of 8192*N rows, strong scaling 8192/N of 8192.
+    global_m = M_FULL * world if args.scaling == "weak" else M_FULL
+    row0, m, _, _ = mcb.shard_plan("rows", global_m, world, rank, align=128)
     flops_step = 2.0 * m * N_DIM * K_DIM
     g = torch.Generator(device=dev)
     g.manual_seed(10 + 1000 * rank)
@@ -306,8 +405,13 @@ def run_ours(args):
     e2e = None
     if not args.no_e2e:
         e2e = _run_e2e(args, lib, ep, sets, descs, dev, stream, world, flops_step, m)
+    others = None
+    if world == 1 and not args.no_other_configs:
+        del sets, dsets, calls
+        torch.cuda.empty_cache()
+        others = run_other_configs(dev)
     _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, working_set, route,
-            clk, e2e)
+            clk, e2e, others)
 
 
 def _run_e2e(args, lib, ep, sets, descs, dev, stream, world, flops_step, m):
@@ -351,7 +455,7 @@ def _run_e2e(args, lib, ep, sets, descs, dev, stream, world, flops_step, m):
 
 
 def _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, working_set, route,
-            clk, e2e):
+            clk, e2e, others=None):
     peaks = _peaks()
     achieved = flops_step / (launch_ms_max / 1e3) / 1e12
     cpu = None
@@ -384,6 +488,7 @@ def _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, wo
             "e2e": e2e,
             "gpu_launches": args.steps,
             "cpu_baseline": cpu,
+            "other_configs": others,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -401,6 +506,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the host-buffer end-to-end leg (used for short profiling runs)")
+    ap.add_argument("--no-other-configs", action="store_true",
+                    help="skip the configs 1/3/4/5 measurements reported beside the headline")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

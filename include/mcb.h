@@ -264,6 +264,23 @@ MCB_API mcb_status mcb_attn_block_region_v1(const mcb_tensor *y, const mcb_tenso
                                             int64_t heads, float eps,
                                             const mcb_exec *exec) MCB_NOEXCEPT;
 
+/* ---- multi-GPU shard plan -------------------------------------------------- */
+/* How one rank's share of a region is chosen when the path is partitioned
+ * across GPUs with no collective on the data path (the reference is
+ * single-GPU; this has no counterpart there). ROWS: the M rows of a GEMM
+ * (configs 2 and 4), in multiples of `align`. UNITS: independent (batch,
+ * head) units of a Family C call (config 3). TOKENS: the B*S tokens of an
+ * attention block (config 5), where `group` = S; each rank owns a token range
+ * inside one batch element (or whole batch elements) and must also compute
+ * K/V for [kv_begin, kv_begin + kv_count), the batch element(s) it reads. */
+enum { MCB_SHARD_ROWS = 0, MCB_SHARD_UNITS = 1, MCB_SHARD_TOKENS = 2 };
+typedef struct mcb_shard {
+  int64_t begin, count;       /* owned rows / units / tokens */
+  int64_t kv_begin, kv_count; /* TOKENS: token range whose K/V this rank computes */
+} mcb_shard;
+MCB_API mcb_status mcb_shard_plan_v1(uint32_t kind, int64_t total, int64_t group, int64_t align,
+                                     int32_t world, int32_t rank, mcb_shard *out) MCB_NOEXCEPT;
+
 /* ---- device buffers ------------------------------------------------------- */
 /* Ownership-tracked device memory; mirrors DeviceBufferHandle and the
  * matcore_device_* functions (include/matcore/device_buffer.h:11-53): a

@@ -83,6 +83,14 @@ class Buffer(ctypes.Structure):
     ]
 
 
+class Shard(ctypes.Structure):
+    _fields_ = [("begin", ctypes.c_int64), ("count", ctypes.c_int64),
+                ("kv_begin", ctypes.c_int64), ("kv_count", ctypes.c_int64)]
+
+
+SHARD_ROWS, SHARD_UNITS, SHARD_TOKENS = 0, 1, 2
+
+
 class Fp8TileConfig(ctypes.Structure):
     _fields_ = [("m_tile", ctypes.c_int32), ("n_tile", ctypes.c_int32),
                 ("k_tile", ctypes.c_int32), ("use_tma", ctypes.c_int32)]
@@ -109,6 +117,9 @@ SIGNATURES = {
     "mcb_attn_block_workspace_bytes_v1": (ctypes.c_uint64, [ctypes.c_int64] * 3),
     "mcb_attn_block_region_v1": (ctypes.c_int32, [_T, _T, _T, _T, _T, _T, ctypes.c_int64,
                                                   ctypes.c_float, _E]),
+    "mcb_shard_plan_v1": (ctypes.c_int32, [ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64,
+                                           ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                           _P(Shard)]),
     "mcb_device_alloc": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_uint64, _P(Buffer)]),
     "mcb_device_free": (ctypes.c_int32, [Buffer]),
     "mcb_device_is_valid": (ctypes.c_int32, [Buffer]),

@@ -208,6 +208,17 @@ def attn_block(x, wq, wk, wv, wo, heads, eps=1e-6, out=None, *, device=-1, flags
     return out
 
 
+def shard_plan(kind, total, world, rank, *, group=0, align=1):
+    """This rank's (begin, count, kv_begin, kv_count) under mcb_shard_plan_v1.
+    kind: "rows" (GEMM M rows), "units" ((batch, head) MSM units) or "tokens"
+    (attention block tokens; group = sequence length)."""
+    k = {"rows": _abi.SHARD_ROWS, "units": _abi.SHARD_UNITS, "tokens": _abi.SHARD_TOKENS}[kind]
+    s = _abi.Shard()
+    _abi.check(_abi.load().mcb_shard_plan_v1(k, int(total), int(group), int(align), int(world),
+                                             int(rank), ctypes.byref(s)), "mcb_shard_plan_v1")
+    return s.begin, s.count, s.kv_begin, s.kv_count
+
+
 def device_status(device=0, clear=False) -> int:
     w = ctypes.c_uint32(0)
     _abi.check(_abi.load().mcb_device_status(device, ctypes.byref(w), 1 if clear else 0),

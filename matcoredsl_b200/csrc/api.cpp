@@ -1029,6 +1029,53 @@ MCB_API mcb_status mcb_attn_block_region_v1(const mcb_tensor *y, const mcb_tenso
   }
 }
 
+MCB_API mcb_status mcb_shard_plan_v1(uint32_t kind, int64_t total, int64_t group, int64_t align,
+                                     int32_t world, int32_t rank, mcb_shard *out) noexcept {
+  if (!out || world <= 0 || rank < 0 || rank >= world || total < 0)
+    return MCB_STATUS_INVALID_ARGUMENT;
+  if (align <= 0) align = 1;
+  *out = mcb_shard{0, 0, 0, 0};
+  // Balanced split of `n` items in chunks of `a` (last chunk may be short):
+  // rank r owns chunks [r*c/w, (r+1)*c/w).
+  auto split = [](int64_t n, int64_t a, int32_t w, int32_t r, int64_t &b, int64_t &cnt) {
+    const int64_t chunks = (n + a - 1) / a;
+    const int64_t c0 = chunks * r / w, c1 = chunks * (r + 1) / w;
+    b = std::min(n, c0 * a);
+    cnt = std::min(n, c1 * a) - b;
+  };
+  switch (kind) {
+    case MCB_SHARD_ROWS:
+    case MCB_SHARD_UNITS:
+      split(total, kind == MCB_SHARD_UNITS ? 1 : align, world, rank, out->begin, out->count);
+      out->kv_begin = out->begin;
+      out->kv_count = out->count;
+      return MCB_STATUS_OK;
+    case MCB_SHARD_TOKENS: {
+      if (group <= 0 || total % group != 0) return MCB_STATUS_INVALID_SHAPE;
+      const int64_t batches = total / group;
+      if (world >= batches) {
+        if (batches == 0 || world % batches != 0) return MCB_STATUS_INVALID_ARGUMENT;
+        const int32_t per = static_cast<int32_t>(world / batches);
+        const int64_t b = rank / per;
+        int64_t tb, tc;
+        split(group, align, per, rank % per, tb, tc);
+        out->begin = b * group + tb;
+        out->count = tc;
+        out->kv_begin = b * group;
+        out->kv_count = group;
+      } else {
+        if (batches % world != 0) return MCB_STATUS_INVALID_ARGUMENT;
+        const int64_t per = batches / world;
+        out->begin = out->kv_begin = rank * per * group;
+        out->count = out->kv_count = per * group;
+      }
+      return MCB_STATUS_OK;
+    }
+    default:
+      return MCB_STATUS_INVALID_ARGUMENT;
+  }
+}
+
 MCB_API mcb_status mcb_device_alloc(int32_t device, uint64_t size_bytes, mcb_buffer *out) noexcept {
   if (!out) return MCB_STATUS_INVALID_ARGUMENT;
   mcb_exec ex{};
