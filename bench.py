@@ -133,12 +133,13 @@ def _dist():
     return world, rank, local
 
 
-def _init_pg(world, backend):
+def _init_pg(world, backend, device=None):
     import datetime
 
     import torch.distributed as dist
     if world > 1 and not dist.is_initialized():
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+        kw = {"device_id": device} if device is not None else {}
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
 
 
 def _max_over_ranks(x: float, world: int, device) -> float:
@@ -279,6 +280,50 @@ def run_other_configs(dev, steps: int = 10):
     return out
 
 
+def run_profile_config(cfg: int, steps: int, warmup: int):
+    """Launch one config's operator warmup+steps times on cuda:0 and exit (the
+    command the committed ncu summaries under profiles/ were taken with)."""
+    import torch
+    import matcoredsl_b200 as mcb
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    if cfg == 1:
+        a, b, d = (torch.rand(*sh, generator=g, device=dev) * 2 - 1
+                   for sh in ((512, 256), (256, 384), (384, 128)))
+        fn = lambda: mcb.strict_fused_pair(a, b, d)  # noqa: E731
+    elif cfg == 2:
+        x = torch.randn(8192, 4096, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.randn(4096, 4096, generator=g, device=dev) / 64).to(torch.bfloat16)
+        bias = (torch.randn(4096, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        y = torch.empty(8192, 4096, dtype=torch.bfloat16, device=dev)
+        fn = lambda: mcb.gemm_epilogue(x, w, bias, act="gelu_tanh", out=y)  # noqa: E731
+    elif cfg == 3:
+        q, k, v = (torch.randn(8, 32, 4096, 128, generator=g, device=dev).to(torch.bfloat16)
+                   for _ in range(3))
+        o = torch.empty_like(q)
+        fn = lambda: mcb.msm(q, k, v, 128 ** -0.5, out=o)  # noqa: E731
+    elif cfg == 4:
+        t = torch.randn(16384, 16384, generator=g, device=dev)
+        qa, sa = mcb.fp8_quantize_blockwise(t, 128, "e4m3")
+        t.normal_(generator=g)
+        qb, sb = mcb.fp8_quantize_blockwise(t, 128, "e4m3")
+        del t
+        c = torch.empty(16384, 16384, dtype=torch.bfloat16, device=dev)
+        fn = lambda: mcb.gemm_fp8_blockscaled(qa, sa, qb, sb, out=c)  # noqa: E731
+    else:
+        x = torch.randn(4, 2048, 4096, generator=g, device=dev).to(torch.bfloat16)
+        ws = [(torch.randn(4096, 4096, generator=g, device=dev) / 64).to(torch.bfloat16)
+              for _ in range(4)]
+        y = torch.empty_like(x)
+        fn = lambda: mcb.attn_block(x, *ws, 32, 1e-6, out=y)  # noqa: E731
+    for _ in range(warmup + steps):
+        fn()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_config": cfg, "launches": warmup + steps,
+                      "route": mcb.api.last_result.route, "device_status": mcb.device_status(0)}))
+
+
 def run_reference(args):
     world, rank, _ = _dist()
     if rank != 0:
@@ -327,7 +372,7 @@ def run_ours(args):
     world, rank, local = _dist()
     if world > 1:
         torch.cuda.set_device(local)
-        _init_pg(world, "nccl")
+        _init_pg(world, "nccl", torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
     dev = torch.device("cuda", torch.cuda.current_device())
@@ -508,7 +553,12 @@ def main():
                     help="skip the host-buffer end-to-end leg (used for short profiling runs)")
     ap.add_argument("--no-other-configs", action="store_true",
                     help="skip the configs 1/3/4/5 measurements reported beside the headline")
+    ap.add_argument("--profile-config", type=int, choices=[1, 2, 3, 4, 5],
+                    help="only launch this config's operator (for ncu captures); no JSON line")
     args = ap.parse_args()
+    if args.profile_config:
+        run_profile_config(args.profile_config, args.steps, args.warmup)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -19,6 +19,42 @@
 namespace mcb {
 namespace {
 
+// acc[r] += sum_h A[r, h] * B[h] for h in [0, k), in increasing h, each step
+// one binary32 multiply then one binary32 add (never fused). A row r starts at
+// a + r * lda (contiguous in h); B steps by ldb. Operands are loaded kU steps
+// ahead of the dependent add chain so the loads overlap instead of each one
+// paying a full memory round trip; the reduction order is unchanged.
+// kLdgA selects the read-only cache for A (inputs); data written earlier in
+// the same kernel (the panel) must use plain loads.
+template <int R, bool kLdgA>
+__device__ __forceinline__ void strict_rows(const float *__restrict__ a, int64_t lda,
+                                            const float *__restrict__ b, int64_t ldb, int64_t k,
+                                            int rows, float (&acc)[R]) {
+  constexpr int kU = 16;
+  int64_t h0 = 0;
+  for (; h0 + kU <= k; h0 += kU) {
+    float bv[kU], av[R][kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) bv[u] = __ldg(b + (h0 + u) * ldb);
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        av[r][u] = r < rows ? (kLdgA ? __ldg(a + r * lda + h0 + u) : a[r * lda + h0 + u]) : 0.0f;
+#pragma unroll
+    for (int u = 0; u < kU; ++u)
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(av[r][u], bv[u]));
+  }
+  for (; h0 < k; ++h0) {
+    const float bv = __ldg(b + h0 * ldb);
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (r < rows)
+        acc[r] = __fadd_rn(acc[r], __fmul_rn(kLdgA ? __ldg(a + r * lda + h0) : a[r * lda + h0], bv));
+  }
+}
+
 template <int R>
 __global__ void __launch_bounds__(256) strict_gemm_kernel(const float *__restrict__ a,
                                                           const float *__restrict__ b,
@@ -32,12 +68,7 @@ __global__ void __launch_bounds__(256) strict_gemm_kernel(const float *__restric
 #pragma unroll
   for (int r = 0; r < R; ++r) acc[r] = 0.0f;
   const int rows = static_cast<int>(m - r0 < R ? m - r0 : R);
-  for (int64_t h = 0; h < k; ++h) {
-    const float bv = __ldg(b + h * ldb + j);
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-      if (r < rows) acc[r] = __fadd_rn(acc[r], __fmul_rn(__ldg(a + (r0 + r) * lda + h), bv));
-  }
+  strict_rows<R, true>(a + r0 * lda, lda, b + j, ldb, k, rows, acc);
 #pragma unroll
   for (int r = 0; r < R; ++r)
     if (r < rows) c[(r0 + r) * ldc + j] = acc[r];
@@ -62,12 +93,7 @@ __global__ void __launch_bounds__(256) strict_pair_kernel(
     float acc[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) acc[r] = 0.0f;
-    for (int64_t h = 0; h < k; ++h) {
-      const float bv = __ldg(b + h * ldb + j);
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-        if (r < rows) acc[r] = __fadd_rn(acc[r], __fmul_rn(__ldg(a + (r0 + r) * lda + h), bv));
-    }
+    strict_rows<R, true>(a + r0 * lda, lda, b + j, ldb, k, rows, acc);
 #pragma unroll
     for (int r = 0; r < R; ++r)
       if (r < rows) panel[r * n + j] = acc[r];
@@ -78,12 +104,7 @@ __global__ void __launch_bounds__(256) strict_pair_kernel(
     float acc[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) acc[r] = 0.0f;
-    for (int64_t j = 0; j < n; ++j) {
-      const float dv = __ldg(d + j * ldd + q);
-#pragma unroll
-      for (int r = 0; r < R; ++r)
-        if (r < rows) acc[r] = __fadd_rn(acc[r], __fmul_rn(panel[r * n + j], dv));
-    }
+    strict_rows<R, false>(panel, n, d + q, ldd, n, rows, acc);
 #pragma unroll
     for (int r = 0; r < R; ++r)
       if (r < rows) e[(r0 + r) * lde + q] = acc[r];
