@@ -214,6 +214,20 @@ MCB_API mcb_status mcb_gemm_epilogue_v1(const mcb_tensor *y, const mcb_tensor *x
                                         const mcb_epilogue *epilogue, uint32_t gemm_flags,
                                         const mcb_exec *exec) MCB_NOEXCEPT;
 
+/* ---- Family B: two-GEMM chain with elementwise glue ------------------------ */
+/* E = glue(A*B) * W where glue is a Family A epilogue (optional boundary
+ * [M,N1] or row bias [N1], added or reverse-subtracted, then one activation).
+ * A [M,K], B [K,N1], W [N1,N2], E [M,N2]. The glue is fused into the first
+ * GEMM's epilogue; the intermediate (bf16 for bf16 operands, f32 for f32) is
+ * kept in device scratch (the caller's workspace when it holds M*N1 elements,
+ * else a library staging buffer) and consumed by the second GEMM. bf16 runs on
+ * tcgen05, f32 on CUDA cores. Replaces the leaf emitted by
+ * FusionMlirEmitter::emitFamilyB (src/fusion_emitter_family_b.cpp:12-408). */
+MCB_API mcb_status mcb_gemm_chain_v1(const mcb_tensor *e, const mcb_tensor *a,
+                                     const mcb_tensor *b, const mcb_tensor *boundary,
+                                     const mcb_epilogue *glue, const mcb_tensor *w,
+                                     const mcb_exec *exec) MCB_NOEXCEPT;
+
 /* ---- Family C: matmul-softmax-matmul -------------------------------------- */
 /* O = softmax(scale * Q*K^T) * V per leading index. Q [.., M, Dqk],
  * K [.., N, Dqk], V [.., N, Dv], O [.., M, Dv] with up to two leading
@@ -263,6 +277,56 @@ MCB_API mcb_status mcb_attn_block_region_v1(const mcb_tensor *y, const mcb_tenso
                                             const mcb_tensor *wv, const mcb_tensor *wo,
                                             int64_t heads, float eps,
                                             const mcb_exec *exec) MCB_NOEXCEPT;
+
+/* ---- execution plans (shape-locked, optional CUDA-graph replay) ------------ */
+/* Mirrors MatcorePlan::create / execute (include/matcore/plan.h:37-107): a
+ * plan freezes the operator and the metadata (dtype, rank, dims, strides,
+ * memory space) of its tensors; execute rejects tensors that differ. With
+ * graph_mode = 1 the first execute captures the operator's launches into a
+ * CUDA graph on a stream the plan owns, and later executes replay it; like
+ * the reference, replay rejects data-pointer changes
+ * (src/jit_runner.cpp:1060-1111). Graph plans need device-resident tensors;
+ * ops that need scratch (GEMM_CHAIN, ATTN_BLOCK) get a workspace the plan
+ * allocates once at create time. Tensor slots follow each entry point's
+ * argument order; an optional slot (bias / boundary) is a tensor with
+ * dtype MCB_DTYPE_INVALID. */
+enum {
+  MCB_PLAN_STRICT_PAIR = 1,   /* e, a, b, d */
+  MCB_PLAN_STRICT_GEMM = 2,   /* c, a, b */
+  MCB_PLAN_GEMM_EPILOGUE = 3, /* y, x, w, bias */
+  MCB_PLAN_GEMM_CHAIN = 4,    /* e, a, b, boundary, w */
+  MCB_PLAN_MSM = 5,           /* o, q, k, v */
+  MCB_PLAN_FP8_GEMM = 6,      /* c, a, sa, bt, sbt */
+  MCB_PLAN_ATTN_BLOCK = 7     /* y, x, wq, wk, wv, wo */
+};
+#define MCB_PLAN_MAX_TENSORS 8
+typedef struct mcb_plan_desc {
+  uint32_t abi_version;
+  uint32_t struct_size;
+  uint32_t op;
+  uint32_t graph_mode;
+  int32_t device;        /* -1 = current device */
+  uint32_t num_tensors;
+  mcb_tensor tensors[MCB_PLAN_MAX_TENSORS]; /* templates: metadata is frozen, data ignored */
+  mcb_epilogue epilogue; /* GEMM_EPILOGUE, GEMM_CHAIN */
+  uint32_t gemm_flags;   /* GEMM_EPILOGUE */
+  uint32_t reserved0;
+  double scale;          /* MSM */
+  int64_t block;         /* FP8_GEMM */
+  int64_t heads;         /* ATTN_BLOCK */
+  float eps;             /* ATTN_BLOCK */
+  uint32_t reserved1;
+  uint64_t reserved[2];
+} mcb_plan_desc;
+typedef struct mcb_plan mcb_plan;
+MCB_API mcb_status mcb_plan_create_v1(const mcb_plan_desc *desc, mcb_plan **out) MCB_NOEXCEPT;
+/* Runs the plan on `stream` (cudaStream_t, NULL = legacy default stream);
+ * asynchronous with respect to the host. */
+MCB_API mcb_status mcb_plan_execute_v1(mcb_plan *plan, const mcb_tensor *tensors,
+                                       uint32_t num_tensors, void *stream) MCB_NOEXCEPT;
+/* Monotonic id of the plan (stale-handle detection, MatcorePlan::generationId). */
+MCB_API uint64_t mcb_plan_generation_v1(const mcb_plan *plan) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_plan_destroy_v1(mcb_plan *plan) MCB_NOEXCEPT;
 
 /* ---- multi-GPU shard plan -------------------------------------------------- */
 /* How one rank's share of a region is chosen when the path is partitioned

@@ -8,10 +8,12 @@ is missing -- there is no CPU fallback.
 """
 from . import _abi
 from ._abi import McbError, load
-from .api import (attn_block, device_status, fp8_quantize_blockwise, gemm_epilogue,
-                  gemm_fp8_blockscaled, msm, shard_plan, strict_fused_pair, strict_gemm)
+from .api import (Plan, attn_block, device_status, fp8_quantize_blockwise, gemm_chain,
+                  gemm_epilogue, gemm_fp8_blockscaled, msm, shard_plan, strict_fused_pair,
+                  strict_gemm)
 
-__all__ = ["McbError", "load", "strict_gemm", "strict_fused_pair", "gemm_epilogue", "msm",
+__all__ = ["McbError", "load", "strict_gemm", "strict_fused_pair", "gemm_epilogue", "gemm_chain",
+           "msm",
            "fp8_quantize_blockwise", "gemm_fp8_blockscaled", "attn_block", "shard_plan",
            "device_status"]
 

@@ -96,6 +96,22 @@ class Fp8TileConfig(ctypes.Structure):
                 ("k_tile", ctypes.c_int32), ("use_tma", ctypes.c_int32)]
 
 
+PLAN_MAX_TENSORS = 8
+PLAN_OPS = {"strict_pair": 1, "strict_gemm": 2, "gemm_epilogue": 3, "gemm_chain": 4, "msm": 5,
+            "fp8_gemm": 6, "attn_block": 7}
+
+
+class PlanDesc(ctypes.Structure):
+    _fields_ = [
+        ("abi_version", ctypes.c_uint32), ("struct_size", ctypes.c_uint32),
+        ("op", ctypes.c_uint32), ("graph_mode", ctypes.c_uint32), ("device", ctypes.c_int32),
+        ("num_tensors", ctypes.c_uint32), ("tensors", Tensor * PLAN_MAX_TENSORS),
+        ("epilogue", Epilogue), ("gemm_flags", ctypes.c_uint32), ("reserved0", ctypes.c_uint32),
+        ("scale", ctypes.c_double), ("block", ctypes.c_int64), ("heads", ctypes.c_int64),
+        ("eps", ctypes.c_float), ("reserved1", ctypes.c_uint32), ("reserved", ctypes.c_uint64 * 2),
+    ]
+
+
 _P = ctypes.POINTER
 _T = _P(Tensor)
 _E = _P(Exec)
@@ -109,6 +125,7 @@ SIGNATURES = {
     "mcb_strict_fused_pair_f32_v1": (ctypes.c_int32, [_T, _T, _T, _T, _E]),
     "mcb_strict_fused_pair_f32_noalloc_v1": (ctypes.c_int32, [_T, _T, _T, _T, _E]),
     "mcb_gemm_epilogue_v1": (ctypes.c_int32, [_T, _T, _T, _T, _P(Epilogue), ctypes.c_uint32, _E]),
+    "mcb_gemm_chain_v1": (ctypes.c_int32, [_T, _T, _T, _T, _P(Epilogue), _T, _E]),
     "mcb_msm_v1": (ctypes.c_int32, [_T, _T, _T, _T, ctypes.c_double, _E]),
     "mcb_fp8_quantize_blockwise_v1": (ctypes.c_int32, [_T, _T, _T, ctypes.c_int64, _E]),
     "mcb_gemm_fp8_blockscaled_v1": (ctypes.c_int32, [_T, _T, _T, _T, _T, ctypes.c_int64, _E]),
@@ -117,6 +134,11 @@ SIGNATURES = {
     "mcb_attn_block_workspace_bytes_v1": (ctypes.c_uint64, [ctypes.c_int64] * 3),
     "mcb_attn_block_region_v1": (ctypes.c_int32, [_T, _T, _T, _T, _T, _T, ctypes.c_int64,
                                                   ctypes.c_float, _E]),
+    "mcb_plan_create_v1": (ctypes.c_int32, [_P(PlanDesc), _P(ctypes.c_void_p)]),
+    "mcb_plan_execute_v1": (ctypes.c_int32, [ctypes.c_void_p, _T, ctypes.c_uint32,
+                                             ctypes.c_void_p]),
+    "mcb_plan_generation_v1": (ctypes.c_uint64, [ctypes.c_void_p]),
+    "mcb_plan_destroy_v1": (ctypes.c_int32, [ctypes.c_void_p]),
     "mcb_shard_plan_v1": (ctypes.c_int32, [ctypes.c_uint32, ctypes.c_int64, ctypes.c_int64,
                                            ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
                                            _P(Shard)]),

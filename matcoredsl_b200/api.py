@@ -157,6 +157,38 @@ def gemm_epilogue(x, w, bias=None, *, bias_mode=None, bias_op="add", act="none",
     return out
 
 
+def gemm_chain(a, b, w, boundary=None, *, bias_mode=None, bias_op="add", act="none", out=None,
+               out_dtype=None, device=-1, flags=0):
+    """E = glue(A @ B) @ W (Family B); glue = act(. (+|r-) boundary)."""
+    if bias_mode is None:
+        bias_mode = "none" if boundary is None else (
+            "full" if len(boundary.shape) == 2 else "row")
+    if out is None:
+        if out_dtype is None:
+            out_dtype = "bf16" if str(getattr(a, "dtype", "")).endswith("bfloat16") else "f32"
+        out = _empty_like_out(a, (a.shape[0], w.shape[1]), out_dtype)
+    ep = _abi.make_epilogue(bias_mode, bias_op, act)
+    lib = _abi.load()
+    global last_result
+    descs = []
+    device_call = False
+    for name, t in (("e", out), ("a", a), ("b", b), ("boundary", boundary), ("w", w)):
+        if t is None:
+            descs.append(None)
+            continue
+        d, dev = _desc(t, name)
+        descs.append(d)
+        device_call = device_call or dev
+    rep = _abi.make_report()
+    ex = _exec(device_call, device, flags, rep)
+    ptr = lambda d: ctypes.byref(d) if d is not None else None  # noqa: E731
+    code = lib.mcb_gemm_chain_v1(ptr(descs[0]), ptr(descs[1]), ptr(descs[2]), ptr(descs[3]),
+                                 ctypes.byref(ep), ptr(descs[4]), ctypes.byref(ex))
+    last_result = Result(rep)
+    _abi.check(code, "mcb_gemm_chain_v1")
+    return out
+
+
 def msm(q, k, v, scale=1.0, out=None, *, device=-1, flags=0):
     """O = softmax(scale * Q @ K^T) @ V over the last two dims (Family C)."""
     if out is None:
@@ -206,6 +238,68 @@ def attn_block(x, wq, wk, wv, wo, heads, eps=1e-6, out=None, *, device=-1, flags
           [("y", out), ("x", x), ("wq", wq), ("wk", wk), ("wv", wv), ("wo", wo)],
           [int(heads), float(eps)], device, flags)
     return out
+
+
+class Plan:
+    """Shape-locked operator call with optional CUDA-graph replay (the
+    reference's create_plan / execute_plan). Tensors are passed in the entry
+    point's argument order (outputs first); None marks an absent optional
+    bias/boundary slot."""
+
+    def __init__(self, op, *templates, graph=False, device=-1, bias_mode="none", bias_op="add",
+                 act="none", w_transposed=False, scale=1.0, block=128, heads=0, eps=1e-6):
+        lib = _abi.load()
+        d = _abi.PlanDesc()
+        d.abi_version = _abi.ABI_VERSION
+        d.struct_size = ctypes.sizeof(_abi.PlanDesc)
+        d.op = _abi.PLAN_OPS[op]
+        d.graph_mode = 1 if graph else 0
+        on_device = any(t is not None and _is_torch(t) and t.is_cuda for t in templates)
+        if device < 0 and on_device:
+            device = _torch().cuda.current_device()
+        d.device = device
+        d.num_tensors = len(templates)
+        for i, t in enumerate(templates):
+            if t is not None:
+                d.tensors[i] = _desc(t, f"slot{i}")[0]
+            else:
+                d.tensors[i].abi_version = _abi.ABI_VERSION
+                d.tensors[i].struct_size = ctypes.sizeof(_abi.Tensor)
+        d.epilogue = _abi.make_epilogue(bias_mode, bias_op, act)
+        d.gemm_flags = _abi.GEMM_W_TRANSPOSED if w_transposed else 0
+        d.scale, d.block, d.heads, d.eps = float(scale), int(block), int(heads), float(eps)
+        self._handle = ctypes.c_void_p()
+        _abi.check(lib.mcb_plan_create_v1(ctypes.byref(d), ctypes.byref(self._handle)),
+                   "mcb_plan_create_v1")
+        self._n = len(templates)
+        self._device_call = on_device
+
+    @property
+    def generation(self) -> int:
+        return int(_abi.load().mcb_plan_generation_v1(self._handle))
+
+    def execute(self, *tensors):
+        arr = (_abi.Tensor * self._n)()
+        for i, t in enumerate(tensors):
+            if t is not None:
+                arr[i] = _desc(t, f"slot{i}")[0]
+            else:
+                arr[i].abi_version = _abi.ABI_VERSION
+                arr[i].struct_size = ctypes.sizeof(_abi.Tensor)
+        stream = _torch().cuda.current_stream().cuda_stream if self._device_call else None
+        _abi.check(_abi.load().mcb_plan_execute_v1(self._handle, arr, len(tensors), stream),
+                   "mcb_plan_execute_v1")
+
+    def close(self):
+        if self._handle:
+            _abi.load().mcb_plan_destroy_v1(self._handle)
+            self._handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def shard_plan(kind, total, world, rank, *, group=0, align=1):

@@ -38,6 +38,7 @@ SOURCES = {
     "msm_tc.cu": [],
     "fp8.cu": [],
     "region.cu": [],
+    "plan.cpp": [],
 }
 HEADERS = ["common.cuh", "internal.h", "epilogue.cuh"]
 

@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -570,6 +571,95 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
   return call.finish(y, dy, info, err);
 }
 
+// ---- Family B -----------------------------------------------------------------------------
+// One GEMM launch on whichever kernel the operands allow (tcgen05 for
+// TMA-compatible bf16, CUDA cores otherwise).
+cudaError_t launch_gemm_any(const void *x, int x_dt, const void *w, int w_dt, void *y, int y_dt,
+                            int64_t m, int64_t n, int64_t k, int64_t ld_x, int64_t ld_w,
+                            int64_t ld_y, const mcb::Epilogue &ep, Call &call, LaunchInfo *info) {
+  const bool bf16 = x_dt == MCB_DTYPE_BF16 && w_dt == MCB_DTYPE_BF16;
+  const bool tma_ok = bf16 && k > 0 && k % 8 == 0 && n % 8 == 0 && ld_x % 8 == 0 &&
+                      ld_w % 8 == 0 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                      (reinterpret_cast<uintptr_t>(w) % 16 == 0) &&
+                      (reinterpret_cast<uintptr_t>(y) % 16 == 0) &&
+                      ld_y % (y_dt == MCB_DTYPE_BF16 ? 8 : 4) == 0;
+  if (tma_ok)
+    return mcb::launch_gemm_tc_bf16(x, w, y, m, n, k, ld_x, ld_w, ld_y, 0,
+                                    y_dt == MCB_DTYPE_BF16 ? 1 : 0, ep, call.ctx()->status,
+                                    call.sms(), call.stream(), info);
+  return mcb::launch_gemm_simt(x, x_dt, w, w_dt, y, y_dt, m, n, k, ld_x, ld_w, ld_y, 0, ep,
+                               call.stream(), info);
+}
+
+mcb_status chain_impl(const mcb_tensor *e, const mcb_tensor *a, const mcb_tensor *b,
+                      const mcb_tensor *boundary, const mcb_epilogue *glue, const mcb_tensor *w,
+                      const mcb_exec *exec) {
+  mcb_status s;
+  if ((s = check_tensor(a, 2, 2)) || (s = check_tensor(b, 2, 2)) || (s = check_tensor(w, 2, 2)) ||
+      (s = check_tensor(e, 2, 2)))
+    return s;
+  const int dt = static_cast<int>(a->dtype);
+  if ((dt != MCB_DTYPE_BF16 && dt != MCB_DTYPE_F32) || b->dtype != a->dtype ||
+      w->dtype != a->dtype || (e->dtype != MCB_DTYPE_BF16 && e->dtype != MCB_DTYPE_F32))
+    return MCB_STATUS_UNSUPPORTED_DTYPE;
+  const int64_t m = a->dims[0], k = a->dims[1], n1 = b->dims[1], n2 = w->dims[1];
+  if (b->dims[0] != k || w->dims[0] != n1 || e->dims[0] != m || e->dims[1] != n2)
+    return MCB_STATUS_SHAPE_MISMATCH;
+  mcb::Epilogue ep;
+  if (glue) {
+    if (glue->abi_version != MCB_ABI_VERSION_V1 || glue->struct_size < sizeof(mcb_epilogue))
+      return MCB_STATUS_ABI_MISMATCH;
+    if (glue->bias_mode > MCB_BIAS_FULL || glue->bias_op > MCB_BIAS_RSUB ||
+        glue->activation > MCB_ACT_TANH)
+      return MCB_STATUS_INVALID_ARGUMENT;
+    ep.bias_mode = static_cast<int>(glue->bias_mode);
+    ep.bias_op = static_cast<int>(glue->bias_op);
+    ep.act = static_cast<int>(glue->activation);
+  }
+  if (ep.bias_mode != MCB_BIAS_NONE) {
+    if ((s = check_tensor(boundary, 1, 2))) return s;
+    if (boundary->dtype != MCB_DTYPE_BF16 && boundary->dtype != MCB_DTYPE_F32)
+      return MCB_STATUS_UNSUPPORTED_DTYPE;
+    if (ep.bias_mode == MCB_BIAS_ROW && numel(boundary) != n1) return MCB_STATUS_SHAPE_MISMATCH;
+    if (ep.bias_mode == MCB_BIAS_FULL &&
+        !(boundary->rank == 2 && boundary->dims[0] == m && boundary->dims[1] == n1))
+      return MCB_STATUS_SHAPE_MISMATCH;
+    ep.bias_bf16 = boundary->dtype == MCB_DTYPE_BF16;
+    ep.ld_bias = boundary->rank == 2 ? boundary->strides[0] : n1;
+  }
+  for (const mcb_tensor *t : {a, b, w}) if (overlaps(e, t)) return MCB_STATUS_ALIAS_VIOLATION;
+  if (ep.bias_mode && overlaps(e, boundary)) return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({a, b, w, e, ep.bias_mode ? boundary : nullptr}, &host))) return s;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  void *da, *db, *dw, *de, *dbnd = nullptr, *mid = nullptr;
+  if ((s = call.device_ptr(a, true, &da)) || (s = call.device_ptr(b, true, &db)) ||
+      (s = call.device_ptr(w, true, &dw)) || (s = call.device_ptr(e, false, &de)))
+    return s;
+  if (ep.bias_mode && (s = call.device_ptr(boundary, true, &dbnd))) return s;
+  ep.bias = dbnd;
+  ep.bias_aligned16 = (reinterpret_cast<uintptr_t>(dbnd) & 15u) == 0;
+  const int64_t ld_mid = (n1 + 7) / 8 * 8;  // 16-byte rows for the second GEMM's TMA
+  const size_t esz = dt == MCB_DTYPE_BF16 ? 2 : 4;
+  if ((s = call.scratch(static_cast<uint64_t>(m) * ld_mid * esz, &mid))) return s;
+  LaunchInfo i1, i2;
+  call.mark_compute_start();
+  cudaError_t err = launch_gemm_any(da, dt, db, dt, mid, dt, m, n1, k, a->strides[0], b->strides[0],
+                                    ld_mid, ep, call, &i1);
+  mcb::Epilogue none;
+  if (err == cudaSuccess)
+    err = launch_gemm_any(mid, dt, dw, dt, de, static_cast<int>(e->dtype), m, n2, n1, ld_mid,
+                          w->strides[0], e->strides[0], none, call, &i2);
+  call.mark_compute_end();
+  LaunchInfo info = i2;
+  info.launches = i1.launches + i2.launches;
+  char route[48];
+  std::snprintf(route, sizeof(route), "chain:%s", i1.route);
+  info.set_route(route);
+  return call.finish(e, de, info, err);
+}
+
 // ---- Family C -----------------------------------------------------------------------------
 constexpr bool kHaveMsmTc = true;
 
@@ -945,6 +1035,17 @@ MCB_API mcb_status mcb_gemm_epilogue_v1(const mcb_tensor *y, const mcb_tensor *x
                                         const mcb_exec *exec) noexcept {
   try {
     return gemm_epilogue_impl(y, x, w, bias, epilogue, gemm_flags, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API mcb_status mcb_gemm_chain_v1(const mcb_tensor *e, const mcb_tensor *a,
+                                     const mcb_tensor *b, const mcb_tensor *boundary,
+                                     const mcb_epilogue *glue, const mcb_tensor *w,
+                                     const mcb_exec *exec) noexcept {
+  try {
+    return chain_impl(e, a, b, boundary, glue, w, exec);
   } catch (...) {
     return MCB_STATUS_CANDIDATE_FAILURE;
   }

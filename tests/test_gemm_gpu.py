@@ -139,3 +139,33 @@ def test_config2_full_size_sampled(mcb, orc):
     got = gu.from_dev(y)[rows]
     assert orc.rel_frobenius(got, ref) < REL_BF16
     assert mcb.device_status(0) == 0
+
+
+@pytest.mark.parametrize("act,bias_mode,bias_op", [("relu", "none", "add"), ("exp", "none", "add"),
+                                                   ("none", "full", "add"),
+                                                   ("gelu_tanh", "full", "rsub"),
+                                                   ("relu", "row", "add")])
+def test_family_b_chain_tcgen05(mcb, orc, act, bias_mode, bias_op):
+    """E = glue(A B) W on tensor cores (two tcgen05 launches, bf16 intermediate)."""
+    import torch
+    m, k, n1, n2 = 384, 512, 256, 320
+    rng = np.random.default_rng(21)
+    a = rng.standard_normal((m, k), dtype=np.float32) * np.float32(0.5)
+    b = rng.standard_normal((k, n1), dtype=np.float32) / np.float32(np.sqrt(k))
+    w = rng.standard_normal((n1, n2), dtype=np.float32) / np.float32(np.sqrt(n1))
+    (ah, af), (bh, bf), (wh, wf) = gu.bf16_pair(a), gu.bf16_pair(b), gu.bf16_pair(w)
+    bnd_np = bnd_dev = None
+    if bias_mode == "full":
+        bnd_np = rng.standard_normal((m, n1), dtype=np.float32) * np.float32(0.3)
+        bnd_dev = gu.to_dev_f32(bnd_np)
+    elif bias_mode == "row":
+        bnd_np = rng.standard_normal(n1, dtype=np.float32) * np.float32(0.3)
+        bnd_dev = gu.to_dev_f32(bnd_np)
+    e = mcb.gemm_chain(gu.to_dev_bf16(ah), gu.to_dev_bf16(bh), gu.to_dev_bf16(wh), bnd_dev,
+                       bias_mode=bias_mode, bias_op=bias_op, act=act, out_dtype="f32")
+    r = mcb.api.last_result
+    assert r.route == "chain:tcgen05_bf16_gemm_epilogue" and r.kernel_launches == 2
+    mid = orc.gemm_epilogue(af, bf, bnd_np, bias_mode=bias_mode, bias_op=bias_op, act=act)
+    ref = orc.gemm_epilogue(mid.astype(np.float32), wf)
+    assert orc.rel_frobenius(gu.from_dev(e), ref) < REL_BF16
+    assert e.dtype == torch.float32

@@ -73,6 +73,34 @@ def test_cuda_family_a_matches_golden(mcb, case):
     assert np.max(np.abs(got - expected)) < TOL["a"]
 
 
+def _b_args(meta, ins):
+    a, b = ins[0], ins[1]
+    if meta["bias_mode"] == "full":
+        return a, b, ins[2], ins[3]
+    return a, b, None, ins[2]
+
+
+@pytest.mark.parametrize("case", _cases("b"), ids=lambda c: c[0]["name"])
+def test_oracle_reproduces_family_b(orc, case):
+    meta, ins, expected = case
+    a, b, bnd, w = _b_args(meta, ins)
+    mid = orc.gemm_epilogue(a, b, bnd, bias_mode=meta["bias_mode"], bias_op=meta["bias_op"],
+                            act=meta["act"]).astype(np.float32)
+    got = orc.gemm_epilogue(mid, w).astype(np.float32)
+    assert np.max(np.abs(got - expected)) <= 1e-6
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", _cases("b"), ids=lambda c: c[0]["name"])
+def test_cuda_family_b_matches_golden(mcb, case):
+    meta, ins, expected = case
+    a, b, bnd, w = _b_args(meta, ins)
+    got = mcb.gemm_chain(a, b, w, bnd, bias_mode=meta["bias_mode"], bias_op=meta["bias_op"],
+                         act=meta["act"])
+    assert mcb.api.last_result.kernel_launches == 2
+    assert np.max(np.abs(got - expected)) < TOL["b"]
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("case", _cases("c"), ids=lambda c: c[0]["name"])
 def test_cuda_family_c_matches_golden(mcb, case):
