@@ -185,6 +185,21 @@ MCB_API mcb_status mcb_strict_fused_pair_f32_noalloc_v1(const mcb_tensor *e, con
                                                         const mcb_tensor *b, const mcb_tensor *d,
                                                         const mcb_exec *exec) MCB_NOEXCEPT;
 
+/* ---- typed isolated GEMMs (bit-exact with the reference's typed references) */
+/* C[M,N] int32 = A[M,K] int8 * B[K,N] int8, accumulated modulo 2^32. Runs on
+ * tcgen05 (kind::i8) when K is a multiple of 16 (B is transposed into device
+ * scratch first), else on CUDA cores; integer sums are exact either way.
+ * Counterpart of cpu_reference_gemm_i8_i32_v1
+ * (compiler/lib/runtime/cpu_numeric_reference.h:58-61, .cpp:185-209). */
+MCB_API mcb_status mcb_gemm_i8_i32_v1(const mcb_tensor *c, const mcb_tensor *a,
+                                      const mcb_tensor *b, const mcb_exec *exec) MCB_NOEXCEPT;
+/* C[M,N] f32 = A[M,K] bf16 * B[K,N] bf16 with one f32 fma per k in
+ * increasing order from +0 (CUDA cores; bit-exact). Counterpart of
+ * cpu_reference_gemm_bf16_f32_v1 (cpu_numeric_reference.h:45-48, .cpp:108-127). */
+MCB_API mcb_status mcb_gemm_bf16_f32_fma_v1(const mcb_tensor *c, const mcb_tensor *a,
+                                            const mcb_tensor *b,
+                                            const mcb_exec *exec) MCB_NOEXCEPT;
+
 /* ---- Family A: GEMM + fused epilogue ------------------------------------ */
 enum { MCB_BIAS_NONE = 0, MCB_BIAS_ROW = 1 /* b[N] broadcast over rows */,
        MCB_BIAS_FULL = 2 /* boundary [M,N] */ };

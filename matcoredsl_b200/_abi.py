@@ -126,6 +126,8 @@ SIGNATURES = {
     "mcb_strict_fused_pair_f32_noalloc_v1": (ctypes.c_int32, [_T, _T, _T, _T, _E]),
     "mcb_gemm_epilogue_v1": (ctypes.c_int32, [_T, _T, _T, _T, _P(Epilogue), ctypes.c_uint32, _E]),
     "mcb_gemm_chain_v1": (ctypes.c_int32, [_T, _T, _T, _T, _P(Epilogue), _T, _E]),
+    "mcb_gemm_i8_i32_v1": (ctypes.c_int32, [_T, _T, _T, _E]),
+    "mcb_gemm_bf16_f32_fma_v1": (ctypes.c_int32, [_T, _T, _T, _E]),
     "mcb_msm_v1": (ctypes.c_int32, [_T, _T, _T, _T, ctypes.c_double, _E]),
     "mcb_fp8_quantize_blockwise_v1": (ctypes.c_int32, [_T, _T, _T, ctypes.c_int64, _E]),
     "mcb_gemm_fp8_blockscaled_v1": (ctypes.c_int32, [_T, _T, _T, _T, _T, ctypes.c_int64, _E]),

@@ -130,6 +130,26 @@ def strict_gemm(a, b, out=None, *, device=-1, flags=0):
     return out
 
 
+def gemm_i8_i32(a, b, out=None, *, device=-1, flags=0):
+    """C = A @ B for int8 operands, int32 result modulo 2^32 (bit-exact)."""
+    if out is None:
+        if _is_torch(a):
+            torch = _torch()
+            out = torch.empty(a.shape[0], b.shape[1], dtype=torch.int32, device=a.device)
+        else:
+            out = np.empty((a.shape[0], b.shape[1]), np.int32)
+    _call("mcb_gemm_i8_i32_v1", [("c", out), ("a", a), ("b", b)], [], device, flags)
+    return out
+
+
+def gemm_bf16_f32_fma(a, b, out=None, *, device=-1, flags=0):
+    """C = A @ B for bf16 operands with one f32 fma per k in order (bit-exact)."""
+    if out is None:
+        out = _empty_like_out(a, (a.shape[0], b.shape[1]), "f32")
+    _call("mcb_gemm_bf16_f32_fma_v1", [("c", out), ("a", a), ("b", b)], [], device, flags)
+    return out
+
+
 def strict_fused_pair(a, b, d, out=None, *, device=-1, flags=0, workspace=None):
     """E = (A @ B) @ D, strict f32, intermediate rounded to f32 (bit-exact)."""
     if out is None:

@@ -39,6 +39,7 @@ SOURCES = {
     "fp8.cu": [],
     "region.cu": [],
     "plan.cpp": [],
+    "typed.cu": [],
 }
 HEADERS = ["common.cuh", "internal.h", "epilogue.cuh"]
 

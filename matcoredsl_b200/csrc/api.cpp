@@ -571,6 +571,60 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
   return call.finish(y, dy, info, err);
 }
 
+// ---- typed GEMMs --------------------------------------------------------------------------
+mcb_status typed_gemm_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_tensor *b,
+                           const mcb_exec *exec, bool int8) {
+  mcb_status s;
+  if ((s = check_tensor(a, 2, 2)) || (s = check_tensor(b, 2, 2)) || (s = check_tensor(c, 2, 2)))
+    return s;
+  const mcb_dtype in_t = int8 ? MCB_DTYPE_I8 : MCB_DTYPE_BF16;
+  const mcb_dtype out_t = int8 ? MCB_DTYPE_I32 : MCB_DTYPE_F32;
+  if (a->dtype != in_t || b->dtype != in_t || c->dtype != out_t) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  const int64_t m = a->dims[0], k = a->dims[1], n = b->dims[1];
+  if (b->dims[0] != k || c->dims[0] != m || c->dims[1] != n) return MCB_STATUS_SHAPE_MISMATCH;
+  if (overlaps(c, a) || overlaps(c, b)) return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({a, b, c}, &host))) return s;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  void *da, *db, *dc;
+  if ((s = call.device_ptr(a, true, &da)) || (s = call.device_ptr(b, true, &db)) ||
+      (s = call.device_ptr(c, false, &dc)))
+    return s;
+  LaunchInfo info;
+  cudaError_t err = cudaErrorNotSupported;
+  call.mark_compute_start();
+  if (!int8) {
+    err = mcb::launch_gemm_bf16_fma(da, db, static_cast<float *>(dc), m, n, k, a->strides[0],
+                                    b->strides[0], c->strides[0], call.stream(), &info);
+  } else {
+    const bool tc = k > 0 && k % 16 == 0 && a->strides[0] == k &&
+                    (reinterpret_cast<uintptr_t>(da) % 16 == 0) && c->strides[0] % 4 == 0 &&
+                    (reinterpret_cast<uintptr_t>(dc) % 16 == 0);
+    if (tc) {
+      void *bt = nullptr;
+      if ((s = call.scratch(static_cast<uint64_t>(n) * k, &bt))) return s;
+      err = mcb::launch_transpose_u8(db, bt, k, n, b->strides[0], call.stream());
+      if (err == cudaSuccess) {
+        info.launches = 1;
+        err = mcb::launch_gemm_i8_tc(static_cast<const int8_t *>(da),
+                                     static_cast<const int8_t *>(bt), static_cast<int32_t *>(dc), m,
+                                     n, k, c->strides[0], call.ctx()->status, call.sms(),
+                                     call.stream(), &info);
+      }
+    }
+    if (err == cudaErrorNotSupported) {
+      info.launches = 0;
+      err = mcb::launch_gemm_i8_simt(static_cast<const int8_t *>(da),
+                                     static_cast<const int8_t *>(db), static_cast<int32_t *>(dc),
+                                     m, n, k, a->strides[0], b->strides[0], c->strides[0],
+                                     call.stream(), &info);
+    }
+  }
+  call.mark_compute_end();
+  return call.finish(c, dc, info, err);
+}
+
 // ---- Family B -----------------------------------------------------------------------------
 // One GEMM launch on whichever kernel the operands allow (tcgen05 for
 // TMA-compatible bf16, CUDA cores otherwise).
@@ -1035,6 +1089,24 @@ MCB_API mcb_status mcb_gemm_epilogue_v1(const mcb_tensor *y, const mcb_tensor *x
                                         const mcb_exec *exec) noexcept {
   try {
     return gemm_epilogue_impl(y, x, w, bias, epilogue, gemm_flags, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API mcb_status mcb_gemm_i8_i32_v1(const mcb_tensor *c, const mcb_tensor *a,
+                                      const mcb_tensor *b, const mcb_exec *exec) noexcept {
+  try {
+    return typed_gemm_impl(c, a, b, exec, true);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API mcb_status mcb_gemm_bf16_f32_fma_v1(const mcb_tensor *c, const mcb_tensor *a,
+                                            const mcb_tensor *b, const mcb_exec *exec) noexcept {
+  try {
+    return typed_gemm_impl(c, a, b, exec, false);
   } catch (...) {
     return MCB_STATUS_CANDIDATE_FAILURE;
   }

@@ -94,6 +94,19 @@ cudaError_t launch_gemm_fp8_simt(const uint8_t *a, int a_e5m2, const float *sa,
                                  int c_bf16, int64_t m, int64_t n, int64_t k, int64_t block,
                                  cudaStream_t stream, LaunchInfo *info);
 
+// ---- typed.cu: int8 and bf16-fma typed GEMMs -------------------------------------------------
+cudaError_t launch_transpose_u8(const void *in, void *out, int64_t rows, int64_t cols,
+                                int64_t ld_in, cudaStream_t stream);
+cudaError_t launch_gemm_i8_tc(const int8_t *a, const int8_t *bt, int32_t *c, int64_t m, int64_t n,
+                              int64_t k, int64_t ld_c, uint32_t *status, int sms,
+                              cudaStream_t stream, LaunchInfo *info);
+cudaError_t launch_gemm_i8_simt(const int8_t *a, const int8_t *b, int32_t *c, int64_t m, int64_t n,
+                                int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                                cudaStream_t stream, LaunchInfo *info);
+cudaError_t launch_gemm_bf16_fma(const void *a, const void *b, float *c, int64_t m, int64_t n,
+                                 int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                                 cudaStream_t stream, LaunchInfo *info);
+
 // ---- rmsnorm (attention block) -------------------------------------------------------------
 cudaError_t launch_residual_rmsnorm(const void *x, const void *attn_proj, void *y, int64_t rows,
                                     int64_t cols, float eps, cudaStream_t stream,

@@ -1,0 +1,323 @@
+// Typed isolated GEMMs, bit-exact with the reference's typed CPU references
+// (compiler/lib/runtime/cpu_numeric_reference.cpp):
+//
+//   int8 x int8 -> int32, accumulated modulo 2^32 (:185-209). Integer
+//     products and sums are exact, so the tensor-core kernel (tcgen05.mma
+//     kind::i8, int32 accumulator in TMEM, no saturation) gives the same bits
+//     as the CPU loop whatever the summation order.
+//   bf16 x bf16 -> f32 with one fused multiply-add per k in increasing order
+//     (:108-127). Rounding depends on the order, so this one runs on CUDA
+//     cores with fmaf in exactly that order.
+//
+// int8 kernel layout: A [M,K] K-major; B is consumed K-major (Bt [N,K]); a
+// B given as [K,N] is first transposed into scratch by a small kernel.
+// Persistent CTAs (one per SM, 192 threads): TMA producer warp, one MMA
+// thread (M=128, N=256, K=32 per instruction) into two 128x256 int32 TMEM
+// accumulators, four epilogue warps storing int32.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace mcb {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;  // BK in bytes == elements
+constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;
+
+__device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+struct Params {
+  int64_t m, n, ld_c;
+  int n_tiles, num_tiles, num_kb;
+  int32_t *c;
+  uint32_t *status;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_i8_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                   const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *sa = smem, *sb = smem + STAGES * A_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+  uint64_t *full = bars, *empty = bars + STAGES, *acc_full = bars + 2 * STAGES;
+  uint64_t *acc_empty = acc_full + 2, *drain = acc_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+        const int m0 = (tile / p.n_tiles) * BM, n0 = (tile % p.n_tiles) * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kErrTimeoutEmpty))
+            goto producer_done;
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_2d(sa + stage * A_BYTES, &ta, &full[stage], kb * BK, m0);
+          tma_load_2d(sb + stage * B_BYTES, &tb, &full[stage], kb * BK, n0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // kind::i8: D s32 (format 2), A and B signed 8-bit (format 1), K-major.
+      const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((BN >> 3) << 17) |
+                             ((BM >> 4) << 24);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        if (!(ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.status,
+                             kErrTimeoutAccum)))
+          break;
+        tc_fence_after();
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!(ok = mbar_wait(&full[stage], phase, abort_flag, p.status, kErrTimeoutFull))) break;
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sa + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sb + stage * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk)
+            mma_i8_ss(tmem + acc * BN, make_sdesc_sw128(a_addr + kk * 32, 16, 1024),
+                      make_sdesc_sw128(b_addr + kk * 32, 16, 1024), idesc, (kb | kk) ? 1u : 0u);
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      mma_commit(drain);
+      if (!mbar_wait(drain, 0, nullptr, p.status, kErrTimeoutDrain)) *abort_flag = 1;
+    }
+  } else {
+    const int sub = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BM;
+      const int64_t n0 = static_cast<int64_t>(tile % p.n_tiles) * BN;
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.status, kErrTimeoutAccum))
+        break;
+      tc_fence_after();
+      const int64_t row = m0 + sub * 32 + lane;
+      const uint32_t t_row = tmem + (static_cast<uint32_t>(sub * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        if (n0 + c >= p.n) break;
+        uint32_t r[32];
+        tmem_ld32_sync(t_row + c, r);
+        if (row < p.m) {
+          int32_t *crow = p.c + row * p.ld_c + n0 + c;
+          if (n0 + c + 32 <= p.n && (p.ld_c % 4 == 0)) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              reinterpret_cast<uint4 *>(crow)[q] =
+                  make_uint4(r[q * 4], r[q * 4 + 1], r[q * 4 + 2], r[q * 4 + 3]);
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (n0 + c + i < p.n) crow[i] = static_cast<int32_t>(r[i]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// B [K,N] -> Bt [N,K] for 1-byte elements, 32x32 tiles through shared memory.
+__global__ void transpose_u8_kernel(const uint8_t *__restrict__ in, uint8_t *__restrict__ out,
+                                    int64_t rows, int64_t cols, int64_t ld_in) {
+  __shared__ uint8_t tile[32][33];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32, c0 = static_cast<int64_t>(blockIdx.x) * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t r = r0 + i, c = c0 + threadIdx.x;
+    tile[i][threadIdx.x] = (r < rows && c < cols) ? in[r * ld_in + c] : 0;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t orow = c0 + i, ocol = r0 + threadIdx.x;
+    if (orow < cols && ocol < rows) out[orow * rows + ocol] = tile[threadIdx.x][i];
+  }
+}
+
+// CUDA-core int8 GEMM (exact; any shape/stride). One thread per output.
+__global__ void gemm_i8_simt_kernel(const int8_t *__restrict__ a, const int8_t *__restrict__ b,
+                                    int32_t *__restrict__ c, int64_t m, int64_t n, int64_t k,
+                                    int64_t lda, int64_t ldb, int64_t ldc) {
+  const int64_t row = blockIdx.y;
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= m || col >= n) return;
+  uint32_t acc = 0;
+  for (int64_t h = 0; h < k; ++h)
+    acc += static_cast<uint32_t>(static_cast<int32_t>(a[row * lda + h]) *
+                                 static_cast<int32_t>(b[h * ldb + col]));
+  c[row * ldc + col] = static_cast<int32_t>(acc);
+}
+
+// bf16 x bf16 -> f32, one fmaf per k in increasing order from +0 (the
+// reference's typed bf16 reference). Coalesced over columns; A row values
+// are loaded 16 steps ahead of the dependent fma chain.
+__global__ void __launch_bounds__(256) gemm_bf16_fma_kernel(const __nv_bfloat16 *__restrict__ a,
+                                                           const __nv_bfloat16 *__restrict__ b,
+                                                           float *__restrict__ c, int64_t m,
+                                                           int64_t n, int64_t k, int64_t lda,
+                                                           int64_t ldb, int64_t ldc) {
+  const int64_t row = blockIdx.y;
+  const int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= m || col >= n) return;
+  float acc = 0.0f;
+  int64_t h0 = 0;
+  for (; h0 + 16 <= k; h0 += 16) {
+    float av[16], bv[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      av[u] = __bfloat162float(a[row * lda + h0 + u]);
+      bv[u] = __bfloat162float(b[(h0 + u) * ldb + col]);
+    }
+#pragma unroll
+    for (int u = 0; u < 16; ++u) acc = __fmaf_rn(av[u], bv[u], acc);
+  }
+  for (; h0 < k; ++h0)
+    acc = __fmaf_rn(__bfloat162float(a[row * lda + h0]), __bfloat162float(b[h0 * ldb + col]), acc);
+  c[row * ldc + col] = acc;
+}
+
+}  // namespace
+
+cudaError_t launch_transpose_u8(const void *in, void *out, int64_t rows, int64_t cols,
+                                int64_t ld_in, cudaStream_t stream) {
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((rows + 31) / 32));
+  if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
+  transpose_u8_kernel<<<grid, dim3(32, 8), 0, stream>>>(static_cast<const uint8_t *>(in),
+                                                        static_cast<uint8_t *>(out), rows, cols,
+                                                        ld_in);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_i8_tc(const int8_t *a, const int8_t *bt, int32_t *c, int64_t m, int64_t n,
+                              int64_t k, int64_t ld_c, uint32_t *status, int sms,
+                              cudaStream_t stream, LaunchInfo *info) {
+  if (m == 0 || n == 0) return cudaSuccess;
+  if (k == 0 || k % 16 != 0) return cudaErrorNotSupported;
+  CUtensorMap ta, tb;
+  if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, m, k, BK, BM,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, bt, k, n, k, BK, BN,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorNotSupported;
+  Params p;
+  p.m = m;
+  p.n = n;
+  p.ld_c = ld_c;
+  p.n_tiles = static_cast<int>((n + BN - 1) / BN);
+  const int64_t tiles = ((m + BM - 1) / BM) * p.n_tiles;
+  if (tiles > 0x7fffffff) return cudaErrorNotSupported;
+  p.num_tiles = static_cast<int>(tiles);
+  p.num_kb = static_cast<int>((k + BK - 1) / BK);
+  p.c = c;
+  p.status = status;
+  const size_t smem = static_cast<size_t>(STAGES) * STAGE_BYTES + 256 + 1024;
+  cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  gemm_i8_kernel<<<grid, THREADS, smem, stream>>>(ta, tb, p);
+  if (info) {
+    info->launches += 1;
+    info->tile_m = BM;
+    info->tile_n = BN;
+    info->tile_k = BK;
+    info->stages = STAGES;
+    info->ctas = grid;
+    info->set_route("tcgen05_i8_gemm");
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_i8_simt(const int8_t *a, const int8_t *b, int32_t *c, int64_t m, int64_t n,
+                                int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                                cudaStream_t stream, LaunchInfo *info) {
+  if (m == 0 || n == 0) return cudaSuccess;
+  if (m > 65535) return cudaErrorInvalidConfiguration;
+  dim3 grid(static_cast<unsigned>((n + 255) / 256), static_cast<unsigned>(m));
+  gemm_i8_simt_kernel<<<grid, 256, 0, stream>>>(a, b, c, m, n, k, lda, ldb, ldc);
+  if (info) {
+    info->launches += 1;
+    info->set_route("simt_i8_gemm");
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm_bf16_fma(const void *a, const void *b, float *c, int64_t m, int64_t n,
+                                 int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                                 cudaStream_t stream, LaunchInfo *info) {
+  if (m == 0 || n == 0) return cudaSuccess;
+  if (m > 65535) return cudaErrorInvalidConfiguration;
+  dim3 grid(static_cast<unsigned>((n + 255) / 256), static_cast<unsigned>(m));
+  gemm_bf16_fma_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16 *>(a),
+                                                 static_cast<const __nv_bfloat16 *>(b), c, m, n, k,
+                                                 lda, ldb, ldc);
+  if (info) {
+    info->launches = 1;
+    info->set_route("simt_bf16_f32_fma_gemm");
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace mcb
