@@ -279,6 +279,20 @@ MCB_API int32_t mcb_fp8_is_legal_shape_v1(int64_t m, int64_t n, int64_t k) MCB_N
 MCB_API mcb_fp8_tile_config mcb_fp8_tile_config_v1(int64_t m, int64_t n,
                                                    int64_t k) MCB_NOEXCEPT;
 
+/* ---- block_attn_res region op (the reference's region_v1 operator) ------------ */
+/* Depth attention over packed block history, f32: for every (b, t), sources
+ * = blocks[0..block_count) (+ partial when has_partial); each source row is
+ * RMS-normalised over D (eps) and dotted with query; softmax over sources;
+ * out = weighted sum of the raw source rows (zeros when there is no source).
+ * blocks [MAX_BLOCKS<=32, B, T, D], partial/out [B, T, D], query [D], all
+ * dense f32. Replaces the kernel RegionMlirEmitter::emitBlockAttnRes emits
+ * (src/region_emitter_block_attn_res.cpp:38-432); argument rules of
+ * matcore/frontend.py:1734-1765. */
+MCB_API mcb_status mcb_block_attn_res_v1(const mcb_tensor *out, const mcb_tensor *blocks,
+                                         const mcb_tensor *partial, const mcb_tensor *query,
+                                         int64_t block_count, int32_t has_partial, float eps,
+                                         const mcb_exec *exec) MCB_NOEXCEPT;
+
 /* ---- attention-residual block region ------------------------------------------- */
 /* Y = RMSNorm(X + Wo * MSM(X Wq, X Wk, X Wv)) with unit gain; X [B,S,D] bf16,
  * W* [D,D] bf16, `heads` heads of D/heads, softmax scale (D/heads)^-0.5.

@@ -8,7 +8,8 @@ is missing -- there is no CPU fallback.
 """
 from . import _abi
 from ._abi import McbError, load
-from .api import (Plan, attn_block, device_status, fp8_quantize_blockwise, gemm_bf16_f32_fma,
+from .api import (Plan, attn_block, block_attn_res, device_status, fp8_quantize_blockwise,
+                  gemm_bf16_f32_fma,
                   gemm_chain, gemm_epilogue, gemm_fp8_blockscaled, gemm_i8_i32, msm, shard_plan,
                   strict_fused_pair, strict_gemm)
 

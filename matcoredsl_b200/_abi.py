@@ -133,6 +133,8 @@ SIGNATURES = {
     "mcb_gemm_fp8_blockscaled_v1": (ctypes.c_int32, [_T, _T, _T, _T, _T, ctypes.c_int64, _E]),
     "mcb_fp8_is_legal_shape_v1": (ctypes.c_int32, [ctypes.c_int64] * 3),
     "mcb_fp8_tile_config_v1": (Fp8TileConfig, [ctypes.c_int64] * 3),
+    "mcb_block_attn_res_v1": (ctypes.c_int32, [_T, _T, _T, _T, ctypes.c_int64, ctypes.c_int32,
+                                               ctypes.c_float, _E]),
     "mcb_attn_block_workspace_bytes_v1": (ctypes.c_uint64, [ctypes.c_int64] * 3),
     "mcb_attn_block_region_v1": (ctypes.c_int32, [_T, _T, _T, _T, _T, _T, ctypes.c_int64,
                                                   ctypes.c_float, _E]),

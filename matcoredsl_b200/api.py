@@ -249,6 +249,17 @@ def gemm_fp8_blockscaled(a, sa, bt, sbt, *, block=128, out=None, out_dtype="bf16
     return out
 
 
+def block_attn_res(blocks, partial, query, *, block_count, has_partial=True, eps=1e-6, out=None,
+                   device=-1, flags=0):
+    """The reference's mc.block_attn_res region op (depth attention, f32)."""
+    if out is None:
+        out = _empty_like_out(partial, tuple(partial.shape), "f32")
+    _call("mcb_block_attn_res_v1",
+          [("out", out), ("blocks", blocks), ("partial", partial), ("query", query)],
+          [int(block_count), 1 if has_partial else 0, float(eps)], device, flags)
+    return out
+
+
 def attn_block(x, wq, wk, wv, wo, heads, eps=1e-6, out=None, *, device=-1, flags=0):
     """Y = RMSNorm(X + MSM(X Wq, X Wk, X Wv) Wo), unit gain, softmax scale
     (D/heads)^-0.5; X [B, S, D] bf16, W* [D, D] bf16."""

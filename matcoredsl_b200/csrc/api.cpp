@@ -884,6 +884,55 @@ mcb_status gemm_fp8_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_ten
   return call.finish(c, dc, info, err);
 }
 
+// ---- block_attn_res ------------------------------------------------------------------------
+mcb_status block_attn_res_impl(const mcb_tensor *out, const mcb_tensor *blocks,
+                               const mcb_tensor *partial, const mcb_tensor *query,
+                               int64_t block_count, int32_t has_partial, float eps,
+                               const mcb_exec *exec) {
+  mcb_status s;
+  if ((s = check_tensor(blocks, 4, 4)) || (s = check_tensor(partial, 3, 3)) ||
+      (s = check_tensor(query, 1, 1)) || (s = check_tensor(out, 3, 3)))
+    return s;
+  for (const mcb_tensor *t : {blocks, partial, query, out})
+    if (t->dtype != MCB_DTYPE_F32) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  const int64_t maxb = blocks->dims[0], B = blocks->dims[1], T = blocks->dims[2],
+                D = blocks->dims[3];
+  if (maxb < 1 || maxb > 32) return MCB_STATUS_INVALID_SHAPE;          // MAX_BLOCKS in [1, 32]
+  if (block_count < 0 || block_count > maxb) return MCB_STATUS_INVALID_ARGUMENT;
+  if (!(eps > 0.0f)) return MCB_STATUS_INVALID_ARGUMENT;               // eps must be positive
+  auto dense = [](const mcb_tensor *t) {
+    int64_t st = 1;
+    for (int i = static_cast<int>(t->rank) - 1; i >= 0; --i) {
+      if (t->dims[i] > 1 && t->strides[i] != st) return false;
+      st *= t->dims[i];
+    }
+    return true;
+  };
+  for (const mcb_tensor *t : {blocks, partial, query, out})
+    if (!dense(t)) return MCB_STATUS_UNSUPPORTED_LAYOUT;
+  for (const mcb_tensor *t : {partial, out})
+    if (t->dims[0] != B || t->dims[1] != T || t->dims[2] != D) return MCB_STATUS_SHAPE_MISMATCH;
+  if (query->dims[0] != D) return MCB_STATUS_SHAPE_MISMATCH;
+  for (const mcb_tensor *t : {blocks, partial, query})
+    if (overlaps(out, t)) return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({blocks, partial, query, out}, &host))) return s;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  void *db, *dp, *dq, *dout;
+  if ((s = call.device_ptr(blocks, true, &db)) || (s = call.device_ptr(partial, true, &dp)) ||
+      (s = call.device_ptr(query, true, &dq)) || (s = call.device_ptr(out, false, &dout)))
+    return s;
+  LaunchInfo info;
+  call.mark_compute_start();
+  cudaError_t err = mcb::launch_block_attn_res(
+      static_cast<const float *>(db), static_cast<const float *>(dp),
+      static_cast<const float *>(dq), static_cast<float *>(dout), B * T, D, B * T * D,
+      static_cast<int>(block_count), has_partial ? 1 : 0, eps, call.sms(), call.stream(), &info);
+  call.mark_compute_end();
+  return call.finish(out, dout, info, err);
+}
+
 // ---- attention-residual block region ------------------------------------------------------
 uint64_t attn_workspace_bytes(int64_t batch, int64_t seq, int64_t d) {
   // Q, K, V, O and the output projection: five [B*S, D] bf16 buffers.
@@ -1179,6 +1228,17 @@ MCB_API mcb_status mcb_gemm_fp8_blockscaled_v1(const mcb_tensor *c, const mcb_te
                                                const mcb_exec *exec) noexcept {
   try {
     return gemm_fp8_impl(c, a, sa, bt, sbt, block, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API mcb_status mcb_block_attn_res_v1(const mcb_tensor *out, const mcb_tensor *blocks,
+                                         const mcb_tensor *partial, const mcb_tensor *query,
+                                         int64_t block_count, int32_t has_partial, float eps,
+                                         const mcb_exec *exec) noexcept {
+  try {
+    return block_attn_res_impl(out, blocks, partial, query, block_count, has_partial, eps, exec);
   } catch (...) {
     return MCB_STATUS_CANDIDATE_FAILURE;
   }

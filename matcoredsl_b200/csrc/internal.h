@@ -107,6 +107,12 @@ cudaError_t launch_gemm_bf16_fma(const void *a, const void *b, float *c, int64_t
                                  int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
                                  cudaStream_t stream, LaunchInfo *info);
 
+// ---- region.cu: block_attn_res (reference region op) ---------------------------------------
+cudaError_t launch_block_attn_res(const float *blocks, const float *partial, const float *query,
+                                  float *out, int64_t rows, int64_t d, int64_t block_stride,
+                                  int block_count, int has_partial, float eps, int sms,
+                                  cudaStream_t stream, LaunchInfo *info);
+
 // ---- rmsnorm (attention block) -------------------------------------------------------------
 cudaError_t launch_residual_rmsnorm(const void *x, const void *attn_proj, void *y, int64_t rows,
                                     int64_t cols, float eps, cudaStream_t stream,

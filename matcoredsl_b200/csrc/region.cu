@@ -84,7 +84,143 @@ __global__ void __launch_bounds__(THREADS) residual_rmsnorm_kernel(
   }
 }
 
+// ---- block_attn_res (the reference's region op) -------------------------------------
+// Depth attention over packed block history, f32 (src/region_emitter_block_
+// attn_res.cpp): for every (b, t) row, sources = blocks[0..block_count) plus
+// the partial; score_s = <x_s / rms(x_s), q>; w = softmax_s(score); out =
+// sum_s w_s x_s. One CTA of 128 threads per row. Pass 1 reads every source
+// row once (sum of squares and dot with q per thread, warp-shuffle then
+// shared-memory reduction); pass 2 re-reads the rows (L1/L2-resident) for the
+// weighted sum. HBM-bound: algorithmic bytes = (S + 1) * B*T*D*4 + D*4.
+constexpr int BAR_THREADS = 128;
+constexpr int BAR_MAX_SOURCES = 33;
+
+__global__ void __launch_bounds__(BAR_THREADS) block_attn_res_kernel(
+    const float *__restrict__ blocks, const float *__restrict__ partial,
+    const float *__restrict__ query, float *__restrict__ out, int64_t rows, int64_t d,
+    int64_t block_stride, int nsrc, int has_partial, int block_count, float eps, int vec4) {
+  __shared__ float red[BAR_THREADS / 32][BAR_MAX_SOURCES][2];
+  __shared__ float weight[BAR_MAX_SOURCES];
+  const int64_t row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto src = [&](int s) -> const float * {
+    return s < block_count ? blocks + s * block_stride + row * d : partial + row * d;
+  };
+  for (int s = 0; s < nsrc; ++s) {
+    const float *x = src(s);
+    float ss = 0.0f, dot = 0.0f;
+    if (vec4) {
+      for (int64_t i = threadIdx.x * 4; i < d; i += BAR_THREADS * 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(x + i);
+        const float4 q = *reinterpret_cast<const float4 *>(query + i);
+        ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+        dot = fmaf(v.x, q.x, fmaf(v.y, q.y, fmaf(v.z, q.z, fmaf(v.w, q.w, dot))));
+      }
+    } else {
+      for (int64_t i = threadIdx.x; i < d; i += BAR_THREADS) {
+        ss = fmaf(x[i], x[i], ss);
+        dot = fmaf(x[i], query[i], dot);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    }
+    if (lane == 0) {
+      red[warp][s][0] = ss;
+      red[warp][s][1] = dot;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    // Softmax over the sources, one lane per source (a 33rd in a second round).
+    float score[2] = {-INFINITY, -INFINITY};
+    for (int r = 0; r < 2; ++r) {
+      const int s = lane + 32 * r;
+      if (s < nsrc) {
+        float ss = 0.0f, dot = 0.0f;
+        for (int w = 0; w < BAR_THREADS / 32; ++w) {
+          ss += red[w][s][0];
+          dot += red[w][s][1];
+        }
+        score[r] = dot / sqrtf(ss / static_cast<float>(d) + eps);
+      }
+    }
+    float mx = fmaxf(score[0], score[1]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float e[2], sum = 0.0f;
+    for (int r = 0; r < 2; ++r) {
+      e[r] = (lane + 32 * r < nsrc) ? expf(score[r] - mx) : 0.0f;
+      sum += e[r];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    for (int r = 0; r < 2; ++r)
+      if (lane + 32 * r < nsrc) weight[lane + 32 * r] = e[r] / sum;
+  }
+  __syncthreads();
+  float *o = out + row * d;
+  if (vec4) {
+    for (int64_t i = threadIdx.x * 4; i < d; i += BAR_THREADS * 4) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int s = 0; s < nsrc; ++s) {
+        const float w = weight[s];
+        const float4 v = *reinterpret_cast<const float4 *>(src(s) + i);
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+      }
+      *reinterpret_cast<float4 *>(o + i) = acc;
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < d; i += BAR_THREADS) {
+      float acc = 0.0f;
+      for (int s = 0; s < nsrc; ++s) acc = fmaf(weight[s], src(s)[i], acc);
+      o[i] = acc;
+    }
+  }
+  (void)has_partial;
+}
+
+__global__ void zero_f32_kernel(float *__restrict__ y, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    y[i] = 0.0f;
+}
+
 }  // namespace
+
+cudaError_t launch_block_attn_res(const float *blocks, const float *partial, const float *query,
+                                  float *out, int64_t rows, int64_t d, int64_t block_stride,
+                                  int block_count, int has_partial, float eps, int sms,
+                                  cudaStream_t stream, LaunchInfo *info) {
+  if (rows == 0 || d == 0) return cudaSuccess;
+  const int nsrc = block_count + (has_partial ? 1 : 0);
+  if (nsrc > BAR_MAX_SOURCES || rows > 0x7fffffff) return cudaErrorInvalidValue;
+  if (info) info->launches = 1;
+  if (nsrc == 0) {  // no sources: zeros (the reference returns zeros_like(partial))
+    zero_f32_kernel<<<sms * 4, 256, 0, stream>>>(out, rows * d);
+    if (info) info->set_route("block_attn_res_zero");
+    return cudaGetLastError();
+  }
+  const bool vec4 = d % 4 == 0 && block_stride % 4 == 0 &&
+                    ((reinterpret_cast<uintptr_t>(blocks) | reinterpret_cast<uintptr_t>(partial) |
+                      reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(out)) &
+                     15u) == 0;
+  block_attn_res_kernel<<<static_cast<unsigned>(rows), BAR_THREADS, 0, stream>>>(
+      blocks, partial, query, out, rows, d, block_stride, nsrc, has_partial, block_count, eps,
+      vec4 ? 1 : 0);
+  if (info) {
+    info->tile_m = 1;
+    info->tile_n = BAR_THREADS;
+    info->ctas = static_cast<int>(rows);
+    info->set_route("block_attn_res");
+  }
+  return cudaGetLastError();
+}
 
 cudaError_t launch_residual_rmsnorm(const void *x, const void *attn_proj, void *y, int64_t rows,
                                     int64_t cols, float eps, cudaStream_t stream,

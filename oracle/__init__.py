@@ -234,6 +234,31 @@ def gemm_fp8_blockscaled(a, sa, bt, sbt, a_fmt="e4m3", b_fmt="e4m3", block=128, 
     return c
 
 
+# ---- block_attn_res (depth attention over packed block history, fp64) -----------
+def block_attn_res(blocks, partial, query, block_count, has_partial=True, eps=1e-6):
+    """The reference's region op (tests/test_block_attn_res.py:16-39): sources
+    = blocks[:block_count] (+ partial), each RMS-normalised over D and dotted
+    with `query`; softmax over sources; output = weighted sum of the raw
+    sources. No sources -> zeros. fp64 throughout, returned as float64."""
+    blocks = np.asarray(blocks, np.float64)
+    partial = np.asarray(partial, np.float64)
+    query = np.asarray(query, np.float64)
+    sources = []
+    if block_count:
+        sources.append(blocks[:block_count])
+    if has_partial:
+        sources.append(partial[None, ...])
+    if not sources:
+        return np.zeros_like(partial)
+    packed = np.concatenate(sources, axis=0)
+    inv_rms = 1.0 / np.sqrt(np.mean(packed * packed, axis=-1, keepdims=True) + eps)
+    scores = np.sum((packed * inv_rms) * query.reshape(1, 1, 1, -1), axis=-1)
+    scores = scores - np.max(scores, axis=0, keepdims=True)
+    w = np.exp(scores)
+    w = w / np.sum(w, axis=0, keepdims=True)
+    return np.sum(w[..., None] * packed, axis=0)
+
+
 # ---- attention-residual block (fp64, numpy) -------------------------------------
 def attn_block(x, wq, wk, wv, wo, heads, eps=1e-6, batch=0, tokens=None):
     """fp64 Y[b, t] = RMSNorm(X + MSM(X Wq, X Wk, X Wv) Wo) for batch element

@@ -12,7 +12,9 @@ the output array. The reference's unmodified test functions
 (tests/test_family_a.py, tests/test_family_b.py, tests/test_family_c.py) then
 run their own numpy expectation and assertion against that result, so every
 recorded case is an oracle output the reference's tests accepted. Each call's
-graph ops, inputs and output are saved to tests/golden/family_{a,b,c}.npz.
+graph ops, inputs and output are saved to tests/golden/family_{a,b,c}.npz;
+the region op block_attn_res (tests/test_block_attn_res.py) goes to
+tests/golden/block_attn_res.npz the same way.
 
 Only the test harness reads these fixtures; nothing here runs on the GPU box
 (the fixtures are committed, the reference is not needed there).
@@ -97,12 +99,22 @@ def main():
     sys.path.insert(0, os.path.join(args.ref, "tests"))
     import matcore  # noqa: F401  (the reference package, pure Python here)
 
-    records = {"a": [], "b": [], "c": []}
+    records = {"a": [], "b": [], "c": [], "r": []}
     current = {"name": ""}
     fake = types.ModuleType("matcore._matcore_native")
 
-    def compile_and_run(kernel_ir, target, *tensors):
+    def compile_and_run(kernel_ir, target, *tensors, **_obs):
         arrays, out = [np.asarray(t) for t in tensors[:-1]], tensors[-1]
+        if kernel_ir.get("version") == "region_v1":
+            node = next(n for n in kernel_ir["region"]["nodes"] if n["op"] == "block_attn_res")
+            attrs = node["attrs"]
+            meta = {"ops": ["block_attn_res"], "block_count": int(attrs["block_count"]),
+                    "has_partial": bool(attrs["has_partial"]), "eps": float(attrs["eps"])}
+            result = oracle.block_attn_res(arrays[0], arrays[1], arrays[2], meta["block_count"],
+                                           meta["has_partial"], meta["eps"]).astype(np.float32)
+            out[...] = result
+            records["r"].append((current["name"], arrays, result.copy(), meta))
+            return
         family, result, meta = _eval_graph(kernel_ir["graph"], arrays)
         out[...] = result
         records[family].append((current["name"], arrays, result.copy(), meta))
@@ -121,6 +133,8 @@ def main():
                           "test_attention_allows_swapped_qk_argument_order",
                           "test_attention_uses_score_cached_dtile64_route",
                           "test_attention_small"],
+        "test_block_attn_res": ["test_block_attn_res_host_correctness",
+                                "test_jit_block_attn_res_host_correctness"],
     }
     np.random.seed(20261201)  # the Family A/B tests draw from numpy's global RNG
     for module, tests in suites.items():
@@ -138,8 +152,9 @@ def main():
             payload[f"c{i}_out"] = result
             index.append({"name": name, "inputs": len(arrays), **meta})
         payload["index"] = np.frombuffer(json.dumps(index).encode(), dtype=np.uint8)
-        np.savez_compressed(os.path.join(HERE, f"family_{family}.npz"), **payload)
-        print(f"family_{family}.npz: {len(recs)} cases")
+        name = "block_attn_res" if family == "r" else f"family_{family}"
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **payload)
+        print(f"{name}.npz: {len(recs)} cases")
 
 
 if __name__ == "__main__":
