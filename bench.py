@@ -425,6 +425,7 @@ def run_ours(args):
     _abi.check(lib.mcb_gemm_epilogue_v1(c[0], c[1], c[2], c[3], ctypes.byref(ep), 0,
                                         ctypes.byref(ex_chk)), "route check")
     route = rep.route.decode()
+    kernel = "gemm_tc_bf16_pair_kernel" if rep.tile_m == 256 else "gemm_tc_bf16_kernel"
 
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
@@ -456,7 +457,7 @@ def run_ours(args):
         torch.cuda.empty_cache()
         others = run_other_configs(dev)
     _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, working_set, route,
-            clk, e2e, others)
+            clk, e2e, others, kernel)
 
 
 def _run_e2e(args, lib, ep, sets, descs, dev, stream, world, flops_step, m):
@@ -500,7 +501,7 @@ def _run_e2e(args, lib, ep, sets, descs, dev, stream, world, flops_step, m):
 
 
 def _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, working_set, route,
-            clk, e2e, others=None):
+            clk, e2e, others=None, kernel="gemm_tc_bf16_kernel"):
     peaks = _peaks()
     achieved = flops_step / (launch_ms_max / 1e3) / 1e12
     cpu = None
@@ -525,9 +526,9 @@ def _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, wo
             "pct_of_peak": value / world / peaks["bf16_tflops"],
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                          "unit": UNIT, "frac": achieved / peaks["bf16_tflops"],
-                         "traffic": _profiled_traffic("gemm_tc_bf16"),
+                         "traffic": _profiled_traffic(kernel),
                          "peak_source": f"{peaks['source']} bf16 burst (cuBLAS)",
-                         "kernel": "gemm_tc_bf16_kernel",
+                         "kernel": kernel,
                          "algorithmic_flops_per_launch": flops_step},
             "clocks": clk.summary(),
             "e2e": e2e,

@@ -15,11 +15,13 @@
 //   warp 1      allocates 512 TMEM columns = two 128x256 f32 partial buffers;
 //               one thread issues 4 tcgen05.mma.kind::f8f6f4 (K=32 each) per
 //               K block into a fresh partial, committing `pfull[buf]`.
-//   warps 2-9   promotion: warp w reads TMEM lane quarter w%4 and column half
-//               (w-2)/4 of the partial, multiplies by sa*sbt of that K block and
-//               accumulates into 128 f32 registers per thread; after the last K
-//               block it rounds to bf16/f32 and stores. Two partial buffers let
-//               the MMA of block kb+1 overlap the promotion of block kb.
+//   warps 2-9   promotion: warp w reads TMEM lane quarter w%4 and 128-column
+//               half (w-2)/4 of the partial (16 columns per tcgen05.ld),
+//               multiplies by sa*sbt of that K block and accumulates into 128
+//               f32 registers per thread; after the last K block it rounds to
+//               bf16/f32 and stores. Two warps per lane quarter overlap their
+//               TMEM-load latencies, and two partial buffers let the MMA of
+//               block kb+1 overlap the promotion of block kb.
 // Tiles are rasterised in groups of 16 M-tiles so the CTAs running at once
 // share A and Bt panels through L2 (config 4's operands are 2x L2).
 //
@@ -39,7 +41,9 @@ constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BKB;    // 16 KiB
 constexpr int B_BYTES = BN * BKB;    // 32 KiB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int THREADS = 320;
+constexpr int PROMO_WARPS = 8;                      // 2 per TMEM lane quarter
+constexpr int COLS_PER_WARP = BN * 4 / PROMO_WARPS;  // 128
+constexpr int THREADS = 64 + 32 * PROMO_WARPS;       // producer, MMA, promotion
 constexpr int GROUP_M = 16;
 
 struct Params {
@@ -85,7 +89,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&pfull[b], 1);
-      mbar_init(&pempty[b], 256);
+      mbar_init(&pempty[b], 32 * PROMO_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -156,21 +160,25 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!mbar_wait(drain, 0, nullptr, p.status, kErrTimeoutDrain)) *abort_flag = 1;
     }
   } else {
-    const int q = warp & 3;             // TMEM lane quarter
-    const int half = (warp - 2) >> 2;   // column half of the 256-wide tile
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(q * 32) << 16) + half * 128;
+    // Promotion warps 2..(2+PROMO_WARPS): warp w reads TMEM lane quarter w%4
+    // and the 64-column group (w-2)/4 of the 256-column partial; four warps
+    // share each lane quarter so their TMEM-load latencies overlap.
+    const int q = warp & 3;
+    const int grp = (warp - 2) >> 2;
+    const uint32_t lane_base =
+        tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(grp * COLS_PER_WARP);
     uint32_t kc = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       int mt, nt;
       tile_coords(p, tile, mt, nt);
       const int64_t row = static_cast<int64_t>(mt) * BM + q * 32 + lane;
-      const int64_t col0 = static_cast<int64_t>(nt) * BN + half * 128;
-      const int sa_row = mt;                  // M block (BM == scale block)
-      const int sb_row = nt * 2 + half;       // N block of this column half
+      const int64_t col0 = static_cast<int64_t>(nt) * BN + grp * COLS_PER_WARP;
+      const int sa_row = mt;                                       // M block (BM == block)
+      const int sb_row = nt * 2 + (grp * COLS_PER_WARP) / 128;     // N block of these columns
       const bool cols_live = col0 < p.n;
-      float acc[128];
+      float acc[COLS_PER_WARP];
 #pragma unroll
-      for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+      for (int i = 0; i < COLS_PER_WARP; ++i) acc[i] = 0.0f;
       bool ok = true;
       for (int kb = 0; kb < p.num_kb; ++kb, ++kc) {
         const int buf = kc & 1;
@@ -181,23 +189,23 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32_sync(lane_base + buf * BN + c * 32, r);
+        for (int c = 0; c < COLS_PER_WARP / 16; ++c) {
+          uint32_t r[16];  // 16-column loads keep 64 acc + 16 live within 96 registers
+          tmem_ld16_sync(lane_base + buf * BN + c * 16, r);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(s, __uint_as_float(r[i]), acc[c * 32 + i]);
+          for (int i = 0; i < 16; ++i) acc[c * 16 + i] = fmaf(s, __uint_as_float(r[i]), acc[c * 16 + i]);
         }
         tc_fence_before();
         mbar_arrive(&pempty[buf]);
       }
       if (!ok) break;
       if (row < p.m && cols_live) {
-        const bool full_cols = col0 + 128 <= p.n;
+        const bool full_cols = col0 + COLS_PER_WARP <= p.n;
         if (p.c_bf16) {
           __nv_bfloat16 *crow = reinterpret_cast<__nv_bfloat16 *>(p.c) + row * p.ld_c + col0;
           if (full_cols) {
 #pragma unroll
-            for (int v = 0; v < 16; ++v) {
+            for (int v = 0; v < COLS_PER_WARP / 8; ++v) {
               uint4 w;
               w.x = pack_bf16x2(acc[v * 8 + 0], acc[v * 8 + 1]);
               w.y = pack_bf16x2(acc[v * 8 + 2], acc[v * 8 + 3]);
@@ -206,18 +214,20 @@ __global__ void __launch_bounds__(THREADS, 1)
               reinterpret_cast<uint4 *>(crow)[v] = w;
             }
           } else {
-            for (int i = 0; i < 128; ++i)
+#pragma unroll
+            for (int i = 0; i < COLS_PER_WARP; ++i)
               if (col0 + i < p.n) crow[i] = __float2bfloat16_rn(acc[i]);
           }
         } else {
           float *crow = reinterpret_cast<float *>(p.c) + row * p.ld_c + col0;
           if (full_cols) {
 #pragma unroll
-            for (int v = 0; v < 32; ++v)
+            for (int v = 0; v < COLS_PER_WARP / 4; ++v)
               reinterpret_cast<float4 *>(crow)[v] =
                   make_float4(acc[v * 4], acc[v * 4 + 1], acc[v * 4 + 2], acc[v * 4 + 3]);
           } else {
-            for (int i = 0; i < 128; ++i)
+#pragma unroll
+            for (int i = 0; i < COLS_PER_WARP; ++i)
               if (col0 + i < p.n) crow[i] = acc[i];
           }
         }

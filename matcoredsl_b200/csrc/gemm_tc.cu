@@ -23,6 +23,9 @@
 // bf16 dense tensor peak; ideal HBM traffic X + W + Y = 160 MiB.
 #include <cuda_bf16.h>
 
+#include <atomic>
+#include <cstdlib>
+
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "internal.h"
@@ -282,6 +285,222 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ---- CTA-pair (2-SM) variant ---------------------------------------------------
+// A cluster of two CTAs on two SMs computes a 256x256 tile with
+// tcgen05.mma.cta_group::2 (M=256, N=256, K=16): CTA r holds rows
+// [128r, 128r+128) of the X tile and columns [128r, 128r+128) of the W tile
+// in its own shared memory, so each SM stages half of W per tile (B operand
+// traffic per SM halves versus the single-SM kernel), and its TMEM receives
+// its own 128 rows x 256 columns of the f32 accumulator. The leader CTA
+// (rank 0) issues every MMA; both CTAs' TMA loads count on the leader's
+// `full` barrier, MMA completion is committed to both CTAs' `empty` /
+// `acc_full` barriers, and both epilogues release the leader's `acc_empty`.
+constexpr int P_BN_CTA = BN / 2;  // W columns staged per CTA
+constexpr int P_A_BYTES = BM * BK * 2;        // 16 KiB
+constexpr int P_B_BYTES = P_BN_CTA * BK * 2;  // 16 KiB
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_STAGES = 6;
+constexpr size_t P_SMEM_BYTES = static_cast<size_t>(P_STAGES) * P_STAGE_BYTES + BAR_BYTES + 1024;
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_tc_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                             const __grid_constant__ CUtensorMap tmap_w, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *sa = smem;
+  uint8_t *sb = smem + P_STAGES * P_A_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + P_STAGES;
+  uint64_t *acc_full = bars + 2 * P_STAGES;
+  uint64_t *acc_empty = acc_full + 2;
+  uint64_t *drain = acc_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 256);  // 128 epilogue threads of each CTA (leader's copy)
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_x);
+    tma_prefetch_desc(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = cluster; tile < p.num_tiles; tile += nclusters) {
+        const int m0 = (tile / p.n_tiles) * (2 * BM) + static_cast<int>(rank) * BM;
+        const int n0 = (tile % p.n_tiles) * BN + static_cast<int>(rank) * P_BN_CTA;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kErrTimeoutEmpty))
+            goto producer_done;
+          const uint32_t fbar = full_leader0 + stage * 8;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          tma_load_2d_pair(sa + stage * P_A_BYTES, &tmap_x, fbar, kb * BK, m0);
+          if (p.w_transposed) {
+            tma_load_2d_pair(sb + stage * P_B_BYTES, &tmap_w, fbar, kb * BK, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < P_BN_CTA / 64; ++j)
+              tma_load_2d_pair(sb + stage * P_B_BYTES + j * (64 * BK * 2), &tmap_w, fbar,
+                               n0 + j * 64, kb * BK);
+          }
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      const uint32_t idesc = make_idesc(1, 1, 0, p.w_transposed ? 0u : 1u, 2 * BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = cluster; tile < p.num_tiles; tile += nclusters) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.status, kErrTimeoutAccum))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sa + stage * P_A_BYTES);
+          const uint32_t b_addr = smem_u32(sb + stage * P_B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t adesc = make_sdesc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bdesc = p.w_transposed
+                                       ? make_sdesc_sw128(b_addr + kk * 32, 16, 1024)
+                                       : make_sdesc_sw128(b_addr + kk * 2048, 64 * BK * 2, 1024);
+            mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair(&empty[stage], 0x3);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(&acc_full[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      mma_commit_pair(drain, 0x1);
+      if (!mbar_wait(drain, 0, nullptr, p.status, kErrTimeoutDrain)) *abort_flag = 1;
+    }
+  } else {
+    const int sub = warp & 3;
+    const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = cluster; tile < p.num_tiles; tile += nclusters) {
+      const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * (2 * BM) + rank * BM;
+      const int64_t n0 = static_cast<int64_t>(tile % p.n_tiles) * BN;
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.status, kErrTimeoutAccum))
+        break;
+      tc_fence_after();
+      const int64_t row = m0 + sub * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        if (n0 + c >= p.n) break;
+        uint32_t r[32];
+        tmem_ld32_sync(t_row + c, r);
+        epilogue_chunk(p, r, row, n0 + c);
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(acc_empty_leader + acc * 8);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // every pair MMA has completed before either CTA frees TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+namespace {
+
+// Clusters of the pair kernel that fit on the device at once (one CTA per SM;
+// a GPC with an odd number of usable SMs leaves one SM out), cached per device.
+int pair_clusters_resident(int device) {
+  static std::atomic<int> cache[64];
+  if (device < 0 || device >= 64) return 0;
+  int v = cache[device].load(std::memory_order_relaxed);
+  if (v != 0) return v;
+  if (cudaFuncSetAttribute(gemm_tc_bf16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(P_SMEM_BYTES)) != cudaSuccess) {
+    (void)cudaGetLastError();
+    cache[device].store(-1, std::memory_order_relaxed);
+    return -1;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = P_SMEM_BYTES;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_bf16_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+    (void)cudaGetLastError();
+    n = -1;  // pair kernel unavailable on this device: use the single-SM kernel
+  }
+  cache[device].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+bool pair_kernel_enabled() {
+  static const bool on = [] {
+    const char *e = getenv("MCB_GEMM_TC_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 }  // namespace
 
 cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m, int64_t n,
@@ -290,13 +509,26 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
                                 uint32_t *status, int sms, cudaStream_t stream,
                                 LaunchInfo *info) {
   if (m == 0 || n == 0) return cudaSuccess;
+  // Rows of 256 go to CTA pairs (M = 256 per MMA, W tile split between the
+  // two SMs); shorter problems keep one 128-row tile per SM.
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  const bool pair = m >= 2 * BM && pair_kernel_enabled() && pair_clusters_resident(device) > 0;
+  if (pair) {
+    e = cudaFuncSetAttribute(gemm_tc_bf16_pair_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(P_SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+  }
+  const int w_rows = pair ? P_BN_CTA : BN;  // W^T box height per CTA
   CUtensorMap tx, tw;
   if (!encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m, ld_x * 2, BK, BM,
                       CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   const bool ok_w =
       w_transposed
-          ? encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, k, n, ld_w * 2, BK, BN,
+          ? encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, k, n, ld_w * 2, BK, w_rows,
                            CU_TENSOR_MAP_SWIZZLE_128B)
           : encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, n, k, ld_w * 2, 64, BK,
                            CU_TENSOR_MAP_SWIZZLE_128B);
@@ -307,7 +539,8 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   p.k = k;
   p.ld_y = ld_y;
   p.n_tiles = static_cast<int>((n + BN - 1) / BN);
-  const int64_t tiles = ((m + BM - 1) / BM) * p.n_tiles;
+  const int64_t tile_rows = pair ? 2 * BM : BM;
+  const int64_t tiles = ((m + tile_rows - 1) / tile_rows) * p.n_tiles;
   if (tiles > 0x7fffffff) return cudaErrorInvalidConfiguration;
   p.num_tiles = static_cast<int>(tiles);
   p.num_kb = static_cast<int>((k + BK - 1) / BK);
@@ -316,19 +549,27 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   p.y = y;
   p.status = status;
   p.epi = epi;
-  // Per-device function attribute; cheap, so set on every launch.
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_bf16_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(SMEM_BYTES));
-  if (e != cudaSuccess) return e;
-  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-  gemm_tc_bf16_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tx, tw, p);
+  int grid;
+  if (pair) {
+    int clusters = pair_clusters_resident(device);
+    if (clusters > sms / 2) clusters = sms / 2;
+    if (clusters < 1) clusters = 1;
+    grid = 2 * static_cast<int>(tiles < clusters ? tiles : clusters);
+    gemm_tc_bf16_pair_kernel<<<grid, THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
+  } else {
+    // Per-device function attribute; cheap, so set on every launch.
+    e = cudaFuncSetAttribute(gemm_tc_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    grid = static_cast<int>(tiles < sms ? tiles : sms);
+    gemm_tc_bf16_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tx, tw, p);
+  }
   if (info) {
     info->launches = 1;
-    info->tile_m = BM;
+    info->tile_m = static_cast<int>(tile_rows);
     info->tile_n = BN;
     info->tile_k = BK;
-    info->stages = STAGES;
+    info->stages = pair ? P_STAGES : STAGES;
     info->ctas = grid;
     info->set_route("tcgen05_bf16_gemm_epilogue");
   }

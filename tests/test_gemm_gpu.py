@@ -29,7 +29,8 @@ def _inputs(m, k, n, seed, wscale=None):
 
 
 @pytest.mark.parametrize("shape", [(128, 64, 256), (256, 1024, 512), (300, 264, 520),
-                                   (1000, 4096, 1032), (128, 8, 8), (129, 16, 264)])
+                                   (1000, 4096, 1032), (128, 8, 8), (129, 16, 264),
+                                   (2048, 256, 2560)])
 @pytest.mark.parametrize("w_transposed", [False, True])
 def test_tcgen05_f32_out_exact_accumulation(mcb, orc, shape, w_transposed):
     import torch
@@ -41,7 +42,10 @@ def test_tcgen05_f32_out_exact_accumulation(mcb, orc, shape, w_transposed):
     tw = gu.to_dev_bf16(np.ascontiguousarray(wh.T) if w_transposed else wh)
     y = torch.empty(m, n, dtype=torch.float32, device="cuda")
     mcb.gemm_epilogue(tx, tw, out=y, w_transposed=w_transposed)
-    assert mcb.api.last_result.route == "tcgen05_bf16_gemm_epilogue"
+    r = mcb.api.last_result
+    assert r.route == "tcgen05_bf16_gemm_epilogue"
+    # M >= 256 runs on SM pairs (256-row tiles), shorter problems on single SMs.
+    assert r.tile[0] == (256 if m >= 256 else 128) and r.ctas % (2 if m >= 256 else 1) == 0
     ref = orc.gemm_epilogue(xf, wf)
     assert orc.rel_frobenius(gu.from_dev(y), ref) < REL_F32_OUT
 
