@@ -105,6 +105,11 @@ struct DeviceCtx {
   uint32_t *status = nullptr;
   void *stage[kStageSlots] = {};
   size_t stage_cap[kStageSlots] = {};
+  // Row pipeline for host operands: uploads and downloads run on their own
+  // streams (separate copy engines, PCIe is full duplex) and are ordered
+  // against the compute stream with events from this pool.
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  std::vector<cudaEvent_t> events;
 };
 DeviceCtx g_dev[kMaxDevices];
 
@@ -349,12 +354,19 @@ class Call {
   mcb_status finish(const mcb_tensor *out, void *dev_out, const LaunchInfo &info,
                     cudaError_t launch_err) {
     if (launch_err != cudaSuccess) return from_cuda(launch_err);
-    if (out && host_ && numel(out) > 0) {
-      const size_t bytes = span_bytes(out);
-      if (cudaMemcpyAsync(out->data, dev_out, bytes, cudaMemcpyDeviceToHost, stream_) !=
-          cudaSuccess)
-        return MCB_STATUS_CANDIDATE_FAILURE;
-      d2h_bytes_ += bytes;
+    if (out && host_ && numel(out) > 0 && !output_staged_) {
+      if (out->rank == 2) {
+        if (copy_rows(out->data, dev_out, out, 0, out->dims[0], cudaMemcpyDeviceToHost,
+                      stream_) != cudaSuccess)
+          return MCB_STATUS_CANDIDATE_FAILURE;
+        d2h_bytes_ += row_bytes(out, 0, out->dims[0]);
+      } else {
+        const size_t bytes = span_bytes(out);
+        if (cudaMemcpyAsync(out->data, dev_out, bytes, cudaMemcpyDeviceToHost, stream_) !=
+            cudaSuccess)
+          return MCB_STATUS_CANDIDATE_FAILURE;
+        d2h_bytes_ += bytes;
+      }
     }
     if (timed_) cudaEventRecord(events_[3], stream_);
     uint32_t word = 0;
@@ -387,13 +399,138 @@ class Call {
     return MCB_STATUS_OK;
   }
 
+  // Row pipeline for a row-splittable operator whose operands are in host
+  // memory: rows [0, m) are processed in chunks of `chunk_rows`. For each
+  // chunk the rows of every `row_inputs` tensor are uploaded on the copy-in
+  // stream, `launch(r0, r1)` runs on the call's stream once they have landed,
+  // and the chunk's rows of `out` are downloaded on the copy-out stream, so the
+  // upload of chunk c+1, the kernels of chunk c and the download of chunk c-1
+  // overlap. Row-chunked tensors are rank 2 with unit column stride; their
+  // staging buffers (`dev`) have the host tensor's strides. Only the output's
+  // own columns are written back (host padding between rows is left alone).
+  struct RowOperand {
+    const mcb_tensor *t;
+    void *dev;
+  };
+  // `whole_inputs` (operands every chunk reads in full, e.g. the weights) are
+  // uploaded first on the copy-in stream, so they arrive at full PCIe
+  // bandwidth and the first chunk's kernels and download start early.
+  template <typename Launch>
+  mcb_status run_row_pipeline(int64_t m, int64_t chunk_rows, const RowOperand *whole_inputs,
+                              int n_whole, const RowOperand *row_inputs, int n_inputs,
+                              RowOperand out, Launch &&launch, cudaError_t *launch_err) {
+    *launch_err = cudaSuccess;
+    const int64_t nchunks = (m + chunk_rows - 1) / chunk_rows;
+    mcb_status s = pipeline_resources(static_cast<int>(2 * nchunks + 2));
+    if (s) return s;
+    cudaEvent_t *ev = ctx_->events.data();
+    cudaStream_t cin = ctx_->copy_in, cout = ctx_->copy_out;
+    // Uploads start after the caller's earlier work on its stream.
+    if (cudaEventRecord(ev[0], stream_) != cudaSuccess ||
+        cudaStreamWaitEvent(cin, ev[0], 0) != cudaSuccess)
+      return MCB_STATUS_CANDIDATE_FAILURE;
+    s = MCB_STATUS_OK;
+    for (int i = 0; i < n_whole && !s; ++i) {
+      const mcb_tensor *t = whole_inputs[i].t;
+      if (!t || numel(t) == 0) continue;
+      const uint64_t bytes = span_bytes(t);
+      if (cudaMemcpyAsync(whole_inputs[i].dev, t->data, bytes, cudaMemcpyHostToDevice, cin) !=
+          cudaSuccess)
+        s = MCB_STATUS_CANDIDATE_FAILURE;
+      else
+        h2d_bytes_ += bytes;
+    }
+    for (int64_t c = 0; c < nchunks && !s; ++c) {
+      const int64_t r0 = c * chunk_rows, r1 = std::min(m, r0 + chunk_rows);
+      cudaEvent_t in_done = ev[2 + 2 * c], out_ready = ev[3 + 2 * c];
+      for (int i = 0; i < n_inputs && !s; ++i) {
+        if (copy_rows(row_inputs[i].dev, row_inputs[i].t->data, row_inputs[i].t, r0, r1,
+                      cudaMemcpyHostToDevice, cin) != cudaSuccess)
+          s = MCB_STATUS_CANDIDATE_FAILURE;
+        else
+          h2d_bytes_ += row_bytes(row_inputs[i].t, r0, r1);
+      }
+      if (s) break;
+      if (cudaEventRecord(in_done, cin) != cudaSuccess ||
+          cudaStreamWaitEvent(stream_, in_done, 0) != cudaSuccess) {
+        s = MCB_STATUS_CANDIDATE_FAILURE;
+        break;
+      }
+      *launch_err = launch(r0, r1);
+      if (*launch_err != cudaSuccess) break;
+      if (cudaEventRecord(out_ready, stream_) != cudaSuccess ||
+          cudaStreamWaitEvent(cout, out_ready, 0) != cudaSuccess ||
+          copy_rows(out.t->data, out.dev, out.t, r0, r1, cudaMemcpyDeviceToHost, cout) !=
+              cudaSuccess) {
+        s = MCB_STATUS_CANDIDATE_FAILURE;
+        break;
+      }
+      d2h_bytes_ += row_bytes(out.t, r0, r1);
+    }
+    // The call's stream (synchronised by finish) waits for the last download;
+    // on any failure every stream is drained before the staging slots can be
+    // reused.
+    if (cudaEventRecord(ev[1], cout) != cudaSuccess ||
+        cudaStreamWaitEvent(stream_, ev[1], 0) != cudaSuccess)
+      s = s ? s : MCB_STATUS_CANDIDATE_FAILURE;
+    if (s || *launch_err != cudaSuccess) {
+      cudaStreamSynchronize(cin);
+      cudaStreamSynchronize(cout);
+      cudaStreamSynchronize(stream_);
+    }
+    output_staged_ = true;
+    return s;
+  }
+
+  bool host_operands() const { return host_; }
+  bool timed() const { return timed_; }
   DeviceCtx *ctx() const { return ctx_; }
   cudaStream_t stream() const { return stream_; }
   int sms() const { return ctx_->sms; }
   const mcb_exec *exec() const { return exec_; }
 
  private:
+  // Bytes of rows [r0, r1) of a rank-2 tensor, its own columns only.
+  static uint64_t row_bytes(const mcb_tensor *t, int64_t r0, int64_t r1) {
+    return static_cast<uint64_t>(r1 - r0) * static_cast<uint64_t>(t->dims[1]) *
+           dtype_size(t->dtype);
+  }
+  // Copies rows [r0, r1) of a rank-2 tensor between host memory and its
+  // staging buffer (same strides on both sides): one linear copy when the
+  // rows are packed, else a pitched copy of the tensor's own columns.
+  static cudaError_t copy_rows(void *dst, const void *src, const mcb_tensor *t, int64_t r0,
+                               int64_t r1, cudaMemcpyKind kind, cudaStream_t stream) {
+    const size_t es = dtype_size(t->dtype);
+    const size_t pitch = static_cast<size_t>(t->strides[0]) * es;
+    const size_t width = static_cast<size_t>(t->dims[1]) * es;
+    const size_t off = static_cast<size_t>(r0) * pitch;
+    const size_t rows = static_cast<size_t>(r1 - r0);
+    if (rows == 0 || width == 0) return cudaSuccess;
+    char *d = static_cast<char *>(dst) + off;
+    const char *s = static_cast<const char *>(src) + off;
+    if (pitch == width || rows == 1) return cudaMemcpyAsync(d, s, rows * width, kind, stream);
+    return cudaMemcpy2DAsync(d, pitch, s, pitch, width, rows, kind, stream);
+  }
+  // Copy streams and at least `n` events of the device's row pipeline
+  // (created once; the device mutex is held for host-operand calls).
+  mcb_status pipeline_resources(int n) {
+    if (!ctx_->copy_in &&
+        cudaStreamCreateWithFlags(&ctx_->copy_in, cudaStreamNonBlocking) != cudaSuccess)
+      return MCB_STATUS_CANDIDATE_FAILURE;
+    if (!ctx_->copy_out &&
+        cudaStreamCreateWithFlags(&ctx_->copy_out, cudaStreamNonBlocking) != cudaSuccess)
+      return MCB_STATUS_CANDIDATE_FAILURE;
+    while (static_cast<int>(ctx_->events.size()) < n) {
+      cudaEvent_t e;
+      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess)
+        return MCB_STATUS_CANDIDATE_FAILURE;
+      ctx_->events.push_back(e);
+    }
+    return MCB_STATUS_OK;
+  }
+
   const mcb_exec *exec_;
+  bool output_staged_ = false;
   int dev_ = -1;
   DeviceGuard *guard_ = nullptr;
   DeviceCtx *ctx_ = nullptr;
@@ -496,6 +633,20 @@ mcb_status strict_pair_impl(const mcb_tensor *e, const mcb_tensor *a, const mcb_
 }
 
 // ---- Family A -------------------------------------------------------------------------
+// Row-chunk size for the host-operand pipeline of a row-splittable operator:
+// a multiple of 256 rows holding about 4 MiB of the row operand `x`, at most
+// 64 chunks; 0 (no pipeline) when `m` gives fewer than two chunks.
+int64_t pipeline_chunk_rows(int64_t m, const mcb_tensor *x) {
+  constexpr int64_t kChunkBytes = 4 << 20, kAlign = 256, kMaxChunks = 64;
+  const int64_t row_bytes = std::max<int64_t>(1, x->strides[0]) *
+                            static_cast<int64_t>(dtype_size(x->dtype));
+  int64_t rows = (kChunkBytes / row_bytes + kAlign - 1) / kAlign * kAlign;
+  rows = std::max(rows, kAlign);
+  const int64_t min_rows = ((m + kMaxChunks - 1) / kMaxChunks + kAlign - 1) / kAlign * kAlign;
+  rows = std::max(rows, min_rows);
+  return m >= 2 * rows ? rows : 0;
+}
+
 mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mcb_tensor *w,
                               const mcb_tensor *bias, const mcb_epilogue *epi,
                               uint32_t gemm_flags, const mcb_exec *exec) {
@@ -541,31 +692,63 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
   if ((s = same_space({x, w, y, ep.bias_mode ? bias : nullptr}, &host))) return s;
   Call call(exec);
   if ((s = call.begin(host))) return s;
+  // Host operands (untimed calls): X, a full bias and Y move in row chunks of
+  // about 4 MiB of X so that uploads, GEMMs and downloads overlap (W and a
+  // row bias are uploaded whole, ahead of the first chunk).
+  const int64_t chunk_rows = host && !call.timed() ? pipeline_chunk_rows(m, x) : 0;
+  const bool full_bias = ep.bias_mode == MCB_BIAS_FULL;
   void *dx, *dw, *dy, *db = nullptr;
-  if ((s = call.device_ptr(x, true, &dx)) || (s = call.device_ptr(w, true, &dw)) ||
+  const bool serial = chunk_rows == 0;
+  if ((s = call.device_ptr(x, serial, &dx)) || (s = call.device_ptr(w, serial, &dw)) ||
       (s = call.device_ptr(y, false, &dy)))
     return s;
-  if (ep.bias_mode && (s = call.device_ptr(bias, true, &db))) return s;
+  if (ep.bias_mode && (s = call.device_ptr(bias, serial, &db))) return s;
   ep.bias = db;
   ep.bias_aligned16 = (reinterpret_cast<uintptr_t>(db) & 15u) == 0;
   LaunchInfo info;
-  cudaError_t err;
+  cudaError_t err = cudaSuccess;
   const int64_t ld_x = x->strides[0], ld_w = w->strides[0], ld_y = y->strides[0];
   // Tensor-core eligibility: TMA wants 16-byte aligned bases and row strides.
+  // Row chunks start at multiples of 256 rows, so they keep the alignment.
   const bool tma_ok = in_bf16 && k > 0 && (k % 8 == 0) && (ld_x % 8 == 0) && (ld_w % 8 == 0) &&
                       (wt || n % 8 == 0) && (reinterpret_cast<uintptr_t>(dx) % 16 == 0) &&
                       (reinterpret_cast<uintptr_t>(dw) % 16 == 0) &&
                       (reinterpret_cast<uintptr_t>(dy) % 16 == 0) &&
                       (ld_y % (y->dtype == MCB_DTYPE_BF16 ? 8 : 4) == 0);
+  const size_t xs = dtype_size(x->dtype), ys = dtype_size(y->dtype);
+  const size_t bs = ep.bias_mode ? dtype_size(bias->dtype) : 0;
+  auto launch_rows = [&](int64_t r0, int64_t r1) -> cudaError_t {
+    const void *xr = static_cast<const char *>(dx) + r0 * ld_x * xs;
+    void *yr = static_cast<char *>(dy) + r0 * ld_y * ys;
+    mcb::Epilogue e = ep;
+    if (full_bias) {
+      e.bias = static_cast<const char *>(db) + r0 * ep.ld_bias * bs;
+      e.bias_aligned16 = (reinterpret_cast<uintptr_t>(e.bias) & 15u) == 0;
+    }
+    if (tma_ok)
+      return mcb::launch_gemm_tc_bf16(xr, dw, yr, r1 - r0, n, k, ld_x, ld_w, ld_y, wt ? 1 : 0,
+                                      y->dtype == MCB_DTYPE_BF16 ? 1 : 0, e, call.ctx()->status,
+                                      call.sms(), call.stream(), &info);
+    return mcb::launch_gemm_simt(xr, static_cast<int>(x->dtype), dw, static_cast<int>(w->dtype),
+                                 yr, static_cast<int>(y->dtype), r1 - r0, n, k, ld_x, ld_w, ld_y,
+                                 wt ? 1 : 0, e, call.stream(), &info);
+  };
   call.mark_compute_start();
-  if (tma_ok) {
-    err = mcb::launch_gemm_tc_bf16(dx, dw, dy, m, n, k, ld_x, ld_w, ld_y, wt ? 1 : 0,
-                                   y->dtype == MCB_DTYPE_BF16 ? 1 : 0, ep, call.ctx()->status,
-                                   call.sms(), call.stream(), &info);
+  if (chunk_rows) {
+    const Call::RowOperand whole[2] = {{w, dw}, {ep.bias_mode ? bias : nullptr, db}};
+    const Call::RowOperand ins[2] = {{x, dx}, {bias, db}};
+    int launches = 0;
+    s = call.run_row_pipeline(
+        m, chunk_rows, whole, full_bias ? 1 : 2, ins, full_bias ? 2 : 1, Call::RowOperand{y, dy},
+        [&](int64_t r0, int64_t r1) {
+          ++launches;
+          return launch_rows(r0, r1);
+        },
+        &err);
+    if (s) return s;
+    info.launches = launches;
   } else {
-    err = mcb::launch_gemm_simt(dx, static_cast<int>(x->dtype), dw, static_cast<int>(w->dtype),
-                                dy, static_cast<int>(y->dtype), m, n, k, ld_x, ld_w, ld_y,
-                                wt ? 1 : 0, ep, call.stream(), &info);
+    err = launch_rows(0, m);
   }
   call.mark_compute_end();
   return call.finish(y, dy, info, err);
