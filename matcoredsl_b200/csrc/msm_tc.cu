@@ -3,7 +3,7 @@
 //   O[b,h] = softmax(scale * Q[b,h] K[b,h]^T) V[b,h]      (src/fusion_emitter_family_c.cpp)
 //
 // One work unit = (b, h, 128-row query block). Persistent CTAs (one per SM,
-// 224 threads) loop over units; consecutive units share (b, h) so K/V stay
+// 192 threads) loop over units; consecutive units share (b, h) so K/V stay
 // in L2 for the CTAs running at the same time.
 //
 //   warp 0      TMA producer: Q (once per unit), K tiles into a 3-stage ring,
