@@ -387,6 +387,400 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ---- two query tiles per CTA (query blocks of 256 rows) ---------------------------------
+// The single-tile kernel above leaves one softmax warp per SM sub-partition,
+// which cannot keep the exp2 unit busy while the tensor core waits for P. Here
+// a work unit is a 256-row query block split into two 128-row tiles g = 0, 1,
+// each with its own softmax warpgroup (warps 2-5 and 6-9, one warp per TMEM
+// lane quarter each), its own S (TMEM columns 128g) and O (256 + 128g)
+// accumulators and its own P buffer in shared memory. Each K/V tile is
+// loaded once and used by both query tiles; K and V share one 3-stage ring,
+// loaded in the order the MMA thread consumes them (K0, K1, V0, K2, V1, ...).
+// The MMA thread issues S0(j+1), S1(j+1) as soon as the warpgroups have read
+// S(j) into registers, then PV0(j), PV1(j) once P(j) is written, so the
+// tensor core computes the next scores while both warpgroups exponentiate.
+// A quarter of the exponentials are evaluated on the FMA pipe (cubic minimax
+// polynomial for 2^f on [0,1), relative error 7.5e-5, exponent added as an
+// integer), which relieves the 16/clk/SM exp2 unit.
+constexpr int NQ = 2;
+constexpr int UNIT_ROWS = NQ * BQ;
+constexpr int KV_STAGES = 3;
+constexpr int THREADS2 = 64 + NQ * 128;
+// One pair of exponentials in kPolyPairs is evaluated by exp2_poly on the
+// FMA pipe instead of the exp2 unit (0: none).
+constexpr int kPolyPairs = 0;
+
+struct Smem2 {
+  uint8_t q[NQ][TILE_BYTES];
+  uint8_t kv[KV_STAGES][TILE_BYTES];
+  uint8_t p[NQ][TILE_BYTES];
+  uint64_t q_full, q_empty;
+  uint64_t kv_full[KV_STAGES], kv_empty[KV_STAGES];
+  uint64_t s_full[NQ], s_free[NQ];
+  uint64_t p_full[NQ], p_free[NQ];
+  uint64_t o_full[NQ], o_empty[NQ];
+  uint64_t drain;
+  uint32_t tmem_slot;
+  int abort_flag;
+};
+constexpr size_t SMEM2_BYTES = sizeof(Smem2) + 1024;
+static_assert(SMEM2_BYTES <= 232448, "two-tile MSM exceeds the opt-in shared memory per block");
+
+// 2^x for x in [-inf, 16]: x = k + f with k = floor(x) (obtained with a
+// round-down add of 1.5 * 2^23, which leaves k in the low mantissa bits), 2^f
+// from a degree-3 minimax polynomial fitted here for relative error on
+// [0, 1] (max 7.5e-5), and k added to the exponent field. Inputs below -126
+// are clamped (2^-126 ~ 0 for a softmax numerator).
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float magic = 12582912.0f;  // 1.5 * 2^23
+  const float t = __fadd_rd(x, magic);
+  const float k = __fsub_rn(t, magic);
+  const float f = __fsub_rn(x, k);
+  float p = fmaf(0.07802452f, f, 0.22606716f);
+  p = fmaf(p, f, 0.69583356f);
+  p = fmaf(p, f, 0.99992520f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// Packed two-lane f32 arithmetic (sm_100 f32x2 instructions): one issue slot
+// computes two softmax elements with the same per-lane rounding as the
+// scalar fma/add.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+__global__ void __launch_bounds__(THREADS2, 1)
+    msm_tc2_bf16_kernel(const __grid_constant__ CUtensorMap tq,
+                        const __grid_constant__ CUtensorMap tk,
+                        const __grid_constant__ CUtensorMap tv, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem2 &sm = *reinterpret_cast<Smem2 *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  volatile int *abort_flag = &sm.abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    mbar_init(&sm.q_empty, 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(&sm.kv_full[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
+    }
+    for (int g = 0; g < NQ; ++g) {
+      mbar_init(&sm.s_full[g], 1);
+      mbar_init(&sm.s_free[g], 128);
+      mbar_init(&sm.p_full[g], 128);
+      mbar_init(&sm.p_free[g], 1);
+      mbar_init(&sm.o_full[g], 1);
+      mbar_init(&sm.o_empty[g], 128);
+    }
+    mbar_init(&sm.drain, 1);
+    sm.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_slot;
+  const int64_t nkv = p.nkv_tiles;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      uint32_t kvc = 0, uc = 0;
+      bool ok = true;
+      auto load_tile = [&](const CUtensorMap *map, int32_t key0, int32_t h, int32_t b) -> bool {
+        const int s = kvc % KV_STAGES;
+        if (!mbar_wait(&sm.kv_empty[s], ((kvc / KV_STAGES) & 1) ^ 1, abort_flag, p.status,
+                       kErrTimeoutEmpty))
+          return false;
+        mbar_arrive_expect_tx(&sm.kv_full[s], TILE_BYTES);
+        tma_load_4d(sm.kv[s], map, &sm.kv_full[s], 0, key0, h, b);
+        tma_load_4d(sm.kv[s] + CHUNK_BYTES, map, &sm.kv_full[s], 64, key0, h, b);
+        ++kvc;
+        return true;
+      };
+      for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uc) {
+        int32_t b, h, q0;
+        unit_coords(p, u, b, h, q0);
+        q0 = static_cast<int32_t>((u % p.qblocks) * UNIT_ROWS);
+        if (!mbar_wait(&sm.q_empty, (uc & 1) ^ 1, abort_flag, p.status, kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&sm.q_full, NQ * TILE_BYTES);
+        for (int g = 0; g < NQ; ++g) {
+          tma_load_4d(sm.q[g], &tq, &sm.q_full, 0, q0 + g * BQ, h, b);
+          tma_load_4d(sm.q[g] + CHUNK_BYTES, &tq, &sm.q_full, 64, q0 + g * BQ, h, b);
+        }
+        if (!(ok = load_tile(&tk, 0, h, b))) break;
+        for (int64_t t = 0; t < nkv && ok; ++t) {
+          if (t + 1 < nkv && !(ok = load_tile(&tk, static_cast<int32_t>((t + 1) * BKV), h, b)))
+            break;
+          ok = load_tile(&tv, static_cast<int32_t>(t * BKV), h, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc_s = make_idesc(1, 1, 0, 0, BQ, BKV);
+      const uint32_t idesc_o = make_idesc(1, 1, 0, 1, BQ, D);
+      uint32_t kvc = 0, s_cnt = 0, p_cnt = 0, uc = 0;
+      bool ok = true;
+      auto kv_stage = [&](uint32_t &addr) -> int {
+        const int s = kvc % KV_STAGES;
+        if (!mbar_wait(&sm.kv_full[s], (kvc / KV_STAGES) & 1, abort_flag, p.status,
+                       kErrTimeoutFull))
+          return -1;
+        addr = smem_u32(sm.kv[s]);
+        return s;
+      };
+      auto s_round = [&]() -> bool {  // S_g = Q_g K^T for both query tiles
+        uint32_t k_addr;
+        const int s = kv_stage(k_addr);
+        if (s < 0) return false;
+        for (int g = 0; g < NQ; ++g) {
+          if (!mbar_wait(&sm.s_free[g], (s_cnt & 1) ^ 1, abort_flag, p.status, kErrTimeoutAccum))
+            return false;
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(sm.q[g]);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            mma_f16_ss(tmem + S_COL0 + g * BKV, kmajor_desc(q_addr, kk), kmajor_desc(k_addr, kk),
+                       idesc_s, kk ? 1u : 0u);
+          mma_commit(&sm.s_full[g]);
+        }
+        mma_commit(&sm.kv_empty[s]);
+        ++kvc;
+        ++s_cnt;
+        return true;
+      };
+      auto pv_round = [&](int64_t t) -> bool {  // O_g += P_g V for both query tiles
+        uint32_t v_addr;
+        const int s = kv_stage(v_addr);
+        if (s < 0) return false;
+        for (int g = 0; g < NQ; ++g) {
+          if (t == 0 &&
+              !mbar_wait(&sm.o_empty[g], (uc & 1) ^ 1, abort_flag, p.status, kErrTimeoutAccum))
+            return false;
+          if (!mbar_wait(&sm.p_full[g], p_cnt & 1, abort_flag, p.status, kErrTimeoutAccum))
+            return false;
+          tc_fence_after();
+          const uint32_t p_addr = smem_u32(sm.p[g]);
+#pragma unroll
+          for (int kk = 0; kk < BKV / 16; ++kk)
+            mma_f16_ss(tmem + O_COL + g * D, kmajor_desc(p_addr, kk), mnmajor_desc(v_addr, kk),
+                       idesc_o, (t | kk) ? 1u : 0u);
+          mma_commit(&sm.p_free[g]);
+        }
+        mma_commit(&sm.kv_empty[s]);
+        ++kvc;
+        ++p_cnt;
+        return true;
+      };
+      for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uc) {
+        if (!mbar_wait(&sm.q_full, uc & 1, abort_flag, p.status, kErrTimeoutFull)) break;
+        tc_fence_after();
+        if (!(ok = s_round())) break;
+        for (int64_t t = 0; t < nkv; ++t) {
+          if (t + 1 < nkv) {
+            if (!(ok = s_round())) break;
+          } else {
+            mma_commit(&sm.q_empty);  // every S MMA of this unit has been issued
+          }
+          if (!(ok = pv_round(t))) break;
+        }
+        if (!ok) break;
+        for (int g = 0; g < NQ; ++g) mma_commit(&sm.o_full[g]);
+      }
+      mma_commit(&sm.drain);
+      if (!mbar_wait(&sm.drain, 0, nullptr, p.status, kErrTimeoutDrain)) *abort_flag = 1;
+    }
+  } else {
+    // ---------------- softmax + output (warpgroup g owns query tile g) ----------------
+    const int g = (warp - 2) >> 2;
+    const int sub = warp & 3;
+    const int row = sub * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(sub * 32) << 16);
+    const uint32_t s_col = S_COL0 + g * BKV, o_col = O_COL + g * D;
+    uint8_t *p_row = sm.p[g] + row * 128;
+    const int rsw = row & 7;
+    uint32_t s_cnt = 0, p_cnt = 0, uc = 0;
+    bool ok = true;
+    for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uc) {
+      int32_t b, h, q0;
+      unit_coords(p, u, b, h, q0);
+      q0 = static_cast<int32_t>((u % p.qblocks) * UNIT_ROWS + g * BQ);
+      float m_ref = -INFINITY, l = 0.0f;
+      for (int64_t t = 0; t < nkv; ++t) {
+        if (!(ok = mbar_wait_warp(&sm.s_full[g], s_cnt & 1, abort_flag, p.status,
+                                  kErrTimeoutAccum)))
+          break;
+        tc_fence_after();
+        uint32_t s[128];
+        {
+          uint32_t (&s0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[0]);
+          uint32_t (&s1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[32]);
+          uint32_t (&s2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[64]);
+          uint32_t (&s3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&s[96]);
+          const uint32_t a = lane_base + s_col;
+          tmem_ld_32x32b_x32(a, s0);
+          tmem_ld_32x32b_x32(a + 32, s1);
+          tmem_ld_32x32b_x32(a + 64, s2);
+          tmem_ld_32x32b_x32(a + 96, s3);
+          tmem_ld_wait();
+          reg_fence(s0);
+          reg_fence(s1);
+          reg_fence(s2);
+          reg_fence(s3);
+        }
+        tc_fence_before();
+        mbar_arrive(&sm.s_free[g]);
+        ++s_cnt;
+        // Row max: four chains of three-input max, two scores per step.
+        float m4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) m4[i] = __uint_as_float(s[i]);
+#pragma unroll
+        for (int i = 4; i < 128; i += 8)
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            m4[j] = fmax3(m4[j], __uint_as_float(s[i + 2 * j]), __uint_as_float(s[i + 2 * j + 1]));
+        const float mx = fmax3(m4[0], m4[1], fmaxf(m4[2], m4[3]));
+        bool need = false;
+        if (t == 0) {
+          m_ref = mx;
+        } else if ((mx - m_ref) * p.c > 8.0f) {
+          need = true;
+        }
+        if (__any_sync(0xffffffffu, need)) {
+          // Rescale O and l for the rows whose max grew: O must be complete
+          // up to PV_{t-1} and PV_t cannot start before this thread signals.
+          if (!(ok = mbar_wait_warp(&sm.p_free[g], (p_cnt - 1) & 1, abort_flag, p.status,
+                                    kErrTimeoutAccum)))
+            break;
+          tc_fence_after();
+          const float f = need ? ex2((m_ref - mx) * p.c) : 1.0f;
+          // 16 columns at a time: the 128 scores stay live across this loop.
+#pragma unroll 1
+          for (int c0 = 0; c0 < D; c0 += 16) {
+            uint32_t o[16];
+            tmem_ld16_sync(lane_base + o_col + c0, o);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            tmem_st_32x32b_x16(lane_base + o_col + c0, o);
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          if (need) {
+            l *= f;
+            m_ref = mx;
+          }
+        }
+        const float mc = m_ref * p.c;
+        const uint64_t c2 = f2_pack(p.c, p.c), nmc2 = f2_pack(-mc, -mc);
+        uint32_t pk[64];
+        uint64_t ps[4] = {0, 0, 0, 0};  // +0.0f pairs
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), c2,
+                           nmc2),
+                    x0, x1);
+          float e0, e1;
+          if (kPolyPairs && (i % kPolyPairs) == kPolyPairs - 1) {
+            e0 = exp2_poly(x0);
+            e1 = exp2_poly(x1);
+          } else {
+            e0 = ex2(x0);
+            e1 = ex2(x1);
+          }
+          ps[i & 3] = f2_add(ps[i & 3], f2_pack(e0, e1));
+          pk[i] = pack_bf16x2(e0, e1);
+        }
+        {
+          float a0, a1;
+          f2_unpack(f2_add(f2_add(ps[0], ps[1]), f2_add(ps[2], ps[3])), a0, a1);
+          l += a0 + a1;
+        }
+        // P_g is free once PV_g of the previous tile has completed.
+        if (!(ok = mbar_wait_warp(&sm.p_free[g], (p_cnt & 1) ^ 1, abort_flag, p.status,
+                                  kErrTimeoutAccum)))
+          break;
+#pragma unroll
+        for (int u16 = 0; u16 < 16; ++u16) {
+          const int chunk = u16 >> 3, j = u16 & 7;
+          uint4 v4 = make_uint4(pk[u16 * 4], pk[u16 * 4 + 1], pk[u16 * 4 + 2], pk[u16 * 4 + 3]);
+          *reinterpret_cast<uint4 *>(p_row + chunk * CHUNK_BYTES + ((j ^ rsw) << 4)) = v4;
+        }
+        fence_async_smem();
+        mbar_arrive(&sm.p_full[g]);
+        ++p_cnt;
+      }
+      if (!ok) break;
+      // ---- output: O_g / l -> bf16 ----
+      if (!(ok = mbar_wait_warp(&sm.o_full[g], uc & 1, abort_flag, p.status, kErrTimeoutAccum)))
+        break;
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      __nv_bfloat16 *orow =
+          p.o + b * p.o_s[0] + h * p.o_s[1] + static_cast<int64_t>(q0 + row) * p.o_s[2];
+#pragma unroll 1
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t o[32];
+        tmem_ld32_sync(lane_base + o_col + c0, o);
+        uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(o[q * 8 + 0]) * inv, __uint_as_float(o[q * 8 + 1]) * inv);
+          w.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv, __uint_as_float(o[q * 8 + 3]) * inv);
+          w.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv, __uint_as_float(o[q * 8 + 5]) * inv);
+          w.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv, __uint_as_float(o[q * 8 + 7]) * inv);
+          dst[q] = w;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sm.o_empty[g]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
 }  // namespace
 
 bool encode_tmap_4d_bf16(CUtensorMap *map, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
@@ -408,27 +802,36 @@ cudaError_t launch_msm_tc_bf16(const void *q, const void *k, const void *v, void
   // cudaErrorNotSupported (nothing launched) lets the caller take another kernel.
   if (!enc(&tq, q, s.m, s.q_s) || !enc(&tk, k, s.n, s.k_s) || !enc(&tv, v, s.n, s.v_s))
     return cudaErrorNotSupported;
+  // Query blocks of 256 rows run two tiles per CTA; otherwise one.
+  const bool two = s.m % UNIT_ROWS == 0;
   Params p;
   p.heads = s.heads;
-  p.qblocks = s.m / BQ;
+  p.qblocks = s.m / (two ? UNIT_ROWS : BQ);
   p.nkv_tiles = s.n / BKV;
   p.units = s.batch * s.heads * p.qblocks;
   for (int i = 0; i < 3; ++i) p.o_s[i] = s.o_s[i];
   p.c = scale * 1.4426950408889634f;
   p.o = static_cast<__nv_bfloat16 *>(o);
   p.status = status;
-  cudaError_t e = cudaFuncSetAttribute(msm_tc_bf16_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(SMEM_BYTES));
-  if (e != cudaSuccess) return e;
-  const int grid = static_cast<int>(p.units < sms ? p.units : sms);
-  msm_tc_bf16_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  cudaError_t e;
+  int grid = static_cast<int>(p.units < sms ? p.units : sms);
+  if (two) {
+    e = cudaFuncSetAttribute(msm_tc2_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(SMEM2_BYTES));
+    if (e != cudaSuccess) return e;
+    msm_tc2_bf16_kernel<<<grid, THREADS2, SMEM2_BYTES, stream>>>(tq, tk, tv, p);
+  } else {
+    e = cudaFuncSetAttribute(msm_tc_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    msm_tc_bf16_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
+  }
   if (info) {
     info->launches = 1;
-    info->tile_m = BQ;
+    info->tile_m = two ? UNIT_ROWS : BQ;
     info->tile_n = BKV;
     info->tile_k = D;
-    info->stages = KSTAGES;
+    info->stages = two ? KV_STAGES : KSTAGES;
     info->ctas = grid;
     info->set_route("tcgen05_bf16_msm");
   }

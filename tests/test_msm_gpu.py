@@ -59,6 +59,8 @@ def _check_msm(mcb, orc, pairs, scale, route, pairs_to_check=None):
     (qh, qf), (kh, kf), (vh, vf) = pairs
     o = mcb.msm(gu.to_dev_bf16(qh), gu.to_dev_bf16(kh), gu.to_dev_bf16(vh), scale)
     assert mcb.api.last_result.route == route
+    if route == "tcgen05_bf16_msm":  # 256-row query blocks run two tiles per CTA
+        assert mcb.api.last_result.tile[0] == (256 if qh.shape[2] % 256 == 0 else 128)
     assert o.dtype == torch.bfloat16
     got = gu.from_dev(o)
     b, h = qh.shape[:2]
@@ -72,6 +74,7 @@ def _check_msm(mcb, orc, pairs, scale, route, pairs_to_check=None):
     ((1, 2, 256, 128), "tcgen05_bf16_msm"),
     ((2, 3, 384, 128), "tcgen05_bf16_msm"),
     ((1, 1, 128, 128), "tcgen05_bf16_msm"),
+    ((3, 5, 768, 128), "tcgen05_bf16_msm"),
     ((1, 1, 200, 128), "simt_online_softmax_msm"),
     ((2, 2, 128, 64), "simt_online_softmax_msm"),
 ])
