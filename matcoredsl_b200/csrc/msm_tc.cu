@@ -716,7 +716,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
                            nmc2),
                     x0, x1);
           float e0, e1;
-          if (kPolyPairs && (i % kPolyPairs) == kPolyPairs - 1) {
+          if (kPolyPairs > 0 && (i % (kPolyPairs > 0 ? kPolyPairs : 1)) == kPolyPairs - 1) {
             e0 = exp2_poly(x0);
             e1 = exp2_poly(x1);
           } else {
