@@ -176,9 +176,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int sa_row = mt;                                       // M block (BM == block)
       const int sb_row = nt * 2 + (grp * COLS_PER_WARP) / 128;     // N block of these columns
       const bool cols_live = col0 < p.n;
-      float acc[COLS_PER_WARP];
+      uint64_t acc2[COLS_PER_WARP / 2];  // f32 accumulator pairs (packed f32x2 FMAs)
 #pragma unroll
-      for (int i = 0; i < COLS_PER_WARP; ++i) acc[i] = 0.0f;
+      for (int i = 0; i < COLS_PER_WARP / 2; ++i) acc2[i] = 0;
       bool ok = true;
       for (int kb = 0; kb < p.num_kb; ++kb, ++kc) {
         const int buf = kc & 1;
@@ -188,17 +188,23 @@ __global__ void __launch_bounds__(THREADS, 1)
                                   kErrTimeoutAccum)))
           break;
         tc_fence_after();
+        const uint64_t s2 = f2_pack(s, s);
 #pragma unroll
         for (int c = 0; c < COLS_PER_WARP / 16; ++c) {
-          uint32_t r[16];  // 16-column loads keep 64 acc + 16 live within 96 registers
+          uint32_t r[16];  // 16-column loads: the 128 accumulators + 16 stay in registers
           tmem_ld16_sync(lane_base + buf * BN + c * 16, r);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc[c * 16 + i] = fmaf(s, __uint_as_float(r[i]), acc[c * 16 + i]);
+          for (int i = 0; i < 8; ++i)
+            acc2[c * 8 + i] = f2_fma(s2, f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
+                                     acc2[c * 8 + i]);
         }
         tc_fence_before();
         mbar_arrive(&pempty[buf]);
       }
       if (!ok) break;
+      float acc[COLS_PER_WARP];
+#pragma unroll
+      for (int i = 0; i < COLS_PER_WARP / 2; ++i) f2_unpack(acc2[i], acc[2 * i], acc[2 * i + 1]);
       if (row < p.m && cols_live) {
         const bool full_cols = col0 + COLS_PER_WARP <= p.n;
         if (p.c_bf16) {
