@@ -111,6 +111,167 @@ __global__ void __launch_bounds__(256) strict_pair_kernel(
   }
 }
 
+// ---- staged fused pair (operands through shared memory) -------------------------
+// Same arithmetic as strict_pair_kernel (one thread per output column, R
+// independent row chains, increasing k, separate multiply and add, C rounded
+// to binary32 in shared memory), but B, the A rows and then D are streamed
+// through a double-buffered shared-memory ring of KC-row chunks with 16-byte
+// cp.async copies: the whole CTA issues the copies of chunk c+1 before it
+// reduces chunk c, so a global round trip is paid once per chunk instead of
+// once per 16 reduction steps per thread. Used when every row is 16-byte
+// aligned and N, P <= 1024 (one column per thread).
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Bulk prefetch of [ptr, ptr + bytes) into L2 (16-byte granules, whole
+// granules only: the range is shrunk to 16-byte boundaries).
+__device__ __forceinline__ void prefetch_l2_range(const void *ptr, int64_t bytes) {
+  uintptr_t lo = (reinterpret_cast<uintptr_t>(ptr) + 15) & ~static_cast<uintptr_t>(15);
+  const uintptr_t hi = (reinterpret_cast<uintptr_t>(ptr) + bytes) & ~static_cast<uintptr_t>(15);
+  while (lo < hi) {
+    const uint32_t chunk = static_cast<uint32_t>(hi - lo > (1u << 20) ? (1u << 20) : hi - lo);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"(chunk) : "memory");
+    lo += chunk;
+  }
+}
+// This CTA's 1/gridDim.x share of [ptr, ptr + bytes).
+__device__ __forceinline__ void prefetch_l2_share(const void *ptr, int64_t bytes) {
+  const int64_t share = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~static_cast<int64_t>(15);
+  const int64_t off = share * blockIdx.x;
+  if (off < bytes)
+    prefetch_l2_range(static_cast<const char *>(ptr) + off, bytes - off < share ? bytes - off : share);
+}
+
+struct StagedShape {
+  int kc;           // rows per chunk
+  int wmax;         // max(n, p) rounded up to 4: row pitch of a chunk in floats
+};
+
+template <int R>
+__global__ void __launch_bounds__(1024) strict_pair_staged_kernel(
+    const float *__restrict__ a, const float *__restrict__ b, const float *__restrict__ d,
+    float *__restrict__ e, int64_t m, int64_t k, int64_t n, int64_t p, int64_t lda,
+    int64_t ldb, int64_t ldd, int64_t lde, StagedShape sh) {
+  extern __shared__ __align__(16) float smem_f[];
+  const int kc = sh.kc, pitch = sh.wmax;
+  float *ring = smem_f;                              // [2][kc][pitch]
+  float *a_s = ring + 2 * kc * pitch;                // [2][R][kc]
+  float *panel = a_s + 2 * R * kc;                   // [R][n]
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * R;
+  if (r0 >= m) return;
+  const int rows = static_cast<int>(m - r0 < R ? m - r0 : R);
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  if (tid == 0) {
+    // Every CTA streams all of B and D: pull this CTA's share of both spans
+    // (and its own A rows) into L2 up front, so the chunk copies below hit L2
+    // instead of paying a DRAM round trip each.
+    prefetch_l2_share(b, ((k - 1) * ldb + n) * 4);
+    prefetch_l2_share(d, ((n - 1) * ldd + p) * 4);
+    prefetch_l2_range(a + r0 * lda, ((rows - 1) * lda + k) * 4);
+  }
+
+  // Copies chunk c of a [K x W] row-major operand (rows of W floats at stride
+  // ld) into ring buffer `buf`, plus (phase 1) the matching A columns.
+  auto stage = [&](const float *src, int64_t ld, int64_t w, int64_t ktot, int64_t c, int buf,
+                   bool with_a) {
+    const int64_t h0 = c * kc;
+    const int nr = static_cast<int>(ktot - h0 < kc ? ktot - h0 : kc);
+    const int v4 = static_cast<int>(w >> 2);
+    float *dst = ring + buf * kc * pitch;
+    for (int i = tid; i < nr * v4; i += nthr) {
+      const int rr = i / v4, cc = (i - rr * v4) * 4;
+      cp_async16(dst + rr * pitch + cc, src + (h0 + rr) * ld + cc);
+    }
+    if (with_a) {
+      const int av4 = nr >> 2;
+      float *ad = a_s + buf * R * kc;
+      for (int i = tid; i < rows * av4; i += nthr) {
+        const int rr = i / av4, cc = (i - rr * av4) * 4;
+        cp_async16(ad + rr * kc + cc, a + (r0 + rr) * lda + h0 + cc);
+      }
+    }
+    cp_async_commit();
+  };
+
+  // Phase 1: C[r, j] = sum_h A[r0+r, h] * B[h, j]
+  {
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+    const int64_t nch = (k + kc - 1) / kc;
+    if (nch > 0) stage(b, ldb, n, k, 0, 0, true);
+    for (int64_t c = 0; c < nch; ++c) {
+      const int buf = static_cast<int>(c & 1);
+      if (c + 1 < nch) {
+        stage(b, ldb, n, k, c + 1, buf ^ 1, true);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncthreads();
+      const int nr = static_cast<int>(k - c * kc < kc ? k - c * kc : kc);
+      if (tid < n) {
+        const float *bs = ring + buf * kc * pitch + tid;
+        const float *as = a_s + buf * R * kc;
+        for (int h = 0; h < nr; ++h) {
+          const float bv = bs[h * pitch];
+#pragma unroll
+          for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(as[r * kc + h], bv));
+        }
+      }
+      __syncthreads();  // buffer `buf` is refilled by the next iteration's copies
+    }
+    if (tid < n) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) panel[r * n + tid] = acc[r];
+    }
+    __syncthreads();
+  }
+  // Phase 2: E[r0+r, q] = sum_j C[r, j] * D[j, q]
+  {
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+    const int64_t nch = (n + kc - 1) / kc;
+    stage(d, ldd, p, n, 0, 0, false);
+    for (int64_t c = 0; c < nch; ++c) {
+      const int buf = static_cast<int>(c & 1);
+      if (c + 1 < nch) {
+        stage(d, ldd, p, n, c + 1, buf ^ 1, false);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncthreads();
+      const int nr = static_cast<int>(n - c * kc < kc ? n - c * kc : kc);
+      if (tid < p) {
+        const float *ds = ring + buf * kc * pitch + tid;
+        const float *cs = panel + c * kc;
+        for (int h = 0; h < nr; ++h) {
+          const float dv = ds[h * pitch];
+#pragma unroll
+          for (int r = 0; r < R; ++r) acc[r] = __fadd_rn(acc[r], __fmul_rn(cs[r * n + h], dv));
+        }
+      }
+      __syncthreads();
+    }
+    if (tid < p) {
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        if (r < rows) e[(r0 + r) * lde + tid] = acc[r];
+    }
+  }
+}
+
 __global__ void fill_zero_kernel(float *__restrict__ y, int64_t rows, int64_t cols, int64_t ld) {
   const int64_t total = rows * cols;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -174,6 +335,59 @@ cudaError_t launch_strict_pair(const float *a, const float *b, const float *d, f
     return cudaGetLastError();
   }
   const int R = pick_rows(m, sms);
+  // Staged kernel: 16-byte aligned rows, one column per thread.
+  const auto al16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+  if (k > 0 && n <= 1024 && p <= 1024 && n % 4 == 0 && p % 4 == 0 && k % 4 == 0 &&
+      lda % 4 == 0 && ldb % 4 == 0 && ldd % 4 == 0 && al16(a) && al16(b) && al16(d)) {
+    StagedShape sh;
+    sh.wmax = static_cast<int>(n > p ? n : p);
+    const int64_t fixed = static_cast<int64_t>(R) * n * 4;
+    // Largest chunk (32 or 16 rows) whose two buffers fit; two CTAs per SM
+    // when the whole footprint stays under ~110 KB.
+    sh.kc = 32;
+    auto bytes = [&](int kc) { return (2LL * kc * sh.wmax + 2LL * R * kc) * 4 + fixed; };
+    if (bytes(32) > 110 * 1024) sh.kc = 16;
+    const int64_t smem = bytes(sh.kc);
+    if (smem <= smem_limit_bytes) {
+      const int threads = static_cast<int>(((sh.wmax + 31) / 32) * 32);
+      const int64_t ctas = (m + R - 1) / R;
+      if (ctas > 0x7fffffff) return cudaErrorInvalidConfiguration;
+      cudaError_t err = cudaSuccess;
+      switch (R) {
+        case 4:
+          err = cudaFuncSetAttribute(strict_pair_staged_kernel<4>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+          if (err == cudaSuccess)
+            strict_pair_staged_kernel<4><<<(unsigned)ctas, threads, smem, stream>>>(
+                a, b, d, e, m, k, n, p, lda, ldb, ldd, lde, sh);
+          break;
+        case 2:
+          err = cudaFuncSetAttribute(strict_pair_staged_kernel<2>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+          if (err == cudaSuccess)
+            strict_pair_staged_kernel<2><<<(unsigned)ctas, threads, smem, stream>>>(
+                a, b, d, e, m, k, n, p, lda, ldb, ldd, lde, sh);
+          break;
+        default:
+          err = cudaFuncSetAttribute(strict_pair_staged_kernel<1>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+          if (err == cudaSuccess)
+            strict_pair_staged_kernel<1><<<(unsigned)ctas, threads, smem, stream>>>(
+                a, b, d, e, m, k, n, p, lda, ldb, ldd, lde, sh);
+          break;
+      }
+      if (err != cudaSuccess) return err;
+      if (info) {
+        info->launches = 1;
+        info->tile_m = R;
+        info->tile_n = threads;
+        info->tile_k = sh.kc;
+        info->ctas = static_cast<int>(ctas);
+        info->set_route("strict_f32_simt_pair_staged");
+      }
+      return cudaGetLastError();
+    }
+  }
   const int64_t panel_bytes = static_cast<int64_t>(R) * n * 4;
   const bool in_smem = panel_bytes <= smem_limit_bytes;
   if (!in_smem && scratch == nullptr) return cudaErrorInvalidValue;

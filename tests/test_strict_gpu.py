@@ -91,3 +91,29 @@ def test_strided_device_operands(mcb, orc):
     te = mcb.strict_fused_pair(ta, torch.from_numpy(b).cuda(), torch.from_numpy(d).cuda())
     torch.cuda.synchronize()
     assert rc.same_bits(te.cpu().numpy(), orc.strict_fused_pair(a, b, d))
+
+
+@pytest.mark.parametrize("m,k,n,p", [(512, 256, 384, 128), (301, 68, 100, 12), (9, 8, 12, 8),
+                                     (600, 512, 1024, 1024), (5, 4, 4, 1024)])
+def test_staged_route_bit_exact(mcb, orc, m, k, n, p):
+    """16-byte aligned operands with N, P <= 1024 take the shared-memory staged
+    kernel: tail panels (M % R), a short last K chunk, 16- and 32-row chunks."""
+    rng = np.random.default_rng(m + k + n + p)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    d = rng.uniform(-1, 1, (n, p)).astype(np.float32)
+    got = mcb.strict_fused_pair(a, b, d)
+    assert mcb.api.last_result.route == "strict_f32_simt_pair_staged"
+    assert rc.same_bits(got, orc.strict_fused_pair(a, b, d))
+
+
+def test_staged_route_ieee_specials(mcb, orc):
+    """Signed zeros, subnormals, infinities and NaNs through the staged kernel."""
+    rng = np.random.default_rng(99)
+    pool = np.array([0.0, -0.0, 1e-40, -3e-39, np.inf, -np.inf, np.nan, 1.5, -2.25, 3e38,
+                     -1e-45, 0.1], np.float32)
+    a, b, d = (rng.choice(pool, size=sh).astype(np.float32)
+               for sh in ((9, 8), (8, 12), (12, 8)))
+    got = mcb.strict_fused_pair(a, b, d)
+    assert mcb.api.last_result.route == "strict_f32_simt_pair_staged"
+    assert rc.same_bits(got, orc.strict_fused_pair(a, b, d))
