@@ -93,6 +93,9 @@ using mcb::LaunchInfo;
 
 constexpr int kMaxDevices = 64;
 constexpr int kStageSlots = 8;
+// Strict pairs with at least this many intermediate elements (M*N) run as two
+// tiled GEMMs; smaller ones as one fused kernel (launch-bound either way).
+constexpr int64_t kStrictTwoPassMinElems = 16384;
 
 // Lazily created per-device state: SM count, the device status word and the
 // grow-only staging buffers used for host-resident operands.
@@ -613,6 +616,40 @@ mcb_status strict_pair_impl(const mcb_tensor *e, const mcb_tensor *a, const mcb_
   if ((s = call.device_ptr(a, true, &da)) || (s = call.device_ptr(b, true, &db)) ||
       (s = call.device_ptr(d, true, &dd)) || (s = call.device_ptr(e, false, &de)))
     return s;
+  // Two tiled strict GEMMs through a binary32 C [M,N] in device memory: the
+  // caller's workspace when it holds C, else a stream-ordered allocation
+  // (cudaMallocAsync / cudaFreeAsync on the call's stream, so the call stays
+  // asynchronous). Small problems, and any allocation failure, take the
+  // single fused kernel below.
+  if (m > 0 && n > 0 && p > 0 && m * n >= kStrictTwoPassMinElems) {
+    const uint64_t cbytes = static_cast<uint64_t>(m) * static_cast<uint64_t>(n) * 4;
+    void *cbuf = nullptr;
+    bool owned = false;
+    if (exec && exec->workspace && exec->workspace_bytes >= cbytes &&
+        (reinterpret_cast<uintptr_t>(exec->workspace) & 15u) == 0) {
+      cbuf = exec->workspace;
+    } else if (cudaMallocAsync(&cbuf, cbytes, call.stream()) == cudaSuccess) {
+      owned = true;
+    } else {
+      (void)cudaGetLastError();
+      cbuf = nullptr;
+    }
+    if (cbuf) {
+      LaunchInfo info;
+      call.mark_compute_start();
+      cudaError_t err = mcb::launch_strict_pair_two_pass(
+          static_cast<const float *>(da), static_cast<const float *>(db),
+          static_cast<const float *>(dd), static_cast<float *>(de), static_cast<float *>(cbuf),
+          m, k, n, p, k ? a->strides[0] : 0, b->strides[0], d->strides[0], e->strides[0],
+          call.sms(), call.stream(), &info);
+      if (owned) {
+        const cudaError_t fe = cudaFreeAsync(cbuf, call.stream());
+        if (err == cudaSuccess) err = fe;
+      }
+      call.mark_compute_end();
+      return call.finish(e, de, info, err);
+    }
+  }
   // The intermediate panel lives in shared memory when it fits; otherwise it
   // needs scratch, taken from the caller's workspace or a staging slot.
   const int smem_limit = call.ctx()->smem_optin;

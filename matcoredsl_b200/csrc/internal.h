@@ -23,6 +23,12 @@ struct LaunchInfo {
 cudaError_t launch_strict_gemm(const float *a, const float *b, float *c, int64_t m, int64_t k,
                                int64_t n, int64_t lda, int64_t ldb, int64_t ldc, int sms,
                                cudaStream_t stream, LaunchInfo *info);
+// Fused pair as two tiled strict GEMMs through a binary32 intermediate
+// C_buf [M,N] (row stride N, 16-byte aligned): C = A B, then E = C D.
+cudaError_t launch_strict_pair_two_pass(const float *a, const float *b, const float *d, float *e,
+                                        float *c_buf, int64_t m, int64_t k, int64_t n, int64_t p,
+                                        int64_t lda, int64_t ldb, int64_t ldd, int64_t lde,
+                                        int sms, cudaStream_t stream, LaunchInfo *info);
 // Floats of global scratch the fused pair needs (0 when the panel fits in
 // shared memory).
 int64_t strict_pair_scratch_floats(int64_t m, int64_t n, int sms, int smem_limit_bytes);

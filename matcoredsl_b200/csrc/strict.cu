@@ -55,25 +55,6 @@ __device__ __forceinline__ void strict_rows(const float *__restrict__ a, int64_t
   }
 }
 
-template <int R>
-__global__ void __launch_bounds__(256) strict_gemm_kernel(const float *__restrict__ a,
-                                                          const float *__restrict__ b,
-                                                          float *__restrict__ c, int64_t m,
-                                                          int64_t k, int64_t n, int64_t lda,
-                                                          int64_t ldb, int64_t ldc) {
-  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * R;
-  const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (j >= n) return;
-  float acc[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) acc[r] = 0.0f;
-  const int rows = static_cast<int>(m - r0 < R ? m - r0 : R);
-  strict_rows<R, true>(a + r0 * lda, lda, b + j, ldb, k, rows, acc);
-#pragma unroll
-  for (int r = 0; r < R; ++r)
-    if (r < rows) c[(r0 + r) * ldc + j] = acc[r];
-}
-
 // One CTA per panel of R rows. Phase 1 writes the panel C[R, N] (binary32) to
 // `panel` (shared memory when it fits, else this CTA's slice of a global
 // scratch buffer); phase 2 reduces it against D.
@@ -272,6 +253,150 @@ __global__ void __launch_bounds__(1024) strict_pair_staged_kernel(
   }
 }
 
+// ---- tiled strict GEMM ------------------------------------------------------------
+// C[M,N] = A[M,K] B[K,N] with each output a strict chain (increasing k, +0
+// seed, separate binary32 multiply and add). A CTA computes a (TY*MR) x
+// (TX*NR) tile; each thread an MR x NR block of chains, so one pair of shared
+// memory reads feeds MR*NR multiply-adds. KC-deep slices of the A and B tiles
+// go through a 3-stage shared-memory ring with cp.async (16-byte copies when
+// every row is 16-byte aligned, 4-byte copies otherwise); two slices are in
+// flight while one is reduced. Out-of-range rows and columns are never
+// copied and their chains are never stored.
+constexpr int TKC = 32;       // k-slice depth
+constexpr int TAP = TKC + 4;  // padded A-tile row pitch (floats)
+constexpr int TST = 3;        // ring stages
+
+__device__ __forceinline__ void cp_async4(void *smem_dst, const void *gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
+               : "memory");
+}
+
+template <int MR, int NR, int TX, int TY, bool kVec>
+__global__ void __launch_bounds__(TX *TY) strict_tiled_kernel(
+    const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ c, int64_t m,
+    int64_t k, int64_t n, int64_t lda, int64_t ldb, int64_t ldc) {
+  constexpr int TM = TY * MR, TN = TX * NR, NT = TX * TY;
+  __shared__ __align__(16) float as[TST][TM][TAP];
+  __shared__ __align__(16) float bs[TST][TKC][TN];
+  const int tid = threadIdx.x, tx = tid % TX, ty = tid / TX;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.y) * TM;
+  const int64_t col0 = static_cast<int64_t>(blockIdx.x) * TN;
+  const int mrows = static_cast<int>(m - row0 < TM ? m - row0 : TM);
+  const int ncols = static_cast<int>(n - col0 < TN ? n - col0 : TN);
+
+  auto stage = [&](int64_t cidx, int buf) {
+    const int64_t h0 = cidx * TKC;
+    const int nr = static_cast<int>(k - h0 < TKC ? k - h0 : TKC);
+    if (kVec && nr == TKC && mrows == TM && ncols == TN) {  // full tile: constant divisors
+#pragma unroll
+      for (int i = tid; i < TM * (TKC / 4); i += NT) {
+        const int r = i / (TKC / 4), q = (i % (TKC / 4)) * 4;
+        cp_async16(&as[buf][r][q], a + (row0 + r) * lda + h0 + q);
+      }
+#pragma unroll
+      for (int i = tid; i < TKC * (TN / 4); i += NT) {
+        const int r = i / (TN / 4), q = (i % (TN / 4)) * 4;
+        cp_async16(&bs[buf][r][q], b + (h0 + r) * ldb + col0 + q);
+      }
+    } else if (kVec) {  // nr, ncols and every row start are multiples of 4 floats
+      const int av = nr >> 2, bv = ncols >> 2;
+      for (int i = tid; i < mrows * av; i += NT) {
+        const int r = i / av, q = (i - r * av) * 4;
+        cp_async16(&as[buf][r][q], a + (row0 + r) * lda + h0 + q);
+      }
+      for (int i = tid; i < nr * bv; i += NT) {
+        const int r = i / bv, q = (i - r * bv) * 4;
+        cp_async16(&bs[buf][r][q], b + (h0 + r) * ldb + col0 + q);
+      }
+    } else {
+      for (int i = tid; i < mrows * nr; i += NT) {
+        const int r = i / nr, q = i - r * nr;
+        cp_async4(&as[buf][r][q], a + (row0 + r) * lda + h0 + q);
+      }
+      for (int i = tid; i < nr * ncols; i += NT) {
+        const int r = i / ncols, q = i - r * ncols;
+        cp_async4(&bs[buf][r][q], b + (h0 + r) * ldb + col0 + q);
+      }
+    }
+    cp_async_commit();
+  };
+
+  float acc[MR][NR];
+#pragma unroll
+  for (int r = 0; r < MR; ++r)
+#pragma unroll
+    for (int j = 0; j < NR; ++j) acc[r][j] = 0.0f;
+  const int64_t nch = (k + TKC - 1) / TKC;
+#pragma unroll
+  for (int st = 0; st < TST - 1; ++st) {
+    if (st < nch)
+      stage(st, st);
+    else
+      cp_async_commit();  // empty group keeps the per-iteration accounting uniform
+  }
+  for (int64_t ci = 0; ci < nch; ++ci) {
+    const int buf = static_cast<int>(ci % TST);
+    cp_async_wait<TST - 2>();  // slice ci has landed
+    __syncthreads();           // ... for every thread, and slice ci-1 is no longer read
+    if (ci + TST - 1 < nch)
+      stage(ci + TST - 1, static_cast<int>((ci + TST - 1) % TST));
+    else
+      cp_async_commit();
+    const int nr = static_cast<int>(k - ci * TKC < TKC ? k - ci * TKC : TKC);
+    int h = 0;
+    for (; h + 4 <= nr; h += 4) {
+      float a4[MR][4];
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        const float4 v = *reinterpret_cast<const float4 *>(&as[buf][ty * MR + r][h]);
+        a4[r][0] = v.x;
+        a4[r][1] = v.y;
+        a4[r][2] = v.z;
+        a4[r][3] = v.w;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float bv[NR];
+        if (NR == 4) {
+          const float4 v = *reinterpret_cast<const float4 *>(&bs[buf][h + u][tx * NR]);
+          bv[0] = v.x;
+          bv[1 % NR] = v.y;
+          bv[2 % NR] = v.z;
+          bv[3 % NR] = v.w;
+        } else {
+          const float2 v = *reinterpret_cast<const float2 *>(&bs[buf][h + u][tx * NR]);
+          bv[0] = v.x;
+          bv[1 % NR] = v.y;
+        }
+#pragma unroll
+        for (int r = 0; r < MR; ++r)
+#pragma unroll
+          for (int j = 0; j < NR; ++j) acc[r][j] = __fadd_rn(acc[r][j], __fmul_rn(a4[r][u], bv[j]));
+      }
+    }
+    for (; h < nr; ++h) {
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        const float av = as[buf][ty * MR + r][h];
+#pragma unroll
+        for (int j = 0; j < NR; ++j)
+          acc[r][j] = __fadd_rn(acc[r][j], __fmul_rn(av, bs[buf][h][tx * NR + j]));
+      }
+    }
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int r = 0; r < MR; ++r) {
+    const int64_t row = row0 + ty * MR + r;
+    if (row >= m) continue;
+#pragma unroll
+    for (int j = 0; j < NR; ++j) {
+      const int64_t col = col0 + tx * NR + j;
+      if (col < n) c[row * ldc + col] = acc[r][j];
+    }
+  }
+}
+
 __global__ void fill_zero_kernel(float *__restrict__ y, int64_t rows, int64_t cols, int64_t ld) {
   const int64_t total = rows * cols;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -288,30 +413,79 @@ int pick_rows(int64_t m, int sms) {
   return (m + 1) / 2 >= sms ? 2 : 1;
 }
 
+// One tiled strict GEMM launch: 16 x 64 tiles (16 x 32 when N is small),
+// 16-byte copies when every row allows them.
+template <int MR, int NR>
+cudaError_t launch_tiled_variant(const float *a, const float *b, float *c, int64_t m, int64_t k,
+                                 int64_t n, int64_t lda, int64_t ldb, int64_t ldc, bool vec,
+                                 cudaStream_t stream, LaunchInfo *info) {
+  constexpr int TX = 16, TY = 8, TM = TY * MR, TN = TX * NR;
+  const int64_t gy = (m + TM - 1) / TM, gx = (n + TN - 1) / TN;
+  if (gy > 65535 || gx > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
+  if (vec)
+    strict_tiled_kernel<MR, NR, TX, TY, true><<<grid, TX * TY, 0, stream>>>(a, b, c, m, k, n, lda,
+                                                                          ldb, ldc);
+  else
+    strict_tiled_kernel<MR, NR, TX, TY, false><<<grid, TX * TY, 0, stream>>>(a, b, c, m, k, n,
+                                                                           lda, ldb, ldc);
+  if (info) {
+    info->launches += 1;
+    info->tile_m = TM;
+    info->tile_n = TN;
+    info->tile_k = TKC;
+    info->ctas += static_cast<int>(grid.x * grid.y);
+  }
+  return cudaGetLastError();
+}
+
+// One tiled strict GEMM launch. The per-thread block shrinks (8 -> 4 -> 2
+// chains) until there are about four warps per SM sub-partition (2368 on 148
+// SMs), so small problems still fill the GPU; 16-byte copies when every row
+// allows them.
+cudaError_t launch_tiled(const float *a, const float *b, float *c, int64_t m, int64_t k, int64_t n,
+                         int64_t lda, int64_t ldb, int64_t ldc, int sms, cudaStream_t stream,
+                         LaunchInfo *info) {
+  const auto al16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
+  const bool vec = k % 4 == 0 && n % 4 == 0 && lda % 4 == 0 && ldb % 4 == 0 &&
+                   (k == 0 || (al16(a) && al16(b)));
+  const int64_t want_threads = static_cast<int64_t>(sms) * 4 * 4 * 32;
+  const int64_t outputs = m * n;
+  if (outputs / 8 >= want_threads && n >= 64)
+    return launch_tiled_variant<2, 4>(a, b, c, m, k, n, lda, ldb, ldc, vec, stream, info);
+  if (outputs / 4 >= want_threads && n >= 32)
+    return launch_tiled_variant<2, 2>(a, b, c, m, k, n, lda, ldb, ldc, vec, stream, info);
+  return launch_tiled_variant<1, 2>(a, b, c, m, k, n, lda, ldb, ldc, vec, stream, info);
+}
+
 }  // namespace
 
 cudaError_t launch_strict_gemm(const float *a, const float *b, float *c, int64_t m, int64_t k,
                                int64_t n, int64_t lda, int64_t ldb, int64_t ldc, int sms,
                                cudaStream_t stream, LaunchInfo *info) {
   if (m == 0 || n == 0) return cudaSuccess;
-  const int R = pick_rows(m, sms);
-  const int threads = n >= 256 ? 256 : 128;
-  dim3 grid(static_cast<unsigned>((n + threads - 1) / threads),
-            static_cast<unsigned>((m + R - 1) / R));
-  if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
-  switch (R) {
-    case 4: strict_gemm_kernel<4><<<grid, threads, 0, stream>>>(a, b, c, m, k, n, lda, ldb, ldc); break;
-    case 2: strict_gemm_kernel<2><<<grid, threads, 0, stream>>>(a, b, c, m, k, n, lda, ldb, ldc); break;
-    default: strict_gemm_kernel<1><<<grid, threads, 0, stream>>>(a, b, c, m, k, n, lda, ldb, ldc); break;
-  }
   if (info) {
-    info->launches = 1;
-    info->tile_m = R;
-    info->tile_n = threads;
-    info->ctas = static_cast<int>(grid.x * grid.y);
-    info->set_route("strict_f32_simt_gemm");
+    info->launches = 0;
+    info->ctas = 0;
   }
-  return cudaGetLastError();
+  const cudaError_t err = launch_tiled(a, b, c, m, k, n, lda, ldb, ldc, sms, stream, info);
+  if (info) info->set_route("strict_f32_simt_gemm_tiled");
+  return err;
+}
+
+cudaError_t launch_strict_pair_two_pass(const float *a, const float *b, const float *d, float *e,
+                                        float *c_buf, int64_t m, int64_t k, int64_t n, int64_t p,
+                                        int64_t lda, int64_t ldb, int64_t ldd, int64_t lde,
+                                        int sms, cudaStream_t stream, LaunchInfo *info) {
+  if (info) {
+    info->launches = 0;
+    info->ctas = 0;
+  }
+  if (m == 0 || p == 0) return cudaSuccess;
+  cudaError_t err = launch_tiled(a, b, c_buf, m, k, n, lda, ldb, n, sms, stream, info);
+  if (err == cudaSuccess) err = launch_tiled(c_buf, d, e, m, n, p, n, ldd, lde, sms, stream, info);
+  if (info) info->set_route("strict_f32_simt_pair_two_pass");
+  return err;
 }
 
 int64_t strict_pair_scratch_floats(int64_t m, int64_t n, int sms, int smem_limit_bytes) {

@@ -45,20 +45,21 @@ def test_execution_suite_bit_exact(mcb, orc):
         _check_pair(mcb, orc, name, a, b, d)
 
 
-def test_scratch_panel_route(mcb, orc):
-    """N large enough that the intermediate panel spills to global scratch."""
+def test_large_n_two_pass(mcb, orc):
+    """N far beyond a shared-memory panel: C goes through device memory."""
     rng = np.random.default_rng(11)
     a = rng.uniform(-1, 1, (37, 5)).astype(np.float32)
     b = rng.uniform(-1, 1, (5, 70001)).astype(np.float32)
     d = rng.uniform(-1, 1, (70001, 3)).astype(np.float32)
     got = mcb.strict_fused_pair(a, b, d)
-    assert "scratch" in mcb.api.last_result.route
+    assert mcb.api.last_result.route == "strict_f32_simt_pair_two_pass"
     assert rc.same_bits(got, orc.strict_fused_pair(a, b, d))
 
 
 def test_strict_gemm_bit_exact(mcb, orc):
     rng = np.random.default_rng(12)
-    for m, k, n in [(1, 1, 1), (7, 0, 5), (33, 65, 129), (300, 257, 513)]:
+    for m, k, n in [(1, 1, 1), (7, 0, 5), (33, 65, 129), (300, 257, 513), (1024, 64, 1024),
+                    (700, 31, 600)]:
         a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
         b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
         assert rc.same_bits(mcb.strict_gemm(a, b), orc.strict_gemm(a, b)), (m, k, n)
@@ -93,11 +94,10 @@ def test_strided_device_operands(mcb, orc):
     assert rc.same_bits(te.cpu().numpy(), orc.strict_fused_pair(a, b, d))
 
 
-@pytest.mark.parametrize("m,k,n,p", [(512, 256, 384, 128), (301, 68, 100, 12), (9, 8, 12, 8),
-                                     (600, 512, 1024, 1024), (5, 4, 4, 1024)])
+@pytest.mark.parametrize("m,k,n,p", [(9, 8, 12, 8), (5, 4, 4, 1024), (64, 36, 200, 4)])
 def test_staged_route_bit_exact(mcb, orc, m, k, n, p):
-    """16-byte aligned operands with N, P <= 1024 take the shared-memory staged
-    kernel: tail panels (M % R), a short last K chunk, 16- and 32-row chunks."""
+    """Small 16-byte aligned pairs (M*N < 16384, N, P <= 1024) take the fused
+    shared-memory staged kernel: tail panels and a short last K chunk."""
     rng = np.random.default_rng(m + k + n + p)
     a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
     b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
@@ -107,13 +107,35 @@ def test_staged_route_bit_exact(mcb, orc, m, k, n, p):
     assert rc.same_bits(got, orc.strict_fused_pair(a, b, d))
 
 
-def test_staged_route_ieee_specials(mcb, orc):
-    """Signed zeros, subnormals, infinities and NaNs through the staged kernel."""
+@pytest.mark.parametrize("m,k,n,p", [(512, 256, 384, 128), (301, 68, 100, 12),
+                                     (600, 512, 1024, 1024), (301, 67, 101, 13),
+                                     (1000, 3, 17, 250), (130, 0, 128, 8), (800, 40, 500, 36)])
+def test_two_pass_bit_exact(mcb, orc, m, k, n, p):
+    """Larger pairs run as two tiled strict GEMMs through a binary32 C: tile
+    edges in M, N and P, 16-byte and 4-byte copy paths, K = 0 (E = +0 * D)."""
+    rng = np.random.default_rng(m + 3 * k + 5 * n + 7 * p)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    d = rng.uniform(-1, 1, (n, p)).astype(np.float32)
+    if k == 0:
+        d[3, 2] = np.inf  # +0 * inf = NaN must reach E
+    got = mcb.strict_fused_pair(a, b, d)
+    assert mcb.api.last_result.route == "strict_f32_simt_pair_two_pass"
+    assert mcb.api.last_result.kernel_launches == 2
+    assert rc.same_bits(got, orc.strict_fused_pair(a, b, d))
+
+
+@pytest.mark.parametrize("shape", [(9, 8, 12, 8), (130, 8, 128, 8)])
+def test_ieee_specials_both_routes(mcb, orc, shape):
+    """Signed zeros, subnormals, infinities and NaNs through the staged and the
+    two-pass routes."""
+    m, k, n, p = shape
     rng = np.random.default_rng(99)
     pool = np.array([0.0, -0.0, 1e-40, -3e-39, np.inf, -np.inf, np.nan, 1.5, -2.25, 3e38,
                      -1e-45, 0.1], np.float32)
     a, b, d = (rng.choice(pool, size=sh).astype(np.float32)
-               for sh in ((9, 8), (8, 12), (12, 8)))
+               for sh in ((m, k), (k, n), (n, p)))
     got = mcb.strict_fused_pair(a, b, d)
-    assert mcb.api.last_result.route == "strict_f32_simt_pair_staged"
+    assert mcb.api.last_result.route == ("strict_f32_simt_pair_staged" if m * n < 16384
+                                         else "strict_f32_simt_pair_two_pass")
     assert rc.same_bits(got, orc.strict_fused_pair(a, b, d))
