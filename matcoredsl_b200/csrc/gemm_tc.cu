@@ -295,14 +295,17 @@ __global__ void __launch_bounds__(THREADS, 1)
 // (rank 0) issues every MMA; both CTAs' TMA loads count on the leader's
 // `full` barrier, MMA completion is committed to both CTAs' `empty` /
 // `acc_full` barriers, and both epilogues release the leader's `acc_empty`.
+// Eight epilogue warps per CTA (two per TMEM lane quarter, one 128-column
+// half each) halve the epilogue time that the last tile of every CTA exposes.
 constexpr int P_BN_CTA = BN / 2;  // W columns staged per CTA
 constexpr int P_A_BYTES = BM * BK * 2;        // 16 KiB
 constexpr int P_B_BYTES = P_BN_CTA * BK * 2;  // 16 KiB
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
 constexpr int P_STAGES = 6;
+constexpr int P_THREADS = 320;  // producer, MMA, 8 epilogue warps (2 per TMEM lane quarter)
 constexpr size_t P_SMEM_BYTES = static_cast<size_t>(P_STAGES) * P_STAGE_BYTES + BAR_BYTES + 1024;
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     gemm_tc_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
                              const __grid_constant__ CUtensorMap tmap_w, const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -333,7 +336,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 256);  // 128 epilogue threads of each CTA (leader's copy)
+      mbar_init(&acc_empty[a], 512);  // 256 epilogue threads of each CTA (leader's copy)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -428,6 +431,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     }
   } else {
     const int sub = warp & 3;
+    const int half = (warp - 2) >> 2;  // 128-column half of the tile
     const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -441,7 +445,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
         if (n0 + c >= p.n) break;
         uint32_t r[32];
         tmem_ld32_sync(t_row + c, r);
@@ -482,7 +486,7 @@ int pair_clusters_resident(int device) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2, 1, 1);
-  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.blockDim = dim3(P_THREADS, 1, 1);
   cfg.dynamicSmemBytes = P_SMEM_BYTES;
   int n = 0;
   if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_bf16_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
@@ -555,7 +559,7 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
     if (clusters > sms / 2) clusters = sms / 2;
     if (clusters < 1) clusters = 1;
     grid = 2 * static_cast<int>(tiles < clusters ? tiles : clusters);
-    gemm_tc_bf16_pair_kernel<<<grid, THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
+    gemm_tc_bf16_pair_kernel<<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
   } else {
     // Per-device function attribute; cheap, so set on every launch.
     e = cudaFuncSetAttribute(gemm_tc_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
