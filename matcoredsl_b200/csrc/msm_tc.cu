@@ -399,16 +399,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 // The MMA thread issues S0(j+1), S1(j+1) as soon as the warpgroups have read
 // S(j) into registers, then PV0(j), PV1(j) once P(j) is written, so the
 // tensor core computes the next scores while both warpgroups exponentiate.
-// A quarter of the exponentials are evaluated on the FMA pipe (cubic minimax
-// polynomial for 2^f on [0,1), relative error 7.5e-5, exponent added as an
-// integer), which relieves the 16/clk/SM exp2 unit.
+// The softmax arithmetic uses packed f32x2 FMA/ADD and three-input max.
 constexpr int NQ = 2;
 constexpr int UNIT_ROWS = NQ * BQ;
 constexpr int KV_STAGES = 3;
 constexpr int THREADS2 = 64 + NQ * 128;
-// One pair of exponentials in kPolyPairs is evaluated by exp2_poly on the
-// FMA pipe instead of the exp2 unit (0: none).
-constexpr int kPolyPairs = 0;
 
 struct Smem2 {
   uint8_t q[NQ][TILE_BYTES];
@@ -425,23 +420,6 @@ struct Smem2 {
 };
 constexpr size_t SMEM2_BYTES = sizeof(Smem2) + 1024;
 static_assert(SMEM2_BYTES <= 232448, "two-tile MSM exceeds the opt-in shared memory per block");
-
-// 2^x for x in [-inf, 16]: x = k + f with k = floor(x) (obtained with a
-// round-down add of 1.5 * 2^23, which leaves k in the low mantissa bits), 2^f
-// from a degree-3 minimax polynomial fitted here for relative error on
-// [0, 1] (max 7.5e-5), and k added to the exponent field. Inputs below -126
-// are clamped (2^-126 ~ 0 for a softmax numerator).
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float magic = 12582912.0f;  // 1.5 * 2^23
-  const float t = __fadd_rd(x, magic);
-  const float k = __fsub_rn(t, magic);
-  const float f = __fsub_rn(x, k);
-  float p = fmaf(0.07802452f, f, 0.22606716f);
-  p = fmaf(p, f, 0.69583356f);
-  p = fmaf(p, f, 0.99992520f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
 
 __global__ void __launch_bounds__(THREADS2, 1)
     msm_tc2_bf16_kernel(const __grid_constant__ CUtensorMap tq,
@@ -688,14 +666,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
           f2_unpack(f2_fma(f2_pack(__uint_as_float(s[2 * i]), __uint_as_float(s[2 * i + 1])), c2,
                            nmc2),
                     x0, x1);
-          float e0, e1;
-          if (kPolyPairs > 0 && (i % (kPolyPairs > 0 ? kPolyPairs : 1)) == kPolyPairs - 1) {
-            e0 = exp2_poly(x0);
-            e1 = exp2_poly(x1);
-          } else {
-            e0 = ex2(x0);
-            e1 = ex2(x1);
-          }
+          const float e0 = ex2(x0), e1 = ex2(x1);
           ps[i & 3] = f2_add(ps[i & 3], f2_pack(e0, e1));
           pk[i] = pack_bf16x2(e0, e1);
         }
