@@ -75,6 +75,8 @@ def _check_msm(mcb, orc, pairs, scale, route, pairs_to_check=None):
     ((2, 3, 384, 128), "tcgen05_bf16_msm"),
     ((1, 1, 128, 128), "tcgen05_bf16_msm"),
     ((3, 5, 768, 128), "tcgen05_bf16_msm"),
+    ((1, 2, 512, 128), "tcgen05_bf16_msm"),
+    ((2, 3, 1536, 128), "tcgen05_bf16_msm"),
     ((1, 1, 200, 128), "simt_online_softmax_msm"),
     ((2, 2, 128, 64), "simt_online_softmax_msm"),
 ])
@@ -88,15 +90,24 @@ def test_tcgen05_rescale_path(mcb, orc):
                128 ** -0.5, "tcgen05_bf16_msm")
 
 
-def test_tcgen05_unscaled_reference_semantics(mcb, orc):
+@pytest.mark.parametrize("rows", [256, 512])
+def test_tcgen05_rescale_path_by_route(mcb, orc, rows):
+    """Growing key tiles with one and two 256-row units per (b, h)."""
+    _check_msm(mcb, orc, _bf16_case((1, 2, rows, 128), 15, kv_len=768, k_growth=0.6),
+               128 ** -0.5, "tcgen05_bf16_msm")
+
+
+@pytest.mark.parametrize("rows", [256, 512])
+def test_tcgen05_unscaled_reference_semantics(mcb, orc, rows):
     """scale = 1 (the reference's mc.softmax(Q @ K.T)): scores of std ~11."""
-    _check_msm(mcb, orc, _bf16_case((1, 1, 256, 128), 6, kv_len=640), 1.0, "tcgen05_bf16_msm")
+    _check_msm(mcb, orc, _bf16_case((1, 1, rows, 128), 6, kv_len=640), 1.0, "tcgen05_bf16_msm")
 
 
-def test_tcgen05_rectangular_and_strided(mcb, orc):
+@pytest.mark.parametrize("s", [256, 512])
+def test_tcgen05_rectangular_and_strided(mcb, orc, s):
     """M != N, and Q/K/V as strided views of a packed [B, S, 3, H, D] tensor."""
     import torch
-    b, s, h, d, n = 2, 256, 2, 128, 384
+    b, h, d, n = 2, 2, 128, 640
     rng = np.random.default_rng(9)
     packed = rng.standard_normal((b, n, 3, h, d), dtype=np.float32)
     ph, pf = gu.bf16_pair(packed)
