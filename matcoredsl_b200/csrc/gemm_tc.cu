@@ -2,6 +2,10 @@
 //
 //   Y[M,N] = act(X[M,K] * W (+|r-) bias)      (Family A, src/fusion_emitter_family_a.cpp)
 //
+// Two kernels: gemm_tc_bf16_pair_kernel (M >= 256; CTA pairs with
+// tcgen05.mma.cta_group::2, described with the kernel below) and
+// gemm_tc_bf16_kernel (single SM), whose design is:
+//
 // Design (one persistent CTA per SM, 192 threads, warp-specialised):
 //   warp 0      TMA producer: streams 128x64 tiles of X and 64x256 (or 256x64
 //               for W^T) tiles of W into a 4-stage shared-memory ring

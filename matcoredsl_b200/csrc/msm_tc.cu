@@ -2,6 +2,10 @@
 //
 //   O[b,h] = softmax(scale * Q[b,h] K[b,h]^T) V[b,h]      (src/fusion_emitter_family_c.cpp)
 //
+// Two kernels: msm_tc2_bf16_kernel (query blocks of 256 rows, two query
+// tiles per CTA; described with the kernel below) and msm_tc_bf16_kernel
+// (blocks of 128 rows), whose design is:
+//
 // One work unit = (b, h, 128-row query block). Persistent CTAs (one per SM,
 // 192 threads) loop over units; consecutive units share (b, h) so K/V stay
 // in L2 for the CTAs running at the same time.
