@@ -222,7 +222,11 @@ typedef struct mcb_epilogue {
  * bf16 or f32. GELU is the tanh form of src/fusion_emitter_common.cpp:86-108.
  * Replaces the Family A leaf emitted by FusionMlirEmitter::emitFamilyA
  * (src/fusion_emitter_family_a.cpp:12-244) and reached through compileAndRun
- * (include/matcore/jit_runner.h:23-26). */
+ * (include/matcore/jit_runner.h:23-26).
+ * Host-memory operands (without MCB_EXEC_TIME) move in row chunks: W and a
+ * row bias first, then each chunk's X rows (and full-bias rows) up, GEMM and
+ * Y rows down, overlapped on separate streams; a call that fails part-way may
+ * already have written the Y rows of completed chunks. */
 enum { MCB_GEMM_W_TRANSPOSED = 1u << 0 };
 MCB_API mcb_status mcb_gemm_epilogue_v1(const mcb_tensor *y, const mcb_tensor *x,
                                         const mcb_tensor *w, const mcb_tensor *bias,
