@@ -311,12 +311,29 @@ def run_profile_config(cfg: int, steps: int, warmup: int):
         del t
         c = torch.empty(16384, 16384, dtype=torch.bfloat16, device=dev)
         fn = lambda: mcb.gemm_fp8_blockscaled(qa, sa, qb, sb, out=c)  # noqa: E731
-    else:
+    elif cfg == 5:
         x = torch.randn(4, 2048, 4096, generator=g, device=dev).to(torch.bfloat16)
         ws = [(torch.randn(4096, 4096, generator=g, device=dev) / 64).to(torch.bfloat16)
               for _ in range(4)]
         y = torch.empty_like(x)
         fn = lambda: mcb.attn_block(x, *ws, 32, 1e-6, out=y)  # noqa: E731
+    elif cfg == 6:  # block_attn_res at the reference's largest benchmark shape
+        blocks = torch.randn(16, 8, 2048, 128, generator=g, device=dev)
+        partial = torch.randn(8, 2048, 128, generator=g, device=dev)
+        query = torch.randn(128, generator=g, device=dev)
+        out = torch.empty_like(partial)
+        fn = lambda: mcb.block_attn_res(blocks, partial, query, block_count=16,  # noqa: E731
+                                        has_partial=True, eps=1e-6, out=out)
+    elif cfg == 7:  # int8 x int8 -> int32 on tcgen05, 4096^3
+        a = torch.randint(-128, 128, (4096, 4096), generator=g, device=dev, dtype=torch.int8)
+        b = torch.randint(-128, 128, (4096, 4096), generator=g, device=dev, dtype=torch.int8)
+        c = torch.empty(4096, 4096, dtype=torch.int32, device=dev)
+        fn = lambda: mcb.gemm_i8_i32(a, b, out=c)  # noqa: E731
+    else:  # bf16 x bf16 -> f32 with the reference's fma order (CUDA cores), 2048^3
+        a = torch.randn(2048, 2048, generator=g, device=dev).to(torch.bfloat16)
+        b = torch.randn(2048, 2048, generator=g, device=dev).to(torch.bfloat16)
+        c = torch.empty(2048, 2048, dtype=torch.float32, device=dev)
+        fn = lambda: mcb.gemm_bf16_f32_fma(a, b, out=c)  # noqa: E731
     for _ in range(warmup + steps):
         fn()
     torch.cuda.synchronize()
@@ -554,7 +571,7 @@ def main():
                     help="skip the host-buffer end-to-end leg (used for short profiling runs)")
     ap.add_argument("--no-other-configs", action="store_true",
                     help="skip the configs 1/3/4/5 measurements reported beside the headline")
-    ap.add_argument("--profile-config", type=int, choices=[1, 2, 3, 4, 5],
+    ap.add_argument("--profile-config", type=int, choices=[1, 2, 3, 4, 5, 6, 7, 8],
                     help="only launch this config's operator (for ncu captures); no JSON line")
     args = ap.parse_args()
     if args.profile_config:

@@ -822,8 +822,20 @@ mcb_status typed_gemm_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_t
                     (reinterpret_cast<uintptr_t>(da) % 16 == 0) && c->strides[0] % 4 == 0 &&
                     (reinterpret_cast<uintptr_t>(dc) % 16 == 0);
     if (tc) {
+      // B^T [N,K] scratch: the caller's workspace when it holds it, else a
+      // stream-ordered allocation, so the call stays asynchronous.
+      const uint64_t bytes = static_cast<uint64_t>(n) * static_cast<uint64_t>(k);
       void *bt = nullptr;
-      if ((s = call.scratch(static_cast<uint64_t>(n) * k, &bt))) return s;
+      bool owned = false;
+      if (exec && exec->workspace && exec->workspace_bytes >= bytes &&
+          (reinterpret_cast<uintptr_t>(exec->workspace) & 15u) == 0) {
+        bt = exec->workspace;
+      } else if (cudaMallocAsync(&bt, bytes, call.stream()) == cudaSuccess) {
+        owned = true;
+      } else {
+        (void)cudaGetLastError();
+        if ((s = call.scratch(bytes, &bt))) return s;
+      }
       err = mcb::launch_transpose_u8(db, bt, k, n, b->strides[0], call.stream());
       if (err == cudaSuccess) {
         info.launches = 1;
@@ -831,6 +843,10 @@ mcb_status typed_gemm_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_t
                                      static_cast<const int8_t *>(bt), static_cast<int32_t *>(dc), m,
                                      n, k, c->strides[0], call.ctx()->status, call.sms(),
                                      call.stream(), &info);
+      }
+      if (owned) {
+        const cudaError_t fe = cudaFreeAsync(bt, call.stream());
+        if (err == cudaSuccess) err = fe;
       }
     }
     if (err == cudaErrorNotSupported) {

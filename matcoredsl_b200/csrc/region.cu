@@ -88,7 +88,8 @@ __global__ void __launch_bounds__(THREADS) residual_rmsnorm_kernel(
 // Depth attention over packed block history, f32 (src/region_emitter_block_
 // attn_res.cpp): for every (b, t) row, sources = blocks[0..block_count) plus
 // the partial; score_s = <x_s / rms(x_s), q>; w = softmax_s(score); out =
-// sum_s w_s x_s. One CTA of 128 threads per row. Pass 1 reads every source
+// sum_s w_s x_s. General kernel (any D, any alignment): one CTA of 128
+// threads per row. Pass 1 reads every source
 // row once (sum of squares and dot with q per thread, warp-shuffle then
 // shared-memory reduction); pass 2 re-reads the rows (L1/L2-resident) for the
 // weighted sum. HBM-bound: algorithmic bytes = (S + 1) * B*T*D*4 + D*4.
@@ -185,6 +186,99 @@ __global__ void __launch_bounds__(BAR_THREADS) block_attn_res_kernel(
   (void)has_partial;
 }
 
+// Row-group kernel for D = 32 * VPL4 (16-byte aligned rows): 8 lanes own one
+// (b, t) row, so one warp instruction serves 4 rows and a 256-thread CTA 32
+// rows. Single pass with an online softmax: every source row is read once
+// (each lane VPL4 float4, loads running up to four sources ahead), its sum of squares
+// and dot with q are reduced over the 8 lanes with three xor-shuffles, and the
+// score is folded into a running max m, running sum l and running weighted sum
+// acc (rescaled by exp(m_old - m_new)). HBM sees one read of the sources and
+// one write of out. The score uses rsqrtf and the weights __expf (a few ulp,
+// far inside the reference's 1e-4 tolerance).
+constexpr int BARG_ROWS = 32;  // rows per CTA (8 lanes each)
+
+template <int VPL4>
+__global__ void __launch_bounds__(256) block_attn_res_rows_kernel(
+    const float *__restrict__ blocks, const float *__restrict__ partial,
+    const float *__restrict__ query, float *__restrict__ out, int64_t rows,
+    int64_t block_stride, int nsrc, int block_count, float eps) {
+  constexpr int D = 32 * VPL4;
+  const int lr = threadIdx.x >> 3;        // row within the CTA
+  const int gl = threadIdx.x & 7;         // lane within the row group
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * BARG_ROWS + lr;
+  const bool live = row < rows;
+  const int64_t rrow = live ? row : 0;    // dead rows read row 0 and store nothing
+  float4 q[VPL4];
+#pragma unroll
+  for (int j = 0; j < VPL4; ++j) q[j] = *reinterpret_cast<const float4 *>(query + (j * 8 + gl) * 4);
+  auto src = [&](int s) -> const float4 * {
+    const float *base = s < block_count ? blocks + s * block_stride + rrow * D : partial + rrow * D;
+    return reinterpret_cast<const float4 *>(base);
+  };
+  const float inv_d = 1.0f / static_cast<float>(D);
+  // Ring of PF source rows in registers: slot f holds source s0 + f and is
+  // refilled with source s0 + f + PF as soon as it has been consumed.
+  constexpr int PF = VPL4 <= 4 ? 4 : 2;
+  float4 buf[PF][VPL4];
+#pragma unroll
+  for (int f = 0; f < PF; ++f)
+    if (f < nsrc) {
+#pragma unroll
+      for (int j = 0; j < VPL4; ++j) buf[f][j] = __ldg(src(f) + j * 8 + gl);
+    }
+  float m = -INFINITY, l = 0.0f;
+  float4 acc[VPL4];
+#pragma unroll
+  for (int j = 0; j < VPL4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = 0; s0 < nsrc; s0 += PF) {
+#pragma unroll
+    for (int f = 0; f < PF; ++f) {
+      const int s = s0 + f;
+      if (s < nsrc) {
+        float4 v[VPL4];
+#pragma unroll
+        for (int j = 0; j < VPL4; ++j) v[j] = buf[f][j];
+        if (s + PF < nsrc) {
+          const float4 *xn = src(s + PF);
+#pragma unroll
+          for (int j = 0; j < VPL4; ++j) buf[f][j] = __ldg(xn + j * 8 + gl);
+        }
+        float ss = 0.0f, dot = 0.0f;
+#pragma unroll
+        for (int j = 0; j < VPL4; ++j) {
+          ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
+          dot = fmaf(v[j].x, q[j].x, fmaf(v[j].y, q[j].y, fmaf(v[j].z, q[j].z, fmaf(v[j].w, q[j].w, dot))));
+        }
+#pragma unroll
+        for (int off = 4; off > 0; off >>= 1) {
+          ss += __shfl_xor_sync(0xffffffffu, ss, off);
+          dot += __shfl_xor_sync(0xffffffffu, dot, off);
+        }
+        const float sc = dot * rsqrtf(fmaf(ss, inv_d, eps));
+        const float m_new = fmaxf(m, sc);
+        const float r = __expf(m - m_new);  // 0 for the first source (m = -inf)
+        const float p = __expf(sc - m_new);
+        l = fmaf(l, r, p);
+#pragma unroll
+        for (int j = 0; j < VPL4; ++j) {
+          acc[j].x = fmaf(p, v[j].x, acc[j].x * r);
+          acc[j].y = fmaf(p, v[j].y, acc[j].y * r);
+          acc[j].z = fmaf(p, v[j].z, acc[j].z * r);
+          acc[j].w = fmaf(p, v[j].w, acc[j].w * r);
+        }
+        m = m_new;
+      }
+    }
+  }
+  if (live) {
+    const float inv = 1.0f / l;
+    float4 *o = reinterpret_cast<float4 *>(out + row * D);
+#pragma unroll
+    for (int j = 0; j < VPL4; ++j)
+      o[j * 8 + gl] = make_float4(acc[j].x * inv, acc[j].y * inv, acc[j].z * inv, acc[j].w * inv);
+  }
+}
+
 __global__ void zero_f32_kernel(float *__restrict__ y, int64_t n) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
@@ -210,6 +304,35 @@ cudaError_t launch_block_attn_res(const float *blocks, const float *partial, con
                     ((reinterpret_cast<uintptr_t>(blocks) | reinterpret_cast<uintptr_t>(partial) |
                       reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(out)) &
                      15u) == 0;
+  const int64_t groups = (rows + BARG_ROWS - 1) / BARG_ROWS;
+  if (vec4 && (d == 32 || d == 64 || d == 128 || d == 256) && groups <= 0x7fffffff) {
+    const unsigned grid = static_cast<unsigned>(groups);
+    switch (d) {
+      case 32:
+        block_attn_res_rows_kernel<1><<<grid, 256, 0, stream>>>(blocks, partial, query, out, rows,
+                                                               block_stride, nsrc, block_count, eps);
+        break;
+      case 64:
+        block_attn_res_rows_kernel<2><<<grid, 256, 0, stream>>>(blocks, partial, query, out, rows,
+                                                               block_stride, nsrc, block_count, eps);
+        break;
+      case 128:
+        block_attn_res_rows_kernel<4><<<grid, 256, 0, stream>>>(blocks, partial, query, out, rows,
+                                                               block_stride, nsrc, block_count, eps);
+        break;
+      default:
+        block_attn_res_rows_kernel<8><<<grid, 256, 0, stream>>>(blocks, partial, query, out, rows,
+                                                               block_stride, nsrc, block_count, eps);
+        break;
+    }
+    if (info) {
+      info->tile_m = BARG_ROWS;
+      info->tile_n = static_cast<int>(d);
+      info->ctas = static_cast<int>(grid);
+      info->set_route("block_attn_res");
+    }
+    return cudaGetLastError();
+  }
   block_attn_res_kernel<<<static_cast<unsigned>(rows), BAR_THREADS, 0, stream>>>(
       blocks, partial, query, out, rows, d, block_stride, nsrc, has_partial, block_count, eps,
       vec4 ? 1 : 0);

@@ -195,6 +195,38 @@ __global__ void transpose_u8_kernel(const uint8_t *__restrict__ in, uint8_t *__r
   }
 }
 
+// Same transpose with 64 x 64 byte tiles and 16-byte global accesses, for
+// rows/cols that are multiples of 16 bytes and 16-byte aligned rows (each
+// thread moves one 16-byte row segment in and one 16-byte column segment out).
+__global__ void __launch_bounds__(256) transpose_u8_v16_kernel(const uint8_t *__restrict__ in,
+                                                               uint8_t *__restrict__ out,
+                                                               int64_t rows, int64_t cols,
+                                                               int64_t ld_in) {
+  __shared__ uint8_t tile[64][64 + 4];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 64, c0 = static_cast<int64_t>(blockIdx.x) * 64;
+  const int t = threadIdx.x, tr = t >> 2, tc = (t & 3) * 16;
+  if (r0 + tr < rows && c0 + tc < cols) {
+    const uint4 v = *reinterpret_cast<const uint4 *>(in + (r0 + tr) * ld_in + c0 + tc);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) tile[tr][tc + i * 4 + b] = static_cast<uint8_t>(w[i] >> (8 * b));
+  }
+  __syncthreads();
+  // out row (c0 + tr) gets bytes r0 + tc .. r0 + tc + 15 of column tr of the tile.
+  if (c0 + tr < cols && r0 + tc < rows) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      w[i] = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) w[i] |= static_cast<uint32_t>(tile[tc + i * 4 + b][tr]) << (8 * b);
+    }
+    *reinterpret_cast<uint4 *>(out + (c0 + tr) * rows + r0 + tc) = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // CUDA-core int8 GEMM (exact; any shape/stride). One thread per output.
 __global__ void gemm_i8_simt_kernel(const int8_t *__restrict__ a, const int8_t *__restrict__ b,
                                     int32_t *__restrict__ c, int64_t m, int64_t n, int64_t k,
@@ -237,11 +269,120 @@ __global__ void __launch_bounds__(256) gemm_bf16_fma_kernel(const __nv_bfloat16 
   c[row * ldc + col] = acc;
 }
 
+// Tiled bf16 x bf16 -> f32 fma GEMM: same chains as gemm_bf16_fma_kernel (one
+// fmaf per k in increasing order from +0, bf16 widened exactly), with a CTA of
+// 128 threads owning a (8*MR) x (16*NR) tile, each thread MR x NR chains, and
+// 32-deep k-slices of A and B in a 3-stage cp.async shared-memory ring (rows
+// must be 16-byte aligned: K, N and both row strides multiples of 8).
+constexpr int FKC = 32, FAP = FKC + 8, FST = 3;
+
+__device__ __forceinline__ void cp_async16_t(void *smem_dst, const void *gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc)
+               : "memory");
+}
+
+template <int MR, int NR>
+__global__ void __launch_bounds__(128) gemm_bf16_fma_tiled_kernel(
+    const __nv_bfloat16 *__restrict__ a, const __nv_bfloat16 *__restrict__ b,
+    float *__restrict__ c, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+    int64_t ldc) {
+  constexpr int TX = 16, TY = 8, TM = TY * MR, TN = TX * NR, NT = TX * TY;
+  __shared__ __align__(16) __nv_bfloat16 as[FST][TM][FAP];
+  __shared__ __align__(16) __nv_bfloat16 bs[FST][FKC][TN];
+  const int tid = threadIdx.x, tx = tid % TX, ty = tid / TX;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.y) * TM;
+  const int64_t col0 = static_cast<int64_t>(blockIdx.x) * TN;
+  const int mrows = static_cast<int>(m - row0 < TM ? m - row0 : TM);
+  const int ncols = static_cast<int>(n - col0 < TN ? n - col0 : TN);
+  auto stage = [&](int64_t ci, int buf) {
+    const int64_t h0 = ci * FKC;
+    const int nr = static_cast<int>(k - h0 < FKC ? k - h0 : FKC);
+    const int av = nr >> 3, bv = ncols >> 3;  // 8 bf16 per 16-byte copy
+    for (int i = tid; i < mrows * av; i += NT) {
+      const int r = i / av, q = (i - r * av) * 8;
+      cp_async16_t(&as[buf][r][q], a + (row0 + r) * lda + h0 + q);
+    }
+    for (int i = tid; i < nr * bv; i += NT) {
+      const int r = i / bv, q = (i - r * bv) * 8;
+      cp_async16_t(&bs[buf][r][q], b + (h0 + r) * ldb + col0 + q);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float acc[MR][NR];
+#pragma unroll
+  for (int r = 0; r < MR; ++r)
+#pragma unroll
+    for (int j = 0; j < NR; ++j) acc[r][j] = 0.0f;
+  const int64_t nch = (k + FKC - 1) / FKC;
+#pragma unroll
+  for (int st = 0; st < FST - 1; ++st) {
+    if (st < nch)
+      stage(st, st);
+    else
+      asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  for (int64_t ci = 0; ci < nch; ++ci) {
+    const int buf = static_cast<int>(ci % FST);
+    asm volatile("cp.async.wait_group %0;" ::"n"(FST - 2) : "memory");
+    __syncthreads();
+    if (ci + FST - 1 < nch)
+      stage(ci + FST - 1, static_cast<int>((ci + FST - 1) % FST));
+    else
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    const int nr = static_cast<int>(k - ci * FKC < FKC ? k - ci * FKC : FKC);
+    for (int h = 0; h < nr; ++h) {
+      float bvv[NR];
+#pragma unroll
+      for (int j = 0; j < NR; ++j) bvv[j] = __bfloat162float(bs[buf][h][tx * NR + j]);
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        const float av = __bfloat162float(as[buf][ty * MR + r][h]);
+#pragma unroll
+        for (int j = 0; j < NR; ++j) acc[r][j] = __fmaf_rn(av, bvv[j], acc[r][j]);
+      }
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+  for (int r = 0; r < MR; ++r) {
+    const int64_t row = row0 + ty * MR + r;
+    if (row >= m) continue;
+#pragma unroll
+    for (int j = 0; j < NR; ++j) {
+      const int64_t col = col0 + tx * NR + j;
+      if (col < n) c[row * ldc + col] = acc[r][j];
+    }
+  }
+}
+
+template <int MR, int NR>
+cudaError_t launch_bf16_fma_tiled(const void *a, const void *b, float *c, int64_t m, int64_t n,
+                                  int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
+                                  cudaStream_t stream) {
+  constexpr int TM = 8 * MR, TN = 16 * NR;
+  const int64_t gy = (m + TM - 1) / TM, gx = (n + TN - 1) / TN;
+  if (gy > 65535 || gx > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  gemm_bf16_fma_tiled_kernel<MR, NR><<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(gy)),
+                                       128, 0, stream>>>(
+      static_cast<const __nv_bfloat16 *>(a), static_cast<const __nv_bfloat16 *>(b), c, m, n, k,
+      lda, ldb, ldc);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_transpose_u8(const void *in, void *out, int64_t rows, int64_t cols,
                                 int64_t ld_in, cudaStream_t stream) {
   if (rows == 0 || cols == 0) return cudaSuccess;
+  const bool v16 = rows % 16 == 0 && cols % 16 == 0 && ld_in % 16 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
+  if (v16) {
+    const dim3 g16(static_cast<unsigned>((cols + 63) / 64), static_cast<unsigned>((rows + 63) / 64));
+    if (g16.y > 65535u) return cudaErrorInvalidConfiguration;
+    transpose_u8_v16_kernel<<<g16, 256, 0, stream>>>(static_cast<const uint8_t *>(in),
+                                                    static_cast<uint8_t *>(out), rows, cols, ld_in);
+    return cudaGetLastError();
+  }
   dim3 grid(static_cast<unsigned>((cols + 31) / 32), static_cast<unsigned>((rows + 31) / 32));
   if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
   transpose_u8_kernel<<<grid, dim3(32, 8), 0, stream>>>(static_cast<const uint8_t *>(in),
@@ -308,6 +449,29 @@ cudaError_t launch_gemm_bf16_fma(const void *a, const void *b, float *c, int64_t
                                  int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
                                  cudaStream_t stream, LaunchInfo *info) {
   if (m == 0 || n == 0) return cudaSuccess;
+  const bool vec = k % 8 == 0 && n % 8 == 0 && lda % 8 == 0 && ldb % 8 == 0 &&
+                   (k == 0 || ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) &
+                               15u) == 0);
+  if (vec) {
+    // Per-thread block shrinks until a launch has ~2 warps per SM sub-partition.
+    const int64_t outputs = m * n;
+    cudaError_t e;
+    const char *route;
+    if (outputs / 8 >= 148LL * 4 * 2 * 32 && n >= 64) {
+      e = launch_bf16_fma_tiled<2, 4>(a, b, c, m, n, k, lda, ldb, ldc, stream);
+      route = "simt_bf16_f32_fma_gemm_tiled";
+    } else {
+      e = launch_bf16_fma_tiled<1, 2>(a, b, c, m, n, k, lda, ldb, ldc, stream);
+      route = "simt_bf16_f32_fma_gemm_tiled";
+    }
+    if (e != cudaErrorInvalidConfiguration) {
+      if (info) {
+        info->launches = 1;
+        info->set_route(route);
+      }
+      return e;
+    }
+  }
   if (m > 65535) return cudaErrorInvalidConfiguration;
   dim3 grid(static_cast<unsigned>((n + 255) / 256), static_cast<unsigned>(m));
   gemm_bf16_fma_kernel<<<grid, 256, 0, stream>>>(static_cast<const __nv_bfloat16 *>(a),

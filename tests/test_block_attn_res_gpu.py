@@ -3,9 +3,12 @@
 CPU: the oracle reproduces the golden fixtures that the reference's own two
 tests accepted (tests/golden/block_attn_res.npz), and the argument rules of
 matcore/frontend.py:1734-1765 are enforced without a GPU.
-GPU: the CUDA kernel matches the fixtures and the oracle at the reference's
+GPU: the CUDA kernels match the fixtures and the oracle at the reference's
 tolerance (rtol = atol = 1e-4) on its test shapes and its benchmark shapes
-([MAX_BLOCKS, B, T, D] = [8,4,512,128] ... [16,8,2048,128]).
+([MAX_BLOCKS, B, T, D] = [8,4,512,128] ... [16,8,2048,128]), plus the shapes
+that select each kernel (warp per row for D = 128/256 with more sources than
+its register cache, 8 lanes per row for D = 32/64, the general kernel
+otherwise) and row counts that leave partial CTAs.
 """
 import json
 import os
@@ -59,7 +62,9 @@ def test_cuda_matches_golden(mcb, case):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("shape", [(8, 4, 512, 128), (8, 8, 1024, 128), (16, 8, 1024, 128),
-                                   (8, 4, 1024, 256), (16, 8, 2048, 128), (5, 2, 33, 7)])
+                                   (8, 4, 1024, 256), (16, 8, 2048, 128), (5, 2, 33, 7),
+                                   (32, 2, 33, 128), (12, 1, 17, 256), (6, 3, 40, 64),
+                                   (4, 2, 30, 32)])
 @pytest.mark.parametrize("block_count,has_partial", [("all", True), ("half", False), (0, True),
                                                      (0, False)])
 def test_cuda_matches_oracle(mcb, orc, shape, block_count, has_partial):

@@ -23,6 +23,8 @@ def _ref_i8(a, b):
 @pytest.mark.parametrize("shape,route", [((256, 512, 384), "tcgen05_i8_gemm"),
                                          ((300, 1024, 520), "tcgen05_i8_gemm"),
                                          ((129, 48, 264), "tcgen05_i8_gemm"),
+                                         ((200, 80, 208), "tcgen05_i8_gemm"),
+                                         ((1024, 2048, 1024), "tcgen05_i8_gemm"),
                                          ((77, 100, 33), "simt_i8_gemm")])
 def test_i8_gemm_bit_exact(mcb, orc, shape, route):
     import torch
@@ -58,8 +60,13 @@ def test_i8_gemm_host_operands(mcb, orc):
     assert np.array_equal(mcb.gemm_i8_i32(a, b), orc.gemm_i8_i32(a, b))
 
 
-@pytest.mark.parametrize("shape", [(37, 53, 29), (256, 1000, 300)])
-def test_bf16_f32_fma_bit_exact(mcb, orc, shape):
+@pytest.mark.parametrize("shape,route", [
+    ((37, 53, 29), "simt_bf16_f32_fma_gemm"),          # unaligned rows: one thread per output
+    ((256, 1000, 300), "simt_bf16_f32_fma_gemm"),      # N % 8 != 0
+    ((256, 1000, 304), "simt_bf16_f32_fma_gemm_tiled"),
+    ((1030, 72, 520), "simt_bf16_f32_fma_gemm_tiled"),
+    ((700, 264, 1024), "simt_bf16_f32_fma_gemm_tiled")])
+def test_bf16_f32_fma_bit_exact(mcb, orc, shape, route):
     import torch
     from tests import gpu_util as gu
     m, k, n = shape
@@ -67,7 +74,7 @@ def test_bf16_f32_fma_bit_exact(mcb, orc, shape):
     ah, _ = gu.bf16_pair(rng.standard_normal((m, k), dtype=np.float32))
     bh, _ = gu.bf16_pair(rng.standard_normal((k, n), dtype=np.float32))
     c = mcb.gemm_bf16_f32_fma(gu.to_dev_bf16(ah), gu.to_dev_bf16(bh))
-    assert mcb.api.last_result.route == "simt_bf16_f32_fma_gemm"
+    assert mcb.api.last_result.route == route
     got = c.cpu().numpy()
     assert np.array_equal(got.view(np.uint32), orc.gemm_bf16_f32_fma(ah, bh).view(np.uint32))
     import oracle
