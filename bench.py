@@ -472,7 +472,10 @@ def run_ours(args):
     if world == 1 and not args.no_other_configs:
         del sets, dsets, calls
         torch.cuda.empty_cache()
-        others = run_other_configs(dev)
+        try:  # side measurements never cost the headline line
+            others = run_other_configs(dev)
+        except Exception as exc:  # noqa: BLE001
+            others = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, working_set, route,
             clk, e2e, others, kernel)
 
