@@ -526,7 +526,10 @@ def _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, wo
     achieved = flops_step / (launch_ms_max / 1e3) / 1e12
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline()
+        try:
+            cpu = cpu_baseline()
+        except Exception as exc:  # noqa: BLE001
+            cpu = {"value": None, "error": f"{type(exc).__name__}: {exc}"[:300]}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
