@@ -671,10 +671,10 @@ mcb_status strict_pair_impl(const mcb_tensor *e, const mcb_tensor *a, const mcb_
 
 // ---- Family A -------------------------------------------------------------------------
 // Row-chunk size for the host-operand pipeline of a row-splittable operator:
-// a multiple of 256 rows holding about 4 MiB of the row operand `x`, at most
+// a multiple of 256 rows holding about 8 MiB of the row operand `x`, at most
 // 64 chunks; 0 (no pipeline) when `m` gives fewer than two chunks.
 int64_t pipeline_chunk_rows(int64_t m, const mcb_tensor *x) {
-  constexpr int64_t kChunkBytes = 4 << 20, kAlign = 256, kMaxChunks = 64;
+  constexpr int64_t kChunkBytes = 8 << 20, kAlign = 256, kMaxChunks = 64;
   const int64_t row_bytes = std::max<int64_t>(1, x->strides[0]) *
                             static_cast<int64_t>(dtype_size(x->dtype));
   int64_t rows = (kChunkBytes / row_bytes + kAlign - 1) / kAlign * kAlign;
@@ -730,7 +730,7 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
   Call call(exec);
   if ((s = call.begin(host))) return s;
   // Host operands (untimed calls): X, a full bias and Y move in row chunks of
-  // about 4 MiB of X so that uploads, GEMMs and downloads overlap (W and a
+  // about 8 MiB of X so that uploads, GEMMs and downloads overlap (W and a
   // row bias are uploaded whole, ahead of the first chunk).
   const int64_t chunk_rows = host && !call.timed() ? pipeline_chunk_rows(m, x) : 0;
   const bool full_bias = ep.bias_mode == MCB_BIAS_FULL;

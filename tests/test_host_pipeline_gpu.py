@@ -23,7 +23,7 @@ def _bf16_host(bits):
 
 def test_bf16_full_bias_padded_output(mcb, orc):
     from matcoredsl_b200 import _abi
-    m, k, n = 1300, 4096, 264  # 8 KiB rows of X: 512-row chunks, 3 launches
+    m, k, n = 2600, 4096, 264  # 8 KiB rows of X: 1024-row chunks, 3 launches
     rng = np.random.default_rng(5)
     x = rng.standard_normal((m, k), dtype=np.float32)
     w = rng.standard_normal((k, n), dtype=np.float32) / np.float32(64)
@@ -49,7 +49,7 @@ def test_bf16_full_bias_padded_output(mcb, orc):
 
 
 def test_bf16_row_bias_bf16_output_many_chunks(mcb, orc):
-    m, k, n = 4100, 2048, 512  # 4 KiB rows: 1024-row chunks, 5 launches (last one 4 rows)
+    m, k, n = 4100, 2048, 512  # 4 KiB rows: 2048-row chunks, 3 launches (last one 4 rows)
     rng = np.random.default_rng(6)
     x = rng.standard_normal((m, k), dtype=np.float32)
     w = rng.standard_normal((k, n), dtype=np.float32) / np.float32(np.sqrt(k))
@@ -58,14 +58,14 @@ def test_bf16_row_bias_bf16_output_many_chunks(mcb, orc):
     y = mcb.gemm_epilogue(_bf16_host(xh), _bf16_host(wh), _bf16_host(bh), act="gelu_tanh",
                           out_dtype="bf16")
     r = mcb.api.last_result
-    assert r.kernel_launches == 5 and r.d2h_bytes == m * n * 2
+    assert r.kernel_launches == 3 and r.d2h_bytes == m * n * 2
     rows = gu.sample_rows(m)
     ref = orc.gemm_epilogue(xf, wf, bf, bias_mode="row", act="gelu_tanh", rows=rows)
     assert orc.rel_frobenius(y.astype(np.float32)[rows], ref) < 1e-2
 
 
 def test_f32_cuda_core_path_pipelined(mcb, orc):
-    m, k, n = 2100, 1024, 96  # f32 X rows of 4 KiB: 1024-row chunks on the CUDA-core kernel
+    m, k, n = 4200, 1024, 96  # f32 X rows of 4 KiB: 2048-row chunks on the CUDA-core kernel
     rng = np.random.default_rng(7)
     x = rng.standard_normal((m, k), dtype=np.float32)
     w = rng.standard_normal((k, n), dtype=np.float32) / np.float32(32)
