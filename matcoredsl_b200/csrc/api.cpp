@@ -818,12 +818,21 @@ mcb_status typed_gemm_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_t
     err = mcb::launch_gemm_bf16_fma(da, db, static_cast<float *>(dc), m, n, k, a->strides[0],
                                     b->strides[0], c->strides[0], call.stream(), &info);
   } else {
-    const bool tc = k > 0 && k % 16 == 0 && a->strides[0] == k &&
-                    (reinterpret_cast<uintptr_t>(da) % 16 == 0) && c->strides[0] % 4 == 0 &&
-                    (reinterpret_cast<uintptr_t>(dc) % 16 == 0);
-    if (tc) {
-      // B^T [N,K] scratch: the caller's workspace when it holds it, else a
-      // stream-ordered allocation, so the call stays asynchronous.
+    const int64_t lda = a->strides[0], ldb = b->strides[0];
+    const bool tc = k > 0 && lda % 16 == 0 && (reinterpret_cast<uintptr_t>(da) % 16 == 0) &&
+                    c->strides[0] % 4 == 0 && (reinterpret_cast<uintptr_t>(dc) % 16 == 0);
+    const bool b_direct = ldb % 16 == 0 && (reinterpret_cast<uintptr_t>(db) % 16 == 0);
+    if (tc && b_direct) {
+      // B [K,N] read MN-major in place: one launch, no scratch.
+      err = mcb::launch_gemm_i8_tc(static_cast<const int8_t *>(da), lda,
+                                   static_cast<const int8_t *>(db), ldb, 1,
+                                   static_cast<int32_t *>(dc), m, n, k, c->strides[0],
+                                   call.ctx()->status, call.sms(), call.stream(), &info);
+    } else if (tc && k % 16 == 0) {
+      // B rows not 16-byte aligned: transpose into a dense B^T [N,K] scratch
+      // (row stride K) first. The scratch is the caller's workspace when it
+      // holds it, else a stream-ordered allocation, so the call stays
+      // asynchronous.
       const uint64_t bytes = static_cast<uint64_t>(n) * static_cast<uint64_t>(k);
       void *bt = nullptr;
       bool owned = false;
@@ -836,13 +845,13 @@ mcb_status typed_gemm_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_t
         (void)cudaGetLastError();
         if ((s = call.scratch(bytes, &bt))) return s;
       }
-      err = mcb::launch_transpose_u8(db, bt, k, n, b->strides[0], call.stream());
+      err = mcb::launch_transpose_u8(db, bt, k, n, ldb, call.stream());
       if (err == cudaSuccess) {
         info.launches = 1;
-        err = mcb::launch_gemm_i8_tc(static_cast<const int8_t *>(da),
-                                     static_cast<const int8_t *>(bt), static_cast<int32_t *>(dc), m,
-                                     n, k, c->strides[0], call.ctx()->status, call.sms(),
-                                     call.stream(), &info);
+        err = mcb::launch_gemm_i8_tc(static_cast<const int8_t *>(da), lda,
+                                     static_cast<const int8_t *>(bt), k, 0,
+                                     static_cast<int32_t *>(dc), m, n, k, c->strides[0],
+                                     call.ctx()->status, call.sms(), call.stream(), &info);
       }
       if (owned) {
         const cudaError_t fe = cudaFreeAsync(bt, call.stream());

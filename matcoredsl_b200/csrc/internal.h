@@ -103,9 +103,12 @@ cudaError_t launch_gemm_fp8_simt(const uint8_t *a, int a_e5m2, const float *sa,
 // ---- typed.cu: int8 and bf16-fma typed GEMMs -------------------------------------------------
 cudaError_t launch_transpose_u8(const void *in, void *out, int64_t rows, int64_t cols,
                                 int64_t ld_in, cudaStream_t stream);
-cudaError_t launch_gemm_i8_tc(const int8_t *a, const int8_t *bt, int32_t *c, int64_t m, int64_t n,
-                              int64_t k, int64_t ld_c, uint32_t *status, int sms,
-                              cudaStream_t stream, LaunchInfo *info);
+// b_mn = 1: b is B [K,N] (row stride ldb), read MN-major; b_mn = 0: b is
+// Bt [N,K] (row stride ldb), read K-major. Returns cudaErrorNotSupported when
+// a stride or base is not 16-byte aligned or k == 0.
+cudaError_t launch_gemm_i8_tc(const int8_t *a, int64_t lda, const int8_t *b, int64_t ldb,
+                              int b_mn, int32_t *c, int64_t m, int64_t n, int64_t k, int64_t ld_c,
+                              uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info);
 cudaError_t launch_gemm_i8_simt(const int8_t *a, const int8_t *b, int32_t *c, int64_t m, int64_t n,
                                 int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
                                 cudaStream_t stream, LaunchInfo *info);

@@ -9,12 +9,25 @@
 //     (:108-127). Rounding depends on the order, so this one runs on CUDA
 //     cores with fmaf in exactly that order.
 //
-// int8 kernel layout: A [M,K] K-major; B is consumed K-major (Bt [N,K]); a
-// B given as [K,N] is first transposed into scratch by a small kernel.
-// Persistent CTAs (one per SM, 192 threads): TMA producer warp, one MMA
-// thread (M=128, N=256, K=32 per instruction) into two 128x256 int32 TMEM
-// accumulators, four epilogue warps storing int32.
+// int8 kernel layout: A [M,K] K-major. B [K,N] is consumed MN-major straight
+// from memory when its rows are 16-byte aligned (tcgen05 takes MN-major 8-bit
+// operands); otherwise it is first transposed into a K-major scratch
+// Bt [N,K] by a small kernel. Two persistent, warp-specialised kernels:
+//
+//   gemm_i8_pair_kernel (M >= 256): clusters of two CTAs on two SMs compute
+//     256x256 tiles with tcgen05.mma.cta_group::2.kind::i8 (M=256, N=256,
+//     K=32). CTA r stages rows [128r, 128r+128) of the A tile and columns
+//     [128r, 128r+128) of the B tile, so each SM moves 32 KiB per 128-deep
+//     K block (half the B bytes of a single-SM 128x256 tile) through a
+//     6-stage TMA ring; its TMEM holds its 128 rows of two 256-column int32
+//     accumulators. The leader CTA issues every MMA; eight epilogue warps per
+//     CTA (two per TMEM lane quarter) store int32 rows.
+//   gemm_i8_kernel (M < 256): one CTA per SM, 128x256 tiles, cta_group::1,
+//     4-stage ring, four epilogue warps.
 #include <cuda_bf16.h>
+
+#include <atomic>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "internal.h"
@@ -25,6 +38,22 @@ namespace {
 constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;  // BK in bytes == elements
 constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK, STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 192;
+constexpr int MN_CHUNK = 128;                // B columns per 128-byte swizzle row
+constexpr int MN_CHUNK_BYTES = MN_CHUNK * BK;  // one MN-major box: 128 columns x BK rows
+constexpr size_t SMEM_BYTES = static_cast<size_t>(STAGES) * STAGE_BYTES + 256 + 1024;
+
+constexpr int P_B_COLS = BN / 2;  // B columns staged per CTA of a pair
+constexpr int P_A_BYTES = BM * BK, P_B_BYTES = P_B_COLS * BK;
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;  // 32 KiB
+constexpr int P_STAGES = 6;
+constexpr int P_THREADS = 320;
+constexpr size_t P_SMEM_BYTES = static_cast<size_t>(P_STAGES) * P_STAGE_BYTES + 256 + 1024;
+
+// kind::i8 instruction descriptor: D s32 (format 2), A and B signed 8-bit
+// (format 1), A K-major, B K-major or MN-major.
+__host__ __device__ constexpr uint32_t idesc_i8(uint32_t b_mn, uint32_t m, uint32_t n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (b_mn << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
 
 __device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                           uint32_t idesc, uint32_t accumulate) {
@@ -36,12 +65,48 @@ __device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
+__device__ __forceinline__ void mma_i8_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// B operand descriptor for the kk-th 32-deep K step of a stage. K-major Bt:
+// K advances 32 bytes inside each 128-byte row. MN-major B: 128-column chunks
+// LBO = MN_CHUNK_BYTES apart, 8-row K groups SBO = 1 KiB apart, and K
+// advances by 32 rows = 4 KiB.
+__device__ __forceinline__ uint64_t b_desc_i8(uint32_t b_addr, int kk, int b_mn) {
+  return b_mn ? make_sdesc_sw128(b_addr + kk * 32 * 128, MN_CHUNK_BYTES, 1024)
+              : make_sdesc_sw128(b_addr + kk * 32, 16, 1024);
+}
+
 struct Params {
   int64_t m, n, ld_c;
   int n_tiles, num_tiles, num_kb;
+  int b_mn;
   int32_t *c;
   uint32_t *status;
 };
+
+// Stores one 32-column int32 chunk of one output row.
+__device__ __forceinline__ void store_chunk(const Params &p, const uint32_t (&r)[32], int64_t row,
+                                            int64_t col0) {
+  if (row >= p.m) return;
+  int32_t *crow = p.c + row * p.ld_c + col0;
+  if (col0 + 32 <= p.n && (p.ld_c % 4 == 0)) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      reinterpret_cast<uint4 *>(crow)[q] =
+          make_uint4(r[q * 4], r[q * 4 + 1], r[q * 4 + 2], r[q * 4 + 3]);
+  } else {
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < p.n) crow[i] = static_cast<int32_t>(r[i]);
+  }
+}
 
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
@@ -90,7 +155,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             goto producer_done;
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           tma_load_2d(sa + stage * A_BYTES, &ta, &full[stage], kb * BK, m0);
-          tma_load_2d(sb + stage * B_BYTES, &tb, &full[stage], kb * BK, n0);
+          if (p.b_mn) {
+#pragma unroll
+            for (int j = 0; j < BN / MN_CHUNK; ++j)
+              tma_load_2d(sb + stage * B_BYTES + j * MN_CHUNK_BYTES, &tb, &full[stage],
+                          n0 + j * MN_CHUNK, kb * BK);
+          } else {
+            tma_load_2d(sb + stage * B_BYTES, &tb, &full[stage], kb * BK, n0);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -101,9 +173,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      // kind::i8: D s32 (format 2), A and B signed 8-bit (format 1), K-major.
-      const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((BN >> 3) << 17) |
-                             ((BM >> 4) << 24);
+      const uint32_t idesc = idesc_i8(p.b_mn ? 1u : 0u, BM, BN);
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
@@ -120,7 +190,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 32; ++kk)
             mma_i8_ss(tmem + acc * BN, make_sdesc_sw128(a_addr + kk * 32, 16, 1024),
-                      make_sdesc_sw128(b_addr + kk * 32, 16, 1024), idesc, (kb | kk) ? 1u : 0u);
+                      b_desc_i8(b_addr, kk, p.b_mn), idesc, (kb | kk) ? 1u : 0u);
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -152,18 +222,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (n0 + c >= p.n) break;
         uint32_t r[32];
         tmem_ld32_sync(t_row + c, r);
-        if (row < p.m) {
-          int32_t *crow = p.c + row * p.ld_c + n0 + c;
-          if (n0 + c + 32 <= p.n && (p.ld_c % 4 == 0)) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              reinterpret_cast<uint4 *>(crow)[q] =
-                  make_uint4(r[q * 4], r[q * 4 + 1], r[q * 4 + 2], r[q * 4 + 3]);
-          } else {
-            for (int i = 0; i < 32; ++i)
-              if (n0 + c + i < p.n) crow[i] = static_cast<int32_t>(r[i]);
-          }
-        }
+        store_chunk(p, r, row, n0 + c);
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
@@ -177,6 +236,172 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
+    gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap ta,
+                        const __grid_constant__ CUtensorMap tb, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *sa = smem, *sb = smem + P_STAGES * P_A_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t *full = bars, *empty = bars + P_STAGES, *acc_full = bars + 2 * P_STAGES;
+  uint64_t *acc_empty = acc_full + 2, *drain = acc_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 512);  // 256 epilogue threads of each CTA (leader's copy)
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&ta);
+    tma_prefetch_desc(&tb);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = cluster; tile < p.num_tiles; tile += nclusters) {
+        const int m0 = (tile / p.n_tiles) * (2 * BM) + static_cast<int>(rank) * BM;
+        const int n0 = (tile % p.n_tiles) * BN + static_cast<int>(rank) * P_B_COLS;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kErrTimeoutEmpty))
+            goto producer_done;
+          const uint32_t fbar = full_leader0 + stage * 8;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+          tma_load_2d_pair(sa + stage * P_A_BYTES, &ta, fbar, kb * BK, m0);
+          if (p.b_mn)
+            tma_load_2d_pair(sb + stage * P_B_BYTES, &tb, fbar, n0, kb * BK);
+          else
+            tma_load_2d_pair(sb + stage * P_B_BYTES, &tb, fbar, kb * BK, n0);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      const uint32_t idesc = idesc_i8(p.b_mn ? 1u : 0u, 2 * BM, BN);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      for (int tile = cluster; tile < p.num_tiles; tile += nclusters) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.status, kErrTimeoutAccum))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sa + stage * P_A_BYTES);
+          const uint32_t b_addr = smem_u32(sb + stage * P_B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk)
+            mma_i8_ss_pair(d_tmem, make_sdesc_sw128(a_addr + kk * 32, 16, 1024),
+                           b_desc_i8(b_addr, kk, p.b_mn), idesc, (kb | kk) != 0 ? 1u : 0u);
+          mma_commit_pair(&empty[stage], 0x3);
+          if (++stage == P_STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(&acc_full[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      mma_commit_pair(drain, 0x1);
+      if (!mbar_wait(drain, 0, nullptr, p.status, kErrTimeoutDrain)) *abort_flag = 1;
+    }
+  } else {
+    const int sub = warp & 3;
+    const int half = (warp - 2) >> 2;  // 128-column half of the tile
+    const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = cluster; tile < p.num_tiles; tile += nclusters) {
+      const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * (2 * BM) + rank * BM;
+      const int64_t n0 = static_cast<int64_t>(tile % p.n_tiles) * BN;
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.status, kErrTimeoutAccum))
+        break;
+      tc_fence_after();
+      const int64_t row = m0 + sub * 32 + lane;
+      const uint32_t t_row =
+          tmem + (static_cast<uint32_t>(sub * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+        if (n0 + c >= p.n) break;
+        uint32_t r[32];
+        tmem_ld32_sync(t_row + c, r);
+        store_chunk(p, r, row, n0 + c);
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(acc_empty_leader + acc * 8);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // every pair MMA has completed before either CTA frees TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
+// Clusters of gemm_i8_pair_kernel that fit on the device at once, cached per
+// device (-1: the pair kernel cannot run here).
+int i8_pair_clusters_resident(int device) {
+  static std::atomic<int> cache[64];
+  if (device < 0 || device >= 64) return -1;
+  int v = cache[device].load(std::memory_order_relaxed);
+  if (v != 0) return v;
+  int n = -1;
+  if (cudaFuncSetAttribute(gemm_i8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(P_SMEM_BYTES)) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(P_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_i8_pair_kernel, &cfg) != cudaSuccess || n <= 0)
+      n = -1;
+  }
+  (void)cudaGetLastError();
+  cache[device].store(n, std::memory_order_relaxed);
+  return n;
 }
 
 // B [K,N] -> Bt [N,K] for 1-byte elements, 32x32 tiles through shared memory.
@@ -391,40 +616,69 @@ cudaError_t launch_transpose_u8(const void *in, void *out, int64_t rows, int64_t
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemm_i8_tc(const int8_t *a, const int8_t *bt, int32_t *c, int64_t m, int64_t n,
-                              int64_t k, int64_t ld_c, uint32_t *status, int sms,
-                              cudaStream_t stream, LaunchInfo *info) {
+cudaError_t launch_gemm_i8_tc(const int8_t *a, int64_t lda, const int8_t *b, int64_t ldb,
+                              int b_mn, int32_t *c, int64_t m, int64_t n, int64_t k, int64_t ld_c,
+                              uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info) {
   if (m == 0 || n == 0) return cudaSuccess;
-  if (k == 0 || k % 16 != 0) return cudaErrorNotSupported;
+  // TMA needs 16-byte aligned bases and row strides; the epilogue's vector
+  // stores need a 16-byte aligned C. K tails are zero-filled by TMA.
+  if (k == 0 || lda % 16 != 0 || ldb % 16 != 0 ||
+      ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+        reinterpret_cast<uintptr_t>(c)) & 15u) != 0)
+    return cudaErrorNotSupported;
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  static const bool pair_on = [] {
+    const char *v = getenv("MCB_GEMM_TC_PAIR");
+    return !(v && v[0] == '0');
+  }();
+  const bool pair = m >= 2 * BM && pair_on && i8_pair_clusters_resident(device) > 0;
+  // B box per CTA: MN-major 128 columns x BK rows; K-major BK bytes x (BN or
+  // BN/2) rows.
+  const int bt_rows = pair ? P_B_COLS : BN;
   CUtensorMap ta, tb;
-  if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, m, k, BK, BM,
-                      CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, bt, k, n, k, BK, BN,
+  if (!encode_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, m, lda, BK, BM,
                       CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorNotSupported;
+  const bool ok_b = b_mn ? encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, n, k, ldb,
+                                          MN_CHUNK, BK, CU_TENSOR_MAP_SWIZZLE_128B)
+                         : encode_tmap_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, k, n, ldb, BK,
+                                          bt_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!ok_b) return cudaErrorNotSupported;
   Params p;
   p.m = m;
   p.n = n;
   p.ld_c = ld_c;
   p.n_tiles = static_cast<int>((n + BN - 1) / BN);
-  const int64_t tiles = ((m + BM - 1) / BM) * p.n_tiles;
+  const int64_t tile_rows = pair ? 2 * BM : BM;
+  const int64_t tiles = ((m + tile_rows - 1) / tile_rows) * p.n_tiles;
   if (tiles > 0x7fffffff) return cudaErrorNotSupported;
   p.num_tiles = static_cast<int>(tiles);
   p.num_kb = static_cast<int>((k + BK - 1) / BK);
+  p.b_mn = b_mn;
   p.c = c;
   p.status = status;
-  const size_t smem = static_cast<size_t>(STAGES) * STAGE_BYTES + 256 + 1024;
-  cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-  gemm_i8_kernel<<<grid, THREADS, smem, stream>>>(ta, tb, p);
+  int grid;
+  if (pair) {
+    int clusters = i8_pair_clusters_resident(device);
+    if (clusters > sms / 2) clusters = sms / 2;
+    if (clusters < 1) clusters = 1;
+    grid = 2 * static_cast<int>(tiles < clusters ? tiles : clusters);
+    gemm_i8_pair_kernel<<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(ta, tb, p);
+  } else {
+    e = cudaFuncSetAttribute(gemm_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    grid = static_cast<int>(tiles < sms ? tiles : sms);
+    gemm_i8_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, p);
+  }
   if (info) {
     info->launches += 1;
-    info->tile_m = BM;
+    info->tile_m = static_cast<int>(tile_rows);
     info->tile_n = BN;
     info->tile_k = BK;
-    info->stages = STAGES;
+    info->stages = pair ? P_STAGES : STAGES;
     info->ctas = grid;
     info->set_route("tcgen05_i8_gemm");
   }

@@ -20,25 +20,50 @@ def _ref_i8(a, b):
     return c
 
 
-@pytest.mark.parametrize("shape,route", [((256, 512, 384), "tcgen05_i8_gemm"),
-                                         ((300, 1024, 520), "tcgen05_i8_gemm"),
-                                         ((129, 48, 264), "tcgen05_i8_gemm"),
-                                         ((200, 80, 208), "tcgen05_i8_gemm"),
-                                         ((1024, 2048, 1024), "tcgen05_i8_gemm"),
-                                         ((77, 100, 33), "simt_i8_gemm")])
-def test_i8_gemm_bit_exact(mcb, orc, shape, route):
+# (shape, route, launches, tile rows): B with 16-byte aligned rows is read
+# MN-major in place (one launch); other B go through a transpose pass (two
+# launches). M >= 256 runs on SM pairs (256-row tiles).
+@pytest.mark.parametrize("shape,route,launches,tile_m", [
+    ((256, 512, 384), "tcgen05_i8_gemm", 1, 256),
+    ((300, 1024, 520), "tcgen05_i8_gemm", 2, 256),
+    ((129, 48, 264), "tcgen05_i8_gemm", 2, 128),
+    ((200, 80, 208), "tcgen05_i8_gemm", 1, 128),
+    ((1024, 2048, 1024), "tcgen05_i8_gemm", 1, 256),
+    ((520, 112, 272), "tcgen05_i8_gemm", 1, 256),
+    ((77, 100, 33), "simt_i8_gemm", 1, None)])
+def test_i8_gemm_bit_exact(mcb, orc, shape, route, launches, tile_m):
     import torch
     m, k, n = shape
     rng = np.random.default_rng(m + k + n)
     a = rng.integers(-128, 128, (m, k), dtype=np.int8)
     b = rng.integers(-128, 128, (k, n), dtype=np.int8)
     c = mcb.gemm_i8_i32(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda())
-    assert mcb.api.last_result.route == route
+    r = mcb.api.last_result
+    assert r.route == route and r.kernel_launches == launches
+    if tile_m is not None:
+        assert r.tile[0] == tile_m
     got = c.cpu().numpy()
     assert np.array_equal(got, orc.gemm_i8_i32(a, b))
     ref = _ref_i8(a, b)
     if ref is not None:
         assert np.array_equal(got, ref)
+
+
+@pytest.mark.parametrize("ldb,launches", [(400, 1), (344, 2)])
+def test_i8_gemm_strided_operands(mcb, orc, ldb, launches):
+    """Row-strided A and B views: an aligned B stride is read in place, an
+    unaligned one is transposed first; both stay bit-exact."""
+    import torch
+    m, k, n = 300, 144, 336
+    rng = np.random.default_rng(ldb)
+    a_big = rng.integers(-128, 128, (m, 160), dtype=np.int8)
+    b_big = rng.integers(-128, 128, (k, ldb), dtype=np.int8)
+    a, b = a_big[:, :k], b_big[:, :n]
+    c = mcb.gemm_i8_i32(torch.from_numpy(a_big).cuda()[:, :k], torch.from_numpy(b_big).cuda()[:, :n])
+    r = mcb.api.last_result
+    assert r.route == "tcgen05_i8_gemm" and r.kernel_launches == launches
+    assert np.array_equal(c.cpu().numpy(), orc.gemm_i8_i32(np.ascontiguousarray(a),
+                                                           np.ascontiguousarray(b)))
 
 
 def test_i8_gemm_wraps_modulo_2_32(mcb, orc):
