@@ -17,6 +17,13 @@
  *    memory (MCB_MEMORY_CUDA_DEVICE: the call is asynchronous on the stream
  *    unless MCB_EXEC_SYNC is set). All operands of one call must live in the
  *    same memory space.
+ *  - Scratch: an entry point that needs device scratch for intermediates
+ *    uses mcb_exec.workspace when it holds enough bytes at a 16-byte aligned
+ *    base; otherwise it allocates stream-ordered from a memory pool the
+ *    library owns on that device (released on the stream when the call ends;
+ *    the pool keeps up to 4 GiB reserved between calls), so device-resident
+ *    calls stay asynchronous either way. Only if that allocation fails does
+ *    the call fall back to a shared staging buffer and synchronise.
  *  - Layout: dims and strides are in elements, row-major, innermost stride 1.
  *  - Errors: all failures return a status; nothing throws across this
  *    boundary. Device-side pipeline stalls are bounded: a kernel that waits
@@ -238,8 +245,8 @@ MCB_API mcb_status mcb_gemm_epilogue_v1(const mcb_tensor *y, const mcb_tensor *x
  * [M,N1] or row bias [N1], added or reverse-subtracted, then one activation).
  * A [M,K], B [K,N1], W [N1,N2], E [M,N2]. The glue is fused into the first
  * GEMM's epilogue; the intermediate (bf16 for bf16 operands, f32 for f32) is
- * kept in device scratch (the caller's workspace when it holds M*N1 elements,
- * else a library staging buffer) and consumed by the second GEMM. bf16 runs on
+ * kept in device scratch (M*N1 elements; see Scratch above) and consumed by
+ * the second GEMM. bf16 runs on
  * tcgen05, f32 on CUDA cores. Replaces the leaf emitted by
  * FusionMlirEmitter::emitFamilyB (src/fusion_emitter_family_b.cpp:12-408). */
 MCB_API mcb_status mcb_gemm_chain_v1(const mcb_tensor *e, const mcb_tensor *a,
@@ -300,8 +307,8 @@ MCB_API mcb_status mcb_block_attn_res_v1(const mcb_tensor *out, const mcb_tensor
 /* ---- attention-residual block region ------------------------------------------- */
 /* Y = RMSNorm(X + Wo * MSM(X Wq, X Wk, X Wv)) with unit gain; X [B,S,D] bf16,
  * W* [D,D] bf16, `heads` heads of D/heads, softmax scale (D/heads)^-0.5.
- * Composed from the kernels above with device-resident intermediates in the
- * caller's workspace (mcb_attn_block_workspace_bytes_v1). Named after the
+ * Composed from the kernels above with device-resident intermediates in
+ * scratch of mcb_attn_block_workspace_bytes_v1 bytes (see Scratch above). Named after the
  * region path of RegionMlirEmitter (src/region_emitter_block_attn_res.cpp:38-432). */
 MCB_API uint64_t mcb_attn_block_workspace_bytes_v1(int64_t batch, int64_t seq,
                                                    int64_t d_model) MCB_NOEXCEPT;

@@ -95,7 +95,6 @@ constexpr int kMaxDevices = 64;
 constexpr int kStageSlots = 8;
 // Strict pairs with at least this many intermediate elements (M*N) run as two
 // tiled GEMMs; smaller ones as one fused kernel (launch-bound either way).
-constexpr int64_t kStrictTwoPassMinElems = 16384;
 
 // Lazily created per-device state: SM count, the device status word and the
 // grow-only staging buffers used for host-resident operands.
@@ -113,7 +112,15 @@ struct DeviceCtx {
   // against the compute stream with events from this pool.
   cudaStream_t copy_in = nullptr, copy_out = nullptr;
   std::vector<cudaEvent_t> events;
+  // Stream-ordered scratch (kernel intermediates of calls without a large
+  // enough workspace): a pool owned by this library, so its retention setting
+  // touches no other allocator in the process. Created on first use.
+  std::once_flag pool_once;
+  cudaMemPool_t pool = nullptr;
 };
+// Bytes the scratch pool keeps reserved across synchronisations, so repeated
+// calls reuse mapped memory instead of mapping it again.
+constexpr uint64_t kPoolKeepBytes = 4ull << 30;
 DeviceCtx g_dev[kMaxDevices];
 
 // Restores the caller's current device on scope exit.
@@ -262,6 +269,7 @@ class Call {
  public:
   explicit Call(const mcb_exec *exec) : exec_(exec) {}
   ~Call() {
+    release_pooled();
     for (auto &e : events_)
       if (e) cudaEventDestroy(e);
     if (lock_.owns_lock()) lock_.unlock();
@@ -324,14 +332,48 @@ class Call {
     return MCB_STATUS_OK;
   }
 
-  // Device scratch for a kernel: the caller's workspace when it is large
-  // enough, else a staging slot. A staging slot is shared by later calls on
-  // this device, so using one forces this call to synchronise before return.
-  mcb_status scratch(uint64_t bytes, void **out) {
-    if (exec_ && exec_->workspace && exec_->workspace_bytes >= bytes) {
+  // Device scratch that keeps the call asynchronous: the caller's workspace
+  // when it holds `bytes` at a 16-byte aligned base, else a stream-ordered
+  // allocation from the library's pool on this device, released on the
+  // call's stream when the call finishes. False when neither is available.
+  bool stream_scratch(uint64_t bytes, void **out) {
+    if (exec_ && exec_->workspace && exec_->workspace_bytes >= bytes &&
+        (reinterpret_cast<uintptr_t>(exec_->workspace) & 15u) == 0) {
       *out = exec_->workspace;
-      return MCB_STATUS_OK;
+      return true;
     }
+    if (n_pooled_ == kMaxPooled) return false;
+    std::call_once(ctx_->pool_once, [this] {
+      cudaMemPoolProps props = {};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.handleTypes = cudaMemHandleTypeNone;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev_;
+      cudaMemPool_t pool = nullptr;
+      if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return;
+      }
+      uint64_t keep = kPoolKeepBytes;
+      (void)cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+      ctx_->pool = pool;
+    });
+    if (!ctx_->pool) return false;
+    void *p = nullptr;
+    if (cudaMallocFromPoolAsync(&p, bytes ? bytes : 1, ctx_->pool, stream_) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return false;
+    }
+    pooled_[n_pooled_++] = p;
+    *out = p;
+    return true;
+  }
+
+  // Device scratch for a kernel: stream_scratch when it succeeds, else a
+  // staging slot. A staging slot is shared by later calls on this device, so
+  // using one forces this call to synchronise before return.
+  mcb_status scratch(uint64_t bytes, void **out) {
+    if (stream_scratch(bytes, out)) return MCB_STATUS_OK;
     if (!lock_.owns_lock()) lock_ = std::unique_lock<std::mutex>(ctx_->mu);
     sync_ = true;
     mcb_tensor tmp{};
@@ -372,6 +414,7 @@ class Call {
       }
     }
     if (timed_) cudaEventRecord(events_[3], stream_);
+    if (release_pooled() != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
     uint32_t word = 0;
     if (sync_) {
       cudaError_t e = cudaStreamSynchronize(stream_);
@@ -493,6 +536,17 @@ class Call {
   const mcb_exec *exec() const { return exec_; }
 
  private:
+  // Returns this call's pool allocations to the pool, in stream order after
+  // everything the call enqueued.
+  cudaError_t release_pooled() {
+    cudaError_t err = cudaSuccess;
+    for (int i = 0; i < n_pooled_; ++i) {
+      const cudaError_t e = cudaFreeAsync(pooled_[i], stream_);
+      if (err == cudaSuccess) err = e;
+    }
+    n_pooled_ = 0;
+    return err;
+  }
   // Bytes of rows [r0, r1) of a rank-2 tensor, its own columns only.
   static uint64_t row_bytes(const mcb_tensor *t, int64_t r0, int64_t r1) {
     return static_cast<uint64_t>(r1 - r0) * static_cast<uint64_t>(t->dims[1]) *
@@ -542,6 +596,9 @@ class Call {
   std::unique_lock<std::mutex> lock_;
   cudaEvent_t events_[4] = {};
   int slot_ = 0;
+  static constexpr int kMaxPooled = 4;
+  void *pooled_[kMaxPooled] = {};
+  int n_pooled_ = 0;
   uint64_t h2d_bytes_ = 0, d2h_bytes_ = 0;
 };
 
@@ -617,24 +674,13 @@ mcb_status strict_pair_impl(const mcb_tensor *e, const mcb_tensor *a, const mcb_
       (s = call.device_ptr(d, true, &dd)) || (s = call.device_ptr(e, false, &de)))
     return s;
   // Two tiled strict GEMMs through a binary32 C [M,N] in device memory: the
-  // caller's workspace when it holds C, else a stream-ordered allocation
-  // (cudaMallocAsync / cudaFreeAsync on the call's stream, so the call stays
-  // asynchronous). Small problems, and any allocation failure, take the
-  // single fused kernel below.
-  if (m > 0 && n > 0 && p > 0 && m * n >= kStrictTwoPassMinElems) {
+  // caller's workspace when it holds C, else a stream-ordered allocation, so
+  // the call stays asynchronous. Small problems, and any allocation failure,
+  // take the single fused kernel below.
+  if (m > 0 && n > 0 && p > 0 && m * n >= mcb::kStrictTwoPassMinElems) {
     const uint64_t cbytes = static_cast<uint64_t>(m) * static_cast<uint64_t>(n) * 4;
     void *cbuf = nullptr;
-    bool owned = false;
-    if (exec && exec->workspace && exec->workspace_bytes >= cbytes &&
-        (reinterpret_cast<uintptr_t>(exec->workspace) & 15u) == 0) {
-      cbuf = exec->workspace;
-    } else if (cudaMallocAsync(&cbuf, cbytes, call.stream()) == cudaSuccess) {
-      owned = true;
-    } else {
-      (void)cudaGetLastError();
-      cbuf = nullptr;
-    }
-    if (cbuf) {
+    if (call.stream_scratch(cbytes, &cbuf)) {
       LaunchInfo info;
       call.mark_compute_start();
       cudaError_t err = mcb::launch_strict_pair_two_pass(
@@ -642,10 +688,6 @@ mcb_status strict_pair_impl(const mcb_tensor *e, const mcb_tensor *a, const mcb_
           static_cast<const float *>(dd), static_cast<float *>(de), static_cast<float *>(cbuf),
           m, k, n, p, k ? a->strides[0] : 0, b->strides[0], d->strides[0], e->strides[0],
           call.sms(), call.stream(), &info);
-      if (owned) {
-        const cudaError_t fe = cudaFreeAsync(cbuf, call.stream());
-        if (err == cudaSuccess) err = fe;
-      }
       call.mark_compute_end();
       return call.finish(e, de, info, err);
     }
@@ -830,21 +872,10 @@ mcb_status typed_gemm_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_t
                                    call.ctx()->status, call.sms(), call.stream(), &info);
     } else if (tc && k % 16 == 0) {
       // B rows not 16-byte aligned: transpose into a dense B^T [N,K] scratch
-      // (row stride K) first. The scratch is the caller's workspace when it
-      // holds it, else a stream-ordered allocation, so the call stays
-      // asynchronous.
+      // (row stride K) first.
       const uint64_t bytes = static_cast<uint64_t>(n) * static_cast<uint64_t>(k);
       void *bt = nullptr;
-      bool owned = false;
-      if (exec && exec->workspace && exec->workspace_bytes >= bytes &&
-          (reinterpret_cast<uintptr_t>(exec->workspace) & 15u) == 0) {
-        bt = exec->workspace;
-      } else if (cudaMallocAsync(&bt, bytes, call.stream()) == cudaSuccess) {
-        owned = true;
-      } else {
-        (void)cudaGetLastError();
-        if ((s = call.scratch(bytes, &bt))) return s;
-      }
+      if ((s = call.scratch(bytes, &bt))) return s;
       err = mcb::launch_transpose_u8(db, bt, k, n, ldb, call.stream());
       if (err == cudaSuccess) {
         info.launches = 1;
@@ -852,10 +883,6 @@ mcb_status typed_gemm_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_t
                                      static_cast<const int8_t *>(bt), k, 0,
                                      static_cast<int32_t *>(dc), m, n, k, c->strides[0],
                                      call.ctx()->status, call.sms(), call.stream(), &info);
-      }
-      if (owned) {
-        const cudaError_t fe = cudaFreeAsync(bt, call.stream());
-        if (err == cudaSuccess) err = fe;
       }
     }
     if (err == cudaErrorNotSupported) {

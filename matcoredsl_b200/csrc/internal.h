@@ -100,6 +100,11 @@ cudaError_t launch_gemm_fp8_simt(const uint8_t *a, int a_e5m2, const float *sa,
                                  int c_bf16, int64_t m, int64_t n, int64_t k, int64_t block,
                                  cudaStream_t stream, LaunchInfo *info);
 
+// Strict pairs with M*N at least this many elements run as two tiled
+// launches through a binary32 C [M,N] in device scratch (api.cpp); the plan
+// sizes its workspace by the same rule (plan.cpp).
+constexpr int64_t kStrictTwoPassMinElems = 16384;
+
 // ---- typed.cu: int8 and bf16-fma typed GEMMs -------------------------------------------------
 cudaError_t launch_transpose_u8(const void *in, void *out, int64_t rows, int64_t cols,
                                 int64_t ld_in, cudaStream_t stream);

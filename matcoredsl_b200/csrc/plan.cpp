@@ -15,6 +15,7 @@
 #include <cstring>
 #include <new>
 
+#include "internal.h"
 #include "mcb.h"
 
 struct mcb_plan {
@@ -106,11 +107,15 @@ uint64_t workspace_for(const mcb_plan_desc &d) {
     return static_cast<uint64_t>(a.dims[0]) * ((b.dims[1] + 7) / 8 * 8) * esz;
   }
   if (d.op == MCB_PLAN_STRICT_PAIR) {
-    // Only intermediates too wide for a shared-memory panel (4 rows of N
-    // floats > 227 KiB) need the global scratch panel.
+    // Pairs of M*N >= kStrictTwoPassMinElems keep the binary32 C [M,N]
+    // between their two launches; smaller ones use a shared-memory panel, or
+    // a global panel when 4 rows of N floats exceed 227 KiB. Holding it in
+    // the plan's workspace keeps allocations out of a captured graph.
     const mcb_tensor &a = d.tensors[1], &b = d.tensors[2];
-    if (b.dims[1] * 16 <= 227 * 1024) return 0;
-    return static_cast<uint64_t>(a.dims[0] + 4) * b.dims[1] * 4;
+    const int64_t m = a.dims[0], n = b.dims[1];
+    if (m * n >= mcb::kStrictTwoPassMinElems) return static_cast<uint64_t>(m) * n * 4;
+    if (n * 16 <= 227 * 1024) return 0;
+    return static_cast<uint64_t>(m + 4) * n * 4;
   }
   return 0;
 }
