@@ -72,6 +72,7 @@ struct Params {
   int64_t heads, qblocks, nkv_tiles, units;
   int64_t o_s[3];  // output element strides [batch, head, row]
   float c;         // scale * log2(e)
+  int o_tma;       // two-tile kernel: O leaves through shared memory and a TMA store
   __nv_bfloat16 *o;
   uint32_t *status;
 };
@@ -84,6 +85,27 @@ __device__ __forceinline__ float ex2(float x) {
 
 __device__ __forceinline__ void fence_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// TMA store of one 64-column x 128-row box from shared memory (bulk group of
+// the issuing thread), and the waits on that thread's bulk groups: until
+// their shared-memory reads are done, or until they have fully completed.
+__device__ __forceinline__ void tma_store_4d(const void *tmap, const void *src, int32_t x,
+                                             int32_t y, int32_t z, int32_t w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // K-major SW128 descriptor for the K=16 slice `kk` (0..7) of a 128x128 bf16
@@ -106,13 +128,17 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const void *tmap, uint64_
       : "memory");
 }
 
+// (batch, head, query block) of work unit u. 32-bit arithmetic (the launcher
+// keeps units below 2^31): 64-bit division is a long software sequence that
+// sat on the path between two units.
 __device__ __forceinline__ void unit_coords(const Params &p, int64_t u, int32_t &b, int32_t &h,
-                                            int32_t &q0) {
-  const int64_t qb = u % p.qblocks;
-  const int64_t bh = u / p.qblocks;
-  h = static_cast<int32_t>(bh % p.heads);
-  b = static_cast<int32_t>(bh / p.heads);
-  q0 = static_cast<int32_t>(qb * BQ);
+                                            int32_t &qb) {
+  const uint32_t uu = static_cast<uint32_t>(u), nqb = static_cast<uint32_t>(p.qblocks);
+  const uint32_t nh = static_cast<uint32_t>(p.heads);
+  const uint32_t bh = uu / nqb, bb = bh / nh;
+  qb = static_cast<int32_t>(uu - bh * nqb);
+  h = static_cast<int32_t>(bh - bb * nh);
+  b = static_cast<int32_t>(bb);
 }
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -169,6 +195,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int64_t u = blockIdx.x; u < p.units; u += gridDim.x, ++uc) {
         int32_t b, h, q0;
         unit_coords(p, u, b, h, q0);
+        q0 *= BQ;
         if (!mbar_wait(&sm.q_empty, (uc & 1) ^ 1, abort_flag, p.status, kErrTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&sm.q_full, TILE_BYTES);
         tma_load_4d(sm.q, &tq, &sm.q_full, 0, q0, h, b);
@@ -265,6 +292,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uc) {
       int32_t b, h, q0;
       unit_coords(p, u, b, h, q0);
+      q0 *= BQ;
       float m_ref = -INFINITY, l = 0.0f;
       for (int64_t t = 0; t < nkv; ++t) {
         const int sb = s_cnt & 1;
@@ -404,6 +432,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 // S(j) into registers, then PV0(j), PV1(j) once P(j) is written, so the
 // tensor core computes the next scores while both warpgroups exponentiate.
 // The softmax arithmetic uses packed f32x2 FMA/ADD and three-input max.
+// At the end of a unit each warpgroup stages its normalised O tile in its P
+// buffer (free once the last PV has completed) and one thread writes it with
+// a TMA store, so the next unit's first scores are not held up by 128
+// threads' row-wise global stores.
 constexpr int NQ = 2;
 constexpr int UNIT_ROWS = NQ * BQ;
 constexpr int KV_STAGES = 3;
@@ -418,6 +450,7 @@ struct Smem2 {
   uint64_t s_full[NQ], s_free[NQ];
   uint64_t p_full[NQ], p_free[NQ];
   uint64_t o_full[NQ], o_empty[NQ];
+  uint64_t o_staged[NQ], o_read[NQ];  // O staged in P_g; P_g read by the O store
   uint64_t drain;
   uint32_t tmem_slot;
   int abort_flag;
@@ -428,7 +461,8 @@ static_assert(SMEM2_BYTES <= 232448, "two-tile MSM exceeds the opt-in shared mem
 __global__ void __launch_bounds__(THREADS2, 1)
     msm_tc2_bf16_kernel(const __grid_constant__ CUtensorMap tq,
                         const __grid_constant__ CUtensorMap tk,
-                        const __grid_constant__ CUtensorMap tv, const Params p) {
+                        const __grid_constant__ CUtensorMap tv,
+                        const __grid_constant__ CUtensorMap to, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   Smem2 &sm = *reinterpret_cast<Smem2 *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -449,6 +483,8 @@ __global__ void __launch_bounds__(THREADS2, 1)
       mbar_init(&sm.p_free[g], 1);
       mbar_init(&sm.o_full[g], 1);
       mbar_init(&sm.o_empty[g], 128);
+      mbar_init(&sm.o_staged[g], 128);
+      mbar_init(&sm.o_read[g], 1);
     }
     mbar_init(&sm.drain, 1);
     sm.abort_flag = 0;
@@ -458,6 +494,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
     tma_prefetch_desc(&tq);
     tma_prefetch_desc(&tk);
     tma_prefetch_desc(&tv);
+    if (p.o_tma) tma_prefetch_desc(&to);
   }
   if (warp == 1) {
     tmem_alloc(&sm.tmem_slot, TMEM_COLS);
@@ -488,7 +525,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
       for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uc) {
         int32_t b, h, q0;
         unit_coords(p, u, b, h, q0);
-        q0 = static_cast<int32_t>((u % p.qblocks) * UNIT_ROWS);
+        q0 *= UNIT_ROWS;
         if (!mbar_wait(&sm.q_empty, (uc & 1) ^ 1, abort_flag, p.status, kErrTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&sm.q_full, NQ * TILE_BYTES);
         for (int g = 0; g < NQ; ++g) {
@@ -555,6 +592,9 @@ __global__ void __launch_bounds__(THREADS2, 1)
             mma_f16_ss(tmem + O_COL + g * D, kmajor_desc(p_addr, kk), mnmajor_desc(v_addr, kk),
                        idesc_o, (t | kk) ? 1u : 0u);
           mma_commit(&sm.p_free[g]);
+          // Query tile g's output is final after its last PV: its epilogue
+          // need not wait for the other tile's.
+          if (t + 1 == nkv) mma_commit(&sm.o_full[g]);
         }
         mma_commit(&sm.kv_empty[s]);
         ++kvc;
@@ -574,7 +614,6 @@ __global__ void __launch_bounds__(THREADS2, 1)
           if (!(ok = pv_round(t))) break;
         }
         if (!ok) break;
-        for (int g = 0; g < NQ; ++g) mma_commit(&sm.o_full[g]);
       }
       mma_commit(&sm.drain);
       if (!mbar_wait(&sm.drain, 0, nullptr, p.status, kErrTimeoutDrain)) *abort_flag = 1;
@@ -588,12 +627,13 @@ __global__ void __launch_bounds__(THREADS2, 1)
     const uint32_t s_col = S_COL0 + g * BKV, o_col = O_COL + g * D;
     uint8_t *p_row = sm.p[g] + row * 128;
     const int rsw = row & 7;
+    const bool leader = (threadIdx.x & 127) == 0;  // issues this warpgroup's O stores
     uint32_t s_cnt = 0, p_cnt = 0, uc = 0;
     bool ok = true;
     for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uc) {
       int32_t b, h, q0;
       unit_coords(p, u, b, h, q0);
-      q0 = static_cast<int32_t>((u % p.qblocks) * UNIT_ROWS + g * BQ);
+      q0 = q0 * UNIT_ROWS + g * BQ;
       float m_ref = -INFINITY, l = 0.0f;
       for (int64_t t = 0; t < nkv; ++t) {
         if (!(ok = mbar_wait_warp(&sm.s_full[g], s_cnt & 1, abort_flag, p.status,
@@ -683,6 +723,17 @@ __global__ void __launch_bounds__(THREADS2, 1)
         if (!(ok = mbar_wait_warp(&sm.p_free[g], (p_cnt & 1) ^ 1, abort_flag, p.status,
                                   kErrTimeoutAccum)))
           break;
+        // At a unit's first tile P_g may still be the source of the previous
+        // unit's O store.
+        if (t == 0 && uc > 0 && p.o_tma) {
+          if (leader) {
+            bulk_wait_read_all();
+            mbar_arrive(&sm.o_read[g]);
+          }
+          if (!(ok = mbar_wait_warp(&sm.o_read[g], (uc - 1) & 1, abort_flag, p.status,
+                                    kErrTimeoutAccum)))
+            break;
+        }
 #pragma unroll
         for (int u16 = 0; u16 < 16; ++u16) {
           const int chunk = u16 >> 3, j = u16 & 7;
@@ -699,26 +750,63 @@ __global__ void __launch_bounds__(THREADS2, 1)
         break;
       tc_fence_after();
       const float inv = 1.0f / l;
-      __nv_bfloat16 *orow =
-          p.o + b * p.o_s[0] + h * p.o_s[1] + static_cast<int64_t>(q0 + row) * p.o_s[2];
+      if (p.o_tma) {
+        // Stage the tile in P_g (free: the last PV_g has completed) in the
+        // 128-byte-swizzled layout of the TMA box, then one thread stores it.
+        // Coalescing through TMA keeps the per-row 16-byte stores of 128
+        // threads off the load/store unit between two work units.
 #pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t o[32];
-        tmem_ld32_sync(lane_base + o_col + c0, o);
-        uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32_sync(lane_base + o_col + c0, o);
+          uint8_t *dst = p_row + (c0 >> 6) * CHUNK_BYTES;
+          const int j0 = (c0 & 63) >> 3;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(o[q * 8 + 0]) * inv, __uint_as_float(o[q * 8 + 1]) * inv);
-          w.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv, __uint_as_float(o[q * 8 + 3]) * inv);
-          w.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv, __uint_as_float(o[q * 8 + 5]) * inv);
-          w.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv, __uint_as_float(o[q * 8 + 7]) * inv);
-          dst[q] = w;
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(o[q * 8 + 0]) * inv, __uint_as_float(o[q * 8 + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv, __uint_as_float(o[q * 8 + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv, __uint_as_float(o[q * 8 + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv, __uint_as_float(o[q * 8 + 7]) * inv);
+            *reinterpret_cast<uint4 *>(dst + (((j0 + q) ^ rsw) << 4)) = w;
+          }
         }
+        fence_async_smem();
+        mbar_arrive(&sm.o_staged[g]);
+        tc_fence_before();
+        mbar_arrive(&sm.o_empty[g]);
+        if (leader) {
+          if (!(ok = mbar_wait(&sm.o_staged[g], uc & 1, abort_flag, p.status, kErrTimeoutAccum)))
+            break;
+          tma_store_4d(&to, sm.p[g], 0, q0, h, b);
+          tma_store_4d(&to, sm.p[g] + CHUNK_BYTES, 64, q0, h, b);
+          bulk_commit();
+        }
+      } else {
+        __nv_bfloat16 *orow =
+            p.o + b * p.o_s[0] + h * p.o_s[1] + static_cast<int64_t>(q0 + row) * p.o_s[2];
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32_sync(lane_base + o_col + c0, o);
+          uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(o[q * 8 + 0]) * inv, __uint_as_float(o[q * 8 + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv, __uint_as_float(o[q * 8 + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv, __uint_as_float(o[q * 8 + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv, __uint_as_float(o[q * 8 + 7]) * inv);
+            dst[q] = w;
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&sm.o_empty[g]);
       }
-      tc_fence_before();
-      mbar_arrive(&sm.o_empty[g]);
     }
+    // Outstanding O stores must finish reading shared memory (and land)
+    // before the block exits.
+    if (p.o_tma && leader) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -750,14 +838,21 @@ cudaError_t launch_msm_tc_bf16(const void *q, const void *k, const void *v, void
   // cudaErrorNotSupported (nothing launched) lets the caller take another kernel.
   if (!enc(&tq, q, s.m, s.q_s) || !enc(&tk, k, s.n, s.k_s) || !enc(&tv, v, s.n, s.v_s))
     return cudaErrorNotSupported;
-  // Query blocks of 256 rows run two tiles per CTA; otherwise one.
+  // Query blocks of 256 rows run two tiles per CTA; otherwise one. The
+  // two-tile kernel stores O by TMA when O's layout can be described by a
+  // tensor map (16-byte aligned base and strides), else with plain stores.
   const bool two = s.m % UNIT_ROWS == 0;
+  CUtensorMap to;
+  const bool o_tma = two && enc(&to, o, s.m, s.o_s);
+  if (!o_tma) to = tq;  // unused by the kernel
   Params p;
   p.heads = s.heads;
   p.qblocks = s.m / (two ? UNIT_ROWS : BQ);
   p.nkv_tiles = s.n / BKV;
   p.units = s.batch * s.heads * p.qblocks;
+  if (p.units > 0x7fffffff) return cudaErrorNotSupported;  // unit indices are 32-bit
   for (int i = 0; i < 3; ++i) p.o_s[i] = s.o_s[i];
+  p.o_tma = o_tma ? 1 : 0;
   p.c = scale * 1.4426950408889634f;
   p.o = static_cast<__nv_bfloat16 *>(o);
   p.status = status;
@@ -767,7 +862,7 @@ cudaError_t launch_msm_tc_bf16(const void *q, const void *k, const void *v, void
     e = cudaFuncSetAttribute(msm_tc2_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(SMEM2_BYTES));
     if (e != cudaSuccess) return e;
-    msm_tc2_bf16_kernel<<<grid, THREADS2, SMEM2_BYTES, stream>>>(tq, tk, tv, p);
+    msm_tc2_bf16_kernel<<<grid, THREADS2, SMEM2_BYTES, stream>>>(tq, tk, tv, to, p);
   } else {
     e = cudaFuncSetAttribute(msm_tc_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(SMEM_BYTES));
