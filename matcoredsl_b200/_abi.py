@@ -179,16 +179,19 @@ def load() -> ctypes.CDLL:
     return lib
 
 
+_TENSOR_SIZE = ctypes.sizeof(Tensor)
+
+
 def make_tensor(ptr: int, dtype: str, shape, strides, device: bool) -> Tensor:
     t = Tensor()
     t.abi_version = ABI_VERSION
-    t.struct_size = ctypes.sizeof(Tensor)
+    t.struct_size = _TENSOR_SIZE
     t.data = ptr
     t.dtype = DTYPE[dtype]
-    t.rank = len(shape)
-    for i, (d, s) in enumerate(zip(shape, strides)):
-        t.dims[i] = int(d)
-        t.strides[i] = int(s)
+    r = len(shape)
+    t.rank = r
+    t.dims[:r] = [int(d) for d in shape]
+    t.strides[:r] = [int(s) for s in strides]
     t.memory_space = MEM_DEVICE if device else MEM_HOST
     return t
 

@@ -44,16 +44,27 @@ def _is_torch(x) -> bool:
     return type(x).__module__.startswith("torch")
 
 
+_TORCH_DTYPE = None  # torch dtype -> ABI dtype name, built on first use
+
+
+def _torch_dtype_names():
+    global _TORCH_DTYPE
+    if _TORCH_DTYPE is None:
+        torch = _torch()
+        _TORCH_DTYPE = {torch.float32: "f32", torch.bfloat16: "bf16", torch.float16: "f16",
+                        torch.int8: "i8", torch.int32: "i32", torch.float64: "f64",
+                        torch.float8_e4m3fn: "e4m3", torch.float8_e5m2: "e5m2"}
+    return _TORCH_DTYPE
+
+
 def _desc(x, what: str):
     """(Tensor descriptor, is_device) for a numpy array or a torch tensor."""
     if _is_torch(x):
-        torch = _torch()
-        tmap = {torch.float32: "f32", torch.bfloat16: "bf16", torch.float16: "f16",
-                torch.int8: "i8", torch.int32: "i32", torch.float64: "f64",
-                torch.float8_e4m3fn: "e4m3", torch.float8_e5m2: "e5m2"}
-        if x.dtype not in tmap:
+        name = _torch_dtype_names().get(x.dtype)
+        if name is None:
             raise TypeError(f"{what}: unsupported torch dtype {x.dtype}")
-        return _abi.make_tensor(x.data_ptr(), tmap[x.dtype], x.shape, x.stride(), x.is_cuda), x.is_cuda
+        dev = x.is_cuda
+        return _abi.make_tensor(x.data_ptr(), name, x.shape, x.stride(), dev), dev
     if isinstance(x, np.ndarray):
         dt = _NP_DTYPE.get(x.dtype)
         if dt is None:
@@ -67,9 +78,12 @@ def _exec(device_call: bool, device: int, flags: int, report):
     stream = 0
     if device_call:
         torch = _torch()
-        stream = torch.cuda.current_stream().cuda_stream
         if device < 0:
             device = torch.cuda.current_device()
+        # The raw handle of torch's current stream; building a Stream object
+        # (torch.cuda.current_stream()) costs several microseconds per call.
+        raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+        stream = raw(device) if raw is not None else torch.cuda.current_stream(device).cuda_stream
     return _abi.make_exec(device=device, stream=stream, flags=flags, report=report)
 
 
