@@ -74,7 +74,17 @@ def _desc(x, what: str):
     raise TypeError(f"{what}: expected a numpy array or torch tensor, got {type(x)}")
 
 
-def _exec(device_call: bool, device: int, flags: int, report):
+def _workspace(ws):
+    """(pointer, bytes) of an optional caller workspace: a device tensor
+    whose storage the library may use as scratch for the call."""
+    if ws is None:
+        return 0, 0
+    if not (_is_torch(ws) and ws.is_cuda):
+        raise TypeError("workspace: expected a CUDA tensor")
+    return ws.data_ptr(), ws.numel() * ws.element_size()
+
+
+def _exec(device_call: bool, device: int, flags: int, report, workspace=None):
     stream = 0
     if device_call:
         torch = _torch()
@@ -84,7 +94,9 @@ def _exec(device_call: bool, device: int, flags: int, report):
         # (torch.cuda.current_stream()) costs several microseconds per call.
         raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
         stream = raw(device) if raw is not None else torch.cuda.current_stream(device).cuda_stream
-    return _abi.make_exec(device=device, stream=stream, flags=flags, report=report)
+    ws_ptr, ws_bytes = _workspace(workspace)
+    return _abi.make_exec(device=device, stream=stream, flags=flags, report=report,
+                          workspace=ws_ptr, workspace_bytes=ws_bytes)
 
 
 def _empty_like_out(ref, shape, dtype_name):
@@ -114,7 +126,7 @@ class Result:
 last_result: Result | None = None
 
 
-def _call(fn_name, tensors, extra_args, device=-1, flags=0):
+def _call(fn_name, tensors, extra_args, device=-1, flags=0, workspace=None):
     global last_result
     lib = _abi.load()
     descs, spaces = [], set()
@@ -127,7 +139,7 @@ def _call(fn_name, tensors, extra_args, device=-1, flags=0):
         spaces.add(dev)
     device_call = True in spaces
     rep = _abi.make_report()
-    ex = _exec(device_call, device, flags, rep)
+    ex = _exec(device_call, device, flags, rep, workspace)
     ptrs = [ctypes.byref(d) if d is not None else None for d in descs]
     # Every entry point is fn(tensor..., extra..., exec).
     code = getattr(lib, fn_name)(*ptrs, *extra_args, ctypes.byref(ex))
@@ -144,15 +156,17 @@ def strict_gemm(a, b, out=None, *, device=-1, flags=0):
     return out
 
 
-def gemm_i8_i32(a, b, out=None, *, device=-1, flags=0):
-    """C = A @ B for int8 operands, int32 result modulo 2^32 (bit-exact)."""
+def gemm_i8_i32(a, b, out=None, *, device=-1, flags=0, workspace=None):
+    """C = A @ B for int8 operands, int32 result modulo 2^32 (bit-exact).
+    `workspace` (optional CUDA tensor) holds the B^T copy that B rows which
+    are not 16-byte aligned need."""
     if out is None:
         if _is_torch(a):
             torch = _torch()
             out = torch.empty(a.shape[0], b.shape[1], dtype=torch.int32, device=a.device)
         else:
             out = np.empty((a.shape[0], b.shape[1]), np.int32)
-    _call("mcb_gemm_i8_i32_v1", [("c", out), ("a", a), ("b", b)], [], device, flags)
+    _call("mcb_gemm_i8_i32_v1", [("c", out), ("a", a), ("b", b)], [], device, flags, workspace)
     return out
 
 
@@ -165,11 +179,13 @@ def gemm_bf16_f32_fma(a, b, out=None, *, device=-1, flags=0):
 
 
 def strict_fused_pair(a, b, d, out=None, *, device=-1, flags=0, workspace=None):
-    """E = (A @ B) @ D, strict f32, intermediate rounded to f32 (bit-exact)."""
+    """E = (A @ B) @ D, strict f32, intermediate rounded to f32 (bit-exact).
+    `workspace` (optional CUDA tensor) holds the intermediate C when it is
+    large enough; otherwise the library allocates stream-ordered scratch."""
     if out is None:
         out = _empty_like_out(a, (a.shape[0], d.shape[1]), "f32")
     _call("mcb_strict_fused_pair_f32_v1", [("e", out), ("a", a), ("b", b), ("d", d)], [],
-          device, flags)
+          device, flags, workspace)
     return out
 
 
@@ -192,7 +208,7 @@ def gemm_epilogue(x, w, bias=None, *, bias_mode=None, bias_op="add", act="none",
 
 
 def gemm_chain(a, b, w, boundary=None, *, bias_mode=None, bias_op="add", act="none", out=None,
-               out_dtype=None, device=-1, flags=0):
+               out_dtype=None, device=-1, flags=0, workspace=None):
     """E = glue(A @ B) @ W (Family B); glue = act(. (+|r-) boundary)."""
     if bias_mode is None:
         bias_mode = "none" if boundary is None else (
@@ -214,7 +230,7 @@ def gemm_chain(a, b, w, boundary=None, *, bias_mode=None, bias_op="add", act="no
         descs.append(d)
         device_call = device_call or dev
     rep = _abi.make_report()
-    ex = _exec(device_call, device, flags, rep)
+    ex = _exec(device_call, device, flags, rep, workspace)
     ptr = lambda d: ctypes.byref(d) if d is not None else None  # noqa: E731
     code = lib.mcb_gemm_chain_v1(ptr(descs[0]), ptr(descs[1]), ptr(descs[2]), ptr(descs[3]),
                                  ctypes.byref(ep), ptr(descs[4]), ctypes.byref(ex))
@@ -274,14 +290,17 @@ def block_attn_res(blocks, partial, query, *, block_count, has_partial=True, eps
     return out
 
 
-def attn_block(x, wq, wk, wv, wo, heads, eps=1e-6, out=None, *, device=-1, flags=0):
+def attn_block(x, wq, wk, wv, wo, heads, eps=1e-6, out=None, *, device=-1, flags=0,
+               workspace=None):
     """Y = RMSNorm(X + MSM(X Wq, X Wk, X Wv) Wo), unit gain, softmax scale
-    (D/heads)^-0.5; X [B, S, D] bf16, W* [D, D] bf16."""
+    (D/heads)^-0.5; X [B, S, D] bf16, W* [D, D] bf16. `workspace` (optional
+    CUDA tensor of at least mcb_attn_block_workspace_bytes_v1 bytes) holds
+    the intermediates."""
     if out is None:
         out = _empty_like_out(x, tuple(x.shape), "bf16")
     _call("mcb_attn_block_region_v1",
           [("y", out), ("x", x), ("wq", wq), ("wk", wk), ("wv", wv), ("wo", wo)],
-          [int(heads), float(eps)], device, flags)
+          [int(heads), float(eps)], device, flags, workspace)
     return out
 
 

@@ -580,6 +580,117 @@ __global__ void __launch_bounds__(128) gemm_bf16_fma_tiled_kernel(
   }
 }
 
+// Large-problem bf16 x bf16 -> f32 fma GEMM, same chains (one fmaf per k in
+// increasing order from +0 per output, bf16 widened exactly), laid out like an
+// SGEMM: 256 threads own a 128x128 tile, each thread 8x8 chains (rows
+// 4*ty.. and 64+4*ty.., columns 4*tx.. and 64+4*tx..). 16-deep k-slices of A
+// (stored transposed, [k][row]) and B ([k][col]) are widened to f32 once, when
+// they are written to shared memory (two buffers; the next slice is fetched
+// into registers while the current one is consumed), and read back with four
+// 16-byte loads per 64 fmas. A k-slice past K is never multiplied (0*Inf
+// would be NaN where the reference has no term): the last slice runs only
+// its real depth. Rows must be 16-byte aligned (K, N and both row strides
+// multiples of 8).
+constexpr int GBM = 128, GBN = 128, GBK = 16, GPAD = 4;
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+__global__ void __launch_bounds__(256) gemm_bf16_fma_big_kernel(
+    const __nv_bfloat16 *__restrict__ a, const __nv_bfloat16 *__restrict__ b,
+    float *__restrict__ c, int64_t m, int64_t n, int64_t k, int64_t lda, int64_t ldb,
+    int64_t ldc) {
+  __shared__ __align__(16) float as[2][GBK][GBM + GPAD];
+  __shared__ __align__(16) float bs[2][GBK][GBN + GPAD];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.y) * GBM;
+  const int64_t col0 = static_cast<int64_t>(blockIdx.x) * GBN;
+  // Staging roles: A row (tid & 127), k-half (tid >> 7); B k-row (tid >> 4),
+  // 8-column group (tid & 15). One 16-byte global load each per slice.
+  const int a_r = tid & 127, a_kh = (tid >> 7) * 8;
+  const int b_k = tid >> 4, b_c = (tid & 15) * 8;
+  const int64_t nslices = (k + GBK - 1) / GBK;
+  uint4 ra = make_uint4(0, 0, 0, 0), rb = make_uint4(0, 0, 0, 0);
+  auto fetch = [&](int64_t sl) {
+    const int64_t h0 = sl * GBK;
+    const int64_t ar = row0 + a_r, ak = h0 + a_kh;
+    ra = (ar < m && ak < k) ? *reinterpret_cast<const uint4 *>(a + ar * lda + ak)
+                            : make_uint4(0, 0, 0, 0);
+    const int64_t bk = h0 + b_k, bc = col0 + b_c;
+    rb = (bk < k && bc < n) ? *reinterpret_cast<const uint4 *>(b + bk * ldb + bc)
+                            : make_uint4(0, 0, 0, 0);
+  };
+  auto stage = [&](int buf) {
+    float f[8];
+    bf16x8_to_f32(ra, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) as[buf][a_kh + i][a_r] = f[i];
+    bf16x8_to_f32(rb, f);
+    *reinterpret_cast<float4 *>(&bs[buf][b_k][b_c]) = make_float4(f[0], f[1], f[2], f[3]);
+    *reinterpret_cast<float4 *>(&bs[buf][b_k][b_c + 4]) = make_float4(f[4], f[5], f[6], f[7]);
+  };
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+  if (nslices > 0) {
+    fetch(0);
+    stage(0);
+  }
+  __syncthreads();
+  for (int64_t sl = 0; sl < nslices; ++sl) {
+    const int buf = static_cast<int>(sl & 1);
+    if (sl + 1 < nslices) fetch(sl + 1);
+    const int depth = static_cast<int>(k - sl * GBK < GBK ? k - sl * GBK : GBK);
+    auto step = [&](int kk) {
+      const float4 a0 = *reinterpret_cast<const float4 *>(&as[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4 *>(&as[buf][kk][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4 *>(&bs[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4 *>(&bs[buf][kk][64 + tx * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(av[i], bv[j], acc[i][j]);
+    };
+    if (depth == GBK) {
+#pragma unroll
+      for (int kk = 0; kk < GBK; ++kk) step(kk);
+    } else {
+      for (int kk = 0; kk < depth; ++kk) step(kk);
+    }
+    if (sl + 1 < nslices) stage(buf ^ 1);
+    __syncthreads();
+  }
+  const bool vec_out = (ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(c) & 15u) == 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t r = row0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    if (r >= m) continue;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t cc = col0 + h * 64 + tx * 4;
+      float *dst = c + r * ldc + cc;
+      if (vec_out && cc + 4 <= n) {
+        *reinterpret_cast<float4 *>(dst) =
+            make_float4(acc[i][h * 4], acc[i][h * 4 + 1], acc[i][h * 4 + 2], acc[i][h * 4 + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (cc + j < n) dst[j] = acc[i][h * 4 + j];
+      }
+    }
+  }
+}
+
 template <int MR, int NR>
 cudaError_t launch_bf16_fma_tiled(const void *a, const void *b, float *c, int64_t m, int64_t n,
                                   int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
@@ -707,11 +818,21 @@ cudaError_t launch_gemm_bf16_fma(const void *a, const void *b, float *c, int64_t
                    (k == 0 || ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) &
                                15u) == 0);
   if (vec) {
-    // Per-thread block shrinks until a launch has ~2 warps per SM sub-partition.
+    // 128x128 tiles once they fill the GPU; otherwise the per-thread block
+    // shrinks until a launch has ~2 warps per SM sub-partition.
     const int64_t outputs = m * n;
+    const int64_t big_tiles = ((m + GBM - 1) / GBM) * ((n + GBN - 1) / GBN);
     cudaError_t e;
     const char *route;
-    if (outputs / 8 >= 148LL * 4 * 2 * 32 && n >= 64) {
+    if (big_tiles >= 148 && (m + GBM - 1) / GBM <= 65535) {
+      gemm_bf16_fma_big_kernel<<<dim3(static_cast<unsigned>((n + GBN - 1) / GBN),
+                                      static_cast<unsigned>((m + GBM - 1) / GBM)),
+                                 256, 0, stream>>>(static_cast<const __nv_bfloat16 *>(a),
+                                                   static_cast<const __nv_bfloat16 *>(b), c, m,
+                                                   n, k, lda, ldb, ldc);
+      e = cudaGetLastError();
+      route = "simt_bf16_f32_fma_gemm_128x128";
+    } else if (outputs / 8 >= 148LL * 4 * 2 * 32 && n >= 64) {
       e = launch_bf16_fma_tiled<2, 4>(a, b, c, m, n, k, lda, ldb, ldc, stream);
       route = "simt_bf16_f32_fma_gemm_tiled";
     } else {

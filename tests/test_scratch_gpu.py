@@ -1,0 +1,72 @@
+"""GPU: device scratch of calls that need it (the strict pair's binary32 C,
+the int8 B^T copy for unaligned B rows). Without a caller workspace it comes
+from the library's stream-ordered pool and the call stays asynchronous;
+calls queued on two streams at once must each see their own scratch. With a
+workspace the same results come out of the caller's memory."""
+import numpy as np
+import pytest
+
+from tests import reference_cases as rc
+
+pytestmark = pytest.mark.gpu
+
+
+def _pair_inputs(seed, m=320, k=96, n=200, p=72):
+    rng = np.random.default_rng(seed)
+    return (rng.uniform(-1, 1, (m, k)).astype(np.float32),
+            rng.uniform(-1, 1, (k, n)).astype(np.float32),
+            rng.uniform(-1, 1, (n, p)).astype(np.float32))
+
+
+def test_strict_pair_concurrent_streams(mcb, orc):
+    import torch
+    cases = [_pair_inputs(s) for s in range(6)]
+    dev = [[torch.from_numpy(x).cuda() for x in c] for c in cases]
+    outs = [torch.empty(c[0].shape[0], c[2].shape[1], device="cuda") for c in cases]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    torch.cuda.synchronize()
+    for i, (a, b, d) in enumerate(dev):
+        with torch.cuda.stream(streams[i % 2]):
+            for _ in range(3):  # repeated calls reuse the pool's memory
+                mcb.strict_fused_pair(a, b, d, out=outs[i])
+    assert mcb.api.last_result.route == "strict_f32_simt_pair_two_pass"
+    torch.cuda.synchronize()
+    for (a, b, d), e in zip(cases, outs):
+        assert rc.same_bits(e.cpu().numpy(), orc.strict_fused_pair(a, b, d))
+
+
+def test_strict_pair_caller_workspace(mcb, orc):
+    import torch
+    a, b, d = _pair_inputs(11)
+    ws = torch.full((a.shape[0] * b.shape[1],), float("nan"), device="cuda")
+    e = mcb.strict_fused_pair(*(torch.from_numpy(x).cuda() for x in (a, b, d)), workspace=ws)
+    assert mcb.api.last_result.route == "strict_f32_simt_pair_two_pass"
+    assert rc.same_bits(e.cpu().numpy(), orc.strict_fused_pair(a, b, d))
+    # C went through the workspace: it now holds A*B in binary32.
+    assert rc.same_bits(ws.view(a.shape[0], b.shape[1]).cpu().numpy(), orc.strict_gemm(a, b))
+
+
+@pytest.mark.parametrize("use_ws", [False, True])
+def test_i8_transposed_b_scratch(mcb, orc, use_ws):
+    import torch
+    m, k, n, ldb = 300, 144, 336, 344  # B rows of 344 bytes: not 16-byte aligned
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    cases, outs = [], []
+    for s in range(4):
+        rng = np.random.default_rng(100 + s)
+        a = rng.integers(-128, 128, (m, k), dtype=np.int8)
+        b_big = rng.integers(-128, 128, (k, ldb), dtype=np.int8)
+        cases.append((a, b_big))
+    keep = []  # operands and workspaces stay alive until the streams are drained
+    torch.cuda.synchronize()
+    for s, (a, b_big) in enumerate(cases):
+        with torch.cuda.stream(streams[s % 2]):
+            ws = torch.empty(n * k, dtype=torch.int8, device="cuda") if use_ws else None
+            da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b_big).cuda()
+            keep.append((ws, da, db))
+            outs.append(mcb.gemm_i8_i32(da, db[:, :n], workspace=ws))
+        assert mcb.api.last_result.kernel_launches == 2
+    torch.cuda.synchronize()
+    for (a, b_big), c in zip(cases, outs):
+        assert np.array_equal(c.cpu().numpy(),
+                              orc.gemm_i8_i32(a, np.ascontiguousarray(b_big[:, :n])))

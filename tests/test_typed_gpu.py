@@ -90,7 +90,9 @@ def test_i8_gemm_host_operands(mcb, orc):
     ((256, 1000, 300), "simt_bf16_f32_fma_gemm"),      # N % 8 != 0
     ((256, 1000, 304), "simt_bf16_f32_fma_gemm_tiled"),
     ((1030, 72, 520), "simt_bf16_f32_fma_gemm_tiled"),
-    ((700, 264, 1024), "simt_bf16_f32_fma_gemm_tiled")])
+    ((700, 264, 1024), "simt_bf16_f32_fma_gemm_tiled"),
+    ((2048, 64, 1280), "simt_bf16_f32_fma_gemm_128x128"),
+    ((1500, 200, 1608), "simt_bf16_f32_fma_gemm_128x128")])  # edge tiles, K % 16 == 8
 def test_bf16_f32_fma_bit_exact(mcb, orc, shape, route):
     import torch
     from tests import gpu_util as gu
