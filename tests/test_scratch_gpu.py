@@ -70,3 +70,28 @@ def test_i8_transposed_b_scratch(mcb, orc, use_ws):
     for (a, b_big), c in zip(cases, outs):
         assert np.array_equal(c.cpu().numpy(),
                               orc.gemm_i8_i32(a, np.ascontiguousarray(b_big[:, :n])))
+
+
+def test_strict_pair_pool_scratch_captured_in_graph(mcb, orc):
+    """A call whose scratch comes from the pool can be captured into a CUDA
+    graph (the allocation becomes a graph memory node) and replayed."""
+    import torch
+    a, b, d = _pair_inputs(21)
+    da, db, dd = (torch.from_numpy(x).cuda() for x in (a, b, d))
+    e = torch.empty(a.shape[0], d.shape[1], device="cuda")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        mcb.strict_fused_pair(da, db, dd, out=e)  # pool created outside the capture
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        mcb.strict_fused_pair(da, db, dd, out=e)
+    assert mcb.api.last_result.route == "strict_f32_simt_pair_two_pass"
+    e.zero_()
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    assert rc.same_bits(e.cpu().numpy(), orc.strict_fused_pair(a, b, d))
+    del g
