@@ -385,6 +385,30 @@ typedef struct mcb_shard {
 MCB_API mcb_status mcb_shard_plan_v1(uint32_t kind, int64_t total, int64_t group, int64_t align,
                                      int32_t world, int32_t rank, mcb_shard *out) MCB_NOEXCEPT;
 
+/* ---- optional output all-gather (NCCL) -------------------------------------- */
+/* The path needs no collective: each rank computes its shard. A caller that
+ * wants the whole output on every rank gathers the shards with one NCCL
+ * all-gather over NVLink / NVSwitch (the optional step of the multi-GPU
+ * plan; no counterpart in the single-GPU reference). Rank 0 makes an id with
+ * mcb_comm_unique_id_v1 and hands it to the others out of band; every rank
+ * then calls mcb_comm_init_v1 (collective, blocking) on its device.
+ * mcb_allgather_v1 queues on `stream` (a cudaStream_t) the gather of
+ * `bytes_per_rank` bytes from every rank into `recv` in rank order
+ * (world * bytes_per_rank bytes; shards of unequal size are padded by the
+ * caller); `send` may be this rank's slot of `recv`. NCCL is loaded at run
+ * time (the copy already in the process if there is one); without it these
+ * return MCB_STATUS_CANDIDATE_UNAVAILABLE. */
+typedef struct mcb_comm mcb_comm;
+typedef struct mcb_comm_id {
+  char internal[128];
+} mcb_comm_id;
+MCB_API mcb_status mcb_comm_unique_id_v1(mcb_comm_id *out) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_comm_init_v1(const mcb_comm_id *id, int32_t world, int32_t rank,
+                                    int32_t device, mcb_comm **out) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_allgather_v1(mcb_comm *comm, const void *send, void *recv,
+                                    uint64_t bytes_per_rank, void *stream) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_comm_destroy_v1(mcb_comm *comm) MCB_NOEXCEPT;
+
 /* ---- device buffers ------------------------------------------------------- */
 /* Ownership-tracked device memory; mirrors DeviceBufferHandle and the
  * matcore_device_* functions (include/matcore/device_buffer.h:11-53): a
@@ -404,6 +428,14 @@ MCB_API mcb_status mcb_device_upload(mcb_buffer dst, const void *host_src,
                                      uint64_t size_bytes) MCB_NOEXCEPT;
 MCB_API mcb_status mcb_device_download(void *host_dst, mcb_buffer src,
                                        uint64_t size_bytes) MCB_NOEXCEPT;
+/* Stream-ordered upload / download: queued on `stream` (a cudaStream_t, NULL =
+ * the legacy default stream); the call returns at once, and pinned host
+ * memory (cudaHostAlloc / cudaHostRegister) lets the copy overlap device work.
+ * The host buffer must stay valid until the stream reaches the copy. */
+MCB_API mcb_status mcb_device_upload_async(mcb_buffer dst, const void *host_src,
+                                           uint64_t size_bytes, void *stream) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_device_download_async(void *host_dst, mcb_buffer src,
+                                             uint64_t size_bytes, void *stream) MCB_NOEXCEPT;
 MCB_API mcb_status mcb_device_zero(mcb_buffer handle) MCB_NOEXCEPT;
 MCB_API mcb_status mcb_device_zero_raw_on_stream(void *device_ptr, uint64_t size_bytes,
                                                  void *stream) MCB_NOEXCEPT;

@@ -116,6 +116,11 @@ _P = ctypes.POINTER
 _T = _P(Tensor)
 _E = _P(Exec)
 # name -> (restype, argtypes); every function include/mcb.h declares.
+class CommId(ctypes.Structure):
+    """mcb_comm_id: an NCCL unique id (128 opaque bytes)."""
+    _fields_ = [("internal", ctypes.c_uint8 * 128)]  # raw bytes (c_char would stop at NUL)
+
+
 SIGNATURES = {
     "mcb_abi_version": (ctypes.c_uint32, []),
     "mcb_status_message": (ctypes.c_char_p, [ctypes.c_int32]),
@@ -151,6 +156,16 @@ SIGNATURES = {
     "mcb_device_is_valid": (ctypes.c_int32, [Buffer]),
     "mcb_device_upload": (ctypes.c_int32, [Buffer, ctypes.c_void_p, ctypes.c_uint64]),
     "mcb_device_download": (ctypes.c_int32, [ctypes.c_void_p, Buffer, ctypes.c_uint64]),
+    "mcb_device_upload_async": (ctypes.c_int32, [Buffer, ctypes.c_void_p, ctypes.c_uint64,
+                                                 ctypes.c_void_p]),
+    "mcb_device_download_async": (ctypes.c_int32, [ctypes.c_void_p, Buffer, ctypes.c_uint64,
+                                                   ctypes.c_void_p]),
+    "mcb_comm_unique_id_v1": (ctypes.c_int32, [_P(CommId)]),
+    "mcb_comm_init_v1": (ctypes.c_int32, [_P(CommId), ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32, _P(ctypes.c_void_p)]),
+    "mcb_allgather_v1": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                          ctypes.c_uint64, ctypes.c_void_p]),
+    "mcb_comm_destroy_v1": (ctypes.c_int32, [ctypes.c_void_p]),
     "mcb_device_zero": (ctypes.c_int32, [Buffer]),
     "mcb_device_zero_raw_on_stream": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_uint64,
                                                        ctypes.c_void_p]),

@@ -377,6 +377,47 @@ def shard_plan(kind, total, world, rank, *, group=0, align=1):
     return s.begin, s.count, s.kv_begin, s.kv_count
 
 
+class Comm:
+    """NCCL communicator for the optional all-gather of output shards
+    (mcb_comm_*_v1). Rank 0 calls Comm.unique_id() and passes the bytes to the
+    other ranks out of band; every rank then constructs Comm(uid, world, rank,
+    device) (collective)."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        cid = _abi.CommId()
+        _abi.check(_abi.load().mcb_comm_unique_id_v1(ctypes.byref(cid)), "mcb_comm_unique_id_v1")
+        return ctypes.string_at(ctypes.addressof(cid), ctypes.sizeof(cid))
+
+    def __init__(self, uid: bytes, world: int, rank: int, device: int):
+        cid = _abi.CommId()
+        if len(uid) != ctypes.sizeof(cid):
+            raise ValueError("Comm: the id must be the 128 bytes of Comm.unique_id()")
+        ctypes.memmove(ctypes.addressof(cid), uid, ctypes.sizeof(cid))
+        self._h = ctypes.c_void_p()
+        self.world, self.rank, self.device = world, rank, device
+        _abi.check(_abi.load().mcb_comm_init_v1(ctypes.byref(cid), world, rank, device,
+                                                ctypes.byref(self._h)), "mcb_comm_init_v1")
+
+    def allgather(self, send, recv):
+        """Gathers every rank's `send` (a CUDA tensor) into `recv` (world x its
+        bytes, rank order) on torch's current stream."""
+        nbytes = send.numel() * send.element_size()
+        if recv.numel() * recv.element_size() != nbytes * self.world:
+            raise ValueError("allgather: recv must hold world x send bytes")
+        if not (send.is_contiguous() and recv.is_contiguous()):
+            raise ValueError("allgather: send and recv must be contiguous")
+        stream = _exec(True, self.device, 0, None).stream
+        _abi.check(_abi.load().mcb_allgather_v1(self._h, send.data_ptr(), recv.data_ptr(), nbytes,
+                                                stream), "mcb_allgather_v1")
+        return recv
+
+    def close(self):
+        if self._h:
+            _abi.check(_abi.load().mcb_comm_destroy_v1(self._h), "mcb_comm_destroy_v1")
+            self._h = ctypes.c_void_p()
+
+
 def device_status(device=0, clear=False) -> int:
     w = ctypes.c_uint32(0)
     _abi.check(_abi.load().mcb_device_status(device, ctypes.byref(w), 1 if clear else 0),

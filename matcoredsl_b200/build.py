@@ -40,6 +40,7 @@ SOURCES = {
     "region.cu": [],
     "plan.cpp": [],
     "typed.cu": [],
+    "comm.cpp": [],
 }
 HEADERS = ["common.cuh", "internal.h", "epilogue.cuh"]
 

@@ -1651,6 +1651,35 @@ MCB_API mcb_status mcb_device_download(void *host_dst, mcb_buffer src,
                               cudaMemcpyDeviceToHost));
 }
 
+// Stream-ordered forms: the copy is queued on `stream` (NULL = the legacy
+// default stream) and the call returns at once; with pinned host memory the
+// transfer overlaps other work on the device.
+MCB_API mcb_status mcb_device_upload_async(mcb_buffer dst, const void *host_src,
+                                           uint64_t size_bytes, void *stream) noexcept {
+  {
+    std::lock_guard<std::mutex> lock(g_buf_mu);
+    if (!live(dst)) return MCB_STATUS_STALE_HANDLE;
+  }
+  if (size_bytes > dst.size_bytes) return MCB_STATUS_ARITHMETIC_OVERFLOW;
+  if (size_bytes && !host_src) return MCB_STATUS_INVALID_ARGUMENT;
+  DeviceGuard g(dst.device);
+  return from_cuda(cudaMemcpyAsync(reinterpret_cast<void *>(dst.ptr), host_src, size_bytes,
+                                   cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream)));
+}
+
+MCB_API mcb_status mcb_device_download_async(void *host_dst, mcb_buffer src, uint64_t size_bytes,
+                                             void *stream) noexcept {
+  {
+    std::lock_guard<std::mutex> lock(g_buf_mu);
+    if (!live(src)) return MCB_STATUS_STALE_HANDLE;
+  }
+  if (size_bytes > src.size_bytes) return MCB_STATUS_ARITHMETIC_OVERFLOW;
+  if (size_bytes && !host_dst) return MCB_STATUS_INVALID_ARGUMENT;
+  DeviceGuard g(src.device);
+  return from_cuda(cudaMemcpyAsync(host_dst, reinterpret_cast<void *>(src.ptr), size_bytes,
+                                   cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)));
+}
+
 MCB_API mcb_status mcb_device_zero(mcb_buffer handle) noexcept {
   {
     std::lock_guard<std::mutex> lock(g_buf_mu);

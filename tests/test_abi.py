@@ -43,7 +43,7 @@ def test_abi_struct_layouts_match_c_compiler(mcb, tmp_path):
     structs = {"mcb_tensor": _abi.Tensor, "mcb_exec": _abi.Exec, "mcb_report": _abi.Report,
                "mcb_epilogue": _abi.Epilogue, "mcb_buffer": _abi.Buffer,
                "mcb_fp8_tile_config": _abi.Fp8TileConfig, "mcb_shard": _abi.Shard,
-               "mcb_plan_desc": _abi.PlanDesc}
+               "mcb_plan_desc": _abi.PlanDesc, "mcb_comm_id": _abi.CommId}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "mcb.h"', "int main(void){"]
     for cname, py in structs.items():
         lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
@@ -138,3 +138,23 @@ def test_stale_buffer_handle_rejected(mcb):
     h.ptr, h.size_bytes, h.alloc_id, h.device = 0x1000, 16, 12345, 0
     assert lib.mcb_device_is_valid(h) == 0
     assert lib.mcb_device_free(h) == _abi.STATUS_CODE["STALE_HANDLE"]
+    buf = ctypes.create_string_buffer(16)
+    assert lib.mcb_device_upload_async(h, buf, 16, None) == _abi.STATUS_CODE["STALE_HANDLE"]
+    assert lib.mcb_device_download_async(buf, h, 16, None) == _abi.STATUS_CODE["STALE_HANDLE"]
+
+
+def test_comm_arguments_checked_without_gpu(mcb):
+    """The all-gather entry points validate their arguments before touching
+    NCCL or a device."""
+    from matcoredsl_b200 import _abi
+    lib = mcb.load()
+    bad = _abi.STATUS_CODE["INVALID_ARGUMENT"]
+    cid = _abi.CommId()
+    out = ctypes.c_void_p()
+    assert lib.mcb_comm_unique_id_v1(None) == bad
+    assert lib.mcb_comm_init_v1(ctypes.byref(cid), 0, 0, 0, ctypes.byref(out)) == bad  # world 0
+    assert lib.mcb_comm_init_v1(ctypes.byref(cid), 2, 2, 0, ctypes.byref(out)) == bad  # rank >= world
+    assert lib.mcb_comm_init_v1(ctypes.byref(cid), 2, 0, -1, ctypes.byref(out)) == bad  # device
+    assert lib.mcb_comm_init_v1(None, 2, 0, 0, ctypes.byref(out)) == bad
+    assert lib.mcb_allgather_v1(None, 0x1000, 0x2000, 16, None) == bad
+    assert lib.mcb_comm_destroy_v1(None) == 0
