@@ -95,3 +95,44 @@ def test_strict_pair_pool_scratch_captured_in_graph(mcb, orc):
     torch.cuda.synchronize()
     assert rc.same_bits(e.cpu().numpy(), orc.strict_fused_pair(a, b, d))
     del g
+
+
+def test_host_threads_on_their_own_streams(mcb, orc):
+    """Calls from several host threads at once (ctypes releases the GIL), each
+    on its own stream: strict pairs with pool scratch and GEMMs with an
+    epilogue. Every result must match what a lone call gives."""
+    import threading
+
+    import torch
+    from tests import gpu_util as gu
+    rng = np.random.default_rng(31)
+    x = rng.standard_normal((512, 256), dtype=np.float32)
+    w = rng.standard_normal((256, 384), dtype=np.float32) / np.float32(16)
+    (xh, _), (wh, _) = gu.bf16_pair(x), gu.bf16_pair(w)
+    dx, dw = gu.to_dev_bf16(xh), gu.to_dev_bf16(wh)
+    pairs = [[torch.from_numpy(t).cuda() for t in _pair_inputs(40 + i)] for i in range(4)]
+    ref_y = mcb.gemm_epilogue(dx, dw, act="gelu_tanh").float()
+    ref_e = [mcb.strict_fused_pair(*p) for p in pairs]
+    torch.cuda.synchronize()
+    errors = []
+
+    def worker(i):
+        try:
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                for _ in range(20):
+                    e = mcb.strict_fused_pair(*pairs[i])
+                    y = mcb.gemm_epilogue(dx, dw, act="gelu_tanh")
+                s.synchronize()
+            if not torch.equal(e, ref_e[i]) or not torch.equal(y.float(), ref_y):
+                errors.append(f"thread {i}: result differs")
+        except Exception as exc:  # noqa: BLE001 - reported below
+            errors.append(f"thread {i}: {exc!r}")
+
+    threads = [threading.Thread(target=worker, args=(i,)) for i in range(4)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    assert not any(t.is_alive() for t in threads), "a worker thread did not finish"
+    assert not errors, errors
