@@ -128,3 +128,31 @@ def test_config4_full_size_sampled(mcb, orc):
     assert mcb.device_status(0) == 0
     del a, b
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_tensor_cores_decode_every_code_like_the_oracle(mcb, orc, fmt):
+    """A holds every fp8 code once on its diagonal (A[i, i] = code i, zeros
+    elsewhere), Bt is the identity in the same format, all block scales are 1:
+    C[i, i] is then exactly the tensor core's decoding of code i, which must
+    equal the oracle's OCP decoding (NaN codes give NaN; signed zeros compare
+    equal, since the MMA sums in +0 products)."""
+    import torch
+    codes = np.arange(256, dtype=np.uint8)
+    a = np.zeros((256, 256), np.uint8)
+    a[codes, codes] = codes
+    one = orc.fp8_encode(np.array([1.0], np.float32), fmt)[0]
+    bt = np.zeros((256, 256), np.uint8)
+    bt[codes, codes] = one
+    tdt = torch.float8_e4m3fn if fmt == "e4m3" else torch.float8_e5m2
+    qa = torch.from_numpy(a).cuda().view(tdt)
+    qb = torch.from_numpy(bt).cuda().view(tdt)
+    ones = torch.ones((2, 2), dtype=torch.float32, device="cuda")
+    c = torch.empty((256, 256), dtype=torch.float32, device="cuda")
+    mcb.gemm_fp8_blockscaled(qa, ones, qb, ones, out=c)
+    assert mcb.api.last_result.route == "tcgen05_fp8_blockscaled_gemm"
+    got = np.diag(c.cpu().numpy())
+    ref = orc.fp8_decode(codes, fmt)
+    nan = np.isnan(ref)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got[~nan], ref[~nan])
