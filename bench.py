@@ -341,6 +341,17 @@ def run_profile_config(cfg: int, steps: int, warmup: int):
                       "route": mcb.api.last_result.route, "device_status": mcb.device_status(0)}))
 
 
+def _workload_config(m, world):
+    """The workload both arms name in `config`: config 2 with m rows per GPU."""
+    return {
+        "workload": "config2: Y = GELU_tanh(X W + b), X [M,4096] bf16, W [4096,4096] "
+                    "bf16 (row-major, consumed MN-major), b [4096] bf16, Y bf16, f32 "
+                    "accumulate",
+        "m_per_gpu": m, "n": N_DIM, "k": K_DIM, "global_m": m * world,
+        "parallelism": f"dp{world} (M rows sharded, no collective)",
+    }
+
+
 def run_reference(args):
     world, rank, _ = _dist()
     if rank != 0:
@@ -375,8 +386,9 @@ def run_reference(args):
         "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config2 GELU_tanh(X W + b) 8192x4096x4096", "rows_per_step": rows,
-                   "parallelism": "cpu (rank 0 only)"},
+        "config": {**_workload_config(M_FULL if args.scaling == "weak" else M_FULL // max(1, world),
+                                      world),
+                   "l2": "host CPU run (rank 0 only); each step is a row sample, see cpu_baseline"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -537,11 +549,7 @@ def _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, wo
             "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
             "config": {
-                "workload": "config2: Y = GELU_tanh(X W + b), X [M,4096] bf16, W [4096,4096] "
-                            "bf16 (row-major, consumed MN-major), b [4096] bf16, Y bf16, f32 "
-                            "accumulate",
-                "m_per_gpu": m, "n": N_DIM, "k": K_DIM, "global_m": m * world,
-                "parallelism": f"dp{world} (M rows sharded, no collective)",
+                **_workload_config(m, world),
                 "l2": f"{ROTATE} rotating X/W/b/Y sets, {working_set / 2**20:.0f} MiB working "
                       f"set > 126 MB L2",
                 "route": route,
