@@ -105,8 +105,9 @@ def test_fp8_gemm_bf16_out_and_simt_route(mcb, orc):
 
 def test_config4_full_size_sampled(mcb, orc):
     """A, B 16384^2 ~ N(0,1), seed 30 (A then B), e4m3,
-    128x128 absmax scales, bf16 out; 32 sampled rows (one in every 4th
-    128-row tile) against the dequantised fp64 product and the unquantised one."""
+    128x128 absmax scales, bf16 out; one sampled row in every 128-row tile
+    (plus the first and last rows) against the dequantised fp64 product and
+    the unquantised one."""
     import torch
     n = 16384
     rng = np.random.default_rng(30)
@@ -118,7 +119,7 @@ def test_config4_full_size_sampled(mcb, orc):
     del bt_dev
     c = mcb.gemm_fp8_blockscaled(qa, sa, qb, sb, out_dtype="bf16")
     assert mcb.api.last_result.route == "tcgen05_fp8_blockscaled_gemm"
-    rows = np.arange(0, n, 512) + np.random.default_rng(1).integers(0, 128, n // 512)
+    rows = gu.sample_rows(n, seed=1)
     got = gu.from_dev(c)[rows]
     qa_h, qb_h = _codes(qa), _codes(qb)
     ref = orc.gemm_fp8_blockscaled(qa_h, sa.cpu().numpy(), qb_h, sb.cpu().numpy(), rows=rows)
