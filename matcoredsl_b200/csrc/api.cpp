@@ -1036,8 +1036,10 @@ mcb_status msm_impl(const mcb_tensor *o, const mcb_tensor *q, const mcb_tensor *
   LaunchInfo info;
   cudaError_t err;
   call.mark_compute_start();
+  // Any M and N: a partial last query block and key tile are handled in the
+  // kernels (zero-filled loads, masked keys, skipped rows).
   const bool tc_ok = kHaveMsmTc && q->dtype == MCB_DTYPE_BF16 && sh.dqk == 128 && sh.dv == 128 &&
-                     sh.m % 128 == 0 && sh.n % 128 == 0 &&
+                     sh.m < (int64_t{1} << 31) && sh.n < (int64_t{1} << 31) &&
                      sh.q_s[2] % 8 == 0 && sh.k_s[2] % 8 == 0 && sh.v_s[2] % 8 == 0 &&
                      sh.o_s[2] % 8 == 0 && sh.q_s[0] % 8 == 0 && sh.q_s[1] % 8 == 0 &&
                      sh.k_s[0] % 8 == 0 && sh.k_s[1] % 8 == 0 && sh.v_s[0] % 8 == 0 &&

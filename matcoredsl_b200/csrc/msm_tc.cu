@@ -73,6 +73,8 @@ struct Params {
   int64_t o_s[3];  // output element strides [batch, head, row]
   float c;         // scale * log2(e)
   int o_tma;       // two-tile kernel: O leaves through shared memory and a TMA store
+  int m_rows;      // query rows: rows of the last query block past it are not stored
+  int n_tail;      // keys in the last key tile when N % 128 != 0, else 0
   __nv_bfloat16 *o;
   uint32_t *status;
 };
@@ -128,6 +130,15 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const void *tmap, uint64_
       : "memory");
 }
 
+// Scores of the keys past N in a partial last key tile become -inf, so they
+// take part in neither the row max nor the sum (the tile's K and V rows past
+// N were zero-filled by TMA).
+__device__ __forceinline__ void mask_key_tail(uint32_t (&s)[128], int n_tail) {
+#pragma unroll
+  for (int i = 0; i < 128; ++i)
+    if (i >= n_tail) s[i] = 0xff800000u;
+}
+
 // (batch, head, query block) of work unit u. 32-bit arithmetic (the launcher
 // keeps units below 2^31): 64-bit division is a long software sequence that
 // sat on the path between two units.
@@ -141,6 +152,7 @@ __device__ __forceinline__ void unit_coords(const Params &p, int64_t u, int32_t 
   b = static_cast<int32_t>(bb);
 }
 
+template <bool kTail>
 __global__ void __launch_bounds__(THREADS, 1)
     msm_tc_bf16_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, const Params p) {
@@ -317,6 +329,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           reg_fence(s2);
           reg_fence(s3);
         }
+        if (kTail && t + 1 == nkv) mask_key_tail(s, p.n_tail);
         tc_fence_before();
         mbar_arrive(&sm.s_free[sb]);
         ++s_cnt;
@@ -389,6 +402,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       tc_fence_after();
       const float inv = 1.0f / l;
+      const bool row_live = q0 + row < p.m_rows;
       __nv_bfloat16 *orow =
           p.o + b * p.o_s[0] + h * p.o_s[1] + static_cast<int64_t>(q0 + row) * p.o_s[2];
 #pragma unroll 1
@@ -403,7 +417,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           w.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv, __uint_as_float(o[q * 8 + 3]) * inv);
           w.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv, __uint_as_float(o[q * 8 + 5]) * inv);
           w.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv, __uint_as_float(o[q * 8 + 7]) * inv);
-          dst[q] = w;
+          if (row_live) dst[q] = w;
         }
       }
       tc_fence_before();
@@ -458,6 +472,7 @@ struct Smem2 {
 constexpr size_t SMEM2_BYTES = sizeof(Smem2) + 1024;
 static_assert(SMEM2_BYTES <= 232448, "two-tile MSM exceeds the opt-in shared memory per block");
 
+template <bool kTail>
 __global__ void __launch_bounds__(THREADS2, 1)
     msm_tc2_bf16_kernel(const __grid_constant__ CUtensorMap tq,
                         const __grid_constant__ CUtensorMap tk,
@@ -657,6 +672,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
           reg_fence(s2);
           reg_fence(s3);
         }
+        if (kTail && t + 1 == nkv) mask_key_tail(s, p.n_tail);
         tc_fence_before();
         mbar_arrive(&sm.s_free[g]);
         ++s_cnt;
@@ -783,6 +799,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
           bulk_commit();
         }
       } else {
+        const bool row_live = q0 + row < p.m_rows;
         __nv_bfloat16 *orow =
             p.o + b * p.o_s[0] + h * p.o_s[1] + static_cast<int64_t>(q0 + row) * p.o_s[2];
 #pragma unroll 1
@@ -797,7 +814,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
             w.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv, __uint_as_float(o[q * 8 + 3]) * inv);
             w.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv, __uint_as_float(o[q * 8 + 5]) * inv);
             w.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv, __uint_as_float(o[q * 8 + 7]) * inv);
-            dst[q] = w;
+            if (row_live) dst[q] = w;
           }
         }
         tc_fence_before();
@@ -825,7 +842,7 @@ bool encode_tmap_4d_bf16(CUtensorMap *map, const void *base, uint64_t d0, uint64
 cudaError_t launch_msm_tc_bf16(const void *q, const void *k, const void *v, void *o,
                                const MsmShape &s, float scale, uint32_t *status, int sms,
                                cudaStream_t stream, LaunchInfo *info) {
-  if (s.m % BQ || s.n % BKV || s.dqk != D || s.dv != D) return cudaErrorNotSupported;
+  if (s.m <= 0 || s.n <= 0 || s.dqk != D || s.dv != D) return cudaErrorNotSupported;
   CUtensorMap tq, tk, tv;
   auto enc = [&](CUtensorMap *map, const void *base, int64_t rows, const int64_t *st) {
     // dims {D, rows, heads, batch}; byte strides of rows/heads/batch. A unit
@@ -841,14 +858,19 @@ cudaError_t launch_msm_tc_bf16(const void *q, const void *k, const void *v, void
   // Query blocks of 256 rows run two tiles per CTA; otherwise one. The
   // two-tile kernel stores O by TMA when O's layout can be described by a
   // tensor map (16-byte aligned base and strides), else with plain stores.
-  const bool two = s.m % UNIT_ROWS == 0;
+  // Ragged M: the last query block is partly past M (TMA zero-fills Q there
+  // and the stores skip those rows). Two-tile units unless that would
+  // waste more than half a unit on a short problem.
+  const bool two = s.m % UNIT_ROWS == 0 || s.m % UNIT_ROWS > BQ || s.m >= 8 * UNIT_ROWS;
   CUtensorMap to;
   const bool o_tma = two && enc(&to, o, s.m, s.o_s);
   if (!o_tma) to = tq;  // unused by the kernel
   Params p;
   p.heads = s.heads;
-  p.qblocks = s.m / (two ? UNIT_ROWS : BQ);
-  p.nkv_tiles = s.n / BKV;
+  p.qblocks = (s.m + (two ? UNIT_ROWS : BQ) - 1) / (two ? UNIT_ROWS : BQ);
+  p.nkv_tiles = (s.n + BKV - 1) / BKV;
+  p.m_rows = static_cast<int>(s.m);
+  p.n_tail = static_cast<int>(s.n % BKV);
   p.units = s.batch * s.heads * p.qblocks;
   if (p.units > 0x7fffffff) return cudaErrorNotSupported;  // unit indices are 32-bit
   for (int i = 0; i < 3; ++i) p.o_s[i] = s.o_s[i];
@@ -858,17 +880,28 @@ cudaError_t launch_msm_tc_bf16(const void *q, const void *k, const void *v, void
   p.status = status;
   cudaError_t e;
   int grid = static_cast<int>(p.units < sms ? p.units : sms);
-  if (two) {
-    e = cudaFuncSetAttribute(msm_tc2_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(SMEM2_BYTES));
-    if (e != cudaSuccess) return e;
-    msm_tc2_bf16_kernel<<<grid, THREADS2, SMEM2_BYTES, stream>>>(tq, tk, tv, to, p);
-  } else {
-    e = cudaFuncSetAttribute(msm_tc_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(SMEM_BYTES));
-    if (e != cudaSuccess) return e;
-    msm_tc_bf16_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
-  }
+  // Key-tail masking is compiled only into the instantiations that need it,
+  // so full key tiles run exactly the unmasked loop.
+  auto run2 = [&](auto kernel) -> cudaError_t {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(SMEM2_BYTES));
+    if (err != cudaSuccess) return err;
+    kernel<<<grid, THREADS2, SMEM2_BYTES, stream>>>(tq, tk, tv, to, p);
+    return cudaSuccess;
+  };
+  auto run1 = [&](auto kernel) -> cudaError_t {
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(SMEM_BYTES));
+    if (err != cudaSuccess) return err;
+    kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
+    return cudaSuccess;
+  };
+  const bool tail = p.n_tail != 0;
+  if (two)
+    e = tail ? run2(msm_tc2_bf16_kernel<true>) : run2(msm_tc2_bf16_kernel<false>);
+  else
+    e = tail ? run1(msm_tc_bf16_kernel<true>) : run1(msm_tc_bf16_kernel<false>);
+  if (e != cudaSuccess) return e;
   if (info) {
     info->launches = 1;
     info->tile_m = two ? UNIT_ROWS : BQ;

@@ -59,8 +59,10 @@ def _check_msm(mcb, orc, pairs, scale, route, pairs_to_check=None):
     (qh, qf), (kh, kf), (vh, vf) = pairs
     o = mcb.msm(gu.to_dev_bf16(qh), gu.to_dev_bf16(kh), gu.to_dev_bf16(vh), scale)
     assert mcb.api.last_result.route == route
-    if route == "tcgen05_bf16_msm":  # 256-row query blocks run two tiles per CTA
-        assert mcb.api.last_result.tile[0] == (256 if qh.shape[2] % 256 == 0 else 128)
+    if route == "tcgen05_bf16_msm":
+        m = qh.shape[2]  # 256-row query blocks (two tiles per CTA) unless that wastes too much
+        two = m % 256 == 0 or m % 256 > 128 or m >= 2048
+        assert mcb.api.last_result.tile[0] == (256 if two else 128)
     assert o.dtype == torch.bfloat16
     got = gu.from_dev(o)
     b, h = qh.shape[:2]
@@ -77,7 +79,9 @@ def _check_msm(mcb, orc, pairs, scale, route, pairs_to_check=None):
     ((3, 5, 768, 128), "tcgen05_bf16_msm"),
     ((1, 2, 512, 128), "tcgen05_bf16_msm"),
     ((2, 3, 1536, 128), "tcgen05_bf16_msm"),
-    ((1, 1, 200, 128), "simt_online_softmax_msm"),
+    ((1, 1, 200, 128), "tcgen05_bf16_msm"),   # ragged M: one partial 256-row block
+    ((2, 3, 1000, 128), "tcgen05_bf16_msm"),  # ragged M, two-tile units
+    ((1, 2, 300, 128), "tcgen05_bf16_msm"),   # ragged M, single-tile units
     ((2, 2, 128, 64), "simt_online_softmax_msm"),
 ])
 def test_bf16_batched(mcb, orc, shape, route):
@@ -97,17 +101,26 @@ def test_tcgen05_rescale_path_by_route(mcb, orc, rows):
                128 ** -0.5, "tcgen05_bf16_msm")
 
 
+@pytest.mark.parametrize("rows,kv", [(256, 333), (129, 1), (517, 130), (1000, 1001)])
+def test_tcgen05_ragged_keys(mcb, orc, rows, kv):
+    """N not a multiple of 128: the partial last key tile is masked (its
+    zero-filled keys must not enter the softmax); M ragged as well."""
+    _check_msm(mcb, orc, _bf16_case((1, 2, rows, 128), rows + kv, kv_len=kv), 128 ** -0.5,
+               "tcgen05_bf16_msm")
+
+
 @pytest.mark.parametrize("rows", [256, 512])
 def test_tcgen05_unscaled_reference_semantics(mcb, orc, rows):
     """scale = 1 (the reference's mc.softmax(Q @ K.T)): scores of std ~11."""
     _check_msm(mcb, orc, _bf16_case((1, 1, rows, 128), 6, kv_len=640), 1.0, "tcgen05_bf16_msm")
 
 
-@pytest.mark.parametrize("s", [256, 512])
-def test_tcgen05_rectangular_and_strided(mcb, orc, s):
-    """M != N, and Q/K/V as strided views of a packed [B, S, 3, H, D] tensor."""
+@pytest.mark.parametrize("s,n", [(256, 640), (512, 640), (300, 601)])
+def test_tcgen05_rectangular_and_strided(mcb, orc, s, n):
+    """M != N, and Q/K/V as strided views of a packed [B, S, 3, H, D] tensor
+    (TMA stores of O clipped at a ragged M, a masked partial key tile)."""
     import torch
-    b, h, d, n = 2, 2, 128, 640
+    b, h, d = 2, 2, 128
     rng = np.random.default_rng(9)
     packed = rng.standard_normal((b, n, 3, h, d), dtype=np.float32)
     ph, pf = gu.bf16_pair(packed)
