@@ -1283,7 +1283,7 @@ mcb_status attn_block_impl(const mcb_tensor *y, const mcb_tensor *x, const mcb_t
     for (int i = 0; i < 3; ++i) sh.q_s[i] = sh.k_s[i] = sh.v_s[i] = sh.o_s[i] = st[i];
     const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
     err = cudaErrorNotSupported;
-    if (hd == 128 && S % 128 == 0 && D % 8 == 0)
+    if (hd == 128 && D % 8 == 0)
       err = mcb::launch_msm_tc_bf16(Q, K, V, O, sh, scale, call.ctx()->status, call.sms(),
                                     call.stream(), &step);
     if (err == cudaErrorNotSupported) {
