@@ -154,6 +154,158 @@ __global__ void __launch_bounds__(MSM_WARPS * 32) msm_simt_kernel(const void *q,
   }
 }
 
+// Tiled CUDA-core MSM for Dqk = Dv = D in {32, 64, 128}: a 256-thread CTA
+// owns 64 query rows of one (batch, head) and walks the keys in tiles of 64.
+// Thread (ty, tx) computes the 4 x 4 scores of rows 4ty.. and keys 4tx.. from
+// Q^T and K^T staged in shared memory (two 16-byte loads per 16 FMAs), keeps
+// the online-softmax state of its 4 rows (the 16 threads of a half warp share
+// a row block and combine their max and sum with shuffles), writes its P
+// block to shared memory and accumulates O[4 rows][D/16 columns] += P V.
+// f32 arithmetic for f32 and bf16 inputs; rows past M and keys past N are
+// zero-filled when staged, and scores of keys past N are masked.
+constexpr int SQ = 64, SK = 64, SPAD = 4;
+
+template <int D>
+constexpr size_t msm_tiled_smem_bytes() {
+  return sizeof(float) * (static_cast<size_t>(D) * (SQ + SPAD) + D * (SK + SPAD) +
+                          SK * (D + SPAD) + SQ * (SK + SPAD));
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) msm_simt_tiled_kernel(const void *q, const void *k,
+                                                             const void *v, void *o, int dtype,
+                                                             MsmShape s, float c2) {
+  extern __shared__ float4 smem_f4[];
+  float *qt = reinterpret_cast<float *>(smem_f4);  // [D][SQ + SPAD]  Q^T
+  float *kt = qt + D * (SQ + SPAD);                // [D][SK + SPAD]  K^T
+  float *vs = kt + D * (SK + SPAD);                // [SK][D + SPAD]  V
+  float *ps = vs + SK * (D + SPAD);                // [SQ][SK + SPAD] P
+  constexpr int DC = D / 16;                       // output columns per thread
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t bh = blockIdx.y, b = bh / s.heads, h = bh % s.heads;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * SQ;
+  const int64_t qoff = b * s.q_s[0] + h * s.q_s[1], koff = b * s.k_s[0] + h * s.k_s[1];
+  const int64_t voff = b * s.v_s[0] + h * s.v_s[1], ooff = b * s.o_s[0] + h * s.o_s[1];
+  for (int i = tid; i < SQ * D; i += 256) {
+    const int r = i / D, d = i - r * D;
+    const int64_t row = q0 + r;
+    qt[d * (SQ + SPAD) + r] = row < s.m ? load_elem(q, dtype, qoff + row * s.q_s[2] + d) : 0.0f;
+  }
+  float m_r[4], l_r[4], acc[4][DC];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    m_r[r] = -INFINITY;
+    l_r[r] = 0.0f;
+#pragma unroll
+    for (int cc = 0; cc < DC; ++cc) acc[r][cc] = 0.0f;
+  }
+  const int64_t ntiles = (s.n + SK - 1) / SK;
+  for (int64_t t = 0; t < ntiles; ++t) {
+    const int64_t k0 = t * SK;
+    __syncthreads();  // every read of the previous tile's K^T, V and P is done
+    for (int i = tid; i < SK * D; i += 256) {
+      const int key = i / D, d = i - key * D;
+      const int64_t j = k0 + key;
+      const bool in = j < s.n;
+      kt[d * (SK + SPAD) + key] = in ? load_elem(k, dtype, koff + j * s.k_s[2] + d) : 0.0f;
+      vs[key * (D + SPAD) + d] = in ? load_elem(v, dtype, voff + j * s.v_s[2] + d) : 0.0f;
+    }
+    __syncthreads();
+    float sc[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) sc[r][cc] = 0.0f;
+#pragma unroll 8
+    for (int d = 0; d < D; ++d) {
+      const float4 a = *reinterpret_cast<const float4 *>(&qt[d * (SQ + SPAD) + ty * 4]);
+      const float4 kk = *reinterpret_cast<const float4 *>(&kt[d * (SK + SPAD) + tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, kv[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) sc[r][cc] = fmaf(av[r], kv[cc], sc[r][cc]);
+    }
+    // Online softmax of the 4 rows (log2 domain: c2 = scale * log2(e)).
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float x[4], mx = -INFINITY;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        x[cc] = k0 + tx * 4 + cc < s.n ? sc[r][cc] * c2 : -INFINITY;
+        mx = fmaxf(mx, x[cc]);
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_new = fmaxf(m_r[r], mx);
+      const float alpha = exp2f(m_r[r] - m_new);  // 0 on the first tile (m_r = -inf)
+      float pv[4], sum = 0.0f;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        pv[cc] = exp2f(x[cc] - m_new);
+        sum += pv[cc];
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      l_r[r] = fmaf(l_r[r], alpha, sum);
+      m_r[r] = m_new;
+#pragma unroll
+      for (int cc = 0; cc < DC; ++cc) acc[r][cc] *= alpha;
+      *reinterpret_cast<float4 *>(&ps[(ty * 4 + r) * (SK + SPAD) + tx * 4]) =
+          make_float4(pv[0], pv[1], pv[2], pv[3]);
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int j = 0; j < SK; ++j) {
+      float pr[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) pr[r] = ps[(ty * 4 + r) * (SK + SPAD) + j];
+      float vv[DC];
+      const float *vrow = &vs[j * (D + SPAD) + tx * DC];
+      if constexpr (DC % 4 == 0) {
+#pragma unroll
+        for (int cc = 0; cc < DC; cc += 4) {
+          const float4 t4 = *reinterpret_cast<const float4 *>(vrow + cc);
+          vv[cc] = t4.x;
+          vv[cc + 1] = t4.y;
+          vv[cc + 2] = t4.z;
+          vv[cc + 3] = t4.w;
+        }
+      } else {
+#pragma unroll
+        for (int cc = 0; cc < DC; ++cc) vv[cc] = vrow[cc];
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int cc = 0; cc < DC; ++cc) acc[r][cc] = fmaf(pr[r], vv[cc], acc[r][cc]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int64_t row = q0 + ty * 4 + r;
+    if (row >= s.m) continue;
+    const float inv = 1.0f / l_r[r];
+#pragma unroll
+    for (int cc = 0; cc < DC; ++cc)
+      store_elem(o, dtype, ooff + row * s.o_s[2] + tx * DC + cc, acc[r][cc] * inv);
+  }
+}
+
+template <int D>
+cudaError_t launch_msm_tiled(const void *q, const void *k, const void *v, void *o, int dtype,
+                             const MsmShape &s, float scale, cudaStream_t stream) {
+  constexpr size_t smem = msm_tiled_smem_bytes<D>();
+  cudaError_t e = cudaFuncSetAttribute(msm_simt_tiled_kernel<D>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const dim3 grid(static_cast<unsigned>((s.m + SQ - 1) / SQ), static_cast<unsigned>(s.batch * s.heads));
+  msm_simt_tiled_kernel<D><<<grid, 256, smem, stream>>>(q, k, v, o, dtype, s,
+                                                        scale * 1.4426950408889634f);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_gemm_simt(const void *x, int x_dtype, const void *w, int w_dtype, void *y,
@@ -181,6 +333,22 @@ cudaError_t launch_msm_simt(const void *q, const void *k, const void *v, void *o
                             LaunchInfo *info) {
   if (s.m == 0 || s.dv == 0 || s.batch * s.heads == 0) return cudaSuccess;
   if (s.dqk > MSM_DMAX || s.dv > MSM_DMAX) return cudaErrorInvalidValue;
+  if (s.n > 0 && s.batch * s.heads <= 65535 && s.dqk == s.dv &&
+      (s.dqk == 32 || s.dqk == 64 || s.dqk == 128)) {
+    // 64 x 64 score tiles with 4 x 4 per thread.
+    const cudaError_t e = s.dqk == 32   ? launch_msm_tiled<32>(q, k, v, o, dtype, s, scale, stream)
+                          : s.dqk == 64 ? launch_msm_tiled<64>(q, k, v, o, dtype, s, scale, stream)
+                                        : launch_msm_tiled<128>(q, k, v, o, dtype, s, scale, stream);
+    if (info) {
+      info->launches = 1;
+      info->tile_m = SQ;
+      info->tile_n = SK;
+      info->tile_k = static_cast<int>(s.dqk);
+      info->ctas = static_cast<int>(((s.m + SQ - 1) / SQ) * s.batch * s.heads);
+      info->set_route("simt_tiled_online_softmax_msm");
+    }
+    return e;
+  }
   dim3 grid(static_cast<unsigned>((s.m + MSM_WARPS - 1) / MSM_WARPS),
             static_cast<unsigned>(s.batch * s.heads));
   if (grid.y > 65535u) return cudaErrorInvalidConfiguration;

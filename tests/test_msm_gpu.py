@@ -82,7 +82,9 @@ def _check_msm(mcb, orc, pairs, scale, route, pairs_to_check=None):
     ((1, 1, 200, 128), "tcgen05_bf16_msm"),   # ragged M: one partial 256-row block
     ((2, 3, 1000, 128), "tcgen05_bf16_msm"),  # ragged M, two-tile units
     ((1, 2, 300, 128), "tcgen05_bf16_msm"),   # ragged M, single-tile units
-    ((2, 2, 128, 64), "simt_online_softmax_msm"),
+    ((2, 2, 128, 64), "simt_tiled_online_softmax_msm"),  # D = 64: tiled CUDA-core kernel
+    ((1, 3, 200, 32), "simt_tiled_online_softmax_msm"),
+    ((1, 2, 100, 96), "simt_online_softmax_msm"),         # other widths: row-per-warp kernel
 ])
 def test_bf16_batched(mcb, orc, shape, route):
     _check_msm(mcb, orc, _bf16_case(shape, sum(shape)), shape[-1] ** -0.5, route)
@@ -151,3 +153,37 @@ def test_config3_full_size_sampled(mcb, orc):
     sample = [(0, 0), (3, 17), (5, 31), (7, 9)]
     _check_msm(mcb, orc, pairs, 128 ** -0.5, "tcgen05_bf16_msm", sample)
     assert mcb.device_status(0) == 0
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("shape", [(1, 2, 300, 1000, 128), (2, 1, 64, 65, 64), (1, 1, 1, 1, 32),
+                                   (1, 1, 70, 7, 64)])
+def test_tiled_cuda_core_msm(mcb, orc, dtype, shape):
+    """The tiled CUDA-core kernel (f32 and bf16 inputs, D in {32, 64, 128}):
+    ragged M and N (zero-filled rows, masked keys), single keys, single
+    queries. f32 at the reference's max-abs 2e-3; bf16 at 1e-2 rel. Frobenius."""
+    import torch
+    b, h, m, n, d = shape
+    rng = np.random.default_rng(sum(shape))
+    q = rng.normal(0.0, 0.65, size=(b, h, m, d)).astype(np.float32)
+    k = rng.normal(0.0, 0.65, size=(b, h, n, d)).astype(np.float32)
+    v = rng.normal(0.0, 1.0, size=(b, h, n, d)).astype(np.float32)
+    if dtype == "bf16":
+        (qh, qf), (kh, kf), (vh, vf) = (gu.bf16_pair(x) for x in (q, k, v))
+        args = [gu.to_dev_bf16(x) for x in (qh, kh, vh)]
+    else:
+        qf, kf, vf = q, k, v
+        args = [torch.from_numpy(x).cuda() for x in (q, k, v)]
+    o = mcb.msm(*args, d ** -0.5)
+    tc = dtype == "bf16" and d == 128  # bf16 at D = 128 runs on the tensor cores
+    assert mcb.api.last_result.route == ("tcgen05_bf16_msm" if tc else
+                                          "simt_tiled_online_softmax_msm")
+    got = gu.from_dev(o)
+    for bi in range(b):
+        for hi in range(h):
+            ref = orc.msm(qf[bi, hi], kf[bi, hi], vf[bi, hi], d ** -0.5)
+            if dtype == "f32":
+                assert np.max(np.abs(got[bi, hi] - ref)) < 2e-3
+            else:
+                assert orc.rel_frobenius(got[bi, hi], ref) < 1e-2
+
