@@ -87,6 +87,97 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const void *x, int x_dty
   }
 }
 
+// Large f32 GEMM + epilogue (f32 X [M,K], f32 W [K,N], 16-byte aligned rows):
+// 256 threads own a 128x128 tile, each thread 8x8 accumulators (rows 4ty..
+// and 64+4ty.., columns 4tx.. and 64+4tx..); 16-deep k-slices of X (stored
+// transposed, [k][row]) and W ([k][col]) are double-buffered in shared memory
+// with the next slice fetched into registers (two 16-byte loads per thread
+// per operand) while the current one is consumed; four 16-byte shared loads
+// per 64 FMAs. The epilogue (bias, activation, f32 or bf16 store) is the one
+// the generic kernel above applies.
+constexpr int FBM = 128, FBN = 128, FBK = 16, FPAD = 4;
+
+__global__ void __launch_bounds__(256, 2) gemm_f32_big_kernel(const float *__restrict__ x,
+                                                           const float *__restrict__ w, void *y,
+                                                           int y_dtype, int64_t m, int64_t n,
+                                                           int64_t k, int64_t ld_x, int64_t ld_w,
+                                                           int64_t ld_y, Epilogue epi) {
+  __shared__ __align__(16) float xs[2][FBK][FBM + FPAD];
+  __shared__ __align__(16) float ws[2][FBK][FBN + FPAD];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.y) * FBM;
+  const int64_t col0 = static_cast<int64_t>(blockIdx.x) * FBN;
+  // Staging roles per slice: X rows (tid & 127) at k-quads (tid >> 7) and
+  // (tid >> 7) + 2; W k-rows (tid >> 5) and 8 + (tid >> 5) at column quad tid & 31.
+  const int xr = tid & 127, xq = (tid >> 7) * 4;
+  const int wk = tid >> 5, wc = (tid & 31) * 4;
+  float4 rx[2], rw[2];
+  auto fetch = [&](int64_t sl) {
+    const int64_t h0 = sl * FBK;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int64_t gr = row0 + xr, gk = h0 + xq + i * 8;
+      rx[i] = (gr < m && gk < k) ? *reinterpret_cast<const float4 *>(x + gr * ld_x + gk)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int64_t wk_g = h0 + wk + i * 8, gc = col0 + wc;
+      rw[i] = (wk_g < k && gc < n) ? *reinterpret_cast<const float4 *>(w + wk_g * ld_w + gc)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto stage = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int kq = xq + i * 8;
+      xs[buf][kq][xr] = rx[i].x;
+      xs[buf][kq + 1][xr] = rx[i].y;
+      xs[buf][kq + 2][xr] = rx[i].z;
+      xs[buf][kq + 3][xr] = rx[i].w;
+      *reinterpret_cast<float4 *>(&ws[buf][wk + i * 8][wc]) = rw[i];
+    }
+  };
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+  const int64_t nslices = (k + FBK - 1) / FBK;
+  if (nslices > 0) {
+    fetch(0);
+    stage(0);
+  }
+  __syncthreads();
+  for (int64_t sl = 0; sl < nslices; ++sl) {
+    const int buf = static_cast<int>(sl & 1);
+    if (sl + 1 < nslices) fetch(sl + 1);
+#pragma unroll
+    for (int kk = 0; kk < FBK; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4 *>(&xs[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4 *>(&xs[buf][kk][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4 *>(&ws[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4 *>(&ws[buf][kk][64 + tx * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    if (sl + 1 < nslices) stage(buf ^ 1);
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t row = row0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    if (row >= m) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t col = col0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+      if (col < n)
+        store_elem(y, y_dtype, row * ld_y + col, apply_epilogue<false>(epi, acc[i][j], row, col));
+    }
+  }
+}
+
 // One warp per query row, keys streamed in chunks of 32 (one key per lane for
 // the score), online softmax with warp-shuffle max/sum, the output row held
 // as Dv/32 accumulators per lane. Dqk, Dv <= 256.
@@ -313,6 +404,29 @@ cudaError_t launch_gemm_simt(const void *x, int x_dtype, const void *w, int w_dt
                              int64_t ld_w, int64_t ld_y, int w_transposed, const Epilogue &epi,
                              cudaStream_t stream, LaunchInfo *info) {
   if (m == 0 || n == 0) return cudaSuccess;
+  // f32 operands with 16-byte aligned rows and at least one wave of 128x128
+  // tiles take the large-tile kernel.
+  const int64_t big_tiles = ((m + FBM - 1) / FBM) * ((n + FBN - 1) / FBN);
+  constexpr int kF32 = 1;  // mcb_dtype code of f32 (bf16 is 3, as load_elem reads them)
+  const bool big = x_dtype == kF32 && w_dtype == kF32 && !w_transposed &&
+                   k % 4 == 0 && n % 4 == 0 && ld_x % 4 == 0 && ld_w % 4 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15u) == 0 &&
+                   big_tiles >= 148 && (m + FBM - 1) / FBM <= 65535;
+  if (big) {
+    const dim3 grid(static_cast<unsigned>((n + FBN - 1) / FBN), static_cast<unsigned>((m + FBM - 1) / FBM));
+    gemm_f32_big_kernel<<<grid, 256, 0, stream>>>(static_cast<const float *>(x),
+                                                  static_cast<const float *>(w), y, y_dtype, m, n,
+                                                  k, ld_x, ld_w, ld_y, epi);
+    if (info) {
+      info->launches = 1;
+      info->tile_m = FBM;
+      info->tile_n = FBN;
+      info->tile_k = FBK;
+      info->ctas = static_cast<int>(grid.x * grid.y);
+      info->set_route("simt_f32_gemm_epilogue");
+    }
+    return cudaGetLastError();
+  }
   dim3 grid(static_cast<unsigned>((n + TN - 1) / TN), static_cast<unsigned>((m + TM - 1) / TM));
   if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
   gemm_simt_kernel<<<grid, 256, 0, stream>>>(x, x_dtype, w, w_dtype, y, y_dtype, m, n, k, ld_x,

@@ -104,6 +104,39 @@ def test_family_a_f32_reference_shapes(mcb, orc, case):
     assert np.max(np.abs(y - ref)) < 1e-3
 
 
+@pytest.mark.parametrize("shape,act,bias_mode,bias_op,out_dtype", [
+    ((2048, 512, 1536), "gelu_tanh", "row", "add", "f32"),
+    ((2000, 300, 1540), "relu", "full", "rsub", "f32"),   # edge tiles, K % 16 != 0
+    ((1920, 256, 1408), "exp", "none", "add", "bf16"),
+])
+def test_f32_large_tile_kernel(mcb, orc, shape, act, bias_mode, bias_op, out_dtype):
+    """f32 operands large enough for 128x128 tiles (8x8 per thread): same
+    epilogue semantics and the reference's max-abs tolerance (1e-3; bf16
+    output at 1e-2 relative Frobenius)."""
+    import torch
+    m, k, n = shape
+    rng = np.random.default_rng(m + k + n)
+    scale = 0.05 if act == "exp" else 1.0
+    a = (rng.standard_normal((m, k)) * scale).astype(np.float32)
+    b = (rng.standard_normal((k, n)) * scale / np.sqrt(k)).astype(np.float32)
+    bias = None
+    if bias_mode == "row":
+        bias = rng.standard_normal(n).astype(np.float32)
+    elif bias_mode == "full":
+        bias = rng.standard_normal((m, n)).astype(np.float32)
+    dev = lambda t: None if t is None else torch.from_numpy(t).cuda()  # noqa: E731
+    y = mcb.gemm_epilogue(dev(a), dev(b), dev(bias), bias_mode=bias_mode, bias_op=bias_op,
+                          act=act, out_dtype=out_dtype)
+    r = mcb.api.last_result
+    assert r.route == "simt_f32_gemm_epilogue" and r.tile[:2] == (128, 128)
+    ref = orc.gemm_epilogue(a, b, bias, bias_mode=bias_mode, bias_op=bias_op, act=act)
+    got = gu.from_dev(y)
+    if out_dtype == "f32":
+        assert np.max(np.abs(got - ref)) < 1e-3
+    else:
+        assert orc.rel_frobenius(got, ref) < 1e-2
+
+
 def test_host_operands_e2e_path(mcb, orc):
     """Host-resident bf16 operands are staged through the C ABI and match."""
     ml = pytest.importorskip("ml_dtypes")
