@@ -413,6 +413,107 @@ int pick_rows(int64_t m, int sms) {
   return (m + 1) / 2 >= sms ? 2 : 1;
 }
 
+// Large strict GEMM: 256 threads own a 128x128 tile of C, each thread 8x8
+// chains (rows 4ty.. and 64+4ty.., columns 4tx.. and 64+4tx..). Every chain
+// is the strict one: starting from +0, c = __fadd_rn(c, __fmul_rn(a, b)) for
+// k = 0, 1, 2, ... in order, so the result is bit-identical to the CPU leaf
+// however the tile is laid out. 16-deep k-slices of A (stored transposed,
+// [k][row]) and B ([k][col]) are double-buffered in shared memory, the next
+// slice fetched into registers (16-byte loads) while the current one is
+// consumed; a partial last slice runs only its real depth.
+constexpr int SBM = 128, SBN = 128, SBK = 16, SBPAD = 4;
+
+__global__ void __launch_bounds__(256, 2) strict_big_kernel(
+    const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ c, int64_t m,
+    int64_t k, int64_t n, int64_t lda, int64_t ldb, int64_t ldc) {
+  __shared__ __align__(16) float as[2][SBK][SBM + SBPAD];
+  __shared__ __align__(16) float bs[2][SBK][SBN + SBPAD];
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.y) * SBM;
+  const int64_t col0 = static_cast<int64_t>(blockIdx.x) * SBN;
+  const int ar = tid & 127, aq = (tid >> 7) * 4;
+  const int bk = tid >> 5, bc = (tid & 31) * 4;
+  float4 ra[2], rb[2];
+  auto fetch = [&](int64_t sl) {
+    const int64_t h0 = sl * SBK;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int64_t gr = row0 + ar, gk = h0 + aq + i * 8;
+      ra[i] = (gr < m && gk < k) ? *reinterpret_cast<const float4 *>(a + gr * lda + gk)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int64_t kb = h0 + bk + i * 8, gc = col0 + bc;
+      rb[i] = (kb < k && gc < n) ? *reinterpret_cast<const float4 *>(b + kb * ldb + gc)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto stage = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int kq = aq + i * 8;
+      as[buf][kq][ar] = ra[i].x;
+      as[buf][kq + 1][ar] = ra[i].y;
+      as[buf][kq + 2][ar] = ra[i].z;
+      as[buf][kq + 3][ar] = ra[i].w;
+      *reinterpret_cast<float4 *>(&bs[buf][bk + i * 8][bc]) = rb[i];
+    }
+  };
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+  const int64_t nslices = (k + SBK - 1) / SBK;
+  if (nslices > 0) {
+    fetch(0);
+    stage(0);
+  }
+  __syncthreads();
+  for (int64_t sl = 0; sl < nslices; ++sl) {
+    const int buf = static_cast<int>(sl & 1);
+    if (sl + 1 < nslices) fetch(sl + 1);
+    const int depth = static_cast<int>(k - sl * SBK < SBK ? k - sl * SBK : SBK);
+    auto step = [&](int kk) {
+      const float4 a0 = *reinterpret_cast<const float4 *>(&as[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4 *>(&as[buf][kk][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4 *>(&bs[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4 *>(&bs[buf][kk][64 + tx * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
+    };
+    if (depth == SBK) {
+#pragma unroll
+      for (int kk = 0; kk < SBK; ++kk) step(kk);
+    } else {
+      for (int kk = 0; kk < depth; ++kk) step(kk);
+    }
+    if (sl + 1 < nslices) stage(buf ^ 1);
+    __syncthreads();
+  }
+  const bool vec_out = (ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(c) & 15u) == 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t r = row0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+    if (r >= m) continue;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int64_t cc = col0 + h * 64 + tx * 4;
+      float *dst = c + r * ldc + cc;
+      if (vec_out && cc + 4 <= n) {
+        *reinterpret_cast<float4 *>(dst) =
+            make_float4(acc[i][h * 4], acc[i][h * 4 + 1], acc[i][h * 4 + 2], acc[i][h * 4 + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (cc + j < n) dst[j] = acc[i][h * 4 + j];
+      }
+    }
+  }
+}
+
 // One tiled strict GEMM launch: 16 x 64 tiles (16 x 32 when N is small),
 // 16-byte copies when every row allows them.
 template <int MR, int NR>
@@ -453,6 +554,20 @@ cudaError_t launch_tiled(const float *a, const float *b, float *c, int64_t m, in
                    (k == 0 || (al16(a) && al16(b)));
   const int64_t warp_slots = static_cast<int64_t>(sms) * 4 * 32;  // one warp per sub-partition
   const int64_t outputs = m * n;
+  // At least one 128x128 tile per SM: 8x8 chains per thread.
+  const int64_t big_rows = (m + SBM - 1) / SBM, big_cols = (n + SBN - 1) / SBN;
+  if (vec && big_rows * big_cols >= sms && big_rows <= 65535) {
+    strict_big_kernel<<<dim3(static_cast<unsigned>(big_cols), static_cast<unsigned>(big_rows)), 256,
+                        0, stream>>>(a, b, c, m, k, n, lda, ldb, ldc);
+    if (info) {
+      info->launches += 1;
+      info->tile_m = SBM;
+      info->tile_n = SBN;
+      info->tile_k = SBK;
+      info->ctas += static_cast<int>(big_rows * big_cols);
+    }
+    return cudaGetLastError();
+  }
   if (outputs / 8 >= 4 * warp_slots && n >= 64)
     return launch_tiled_variant<2, 4>(a, b, c, m, k, n, lda, ldb, ldc, vec, stream, info);
   if (outputs / 4 >= warp_slots && n >= 32)

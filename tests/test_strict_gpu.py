@@ -65,6 +65,25 @@ def test_strict_gemm_bit_exact(mcb, orc):
         assert rc.same_bits(mcb.strict_gemm(a, b), orc.strict_gemm(a, b)), (m, k, n)
 
 
+@pytest.mark.parametrize("m,k,n", [(2048, 96, 2048), (2000, 100, 1992), (1664, 20, 1536)])
+def test_strict_gemm_large_tiles_bit_exact(mcb, orc, m, k, n):
+    """Problems of at least one 128x128 tile per SM run 8x8 chains per thread
+    (edge tiles, K not a multiple of the 16-deep slice); still bit-exact, with
+    IEEE specials in A and B."""
+    import torch
+    rng = np.random.default_rng(m + k + n)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    a[3, 5] = np.inf
+    a[10, :] = -0.0
+    b[7, 11] = np.nan
+    b[:, 13] = 1e-39  # subnormal
+    c = mcb.strict_gemm(torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda())
+    r = mcb.api.last_result
+    assert r.route == "strict_f32_simt_gemm_tiled" and r.tile[:2] == (128, 128)
+    assert rc.same_bits(c.cpu().numpy(), orc.strict_gemm(a, b))
+
+
 def _config1():
     a = np.random.default_rng(0).uniform(-1, 1, (512, 256)).astype(np.float32)
     b = np.random.default_rng(1).uniform(-1, 1, (256, 384)).astype(np.float32)
