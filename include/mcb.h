@@ -258,8 +258,8 @@ MCB_API mcb_status mcb_gemm_chain_v1(const mcb_tensor *e, const mcb_tensor *a,
 /* O = softmax(scale * Q*K^T) * V per leading index. Q [.., M, Dqk],
  * K [.., N, Dqk], V [.., N, Dv], O [.., M, Dv] with up to two leading
  * (batch, head) dims. scale = 1 gives the reference's unscaled softmax
- * (tests/test_family_c.py:102-113). bf16 with Dqk = Dv = 128 (any M and N,
- * 16-byte aligned rows) runs the tcgen05 kernels (S and O in TMEM, online
+ * (tests/test_family_c.py:102-113). bf16 with Dqk = Dv = 64 or 128 (any M
+ * and N, 16-byte aligned rows) runs the tcgen05 kernels (S and O in TMEM, online
  * softmax, S never in HBM); other shapes and f32 run a CUDA-core
  * online-softmax kernel. Replaces the kernel emitted by
  * FusionMlirEmitter::emitFamilyC (src/fusion_emitter_family_c.cpp:13-596). */

@@ -1038,7 +1038,8 @@ mcb_status msm_impl(const mcb_tensor *o, const mcb_tensor *q, const mcb_tensor *
   call.mark_compute_start();
   // Any M and N: a partial last query block and key tile are handled in the
   // kernels (zero-filled loads, masked keys, skipped rows).
-  const bool tc_ok = kHaveMsmTc && q->dtype == MCB_DTYPE_BF16 && sh.dqk == 128 && sh.dv == 128 &&
+  const bool tc_ok = kHaveMsmTc && q->dtype == MCB_DTYPE_BF16 && sh.dqk == sh.dv &&
+                     (sh.dqk == 64 || sh.dqk == 128) &&
                      sh.m < (int64_t{1} << 31) && sh.n < (int64_t{1} << 31) &&
                      sh.q_s[2] % 8 == 0 && sh.k_s[2] % 8 == 0 && sh.v_s[2] % 8 == 0 &&
                      sh.o_s[2] % 8 == 0 && sh.q_s[0] % 8 == 0 && sh.q_s[1] % 8 == 0 &&
@@ -1283,7 +1284,7 @@ mcb_status attn_block_impl(const mcb_tensor *y, const mcb_tensor *x, const mcb_t
     for (int i = 0; i < 3; ++i) sh.q_s[i] = sh.k_s[i] = sh.v_s[i] = sh.o_s[i] = st[i];
     const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
     err = cudaErrorNotSupported;
-    if (hd == 128 && D % 8 == 0)
+    if ((hd == 64 || hd == 128) && D % 8 == 0)
       err = mcb::launch_msm_tc_bf16(Q, K, V, O, sh, scale, call.ctx()->status, call.sms(),
                                     call.stream(), &step);
     if (err == cudaErrorNotSupported) {

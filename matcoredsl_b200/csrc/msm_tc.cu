@@ -1,4 +1,5 @@
-// Matmul-softmax-matmul (Family C) on tcgen05 tensor cores, bf16, D = 128.
+// Matmul-softmax-matmul (Family C) on tcgen05 tensor cores, bf16, head dim
+// HD = 64 or 128 (Dqk = Dv).
 //
 //   O[b,h] = softmax(scale * Q[b,h] K[b,h]^T) V[b,h]      (src/fusion_emitter_family_c.cpp)
 //
@@ -11,9 +12,10 @@
 // in L2 for the CTAs running at the same time.
 //
 //   warp 0      TMA producer: Q (once per unit), K tiles into a 3-stage ring,
-//               V tiles into a 2-stage ring (128 keys x 128 dims, 128B swizzle).
+//               V tiles into a 2-stage ring (128 keys x HD dims, stored as
+//               HD/64 column chunks of 128 rows x 128 bytes, 128B swizzle).
 //   warp 1      TMEM owner (512 columns: S0 | S1 | O) and single-thread MMA
-//               issuer: S_t = Q K_t^T (M=128, N=128, K=128) into S[t%2], then
+//               issuer: S_t = Q K_t^T (M=128, N=128, K=HD) into S[t%2], then
 //               O += P_{t-1} V_{t-1} with P from shared memory and V consumed
 //               MN-major. S_{t+1} is issued before PV_t so the tensor core
 //               works on the next score tile while the softmax runs.
@@ -41,21 +43,26 @@
 namespace mcb {
 namespace {
 
-constexpr int D = 128;        // head dim (QK and V)
 constexpr int BQ = 128;       // query rows per unit
 constexpr int BKV = 128;      // keys per tile
 constexpr int KSTAGES = 3, VSTAGES = 2;
-constexpr int TILE_BYTES = BKV * D * 2;  // 32 KiB (also Q and P)
-constexpr int CHUNK_BYTES = 128 * 128;   // one 64-column half of a tile
+constexpr int CHUNK_BYTES = 128 * 128;   // 128 rows x 64 bf16 columns (one swizzle span)
+constexpr int P_BYTES = BQ * BKV * 2;    // 32 KiB: the P tile, and O staged for its store
+// A Q, K or V tile: 128 rows x HD bf16 columns, HD/64 chunks (16 or 32 KiB).
+template <int HD>
+constexpr int tile_bytes() {
+  return BKV * HD * 2;
+}
 constexpr int THREADS = 192;  // 6 warps: producer, MMA, 4 softmax (one per TMEM lane quarter)
 constexpr int TMEM_COLS = 512;
 constexpr uint32_t S_COL0 = 0, O_COL = 256;
 
+template <int HD>
 struct Smem {
-  uint8_t q[TILE_BYTES];
-  uint8_t k[KSTAGES][TILE_BYTES];
-  uint8_t v[VSTAGES][TILE_BYTES];
-  uint8_t p[TILE_BYTES];
+  uint8_t q[tile_bytes<HD>()];
+  uint8_t k[KSTAGES][tile_bytes<HD>()];
+  uint8_t v[VSTAGES][tile_bytes<HD>()];
+  uint8_t p[P_BYTES];
   uint64_t q_full, q_empty;
   uint64_t k_full[KSTAGES], k_empty[KSTAGES];
   uint64_t v_full[VSTAGES], v_empty[VSTAGES];
@@ -66,7 +73,10 @@ struct Smem {
   uint32_t tmem_slot;
   int abort_flag;
 };
-constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
+template <int HD>
+constexpr size_t smem_bytes() {
+  return sizeof(Smem<HD>) + 1024;
+}
 
 struct Params {
   int64_t heads, qblocks, nkv_tiles, units;
@@ -130,6 +140,14 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const void *tmap, uint64_
       : "memory");
 }
 
+// One Q, K or V tile (rows r0.. of head h, batch b): HD/64 boxes of 64 columns.
+template <int HD>
+__device__ __forceinline__ void tma_load_tile(uint8_t *dst, const CUtensorMap *map, uint64_t *bar,
+                                              int32_t r0, int32_t h, int32_t b) {
+#pragma unroll
+  for (int c = 0; c < HD / 64; ++c) tma_load_4d(dst + c * CHUNK_BYTES, map, bar, c * 64, r0, h, b);
+}
+
 // Scores of the keys past N in a partial last key tile become -inf, so they
 // take part in neither the row max nor the sum (the tile's K and V rows past
 // N were zero-filled by TMA).
@@ -152,12 +170,12 @@ __device__ __forceinline__ void unit_coords(const Params &p, int64_t u, int32_t 
   b = static_cast<int32_t>(bb);
 }
 
-template <bool kTail>
+template <int HD, bool kTail>
 __global__ void __launch_bounds__(THREADS, 1)
     msm_tc_bf16_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, const Params p) {
   extern __shared__ uint8_t smem_raw[];
-  Smem &sm = *reinterpret_cast<Smem *>(
+  Smem<HD> &sm = *reinterpret_cast<Smem<HD> *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   volatile int *abort_flag = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -209,9 +227,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         unit_coords(p, u, b, h, q0);
         q0 *= BQ;
         if (!mbar_wait(&sm.q_empty, (uc & 1) ^ 1, abort_flag, p.status, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&sm.q_full, TILE_BYTES);
-        tma_load_4d(sm.q, &tq, &sm.q_full, 0, q0, h, b);
-        tma_load_4d(sm.q + CHUNK_BYTES, &tq, &sm.q_full, 64, q0, h, b);
+        mbar_arrive_expect_tx(&sm.q_full, tile_bytes<HD>());
+        tma_load_tile<HD>(sm.q, &tq, &sm.q_full, q0, h, b);
         bool ok = true;
         for (int64_t t = 0; t < nkv && ok; ++t, ++kt, ++vt) {
           const int ks = kt % KSTAGES, vs = vt % VSTAGES;
@@ -219,15 +236,13 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = mbar_wait(&sm.k_empty[ks], ((kt / KSTAGES) & 1) ^ 1, abort_flag, p.status,
                          kErrTimeoutEmpty);
           if (!ok) break;
-          mbar_arrive_expect_tx(&sm.k_full[ks], TILE_BYTES);
-          tma_load_4d(sm.k[ks], &tk, &sm.k_full[ks], 0, key0, h, b);
-          tma_load_4d(sm.k[ks] + CHUNK_BYTES, &tk, &sm.k_full[ks], 64, key0, h, b);
+          mbar_arrive_expect_tx(&sm.k_full[ks], tile_bytes<HD>());
+          tma_load_tile<HD>(sm.k[ks], &tk, &sm.k_full[ks], key0, h, b);
           ok = mbar_wait(&sm.v_empty[vs], ((vt / VSTAGES) & 1) ^ 1, abort_flag, p.status,
                          kErrTimeoutEmpty);
           if (!ok) break;
-          mbar_arrive_expect_tx(&sm.v_full[vs], TILE_BYTES);
-          tma_load_4d(sm.v[vs], &tv, &sm.v_full[vs], 0, key0, h, b);
-          tma_load_4d(sm.v[vs] + CHUNK_BYTES, &tv, &sm.v_full[vs], 64, key0, h, b);
+          mbar_arrive_expect_tx(&sm.v_full[vs], tile_bytes<HD>());
+          tma_load_tile<HD>(sm.v[vs], &tv, &sm.v_full[vs], key0, h, b);
         }
         if (!ok) break;
       }
@@ -236,7 +251,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc_s = make_idesc(1, 1, 0, 0, BQ, BKV);
-      const uint32_t idesc_o = make_idesc(1, 1, 0, 1, BQ, D);
+      const uint32_t idesc_o = make_idesc(1, 1, 0, 1, BQ, HD);
       const uint32_t q_addr = smem_u32(sm.q), p_addr = smem_u32(sm.p);
       uint32_t st = 0, pt = 0, uc = 0;
       bool ok = true;
@@ -250,7 +265,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t k_addr = smem_u32(sm.k[ks]);
         const uint32_t d_tmem = tmem + S_COL0 + sb * BKV;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
+        for (int kk = 0; kk < HD / 16; ++kk)
           mma_f16_ss(d_tmem, kmajor_desc(q_addr, kk), kmajor_desc(k_addr, kk), idesc_s,
                      kk ? 1u : 0u);
         mma_commit(&sm.k_empty[ks]);
@@ -350,9 +365,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           tc_fence_after();
           const float f = need ? ex2((m_ref - mx) * p.c) : 1.0f;
-          // Load / scale / store the 128 O columns of this row in 4 chunks.
+          // Load / scale / store the HD O columns of this row, 32 at a time.
 #pragma unroll 1
-          for (int c0 = 0; c0 < D; c0 += 32) {
+          for (int c0 = 0; c0 < HD; c0 += 32) {
             uint32_t o[32];
             tmem_ld32_sync(lane_base + O_COL + c0, o);
             uint32_t lo[16], hi[16];
@@ -406,7 +421,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __nv_bfloat16 *orow =
           p.o + b * p.o_s[0] + h * p.o_s[1] + static_cast<int64_t>(q0 + row) * p.o_s[2];
 #pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 32) {
+      for (int c0 = 0; c0 < HD; c0 += 32) {
         uint32_t o[32];
         tmem_ld32_sync(lane_base + O_COL + c0, o);
         uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
@@ -438,9 +453,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 // which cannot keep the exp2 unit busy while the tensor core waits for P. Here
 // a work unit is a 256-row query block split into two 128-row tiles g = 0, 1,
 // each with its own softmax warpgroup (warps 2-5 and 6-9, one warp per TMEM
-// lane quarter each), its own S (TMEM columns 128g) and O (256 + 128g)
+// lane quarter each), its own S (TMEM columns 128g) and O (256 + HD g)
 // accumulators and its own P buffer in shared memory. Each K/V tile is
-// loaded once and used by both query tiles; K and V share one 3-stage ring,
+// loaded once and used by both query tiles; K and V share one ring (3 stages
+// of 32 KiB at HD = 128, 6 of 16 KiB at HD = 64),
 // loaded in the order the MMA thread consumes them (K0, K1, V0, K2, V1, ...).
 // The MMA thread issues S0(j+1), S1(j+1) as soon as the warpgroups have read
 // S(j) into registers, then PV0(j), PV1(j) once P(j) is written, so the
@@ -452,13 +468,18 @@ __global__ void __launch_bounds__(THREADS, 1)
 // threads' row-wise global stores.
 constexpr int NQ = 2;
 constexpr int UNIT_ROWS = NQ * BQ;
-constexpr int KV_STAGES = 3;
 constexpr int THREADS2 = 64 + NQ * 128;
+template <int HD>
+constexpr int kv_stages() {
+  return HD == 128 ? 3 : 6;
+}
 
+template <int HD>
 struct Smem2 {
-  uint8_t q[NQ][TILE_BYTES];
-  uint8_t kv[KV_STAGES][TILE_BYTES];
-  uint8_t p[NQ][TILE_BYTES];
+  static constexpr int KV_STAGES = kv_stages<HD>();
+  uint8_t q[NQ][tile_bytes<HD>()];
+  uint8_t kv[KV_STAGES][tile_bytes<HD>()];
+  uint8_t p[NQ][P_BYTES];
   uint64_t q_full, q_empty;
   uint64_t kv_full[KV_STAGES], kv_empty[KV_STAGES];
   uint64_t s_full[NQ], s_free[NQ];
@@ -469,17 +490,23 @@ struct Smem2 {
   uint32_t tmem_slot;
   int abort_flag;
 };
-constexpr size_t SMEM2_BYTES = sizeof(Smem2) + 1024;
-static_assert(SMEM2_BYTES <= 232448, "two-tile MSM exceeds the opt-in shared memory per block");
+template <int HD>
+constexpr size_t smem2_bytes() {
+  return sizeof(Smem2<HD>) + 1024;
+}
+static_assert(smem2_bytes<128>() <= 232448 && smem2_bytes<64>() <= 232448,
+              "two-tile MSM exceeds the opt-in shared memory per block");
+static_assert(smem_bytes<128>() <= 232448, "single-tile MSM exceeds the opt-in shared memory");
 
-template <bool kTail>
+template <int HD, bool kTail>
 __global__ void __launch_bounds__(THREADS2, 1)
     msm_tc2_bf16_kernel(const __grid_constant__ CUtensorMap tq,
                         const __grid_constant__ CUtensorMap tk,
                         const __grid_constant__ CUtensorMap tv,
                         const __grid_constant__ CUtensorMap to, const Params p) {
   extern __shared__ uint8_t smem_raw[];
-  Smem2 &sm = *reinterpret_cast<Smem2 *>(
+  constexpr int KV_STAGES = kv_stages<HD>();
+  Smem2<HD> &sm = *reinterpret_cast<Smem2<HD> *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   volatile int *abort_flag = &sm.abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -531,9 +558,8 @@ __global__ void __launch_bounds__(THREADS2, 1)
         if (!mbar_wait(&sm.kv_empty[s], ((kvc / KV_STAGES) & 1) ^ 1, abort_flag, p.status,
                        kErrTimeoutEmpty))
           return false;
-        mbar_arrive_expect_tx(&sm.kv_full[s], TILE_BYTES);
-        tma_load_4d(sm.kv[s], map, &sm.kv_full[s], 0, key0, h, b);
-        tma_load_4d(sm.kv[s] + CHUNK_BYTES, map, &sm.kv_full[s], 64, key0, h, b);
+        mbar_arrive_expect_tx(&sm.kv_full[s], tile_bytes<HD>());
+        tma_load_tile<HD>(sm.kv[s], map, &sm.kv_full[s], key0, h, b);
         ++kvc;
         return true;
       };
@@ -542,11 +568,8 @@ __global__ void __launch_bounds__(THREADS2, 1)
         unit_coords(p, u, b, h, q0);
         q0 *= UNIT_ROWS;
         if (!mbar_wait(&sm.q_empty, (uc & 1) ^ 1, abort_flag, p.status, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&sm.q_full, NQ * TILE_BYTES);
-        for (int g = 0; g < NQ; ++g) {
-          tma_load_4d(sm.q[g], &tq, &sm.q_full, 0, q0 + g * BQ, h, b);
-          tma_load_4d(sm.q[g] + CHUNK_BYTES, &tq, &sm.q_full, 64, q0 + g * BQ, h, b);
-        }
+        mbar_arrive_expect_tx(&sm.q_full, NQ * tile_bytes<HD>());
+        for (int g = 0; g < NQ; ++g) tma_load_tile<HD>(sm.q[g], &tq, &sm.q_full, q0 + g * BQ, h, b);
         if (!(ok = load_tile(&tk, 0, h, b))) break;
         for (int64_t t = 0; t < nkv && ok; ++t) {
           if (t + 1 < nkv && !(ok = load_tile(&tk, static_cast<int32_t>((t + 1) * BKV), h, b)))
@@ -559,7 +582,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc_s = make_idesc(1, 1, 0, 0, BQ, BKV);
-      const uint32_t idesc_o = make_idesc(1, 1, 0, 1, BQ, D);
+      const uint32_t idesc_o = make_idesc(1, 1, 0, 1, BQ, HD);
       uint32_t kvc = 0, s_cnt = 0, p_cnt = 0, uc = 0;
       bool ok = true;
       auto kv_stage = [&](uint32_t &addr) -> int {
@@ -580,7 +603,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
           tc_fence_after();
           const uint32_t q_addr = smem_u32(sm.q[g]);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
+          for (int kk = 0; kk < HD / 16; ++kk)
             mma_f16_ss(tmem + S_COL0 + g * BKV, kmajor_desc(q_addr, kk), kmajor_desc(k_addr, kk),
                        idesc_s, kk ? 1u : 0u);
           mma_commit(&sm.s_full[g]);
@@ -604,7 +627,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
           const uint32_t p_addr = smem_u32(sm.p[g]);
 #pragma unroll
           for (int kk = 0; kk < BKV / 16; ++kk)
-            mma_f16_ss(tmem + O_COL + g * D, kmajor_desc(p_addr, kk), mnmajor_desc(v_addr, kk),
+            mma_f16_ss(tmem + O_COL + g * HD, kmajor_desc(p_addr, kk), mnmajor_desc(v_addr, kk),
                        idesc_o, (t | kk) ? 1u : 0u);
           mma_commit(&sm.p_free[g]);
           // Query tile g's output is final after its last PV: its epilogue
@@ -639,7 +662,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
     const int sub = warp & 3;
     const int row = sub * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(sub * 32) << 16);
-    const uint32_t s_col = S_COL0 + g * BKV, o_col = O_COL + g * D;
+    const uint32_t s_col = S_COL0 + g * BKV, o_col = O_COL + g * HD;
     uint8_t *p_row = sm.p[g] + row * 128;
     const int rsw = row & 7;
     const bool leader = (threadIdx.x & 127) == 0;  // issues this warpgroup's O stores
@@ -702,7 +725,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
           const float f = need ? ex2((m_ref - mx) * p.c) : 1.0f;
           // 16 columns at a time: the 128 scores stay live across this loop.
 #pragma unroll 1
-          for (int c0 = 0; c0 < D; c0 += 16) {
+          for (int c0 = 0; c0 < HD; c0 += 16) {
             uint32_t o[16];
             tmem_ld16_sync(lane_base + o_col + c0, o);
 #pragma unroll
@@ -772,7 +795,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
         // Coalescing through TMA keeps the per-row 16-byte stores of 128
         // threads off the load/store unit between two work units.
 #pragma unroll 1
-        for (int c0 = 0; c0 < D; c0 += 32) {
+        for (int c0 = 0; c0 < HD; c0 += 32) {
           uint32_t o[32];
           tmem_ld32_sync(lane_base + o_col + c0, o);
           uint8_t *dst = p_row + (c0 >> 6) * CHUNK_BYTES;
@@ -794,8 +817,9 @@ __global__ void __launch_bounds__(THREADS2, 1)
         if (leader) {
           if (!(ok = mbar_wait(&sm.o_staged[g], uc & 1, abort_flag, p.status, kErrTimeoutAccum)))
             break;
-          tma_store_4d(&to, sm.p[g], 0, q0, h, b);
-          tma_store_4d(&to, sm.p[g] + CHUNK_BYTES, 64, q0, h, b);
+#pragma unroll
+          for (int c = 0; c < HD / 64; ++c)
+            tma_store_4d(&to, sm.p[g] + c * CHUNK_BYTES, c * 64, q0, h, b);
           bulk_commit();
         }
       } else {
@@ -803,7 +827,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
         __nv_bfloat16 *orow =
             p.o + b * p.o_s[0] + h * p.o_s[1] + static_cast<int64_t>(q0 + row) * p.o_s[2];
 #pragma unroll 1
-        for (int c0 = 0; c0 < D; c0 += 32) {
+        for (int c0 = 0; c0 < HD; c0 += 32) {
           uint32_t o[32];
           tmem_ld32_sync(lane_base + o_col + c0, o);
           uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
@@ -842,15 +866,17 @@ bool encode_tmap_4d_bf16(CUtensorMap *map, const void *base, uint64_t d0, uint64
 cudaError_t launch_msm_tc_bf16(const void *q, const void *k, const void *v, void *o,
                                const MsmShape &s, float scale, uint32_t *status, int sms,
                                cudaStream_t stream, LaunchInfo *info) {
-  if (s.m <= 0 || s.n <= 0 || s.dqk != D || s.dv != D) return cudaErrorNotSupported;
+  if (s.m <= 0 || s.n <= 0 || s.dqk != s.dv || (s.dqk != 64 && s.dqk != 128))
+    return cudaErrorNotSupported;
+  const int hd = static_cast<int>(s.dqk);
   CUtensorMap tq, tk, tv;
   auto enc = [&](CUtensorMap *map, const void *base, int64_t rows, const int64_t *st) {
-    // dims {D, rows, heads, batch}; byte strides of rows/heads/batch. A unit
+    // dims {HD, rows, heads, batch}; byte strides of rows/heads/batch. A unit
     // dimension gets a harmless stride (TMA only needs it 16-byte aligned).
     const uint64_t srow = static_cast<uint64_t>(st[2]) * 2;
     const uint64_t sh = s.heads > 1 ? static_cast<uint64_t>(st[1]) * 2 : srow * rows;
     const uint64_t sb = s.batch > 1 ? static_cast<uint64_t>(st[0]) * 2 : sh * s.heads;
-    return encode_tmap_4d_bf16(map, base, D, rows, s.heads, s.batch, srow, sh, sb);
+    return encode_tmap_4d_bf16(map, base, hd, rows, s.heads, s.batch, srow, sh, sb);
   };
   // cudaErrorNotSupported (nothing launched) lets the caller take another kernel.
   if (!enc(&tq, q, s.m, s.q_s) || !enc(&tk, k, s.n, s.k_s) || !enc(&tv, v, s.n, s.v_s))
@@ -882,32 +908,43 @@ cudaError_t launch_msm_tc_bf16(const void *q, const void *k, const void *v, void
   int grid = static_cast<int>(p.units < sms ? p.units : sms);
   // Key-tail masking is compiled only into the instantiations that need it,
   // so full key tiles run exactly the unmasked loop.
-  auto run2 = [&](auto kernel) -> cudaError_t {
+  auto run2 = [&](auto kernel, size_t smem) -> cudaError_t {
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(SMEM2_BYTES));
+                                           static_cast<int>(smem));
     if (err != cudaSuccess) return err;
-    kernel<<<grid, THREADS2, SMEM2_BYTES, stream>>>(tq, tk, tv, to, p);
+    kernel<<<grid, THREADS2, smem, stream>>>(tq, tk, tv, to, p);
     return cudaSuccess;
   };
-  auto run1 = [&](auto kernel) -> cudaError_t {
+  auto run1 = [&](auto kernel, size_t smem) -> cudaError_t {
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(SMEM_BYTES));
+                                           static_cast<int>(smem));
     if (err != cudaSuccess) return err;
-    kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tq, tk, tv, p);
+    kernel<<<grid, THREADS, smem, stream>>>(tq, tk, tv, p);
     return cudaSuccess;
   };
   const bool tail = p.n_tail != 0;
-  if (two)
-    e = tail ? run2(msm_tc2_bf16_kernel<true>) : run2(msm_tc2_bf16_kernel<false>);
-  else
-    e = tail ? run1(msm_tc_bf16_kernel<true>) : run1(msm_tc_bf16_kernel<false>);
+  if (hd == 128) {
+    if (two)
+      e = tail ? run2(msm_tc2_bf16_kernel<128, true>, smem2_bytes<128>())
+               : run2(msm_tc2_bf16_kernel<128, false>, smem2_bytes<128>());
+    else
+      e = tail ? run1(msm_tc_bf16_kernel<128, true>, smem_bytes<128>())
+               : run1(msm_tc_bf16_kernel<128, false>, smem_bytes<128>());
+  } else {
+    if (two)
+      e = tail ? run2(msm_tc2_bf16_kernel<64, true>, smem2_bytes<64>())
+               : run2(msm_tc2_bf16_kernel<64, false>, smem2_bytes<64>());
+    else
+      e = tail ? run1(msm_tc_bf16_kernel<64, true>, smem_bytes<64>())
+               : run1(msm_tc_bf16_kernel<64, false>, smem_bytes<64>());
+  }
   if (e != cudaSuccess) return e;
   if (info) {
     info->launches = 1;
     info->tile_m = two ? UNIT_ROWS : BQ;
     info->tile_n = BKV;
-    info->tile_k = D;
-    info->stages = two ? KV_STAGES : KSTAGES;
+    info->tile_k = hd;
+    info->stages = two ? (hd == 128 ? kv_stages<128>() : kv_stages<64>()) : KSTAGES;
     info->ctas = grid;
     info->set_route("tcgen05_bf16_msm");
   }

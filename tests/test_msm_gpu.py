@@ -3,7 +3,8 @@
 * The reference's own Family C cases (tests/test_family_c.py:102-179): f32,
   unscaled softmax, N(0, 0.65) inputs from default_rng(seed), max-abs
   tolerance 2e-3 -- M != N, V width != QK width, and the D=64 route.
-* bf16 batched [B,H,S,D] at D=128: relative Frobenius error <= 1e-2.
+* bf16 batched [B,H,S,D] at D=64 and D=128 (tensor cores): relative
+  Frobenius error <= 1e-2.
 """
 import numpy as np
 import pytest
@@ -82,7 +83,11 @@ def _check_msm(mcb, orc, pairs, scale, route, pairs_to_check=None):
     ((1, 1, 200, 128), "tcgen05_bf16_msm"),   # ragged M: one partial 256-row block
     ((2, 3, 1000, 128), "tcgen05_bf16_msm"),  # ragged M, two-tile units
     ((1, 2, 300, 128), "tcgen05_bf16_msm"),   # ragged M, single-tile units
-    ((2, 2, 128, 64), "simt_tiled_online_softmax_msm"),  # D = 64: tiled CUDA-core kernel
+    ((2, 2, 128, 64), "tcgen05_bf16_msm"),    # D = 64: one 64-column chunk per tile
+    ((2, 3, 1536, 64), "tcgen05_bf16_msm"),
+    ((1, 1, 200, 64), "tcgen05_bf16_msm"),
+    ((2, 3, 1000, 64), "tcgen05_bf16_msm"),
+    ((1, 2, 300, 64), "tcgen05_bf16_msm"),
     ((1, 3, 200, 32), "simt_tiled_online_softmax_msm"),
     ((1, 2, 100, 96), "simt_online_softmax_msm"),         # other widths: row-per-warp kernel
 ])
@@ -96,18 +101,21 @@ def test_tcgen05_rescale_path(mcb, orc):
                128 ** -0.5, "tcgen05_bf16_msm")
 
 
-@pytest.mark.parametrize("rows", [256, 512])
-def test_tcgen05_rescale_path_by_route(mcb, orc, rows):
-    """Growing key tiles with one and two 256-row units per (b, h)."""
-    _check_msm(mcb, orc, _bf16_case((1, 2, rows, 128), 15, kv_len=768, k_growth=0.6),
-               128 ** -0.5, "tcgen05_bf16_msm")
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("rows", [128, 256, 512])
+def test_tcgen05_rescale_path_by_route(mcb, orc, rows, d):
+    """Growing key tiles with one and two 256-row units per (b, h), and
+    single-tile (128-row) units."""
+    _check_msm(mcb, orc, _bf16_case((1, 2, rows, d), 15, kv_len=768, k_growth=0.6),
+               d ** -0.5, "tcgen05_bf16_msm")
 
 
+@pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("rows,kv", [(256, 333), (129, 1), (517, 130), (1000, 1001)])
-def test_tcgen05_ragged_keys(mcb, orc, rows, kv):
+def test_tcgen05_ragged_keys(mcb, orc, rows, kv, d):
     """N not a multiple of 128: the partial last key tile is masked (its
     zero-filled keys must not enter the softmax); M ragged as well."""
-    _check_msm(mcb, orc, _bf16_case((1, 2, rows, 128), rows + kv, kv_len=kv), 128 ** -0.5,
+    _check_msm(mcb, orc, _bf16_case((1, 2, rows, d), rows + kv, kv_len=kv), d ** -0.5,
                "tcgen05_bf16_msm")
 
 
@@ -117,12 +125,13 @@ def test_tcgen05_unscaled_reference_semantics(mcb, orc, rows):
     _check_msm(mcb, orc, _bf16_case((1, 1, rows, 128), 6, kv_len=640), 1.0, "tcgen05_bf16_msm")
 
 
+@pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("s,n", [(256, 640), (512, 640), (300, 601)])
-def test_tcgen05_rectangular_and_strided(mcb, orc, s, n):
+def test_tcgen05_rectangular_and_strided(mcb, orc, s, n, d):
     """M != N, and Q/K/V as strided views of a packed [B, S, 3, H, D] tensor
     (TMA stores of O clipped at a ragged M, a masked partial key tile)."""
     import torch
-    b, h, d = 2, 2, 128
+    b, h = 2, 2
     rng = np.random.default_rng(9)
     packed = rng.standard_normal((b, n, 3, h, d), dtype=np.float32)
     ph, pf = gu.bf16_pair(packed)
@@ -161,7 +170,9 @@ def test_config3_full_size_sampled(mcb, orc):
 def test_tiled_cuda_core_msm(mcb, orc, dtype, shape):
     """The tiled CUDA-core kernel (f32 and bf16 inputs, D in {32, 64, 128}):
     ragged M and N (zero-filled rows, masked keys), single keys, single
-    queries. f32 at the reference's max-abs 2e-3; bf16 at 1e-2 rel. Frobenius."""
+    queries. f32 at the reference's max-abs 2e-3; bf16 at 1e-2 rel. Frobenius.
+    bf16 operands are row-padded views (row stride D + 2, not 16-byte
+    aligned), which the tensor-core kernels do not take."""
     import torch
     b, h, m, n, d = shape
     rng = np.random.default_rng(sum(shape))
@@ -170,14 +181,13 @@ def test_tiled_cuda_core_msm(mcb, orc, dtype, shape):
     v = rng.normal(0.0, 1.0, size=(b, h, n, d)).astype(np.float32)
     if dtype == "bf16":
         (qh, qf), (kh, kf), (vh, vf) = (gu.bf16_pair(x) for x in (q, k, v))
-        args = [gu.to_dev_bf16(x) for x in (qh, kh, vh)]
+        pad = [(0, 0)] * 3 + [(0, 2)]
+        args = [gu.to_dev_bf16(np.pad(x, pad))[..., :d] for x in (qh, kh, vh)]
     else:
         qf, kf, vf = q, k, v
         args = [torch.from_numpy(x).cuda() for x in (q, k, v)]
     o = mcb.msm(*args, d ** -0.5)
-    tc = dtype == "bf16" and d == 128  # bf16 at D = 128 runs on the tensor cores
-    assert mcb.api.last_result.route == ("tcgen05_bf16_msm" if tc else
-                                          "simt_tiled_online_softmax_msm")
+    assert mcb.api.last_result.route == "simt_tiled_online_softmax_msm"
     got = gu.from_dev(o)
     for bi in range(b):
         for hi in range(h):

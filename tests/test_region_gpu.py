@@ -20,7 +20,7 @@ def _inputs(b, s, d, seed):
 # (2, 300, 512, 4): a sequence length that is not a multiple of 128 (ragged
 # query block and masked last key tile in the MSM).
 @pytest.mark.parametrize("shape", [(1, 256, 512, 4), (2, 128, 256, 2), (1, 384, 1024, 8),
-                                   (2, 300, 512, 4)])
+                                   (2, 300, 512, 4), (1, 256, 512, 8), (2, 300, 256, 4)])
 def test_block_small_full(mcb, orc, shape):
     b, s, d, heads = shape
     pairs = _inputs(b, s, d, seed=sum(shape))
