@@ -194,12 +194,27 @@ MCB_API mcb_status mcb_strict_fused_pair_f32_noalloc_v1(const mcb_tensor *e, con
 
 /* ---- typed isolated GEMMs (bit-exact with the reference's typed references) */
 /* C[M,N] int32 = A[M,K] int8 * B[K,N] int8, accumulated modulo 2^32. Runs on
- * tcgen05 (kind::i8) when K is a multiple of 16 (B is transposed into device
- * scratch first), else on CUDA cores; integer sums are exact either way.
- * Counterpart of cpu_reference_gemm_i8_i32_v1
+ * tcgen05 (kind::i8) when A's rows and C are 16-byte aligned: B is read in
+ * place when its rows are 16-byte aligned, else (K a multiple of 16) it is
+ * transposed into device scratch first. Other layouts run on CUDA cores;
+ * integer sums are exact either way. Counterpart of
+ * cpu_reference_gemm_i8_i32_v1
  * (compiler/lib/runtime/cpu_numeric_reference.h:58-61, .cpp:185-209). */
 MCB_API mcb_status mcb_gemm_i8_i32_v1(const mcb_tensor *c, const mcb_tensor *a,
                                       const mcb_tensor *b, const mcb_exec *exec) MCB_NOEXCEPT;
+/* Quantized matmul with zero points: C[m,n] = sum_k (A[m,k] - a_zero_point) *
+ * (B[k,n] - b_zero_point) in wrapping int32 arithmetic, the legacy int8
+ * path's linalg.quantized_matmul (src/mlir_engine.cpp:944-958; the zero
+ * point of each operand is its own when its quantization is enabled, else
+ * the kernel's global one: the caller passes the resolved values). Same
+ * routes as mcb_gemm_i8_i32_v1; on tcgen05 the raw codes are multiplied and
+ * the epilogue adds K*za*zb - zb*rowsum(A) - za*colsum(B) (one pre-pass
+ * computes the sums into device scratch). Zero points 0 give
+ * mcb_gemm_i8_i32_v1's result. */
+MCB_API mcb_status mcb_gemm_i8_i32_zp_v1(const mcb_tensor *c, const mcb_tensor *a,
+                                         const mcb_tensor *b, int32_t a_zero_point,
+                                         int32_t b_zero_point,
+                                         const mcb_exec *exec) MCB_NOEXCEPT;
 /* C[M,N] f32 = A[M,K] bf16 * B[K,N] bf16 with one f32 fma per k in
  * increasing order from +0 (CUDA cores; bit-exact). Counterpart of
  * cpu_reference_gemm_bf16_f32_v1 (cpu_numeric_reference.h:45-48, .cpp:108-127). */
@@ -338,7 +353,8 @@ enum {
   MCB_PLAN_GEMM_CHAIN = 4,    /* e, a, b, boundary, w */
   MCB_PLAN_MSM = 5,           /* o, q, k, v */
   MCB_PLAN_FP8_GEMM = 6,      /* c, a, sa, bt, sbt */
-  MCB_PLAN_ATTN_BLOCK = 7     /* y, x, wq, wk, wv, wo */
+  MCB_PLAN_ATTN_BLOCK = 7,    /* y, x, wq, wk, wv, wo */
+  MCB_PLAN_GEMM_I8 = 8        /* c, a, b (zero points from the descriptor) */
 };
 #define MCB_PLAN_MAX_TENSORS 8
 typedef struct mcb_plan_desc {
@@ -357,7 +373,9 @@ typedef struct mcb_plan_desc {
   int64_t heads;         /* ATTN_BLOCK */
   float eps;             /* ATTN_BLOCK */
   uint32_t reserved1;
-  uint64_t reserved[2];
+  int32_t a_zero_point;  /* GEMM_I8 */
+  int32_t b_zero_point;  /* GEMM_I8 */
+  uint64_t reserved;
 } mcb_plan_desc;
 typedef struct mcb_plan mcb_plan;
 MCB_API mcb_status mcb_plan_create_v1(const mcb_plan_desc *desc, mcb_plan **out) MCB_NOEXCEPT;

@@ -98,7 +98,7 @@ class Fp8TileConfig(ctypes.Structure):
 
 PLAN_MAX_TENSORS = 8
 PLAN_OPS = {"strict_pair": 1, "strict_gemm": 2, "gemm_epilogue": 3, "gemm_chain": 4, "msm": 5,
-            "fp8_gemm": 6, "attn_block": 7}
+            "fp8_gemm": 6, "attn_block": 7, "gemm_i8_i32": 8}
 
 
 class PlanDesc(ctypes.Structure):
@@ -108,7 +108,9 @@ class PlanDesc(ctypes.Structure):
         ("num_tensors", ctypes.c_uint32), ("tensors", Tensor * PLAN_MAX_TENSORS),
         ("epilogue", Epilogue), ("gemm_flags", ctypes.c_uint32), ("reserved0", ctypes.c_uint32),
         ("scale", ctypes.c_double), ("block", ctypes.c_int64), ("heads", ctypes.c_int64),
-        ("eps", ctypes.c_float), ("reserved1", ctypes.c_uint32), ("reserved", ctypes.c_uint64 * 2),
+        ("eps", ctypes.c_float), ("reserved1", ctypes.c_uint32),
+        ("a_zero_point", ctypes.c_int32), ("b_zero_point", ctypes.c_int32),
+        ("reserved", ctypes.c_uint64),
     ]
 
 
@@ -132,6 +134,7 @@ SIGNATURES = {
     "mcb_gemm_epilogue_v1": (ctypes.c_int32, [_T, _T, _T, _T, _P(Epilogue), ctypes.c_uint32, _E]),
     "mcb_gemm_chain_v1": (ctypes.c_int32, [_T, _T, _T, _T, _P(Epilogue), _T, _E]),
     "mcb_gemm_i8_i32_v1": (ctypes.c_int32, [_T, _T, _T, _E]),
+    "mcb_gemm_i8_i32_zp_v1": (ctypes.c_int32, [_T, _T, _T, ctypes.c_int32, ctypes.c_int32, _E]),
     "mcb_gemm_bf16_f32_fma_v1": (ctypes.c_int32, [_T, _T, _T, _E]),
     "mcb_msm_v1": (ctypes.c_int32, [_T, _T, _T, _T, ctypes.c_double, _E]),
     "mcb_fp8_quantize_blockwise_v1": (ctypes.c_int32, [_T, _T, _T, ctypes.c_int64, _E]),

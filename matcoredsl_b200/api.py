@@ -156,18 +156,35 @@ def strict_gemm(a, b, out=None, *, device=-1, flags=0):
     return out
 
 
-def gemm_i8_i32(a, b, out=None, *, device=-1, flags=0, workspace=None):
-    """C = A @ B for int8 operands, int32 result modulo 2^32 (bit-exact).
+def gemm_i8_i32(a, b, out=None, *, a_zero_point=0, b_zero_point=0, device=-1, flags=0,
+                workspace=None):
+    """C = (A - a_zero_point) @ (B - b_zero_point) for int8 operands, int32
+    result modulo 2^32 (bit-exact); zero points 0 give the plain int8 GEMM,
+    non-zero ones the legacy quantized matmul (mcb_gemm_i8_i32_zp_v1).
     `workspace` (optional CUDA tensor) holds the B^T copy that B rows which
-    are not 16-byte aligned need."""
+    are not 16-byte aligned need, and the zero points' row/column sums."""
     if out is None:
         if _is_torch(a):
             torch = _torch()
             out = torch.empty(a.shape[0], b.shape[1], dtype=torch.int32, device=a.device)
         else:
             out = np.empty((a.shape[0], b.shape[1]), np.int32)
-    _call("mcb_gemm_i8_i32_v1", [("c", out), ("a", a), ("b", b)], [], device, flags, workspace)
+    za, zb = _zero_point(a_zero_point), _zero_point(b_zero_point)
+    if za or zb:
+        _call("mcb_gemm_i8_i32_zp_v1", [("c", out), ("a", a), ("b", b)],
+              [ctypes.c_int32(za), ctypes.c_int32(zb)], device, flags, workspace)
+    else:
+        _call("mcb_gemm_i8_i32_v1", [("c", out), ("a", a), ("b", b)], [], device, flags,
+              workspace)
     return out
+
+
+def _zero_point(z) -> int:
+    """An int32 zero point (the reference stores them as std::int32_t)."""
+    z = int(z)
+    if not -2 ** 31 <= z < 2 ** 31:
+        raise ValueError(f"zero point {z} does not fit in int32")
+    return z
 
 
 def gemm_bf16_f32_fma(a, b, out=None, *, device=-1, flags=0):
@@ -311,7 +328,8 @@ class Plan:
     bias/boundary slot."""
 
     def __init__(self, op, *templates, graph=False, device=-1, bias_mode="none", bias_op="add",
-                 act="none", w_transposed=False, scale=1.0, block=128, heads=0, eps=1e-6):
+                 act="none", w_transposed=False, scale=1.0, block=128, heads=0, eps=1e-6,
+                 a_zero_point=0, b_zero_point=0):
         lib = _abi.load()
         d = _abi.PlanDesc()
         d.abi_version = _abi.ABI_VERSION
@@ -332,6 +350,8 @@ class Plan:
         d.epilogue = _abi.make_epilogue(bias_mode, bias_op, act)
         d.gemm_flags = _abi.GEMM_W_TRANSPOSED if w_transposed else 0
         d.scale, d.block, d.heads, d.eps = float(scale), int(block), int(heads), float(eps)
+        d.a_zero_point, d.b_zero_point = _zero_point(a_zero_point), _zero_point(b_zero_point)
+        self._zero_points = (d.a_zero_point, d.b_zero_point)
         self._handle = ctypes.c_void_p()
         _abi.check(lib.mcb_plan_create_v1(ctypes.byref(d), ctypes.byref(self._handle)),
                    "mcb_plan_create_v1")
@@ -342,7 +362,15 @@ class Plan:
     def generation(self) -> int:
         return int(_abi.load().mcb_plan_generation_v1(self._handle))
 
-    def execute(self, *tensors):
+    def execute(self, *tensors, a_zero_point=None, b_zero_point=None):
+        """Runs the plan. Zero points given here must equal the plan's (the
+        reference's execute_plan rejects tensors whose quantization metadata
+        differs from the plan's)."""
+        for given, frozen, name in ((a_zero_point, self._zero_points[0], "a"),
+                                    (b_zero_point, self._zero_points[1], "b")):
+            if given is not None and _zero_point(given) != frozen:
+                raise RuntimeError(f"quantization mismatch: {name}_zero_point {given} "
+                                   f"differs from the plan's {frozen}")
         arr = (_abi.Tensor * self._n)()
         for i, t in enumerate(tensors):
             if t is not None:

@@ -835,7 +835,7 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
 
 // ---- typed GEMMs --------------------------------------------------------------------------
 mcb_status typed_gemm_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_tensor *b,
-                           const mcb_exec *exec, bool int8) {
+                           const mcb_exec *exec, bool int8, int32_t za = 0, int32_t zb = 0) {
   mcb_status s;
   if ((s = check_tensor(a, 2, 2)) || (s = check_tensor(b, 2, 2)) || (s = check_tensor(c, 2, 2)))
     return s;
@@ -864,32 +864,56 @@ mcb_status typed_gemm_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_t
     const bool tc = k > 0 && lda % 16 == 0 && (reinterpret_cast<uintptr_t>(da) % 16 == 0) &&
                     c->strides[0] % 4 == 0 && (reinterpret_cast<uintptr_t>(dc) % 16 == 0);
     const bool b_direct = ldb % 16 == 0 && (reinterpret_cast<uintptr_t>(db) % 16 == 0);
-    if (tc && b_direct) {
-      // B [K,N] read MN-major in place: one launch, no scratch.
-      err = mcb::launch_gemm_i8_tc(static_cast<const int8_t *>(da), lda,
-                                   static_cast<const int8_t *>(db), ldb, 1,
-                                   static_cast<int32_t *>(dc), m, n, k, c->strides[0],
-                                   call.ctx()->status, call.sms(), call.stream(), &info);
-    } else if (tc && k % 16 == 0) {
-      // B rows not 16-byte aligned: transpose into a dense B^T [N,K] scratch
-      // (row stride K) first.
-      const uint64_t bytes = static_cast<uint64_t>(n) * static_cast<uint64_t>(k);
-      void *bt = nullptr;
-      if ((s = call.scratch(bytes, &bt))) return s;
-      err = mcb::launch_transpose_u8(db, bt, k, n, ldb, call.stream());
-      if (err == cudaSuccess) {
-        info.launches = 1;
-        err = mcb::launch_gemm_i8_tc(static_cast<const int8_t *>(da), lda,
-                                     static_cast<const int8_t *>(bt), k, 0,
-                                     static_cast<int32_t *>(dc), m, n, k, c->strides[0],
-                                     call.ctx()->status, call.sms(), call.stream(), &info);
+    if (tc && (b_direct || k % 16 == 0)) {
+      // B [K,N] is read MN-major in place when its rows are 16-byte aligned;
+      // otherwise it is first transposed into a dense B^T [N,K] (row stride
+      // K). Zero points add a pre-pass for the row sums of A and column
+      // sums of B. One scratch block: [B^T][row sums][column sums], each
+      // part 16-byte aligned.
+      auto up16 = [](uint64_t x) { return (x + 15) & ~uint64_t{15}; };
+      const uint64_t bt_bytes =
+          b_direct ? 0 : up16(static_cast<uint64_t>(n) * static_cast<uint64_t>(k));
+      const uint64_t rs_bytes = zb != 0 ? up16(static_cast<uint64_t>(m) * 4) : 0;
+      const uint64_t cs_bytes = za != 0 ? up16(static_cast<uint64_t>(n) * 4) : 0;
+      uint8_t *scr = nullptr;
+      if (bt_bytes + rs_bytes + cs_bytes > 0) {
+        void *p = nullptr;
+        if ((s = call.scratch(bt_bytes + rs_bytes + cs_bytes, &p))) return s;
+        scr = static_cast<uint8_t *>(p);
       }
+      const int8_t *bop = static_cast<const int8_t *>(db);
+      int64_t ld_bop = ldb;
+      int b_mn = 1;
+      err = cudaSuccess;
+      if (!b_direct) {
+        err = mcb::launch_transpose_u8(db, scr, k, n, ldb, call.stream());
+        info.launches = 1;
+        bop = reinterpret_cast<const int8_t *>(scr);
+        ld_bop = k;
+        b_mn = 0;
+      }
+      mcb::I8ZeroPoints zpv;
+      zpv.za = za;
+      zpv.zb = zb;
+      zpv.row_sum = rs_bytes ? reinterpret_cast<int32_t *>(scr + bt_bytes) : nullptr;
+      zpv.col_sum = cs_bytes ? reinterpret_cast<int32_t *>(scr + bt_bytes + rs_bytes) : nullptr;
+      const bool zp_on = za != 0 || zb != 0;
+      if (err == cudaSuccess && zp_on)
+        err = mcb::launch_i8_zero_point_sums(
+            static_cast<const int8_t *>(da), lda, bop, ld_bop, b_mn, m, n, k, zpv,
+            const_cast<int32_t *>(zpv.row_sum), const_cast<int32_t *>(zpv.col_sum), call.sms(),
+            call.stream(), &info);
+      if (err == cudaSuccess)
+        err = mcb::launch_gemm_i8_tc(static_cast<const int8_t *>(da), lda, bop, ld_bop, b_mn,
+                                     static_cast<int32_t *>(dc), m, n, k, c->strides[0],
+                                     zp_on ? &zpv : nullptr, call.ctx()->status, call.sms(),
+                                     call.stream(), &info);
     }
     if (err == cudaErrorNotSupported) {
       info.launches = 0;
       err = mcb::launch_gemm_i8_simt(static_cast<const int8_t *>(da),
                                      static_cast<const int8_t *>(db), static_cast<int32_t *>(dc),
-                                     m, n, k, a->strides[0], b->strides[0], c->strides[0],
+                                     m, n, k, a->strides[0], b->strides[0], c->strides[0], za, zb,
                                      call.stream(), &info);
     }
   }
@@ -1422,6 +1446,16 @@ MCB_API mcb_status mcb_gemm_i8_i32_v1(const mcb_tensor *c, const mcb_tensor *a,
                                       const mcb_tensor *b, const mcb_exec *exec) noexcept {
   try {
     return typed_gemm_impl(c, a, b, exec, true);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API mcb_status mcb_gemm_i8_i32_zp_v1(const mcb_tensor *c, const mcb_tensor *a,
+                                         const mcb_tensor *b, int32_t a_zero_point,
+                                         int32_t b_zero_point, const mcb_exec *exec) noexcept {
+  try {
+    return typed_gemm_impl(c, a, b, exec, true, a_zero_point, b_zero_point);
   } catch (...) {
     return MCB_STATUS_CANDIDATE_FAILURE;
   }

@@ -111,12 +111,30 @@ cudaError_t launch_transpose_u8(const void *in, void *out, int64_t rows, int64_t
 // b_mn = 1: b is B [K,N] (row stride ldb), read MN-major; b_mn = 0: b is
 // Bt [N,K] (row stride ldb), read K-major. Returns cudaErrorNotSupported when
 // a stride or base is not 16-byte aligned or k == 0.
+// Zero points of a quantized int8 GEMM, C = sum_k (A - za)(B - zb) modulo
+// 2^32, applied in the epilogue as C = A.B + k*za*zb - zb*row_sum[m] -
+// za*col_sum[n] (an identity in wrapping int32 arithmetic). row_sum is
+// needed when zb != 0, col_sum when za != 0 (each 16-byte aligned).
+struct I8ZeroPoints {
+  int32_t za = 0, zb = 0;
+  const int32_t *row_sum = nullptr;  // sum_k A[m,k], M entries
+  const int32_t *col_sum = nullptr;  // sum_k B[k,n], N entries
+};
 cudaError_t launch_gemm_i8_tc(const int8_t *a, int64_t lda, const int8_t *b, int64_t ldb,
                               int b_mn, int32_t *c, int64_t m, int64_t n, int64_t k, int64_t ld_c,
-                              uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info);
+                              const I8ZeroPoints *zp, uint32_t *status, int sms,
+                              cudaStream_t stream, LaunchInfo *info);
+// The sums I8ZeroPoints needs: row_sum of A [M,K] (when zb != 0) and col_sum
+// of B (when za != 0), B given as [K,N] (b_mn = 1, row stride ldb) or as its
+// transpose Bt [N,K] (b_mn = 0). Rows must be 16-byte aligned for the
+// vector path (other strides use byte loads).
+cudaError_t launch_i8_zero_point_sums(const int8_t *a, int64_t lda, const int8_t *b, int64_t ldb,
+                                      int b_mn, int64_t m, int64_t n, int64_t k,
+                                      const I8ZeroPoints &zp, int32_t *row_sum, int32_t *col_sum,
+                                      int sms, cudaStream_t stream, LaunchInfo *info);
 cudaError_t launch_gemm_i8_simt(const int8_t *a, const int8_t *b, int32_t *c, int64_t m, int64_t n,
-                                int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
-                                cudaStream_t stream, LaunchInfo *info);
+                                int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t za,
+                                int32_t zb, cudaStream_t stream, LaunchInfo *info);
 cudaError_t launch_gemm_bf16_fma(const void *a, const void *b, float *c, int64_t m, int64_t n,
                                  int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
                                  cudaStream_t stream, LaunchInfo *info);

@@ -48,6 +48,7 @@ uint32_t slots_for(uint32_t op) {
     case MCB_PLAN_MSM: return 4;
     case MCB_PLAN_FP8_GEMM: return 5;
     case MCB_PLAN_ATTN_BLOCK: return 6;
+    case MCB_PLAN_GEMM_I8: return 3;
     default: return 0;
   }
 }
@@ -91,6 +92,9 @@ mcb_status run_op(const mcb_plan &p, const mcb_tensor *t, cudaStream_t stream) {
     case MCB_PLAN_ATTN_BLOCK:
       return mcb_attn_block_region_v1(&t[0], &t[1], &t[2], &t[3], &t[4], &t[5], p.desc.heads,
                                       p.desc.eps, &ex);
+    case MCB_PLAN_GEMM_I8:
+      return mcb_gemm_i8_i32_zp_v1(&t[0], &t[1], &t[2], p.desc.a_zero_point,
+                                   p.desc.b_zero_point, &ex);
     default:
       return MCB_STATUS_INVALID_ARGUMENT;
   }
@@ -105,6 +109,18 @@ uint64_t workspace_for(const mcb_plan_desc &d) {
     const mcb_tensor &a = d.tensors[1], &b = d.tensors[2];
     const uint64_t esz = a.dtype == MCB_DTYPE_BF16 ? 2 : 4;
     return static_cast<uint64_t>(a.dims[0]) * ((b.dims[1] + 7) / 8 * 8) * esz;
+  }
+  if (d.op == MCB_PLAN_GEMM_I8) {
+    // B^T when B's rows are not 16-byte aligned, then the zero-point row and
+    // column sums (the int8 entry point's scratch layout).
+    const mcb_tensor &a = d.tensors[1], &b = d.tensors[2];
+    auto up16 = [](uint64_t x) { return (x + 15) & ~uint64_t{15}; };
+    const uint64_t m = static_cast<uint64_t>(a.dims[0]), k = static_cast<uint64_t>(a.dims[1]);
+    const uint64_t n = static_cast<uint64_t>(b.dims[1]);
+    uint64_t bytes = b.strides[0] % 16 != 0 ? up16(n * k) : 0;
+    if (d.b_zero_point != 0) bytes += up16(m * 4);
+    if (d.a_zero_point != 0) bytes += up16(n * 4);
+    return bytes;
   }
   if (d.op == MCB_PLAN_STRICT_PAIR) {
     // Pairs of M*N >= kStrictTwoPassMinElems keep the binary32 C [M,N]

@@ -24,6 +24,12 @@
 //     CTA (two per TMEM lane quarter) store int32 rows.
 //   gemm_i8_kernel (M < 256): one CTA per SM, 128x256 tiles, cta_group::1,
 //     4-stage ring, four epilogue warps.
+//
+// Zero points (the legacy quantized_i8 matmul, src/mlir_engine.cpp:944-958:
+// C = sum_k (A - za)(B - zb) in wrapping int32): in Z/2^32 the sum expands to
+// A.B + K*za*zb - zb*rowsum(A) - za*colsum(B), so the tensor cores still
+// multiply the raw codes and the epilogue adds one per-row and one
+// per-column term (sums from a short pre-pass over A and B).
 #include <cuda_bf16.h>
 
 #include <atomic>
@@ -88,14 +94,44 @@ struct Params {
   int64_t m, n, ld_c;
   int n_tiles, num_tiles, num_kb;
   int b_mn;
+  int zp;                   // zero-point correction on
+  uint32_t za, zb, kzz;     // zero points and K*za*zb, modulo 2^32
+  const int32_t *row_sum;   // sum_k A[m,k] (null when zb == 0)
+  const int32_t *col_sum;   // sum_k B[k,n] (null when za == 0)
   int32_t *c;
   uint32_t *status;
 };
 
+// Adds K*za*zb - zb*row_sum[row] - za*col_sum[col] to one 32-column chunk
+// (uint32 arithmetic: the wrapping int32 result of the reference).
+__device__ __forceinline__ void zero_point_chunk(const Params &p, uint32_t (&r)[32], int64_t row,
+                                                 int64_t col0) {
+  const uint32_t rc = p.kzz - (p.row_sum ? p.zb * static_cast<uint32_t>(p.row_sum[row]) : 0u);
+  if (!p.col_sum) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) r[i] += rc;
+  } else if (col0 + 32 <= p.n) {
+    // Every lane of the warp reads the same 128 bytes (a broadcast).
+    const int4 *cs = reinterpret_cast<const int4 *>(p.col_sum + col0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int4 v = cs[q];
+      r[q * 4 + 0] += rc - p.za * static_cast<uint32_t>(v.x);
+      r[q * 4 + 1] += rc - p.za * static_cast<uint32_t>(v.y);
+      r[q * 4 + 2] += rc - p.za * static_cast<uint32_t>(v.z);
+      r[q * 4 + 3] += rc - p.za * static_cast<uint32_t>(v.w);
+    }
+  } else {
+    for (int i = 0; i < 32; ++i)
+      if (col0 + i < p.n) r[i] += rc - p.za * static_cast<uint32_t>(p.col_sum[col0 + i]);
+  }
+}
+
 // Stores one 32-column int32 chunk of one output row.
-__device__ __forceinline__ void store_chunk(const Params &p, const uint32_t (&r)[32], int64_t row,
+__device__ __forceinline__ void store_chunk(const Params &p, uint32_t (&r)[32], int64_t row,
                                             int64_t col0) {
   if (row >= p.m) return;
+  if (p.zp) zero_point_chunk(p, r, row, col0);
   int32_t *crow = p.c + row * p.ld_c + col0;
   if (col0 + 32 <= p.n && (p.ld_c % 4 == 0)) {
 #pragma unroll
@@ -452,18 +488,103 @@ __global__ void __launch_bounds__(256) transpose_u8_v16_kernel(const uint8_t *__
   }
 }
 
-// CUDA-core int8 GEMM (exact; any shape/stride). One thread per output.
+// CUDA-core int8 GEMM (exact; any shape/stride). One thread per output;
+// (A - za)(B - zb) per k in uint32 arithmetic (za = zb = 0: the plain GEMM).
 __global__ void gemm_i8_simt_kernel(const int8_t *__restrict__ a, const int8_t *__restrict__ b,
                                     int32_t *__restrict__ c, int64_t m, int64_t n, int64_t k,
-                                    int64_t lda, int64_t ldb, int64_t ldc) {
+                                    int64_t lda, int64_t ldb, int64_t ldc, uint32_t za,
+                                    uint32_t zb) {
   const int64_t row = blockIdx.y;
   const int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (row >= m || col >= n) return;
   uint32_t acc = 0;
   for (int64_t h = 0; h < k; ++h)
-    acc += static_cast<uint32_t>(static_cast<int32_t>(a[row * lda + h]) *
-                                 static_cast<int32_t>(b[h * ldb + col]));
+    acc += (static_cast<uint32_t>(static_cast<int32_t>(a[row * lda + h])) - za) *
+           (static_cast<uint32_t>(static_cast<int32_t>(b[h * ldb + col])) - zb);
   c[row * ldc + col] = static_cast<int32_t>(acc);
+}
+
+// Sum over k of each row of an int8 matrix x [rows, k] (row stride ld), one
+// warp per row; 16-byte loads reduced with dp4a when the rows are aligned.
+// The sums are exact for K < 2^24 and wrap modulo 2^32 beyond, which is all
+// the zero-point identity needs.
+__global__ void __launch_bounds__(256) i8_row_sums_kernel(const int8_t *__restrict__ x,
+                                                          int64_t rows, int64_t k, int64_t ld,
+                                                          int32_t *__restrict__ out) {
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const int8_t *row = x + r * ld;
+  uint32_t acc = 0;
+  int64_t k0 = 0;
+  if ((reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
+    k0 = k & ~int64_t{15};
+#pragma unroll 4
+    for (int64_t j = static_cast<int64_t>(lane) * 16; j < k0; j += 512) {
+      const int4 v = *reinterpret_cast<const int4 *>(row + j);
+      int s4 = __dp4a(v.x, 0x01010101, 0);
+      s4 = __dp4a(v.y, 0x01010101, s4);
+      s4 = __dp4a(v.z, 0x01010101, s4);
+      s4 = __dp4a(v.w, 0x01010101, s4);
+      acc += static_cast<uint32_t>(s4);
+    }
+  }
+  for (int64_t j = k0 + lane; j < k; j += 32) acc += static_cast<uint32_t>(static_cast<int32_t>(row[j]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) out[r] = static_cast<int32_t>(acc);
+}
+
+// Sum over k of each column of an int8 matrix x [k, cols] (row stride ld).
+// A CTA covers 512 columns and one K slice: lane l of each of the 8 warps
+// owns columns 16l..16l+15 (one 16-byte load per row; a warp reads 512
+// contiguous bytes), warp w takes rows w, w+8, ... of the slice. The warps'
+// partial sums meet in shared memory, and each CTA adds its 512 totals to
+// out (zeroed first) with integer atomics, whose result does not depend on
+// their order.
+constexpr int CS_COLS = 512;
+__global__ void __launch_bounds__(256) i8_col_sums_kernel(const int8_t *__restrict__ x, int64_t k,
+                                                          int64_t cols, int64_t ld,
+                                                          int64_t k_slice,
+                                                          int32_t *__restrict__ out) {
+  __shared__ uint32_t part[8][CS_COLS];  // [warp][j * 32 + lane]: conflict-free
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t c0 = static_cast<int64_t>(blockIdx.x) * CS_COLS + lane * 16;
+  const int64_t k_begin = static_cast<int64_t>(blockIdx.y) * k_slice;
+  const int64_t k_end = k_begin + k_slice < k ? k_begin + k_slice : k;
+  uint32_t s[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) s[j] = 0;
+  const bool vec = c0 + 16 <= cols && ((reinterpret_cast<uintptr_t>(x) | ld) & 15) == 0;
+  if (vec) {
+#pragma unroll 4
+    for (int64_t r = k_begin + warp; r < k_end; r += 8) {
+      const int4 v = *reinterpret_cast<const int4 *>(x + r * ld + c0);
+      const uint32_t w[4] = {static_cast<uint32_t>(v.x), static_cast<uint32_t>(v.y),
+                             static_cast<uint32_t>(v.z), static_cast<uint32_t>(v.w)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          s[i * 4 + b] += static_cast<uint32_t>(static_cast<int32_t>(static_cast<int8_t>(w[i] >> (8 * b))));
+    }
+  } else {
+    for (int64_t r = k_begin + warp; r < k_end; r += 8)
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (c0 + j < cols) s[j] += static_cast<uint32_t>(static_cast<int32_t>(x[r * ld + c0 + j]));
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) part[warp][j * 32 + lane] = s[j];
+  __syncthreads();
+  for (int q = threadIdx.x; q < CS_COLS; q += 256) {
+    const int64_t col = static_cast<int64_t>(blockIdx.x) * CS_COLS + q;
+    if (col >= cols) break;
+    uint32_t tot = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) tot += part[w][(q & 15) * 32 + (q >> 4)];
+    atomicAdd(reinterpret_cast<unsigned int *>(out) + col, tot);
+  }
 }
 
 // bf16 x bf16 -> f32, one fmaf per k in increasing order from +0 (the
@@ -727,9 +848,47 @@ cudaError_t launch_transpose_u8(const void *in, void *out, int64_t rows, int64_t
   return cudaGetLastError();
 }
 
+cudaError_t launch_i8_zero_point_sums(const int8_t *a, int64_t lda, const int8_t *b, int64_t ldb,
+                                      int b_mn, int64_t m, int64_t n, int64_t k,
+                                      const I8ZeroPoints &zp, int32_t *row_sum, int32_t *col_sum,
+                                      int sms, cudaStream_t stream, LaunchInfo *info) {
+  auto row_sums = [&](const int8_t *x, int64_t rows, int64_t ld, int32_t *out) -> cudaError_t {
+    const int64_t blocks = (rows + 7) / 8;
+    if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+    i8_row_sums_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, rows, k, ld, out);
+    if (info) info->launches += 1;
+    return cudaGetLastError();
+  };
+  cudaError_t e = cudaSuccess;
+  if (zp.zb != 0 && m > 0 && (e = row_sums(a, m, lda, row_sum)) != cudaSuccess) return e;
+  if (zp.za != 0 && n > 0) {
+    if (!b_mn) return row_sums(b, n, ldb, col_sum);  // Bt [N,K]: its row sums
+    if ((e = cudaMemsetAsync(col_sum, 0, static_cast<size_t>(n) * 4, stream)) != cudaSuccess)
+      return e;
+    // About two CTAs per SM: split K so the column groups x slices fill
+    // them, each warp reading at least 8 rows.
+    const int64_t gx = (n + CS_COLS - 1) / CS_COLS;
+    int64_t slices = (2 * static_cast<int64_t>(sms) + gx - 1) / gx;
+    if (slices > (k + 63) / 64) slices = (k + 63) / 64;
+    if (slices < 1) slices = 1;
+    if (slices > 65535) slices = 65535;
+    const int64_t k_slice = (k + slices - 1) / slices;
+    slices = (k + k_slice - 1) / k_slice;
+    if (gx > 0x7fffffff) return cudaErrorInvalidConfiguration;
+    if (k > 0) {
+      i8_col_sums_kernel<<<dim3(static_cast<unsigned>(gx), static_cast<unsigned>(slices)), 256, 0,
+                           stream>>>(b, k, n, ldb, k_slice, col_sum);
+      if (info) info->launches += 1;
+      e = cudaGetLastError();
+    }
+  }
+  return e;
+}
+
 cudaError_t launch_gemm_i8_tc(const int8_t *a, int64_t lda, const int8_t *b, int64_t ldb,
                               int b_mn, int32_t *c, int64_t m, int64_t n, int64_t k, int64_t ld_c,
-                              uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info) {
+                              const I8ZeroPoints *zp, uint32_t *status, int sms,
+                              cudaStream_t stream, LaunchInfo *info) {
   if (m == 0 || n == 0) return cudaSuccess;
   // TMA needs 16-byte aligned bases and row strides; the epilogue's vector
   // stores need a 16-byte aligned C. K tails are zero-filled by TMA.
@@ -768,6 +927,15 @@ cudaError_t launch_gemm_i8_tc(const int8_t *a, int64_t lda, const int8_t *b, int
   p.num_tiles = static_cast<int>(tiles);
   p.num_kb = static_cast<int>((k + BK - 1) / BK);
   p.b_mn = b_mn;
+  p.zp = zp && (zp->za != 0 || zp->zb != 0) ? 1 : 0;
+  p.za = zp ? static_cast<uint32_t>(zp->za) : 0u;
+  p.zb = zp ? static_cast<uint32_t>(zp->zb) : 0u;
+  p.kzz = static_cast<uint32_t>(static_cast<uint64_t>(k)) * p.za * p.zb;
+  p.row_sum = zp && zp->zb != 0 ? zp->row_sum : nullptr;
+  p.col_sum = zp && zp->za != 0 ? zp->col_sum : nullptr;
+  if (p.zp && ((p.zb != 0 && !p.row_sum) || (p.za != 0 && !p.col_sum) ||
+               (reinterpret_cast<uintptr_t>(p.col_sum) & 15u) != 0))
+    return cudaErrorInvalidValue;
   p.c = c;
   p.status = status;
   int grid;
@@ -797,12 +965,14 @@ cudaError_t launch_gemm_i8_tc(const int8_t *a, int64_t lda, const int8_t *b, int
 }
 
 cudaError_t launch_gemm_i8_simt(const int8_t *a, const int8_t *b, int32_t *c, int64_t m, int64_t n,
-                                int64_t k, int64_t lda, int64_t ldb, int64_t ldc,
-                                cudaStream_t stream, LaunchInfo *info) {
+                                int64_t k, int64_t lda, int64_t ldb, int64_t ldc, int32_t za,
+                                int32_t zb, cudaStream_t stream, LaunchInfo *info) {
   if (m == 0 || n == 0) return cudaSuccess;
   if (m > 65535) return cudaErrorInvalidConfiguration;
   dim3 grid(static_cast<unsigned>((n + 255) / 256), static_cast<unsigned>(m));
-  gemm_i8_simt_kernel<<<grid, 256, 0, stream>>>(a, b, c, m, n, k, lda, ldb, ldc);
+  gemm_i8_simt_kernel<<<grid, 256, 0, stream>>>(a, b, c, m, n, k, lda, ldb, ldc,
+                                                static_cast<uint32_t>(za),
+                                                static_cast<uint32_t>(zb));
   if (info) {
     info->launches += 1;
     info->set_route("simt_i8_gemm");

@@ -59,6 +59,8 @@ def lib() -> ctypes.CDLL:
             "orc_bf16_to_f32": [_u16p, _f32p, _i64],
             "orc_gemm_bf16_f32_fma": [_u16p, _u16p, _f32p, _i64, _i64, _i64],
             "orc_gemm_i8_i32": [_i8p, _i8p, _i32p, _i64, _i64, _i64],
+            "orc_gemm_i8_i32_zp": [_i8p, _i8p, _i32p, _i64, _i64, _i64, ctypes.c_int32,
+                                   ctypes.c_int32],
             "orc_gemm_epilogue_f64": [_f32p, _f32p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_int, _f64p, _i64, _i64, _i64, ctypes.c_void_p, _i64],
             "orc_msm_f64": [_f32p, _f32p, _f32p, _f64p, _i64, _i64, _i64, _i64, ctypes.c_double],
@@ -158,6 +160,16 @@ def gemm_i8_i32(a, b):
     n = b.shape[1]
     c = np.empty((m, n), np.int32)
     lib().orc_gemm_i8_i32(a, b, c, m, k, n)
+    return c
+
+
+def gemm_i8_i32_zp(a, b, a_zero_point, b_zero_point):
+    """sum_k (A - za)(B - zb) in wrapping int32 (the legacy quantized_i8 matmul)."""
+    a, b = _c(a, np.int8), _c(b, np.int8)
+    m, k = a.shape
+    n = b.shape[1]
+    c = np.empty((m, n), np.int32)
+    lib().orc_gemm_i8_i32_zp(a, b, c, m, k, n, int(a_zero_point), int(b_zero_point))
     return c
 
 

@@ -145,6 +145,29 @@ void orc_gemm_i8_i32(const int8_t *a, const int8_t *b, int32_t *c, int64_t m,
     }
 }
 
+// Quantized int8 matmul with zero points, as the legacy path lowers it
+// (src/mlir_engine.cpp:944-958, linalg.quantized_matmul):
+// C[i,j] = sum_h (sext(A[i,h]) - za) * (sext(B[h,j]) - zb) in wrapping int32
+// arithmetic; the per-tensor zero point, else the kernel's global one. The
+// reference's plan test expects exactly (A - zp) @ (B - zp)
+// (tests/test_plan_quantization.py:22-25).
+void orc_gemm_i8_i32_zp(const int8_t *a, const int8_t *b, int32_t *c, int64_t m, int64_t k,
+                        int64_t n, int32_t za, int32_t zb) {
+  const uint32_t uza = static_cast<uint32_t>(za), uzb = static_cast<uint32_t>(zb);
+  for (int64_t i = 0; i < m; ++i)
+    for (int64_t j = 0; j < n; ++j) {
+      uint32_t acc = 0;
+      for (int64_t h = 0; h < k; ++h) {
+        const uint32_t x = static_cast<uint32_t>(static_cast<int32_t>(a[i * k + h])) - uza;
+        const uint32_t y = static_cast<uint32_t>(static_cast<int32_t>(b[h * n + j])) - uzb;
+        acc += x * y;
+      }
+      int32_t out;
+      std::memcpy(&out, &acc, 4);
+      c[i * n + j] = out;
+    }
+}
+
 void orc_gemm_epilogue_f64(const float *x, const float *w, const float *bias,
                            int bias_mode, int bias_op, int act, double *y,
                            int64_t m, int64_t k, int64_t n,

@@ -67,6 +67,10 @@ void orc_gemm_bf16_f32_fma(const uint16_t *a, const uint16_t *b, float *c,
  * compiler/lib/runtime/cpu_numeric_reference.cpp:185-209 */
 void orc_gemm_i8_i32(const int8_t *a, const int8_t *b, int32_t *c, int64_t m,
                      int64_t k, int64_t n);
+/* Quantized i8 x i8 -> i32 with zero points: sum (A - za)(B - zb), wrapping.
+ * src/mlir_engine.cpp:944-958 (linalg.quantized_matmul) */
+void orc_gemm_i8_i32_zp(const int8_t *a, const int8_t *b, int32_t *c, int64_t m,
+                        int64_t k, int64_t n, int32_t za, int32_t zb);
 
 /* ---- Family A: GEMM + epilogue (fp64) ----------------------------------- */
 enum {

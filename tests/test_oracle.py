@@ -113,6 +113,33 @@ def test_i8_gemm_matches_reference(orc):
     assert np.array_equal(mine, ref)
 
 
+def test_quantized_i8_reference_case(orc):
+    """The reference's quantized int8 plan and matmul cases
+    (tests/test_plan_quantization.py:22-25,32-43; tests/test_matmul.py:60-70):
+    2x3 @ 3x2 with zero point 2 on both operands equals (A - 2) @ (B - 2)."""
+    lhs = np.array([[4, -3, 2], [1, 0, -2]], dtype=np.int8)
+    rhs = np.array([[2, -1], [3, 4], [-2, 1]], dtype=np.int8)
+    expected = (lhs.astype(np.int32) - 2) @ (rhs.astype(np.int32) - 2)
+    assert np.array_equal(orc.gemm_i8_i32_zp(lhs, rhs, 2, 2), expected)
+    assert np.array_equal(expected, [[-5, -16], [14, 3]])
+
+
+@pytest.mark.parametrize("za,zb", [(0, 0), (2, 2), (-7, 0), (0, 113), (2 ** 30 + 3, -2 ** 31)])
+def test_quantized_i8_wraps_like_int32(orc, za, zb):
+    """Zero points 0 give the plain int8 GEMM; any others give the exact sum
+    reduced modulo 2^32 (int32 wrap-around, as linalg.quantized_matmul)."""
+    rng = np.random.default_rng(abs(za) + abs(zb))
+    a = rng.integers(-128, 128, (13, 70), dtype=np.int8)
+    b = rng.integers(-128, 128, (70, 11), dtype=np.int8)
+    exact = (a.astype(object) - za).dot(b.astype(object) - zb)
+    wrapped = np.array([[((int(v) + 2 ** 31) % 2 ** 32) - 2 ** 31 for v in row] for row in exact],
+                       dtype=np.int64).astype(np.int32)
+    got = orc.gemm_i8_i32_zp(a, b, za, zb)
+    assert np.array_equal(got, wrapped)
+    if za == 0 and zb == 0:
+        assert np.array_equal(got, orc.gemm_i8_i32(a, b))
+
+
 @pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
 def test_fp8_codec_exhaustive(orc, fmt):
     ml = pytest.importorskip("ml_dtypes")
