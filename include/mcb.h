@@ -239,9 +239,13 @@ typedef struct mcb_epilogue {
 } mcb_epilogue;
 /* Y = act(X*W (+|r-) bias). X [M,K], W [K,N] (row-major, "MN-major" B) or,
  * with w given as [N,K] and rank-2 dims {N,K} plus MCB_GEMM_W_TRANSPOSED in
- * flags, W^T. bf16 X/W run on tcgen05 tensor cores with an f32 TMEM
- * accumulator; f32 X/W run on CUDA cores with f32 FMA accumulation. Output
- * bf16 or f32. GELU is the tanh form of src/fusion_emitter_common.cpp:86-108.
+ * flags, W^T. X and W are both bf16, both f16 or both f32 (the reference's
+ * matmul signatures, src/mlir_engine.cpp:114-152). 16-bit X/W with 16-byte
+ * aligned rows run on tcgen05 tensor cores (kind::f16, bf16 or f16 operand
+ * format) with an f32 TMEM accumulator; f32 X/W and unaligned rows run on
+ * CUDA cores with f32 FMA accumulation. Output f32 or the inputs' 16-bit
+ * type; bias f32, bf16 or f16. GELU is the tanh form of
+ * src/fusion_emitter_common.cpp:86-108.
  * Replaces the Family A leaf emitted by FusionMlirEmitter::emitFamilyA
  * (src/fusion_emitter_family_a.cpp:12-244) and reached through compileAndRun
  * (include/matcore/jit_runner.h:23-26).

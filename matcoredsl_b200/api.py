@@ -28,7 +28,7 @@ except ImportError:  # pragma: no cover
     _mld = None
 
 _NP_DTYPE = {np.dtype(np.float32): "f32", np.dtype(np.float64): "f64",
-             np.dtype(np.int8): "i8", np.dtype(np.int32): "i32"}
+             np.dtype(np.float16): "f16", np.dtype(np.int8): "i8", np.dtype(np.int32): "i32"}
 if _mld is not None:
     _NP_DTYPE[np.dtype(_mld.bfloat16)] = "bf16"
     _NP_DTYPE[np.dtype(_mld.float8_e4m3fn)] = "e4m3"
@@ -102,9 +102,10 @@ def _exec(device_call: bool, device: int, flags: int, report, workspace=None):
 def _empty_like_out(ref, shape, dtype_name):
     if _is_torch(ref):
         torch = _torch()
-        td = {"f32": torch.float32, "bf16": torch.bfloat16}[dtype_name]
+        td = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[dtype_name]
         return torch.empty(shape, dtype=td, device=ref.device)
-    nd = {"f32": np.float32, "bf16": (_mld.bfloat16 if _mld else None)}[dtype_name]
+    nd = {"f32": np.float32, "f16": np.float16,
+          "bf16": (_mld.bfloat16 if _mld else None)}[dtype_name]
     return np.empty(shape, dtype=nd)
 
 
@@ -209,13 +210,16 @@ def strict_fused_pair(a, b, d, out=None, *, device=-1, flags=0, workspace=None):
 def gemm_epilogue(x, w, bias=None, *, bias_mode=None, bias_op="add", act="none", out=None,
                   out_dtype=None, w_transposed=False, device=-1, flags=0):
     """Y = act(X @ W (+|r-) bias) (Family A). bias [N] broadcasts over rows;
-    bias [M,N] is the reference's exact-shape boundary."""
+    bias [M,N] is the reference's exact-shape boundary. X and W both bf16,
+    both f16 or both f32; Y (default: the inputs' type) f32 or that type."""
     if bias_mode is None:
         bias_mode = "none" if bias is None else ("full" if len(bias.shape) == 2 else "row")
     n = w.shape[0] if w_transposed else w.shape[1]
     if out is None:
         if out_dtype is None:
-            out_dtype = "bf16" if str(getattr(x, "dtype", "")).endswith("bfloat16") else "f32"
+            xd = str(getattr(x, "dtype", ""))
+            out_dtype = ("bf16" if xd.endswith("bfloat16") else
+                         "f16" if xd.endswith("float16") else "f32")
         out = _empty_like_out(x, (x.shape[0], n), out_dtype)
     ep = _abi.make_epilogue(bias_mode, bias_op, act)
     gflags = _abi.GEMM_W_TRANSPOSED if w_transposed else 0

@@ -748,13 +748,19 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
   const int64_t n = wt ? w->dims[0] : w->dims[1];
   if ((wt ? w->dims[1] : w->dims[0]) != k || y->dims[0] != m || y->dims[1] != n)
     return MCB_STATUS_SHAPE_MISMATCH;
+  // X and W: both bf16, both f16 or both f32 (the reference's matmul
+  // signatures, src/mlir_engine.cpp:114-152); Y f32 or the inputs' 16-bit
+  // type; a bias f32 or 16-bit.
   const bool in_bf16 = x->dtype == MCB_DTYPE_BF16 && w->dtype == MCB_DTYPE_BF16;
+  const bool in_f16 = x->dtype == MCB_DTYPE_F16 && w->dtype == MCB_DTYPE_F16;
   const bool in_f32 = x->dtype == MCB_DTYPE_F32 && w->dtype == MCB_DTYPE_F32;
-  if (!in_bf16 && !in_f32) return MCB_STATUS_UNSUPPORTED_DTYPE;
-  if (y->dtype != MCB_DTYPE_BF16 && y->dtype != MCB_DTYPE_F32) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  if (!in_bf16 && !in_f16 && !in_f32) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  if (y->dtype != MCB_DTYPE_F32 && y->dtype != (in_f16 ? MCB_DTYPE_F16 : MCB_DTYPE_BF16))
+    return MCB_STATUS_UNSUPPORTED_DTYPE;
   if (ep.bias_mode != MCB_BIAS_NONE) {
     if ((s = check_tensor(bias, 1, 2))) return s;
-    if (bias->dtype != MCB_DTYPE_BF16 && bias->dtype != MCB_DTYPE_F32)
+    if (bias->dtype != MCB_DTYPE_BF16 && bias->dtype != MCB_DTYPE_F32 &&
+        bias->dtype != MCB_DTYPE_F16)
       return MCB_STATUS_UNSUPPORTED_DTYPE;
     if (ep.bias_mode == MCB_BIAS_ROW &&
         !(numel(bias) == n && (bias->rank == 1 || bias->dims[0] == 1)))
@@ -763,6 +769,7 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
         !(bias->rank == 2 && bias->dims[0] == m && bias->dims[1] == n))
       return MCB_STATUS_SHAPE_MISMATCH;
     ep.bias_bf16 = bias->dtype == MCB_DTYPE_BF16;
+    ep.bias_f16 = bias->dtype == MCB_DTYPE_F16;
     ep.ld_bias = bias->rank == 2 ? bias->strides[0] : n;
   }
   if (overlaps(y, x) || overlaps(y, w) || (ep.bias_mode && overlaps(y, bias)))
@@ -789,11 +796,15 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
   const int64_t ld_x = x->strides[0], ld_w = w->strides[0], ld_y = y->strides[0];
   // Tensor-core eligibility: TMA wants 16-byte aligned bases and row strides.
   // Row chunks start at multiples of 256 rows, so they keep the alignment.
-  const bool tma_ok = in_bf16 && k > 0 && (k % 8 == 0) && (ld_x % 8 == 0) && (ld_w % 8 == 0) &&
-                      (wt || n % 8 == 0) && (reinterpret_cast<uintptr_t>(dx) % 16 == 0) &&
+  const bool tma_ok = (in_bf16 || in_f16) && k > 0 && (k % 8 == 0) && (ld_x % 8 == 0) &&
+                      (ld_w % 8 == 0) && (wt || n % 8 == 0) &&
+                      (reinterpret_cast<uintptr_t>(dx) % 16 == 0) &&
                       (reinterpret_cast<uintptr_t>(dw) % 16 == 0) &&
                       (reinterpret_cast<uintptr_t>(dy) % 16 == 0) &&
-                      (ld_y % (y->dtype == MCB_DTYPE_BF16 ? 8 : 4) == 0);
+                      (ld_y % (y->dtype == MCB_DTYPE_F32 ? 4 : 8) == 0);
+  const int y_kind = y->dtype == MCB_DTYPE_F32   ? mcb::kOutF32
+                     : y->dtype == MCB_DTYPE_F16 ? mcb::kOutF16
+                                                 : mcb::kOutBf16;
   const size_t xs = dtype_size(x->dtype), ys = dtype_size(y->dtype);
   const size_t bs = ep.bias_mode ? dtype_size(bias->dtype) : 0;
   auto launch_rows = [&](int64_t r0, int64_t r1) -> cudaError_t {
@@ -806,8 +817,8 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
     }
     if (tma_ok)
       return mcb::launch_gemm_tc_bf16(xr, dw, yr, r1 - r0, n, k, ld_x, ld_w, ld_y, wt ? 1 : 0,
-                                      y->dtype == MCB_DTYPE_BF16 ? 1 : 0, e, call.ctx()->status,
-                                      call.sms(), call.stream(), &info);
+                                      y_kind, e, call.ctx()->status, call.sms(), call.stream(),
+                                      &info, in_f16 ? 1 : 0);
     return mcb::launch_gemm_simt(xr, static_cast<int>(x->dtype), dw, static_cast<int>(w->dtype),
                                  yr, static_cast<int>(y->dtype), r1 - r0, n, k, ld_x, ld_w, ld_y,
                                  wt ? 1 : 0, e, call.stream(), &info);

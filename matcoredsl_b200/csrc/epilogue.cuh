@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "internal.h"
@@ -35,6 +36,7 @@ __device__ __forceinline__ float load_bias(const Epilogue &e, int64_t row, int64
   const int64_t idx = e.bias_mode == 1 ? col : row * e.ld_bias + col;
   if (e.bias_bf16)
     return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(e.bias)[idx]);
+  if (e.bias_f16) return __half2float(reinterpret_cast<const __half *>(e.bias)[idx]);
   return reinterpret_cast<const float *>(e.bias)[idx];
 }
 

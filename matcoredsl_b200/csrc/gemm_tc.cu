@@ -1,4 +1,6 @@
-// bf16 GEMM with a fused epilogue on the B200's 5th-generation tensor cores.
+// bf16 (or f16) GEMM with a fused epilogue on the B200's 5th-generation
+// tensor cores. f16 operands change only the MMA's operand format, the TMA
+// element type and the epilogue's output conversion.
 //
 //   Y[M,N] = act(X[M,K] * W (+|r-) bias)      (Family A, src/fusion_emitter_family_a.cpp)
 //
@@ -49,7 +51,7 @@ constexpr size_t SMEM_BYTES = static_cast<size_t>(STAGES) * STAGE_BYTES + BAR_BY
 struct Params {
   int64_t m, n, k, ld_y;
   int n_tiles, num_tiles, num_kb;
-  int w_transposed, y_bf16;
+  int w_transposed, y_kind, in_f16;  // y_kind: kOutF32 / kOutBf16 / kOutF16
   void *y;
   uint32_t *status;
   Epilogue epi;
@@ -80,6 +82,21 @@ __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (
         x1 = e.bias_op == 1 ? b1 - x1 : x1 + b1;
       }
     }
+  } else if (e.bias_mode == 1 && e.bias_f16 && e.bias_aligned16 && full_chunk) {
+    const uint4 *bp = reinterpret_cast<const uint4 *>(reinterpret_cast<const __half *>(e.bias) + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 w4 = __ldg(bp + q);
+      const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float b0 = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[h] & 0xffffu)));
+        const float b1 = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[h] >> 16)));
+        float &x0 = v[q * 8 + h * 2], &x1 = v[q * 8 + h * 2 + 1];
+        x0 = e.bias_op == 1 ? b0 - x0 : x0 + b0;
+        x1 = e.bias_op == 1 ? b1 - x1 : x1 + b1;
+      }
+    }
   } else if (e.bias_mode != 0) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -101,7 +118,24 @@ __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (
       break;
   }
   if (row >= p.m) return;
-  if (p.y_bf16) {
+  if (p.y_kind == kOutF16) {
+    __half *yr = reinterpret_cast<__half *>(p.y) + row * p.ld_y + col0;
+    if (full_chunk) {
+      uint4 *dst = reinterpret_cast<uint4 *>(yr);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 o;
+        o.x = pack_f16x2(v[q * 8 + 0], v[q * 8 + 1]);
+        o.y = pack_f16x2(v[q * 8 + 2], v[q * 8 + 3]);
+        o.z = pack_f16x2(v[q * 8 + 4], v[q * 8 + 5]);
+        o.w = pack_f16x2(v[q * 8 + 6], v[q * 8 + 7]);
+        dst[q] = o;
+      }
+    } else {
+      for (int i = 0; i < 32; ++i)
+        if (col0 + i < p.n) yr[i] = __float2half_rn(v[i]);
+    }
+  } else if (p.y_kind == kOutBf16) {
     __nv_bfloat16 *yr = reinterpret_cast<__nv_bfloat16 *>(p.y) + row * p.ld_y + col0;
     if (full_chunk) {
       uint4 *dst = reinterpret_cast<uint4 *>(yr);
@@ -208,7 +242,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc = make_idesc(1, 1, 0, p.w_transposed ? 0u : 1u, BM, BN);
+      const uint32_t fmt = p.in_f16 ? 0u : 1u;  // kind::f16 operand format: f16 0, bf16 1
+      const uint32_t idesc = make_idesc(fmt, fmt, 0, p.w_transposed ? 0u : 1u, BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -392,7 +427,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     }
   } else if (warp == 1) {
     if (leader && lane == 0) {
-      const uint32_t idesc = make_idesc(1, 1, 0, p.w_transposed ? 0u : 1u, 2 * BM, BN);
+      const uint32_t fmt = p.in_f16 ? 0u : 1u;  // kind::f16 operand format: f16 0, bf16 1
+      const uint32_t idesc = make_idesc(fmt, fmt, 0, p.w_transposed ? 0u : 1u, 2 * BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -513,9 +549,9 @@ bool pair_kernel_enabled() {
 
 cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m, int64_t n,
                                 int64_t k, int64_t ld_x, int64_t ld_w, int64_t ld_y,
-                                int w_transposed, int y_bf16, const Epilogue &epi,
-                                uint32_t *status, int sms, cudaStream_t stream,
-                                LaunchInfo *info) {
+                                int w_transposed, int y_kind, const Epilogue &epi,
+                                uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info,
+                                int in_f16) {
   if (m == 0 || n == 0) return cudaSuccess;
   // Rows of 256 go to CTA pairs (M = 256 per MMA, W tile split between the
   // two SMs); shorter problems keep one 128-row tile per SM.
@@ -531,15 +567,14 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   }
   const int w_rows = pair ? P_BN_CTA : BN;  // W^T box height per CTA
   CUtensorMap tx, tw;
-  if (!encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, k, m, ld_x * 2, BK, BM,
-                      CU_TENSOR_MAP_SWIZZLE_128B))
+  const CUtensorMapDataType dt =
+      in_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (!encode_tmap_2d(&tx, dt, x, k, m, ld_x * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   const bool ok_w =
       w_transposed
-          ? encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, k, n, ld_w * 2, BK, w_rows,
-                           CU_TENSOR_MAP_SWIZZLE_128B)
-          : encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, n, k, ld_w * 2, 64, BK,
-                           CU_TENSOR_MAP_SWIZZLE_128B);
+          ? encode_tmap_2d(&tw, dt, w, k, n, ld_w * 2, BK, w_rows, CU_TENSOR_MAP_SWIZZLE_128B)
+          : encode_tmap_2d(&tw, dt, w, n, k, ld_w * 2, 64, BK, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok_w) return cudaErrorInvalidValue;
   Params p;
   p.m = m;
@@ -553,7 +588,8 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   p.num_tiles = static_cast<int>(tiles);
   p.num_kb = static_cast<int>((k + BK - 1) / BK);
   p.w_transposed = w_transposed;
-  p.y_bf16 = y_bf16;
+  p.y_kind = y_kind;
+  p.in_f16 = in_f16;
   p.y = y;
   p.status = status;
   p.epi = epi;
@@ -579,7 +615,7 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
     info->tile_k = BK;
     info->stages = pair ? P_STAGES : STAGES;
     info->ctas = grid;
-    info->set_route("tcgen05_bf16_gemm_epilogue");
+    info->set_route(in_f16 ? "tcgen05_f16_gemm_epilogue" : "tcgen05_bf16_gemm_epilogue");
   }
   return cudaGetLastError();
 }

@@ -50,23 +50,27 @@ struct Epilogue {
   int bias_mode = 0;  // 0 none, 1 row-broadcast [N], 2 full [M,N]
   int bias_op = 0;    // 0 add, 1 reverse subtract
   int act = 0;        // 0 none, 1 relu, 2 gelu_tanh, 3 exp, 4 sigmoid, 5 tanh
-  int bias_bf16 = 0;  // bias element type (1 bf16, 0 f32)
+  int bias_bf16 = 0;  // bias element type: bf16 (else f16 when bias_f16, else f32)
+  int bias_f16 = 0;
   int bias_aligned16 = 0;  // bias base is 16-byte aligned (vector loads allowed)
   const void *bias = nullptr;
   int64_t ld_bias = 0;
 };
 
-// ---- gemm_tc.cu: tcgen05 bf16 GEMM + epilogue -------------------------------------
-// X [M,K] bf16 (ld_x), W [K,N] bf16 (ld_w, w_transposed=0) or W^T [N,K]
-// (w_transposed=1), Y [M,N] bf16 or f32 (y_bf16). Requires K, N, ld_x, ld_w
-// multiples of 8 and 16-byte aligned bases (TMA); the caller checks.
+// ---- gemm_tc.cu: tcgen05 bf16 / f16 GEMM + epilogue ------------------------------
+// X [M,K] (ld_x), W [K,N] (ld_w, w_transposed=0) or W^T [N,K] (w_transposed=1),
+// both bf16 or both f16 (in_f16); Y [M,N] f32, bf16 or f16 (y_kind). Requires
+// K, N, ld_x, ld_w multiples of 8 and 16-byte aligned bases (TMA); the caller
+// checks.
+enum : int { kOutF32 = 0, kOutBf16 = 1, kOutF16 = 2 };
 cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m, int64_t n,
                                 int64_t k, int64_t ld_x, int64_t ld_w, int64_t ld_y,
-                                int w_transposed, int y_bf16, const Epilogue &epi,
-                                uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info);
+                                int w_transposed, int y_kind, const Epilogue &epi,
+                                uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info,
+                                int in_f16 = 0);
 
 // ---- simt.cu: CUDA-core fallbacks for shapes/dtypes the tensor-core kernels do not take
-// dtype codes: 1 f32, 3 bf16 (as in mcb.h)
+// dtype codes: 1 f32, 3 bf16, 6 f16 (as in mcb.h)
 cudaError_t launch_gemm_simt(const void *x, int x_dtype, const void *w, int w_dtype, void *y,
                              int y_dtype, int64_t m, int64_t n, int64_t k, int64_t ld_x,
                              int64_t ld_w, int64_t ld_y, int w_transposed, const Epilogue &epi,

@@ -4,6 +4,7 @@
 // arbitrary Dqk/Dv (Family C, tests/test_family_c.py). These are still the
 // GPU path -- there is no CPU fallback anywhere in the library.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "epilogue.cuh"
@@ -14,11 +15,14 @@ namespace {
 
 __device__ __forceinline__ float load_elem(const void *p, int dtype, int64_t idx) {
   if (dtype == 3) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[idx]);
+  if (dtype == 6) return __half2float(reinterpret_cast<const __half *>(p)[idx]);
   return reinterpret_cast<const float *>(p)[idx];
 }
 __device__ __forceinline__ void store_elem(void *p, int dtype, int64_t idx, float v) {
   if (dtype == 3)
     reinterpret_cast<__nv_bfloat16 *>(p)[idx] = __float2bfloat16_rn(v);
+  else if (dtype == 6)
+    reinterpret_cast<__half *>(p)[idx] = __float2half_rn(v);
   else
     reinterpret_cast<float *>(p)[idx] = v;
 }
