@@ -122,6 +122,42 @@ def test_f16_graph_plan(mcb, orc):
     plan.close()
 
 
+def test_reference_staging_case(mcb):
+    """The reference's staging case: f16 [16,16] @ [16,8] from
+    default_rng(42/43), compared at atol 1e-2 + rtol 1e-1
+    (tests/test_gpu_staging.py)."""
+    lhs = np.random.default_rng(42).standard_normal((16, 16), dtype=np.float32).astype(np.float16)
+    rhs = np.random.default_rng(43).standard_normal((16, 8), dtype=np.float32).astype(np.float16)
+    out = np.zeros((16, 8), dtype=np.float16)
+    mcb.gemm_epilogue(lhs, rhs, out=out)
+    assert mcb.api.last_result.route == "tcgen05_f16_gemm_epilogue"
+    expected = lhs.astype(np.float32) @ rhs.astype(np.float32)
+    np.testing.assert_allclose(out.astype(np.float32), expected, atol=1e-2, rtol=1e-1)
+
+
+def test_reference_graph_minimal(mcb):
+    """The reference's minimal graph case (tests/test_graph_minimal.py): a
+    normal plan, then a graph plan captured and replayed, N = 16 f16."""
+    import torch
+    n = 16
+    rng = np.random.default_rng(16)
+    a = rng.standard_normal((n, n)).astype(np.float16)
+    b = rng.standard_normal((n, n)).astype(np.float16)
+    da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    dc = torch.zeros((n, n), dtype=torch.float16, device="cuda")
+    expected = (a.astype(np.float32) @ b.astype(np.float32)).astype(np.float16).astype(np.float32)
+    for graph in (False, True, True):
+        dc.zero_()
+        plan = mcb.Plan("gemm_epilogue", dc, da, db, None, graph=graph)
+        plan.execute(dc, da, db, None)
+        if graph:
+            dc.zero_()
+            plan.execute(dc, da, db, None)   # replay
+        torch.cuda.synchronize()
+        assert np.max(np.abs(dc.float().cpu().numpy() - expected)) < 1.0
+        plan.close()
+
+
 def test_f16_mixed_dtypes_rejected(mcb):
     """Mixed operand types and a bf16 output for f16 inputs are not signatures
     of the reference's matmul."""
