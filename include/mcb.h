@@ -259,6 +259,38 @@ MCB_API mcb_status mcb_gemm_epilogue_v1(const mcb_tensor *y, const mcb_tensor *x
                                         const mcb_epilogue *epilogue, uint32_t gemm_flags,
                                         const mcb_exec *exec) MCB_NOEXCEPT;
 
+/* General Family A epilogue chain: Y = op_n(...op_1(X*W)...), the chain
+ * FusionMlirEmitter::emitFamilyA accepts (src/fusion_emitter_family_a.cpp:
+ * 149-220; op semantics src/fusion_emitter_common.cpp:38-160). Each op is
+ * unary, or binary against an exact-shape [M,N] boundary tensor with the
+ * running value on the left (value_pos 0: v op b) or right (1: b op v).
+ * Up to MCB_EPILOGUE_MAX_OPS ops and MCB_EPILOGUE_MAX_BOUNDARIES boundaries
+ * (f32, bf16 or f16, any row stride). Arithmetic is f32 on the accumulator;
+ * relu / min / max propagate NaN and order -0 < +0 (arith.maximumf /
+ * minimumf). Same kernels and routes as mcb_gemm_epilogue_v1. */
+enum {
+  MCB_EW_RELU = 1, MCB_EW_EXP = 2, MCB_EW_LOG = 3, MCB_EW_TANH = 4, MCB_EW_SQRT = 5,
+  MCB_EW_NEG = 6, MCB_EW_ABS = 7, MCB_EW_SIN = 8, MCB_EW_COS = 9, MCB_EW_RSQRT = 10,
+  MCB_EW_SIGMOID = 11, MCB_EW_GELU_TANH = 12,
+  MCB_EW_ADD = 32, MCB_EW_SUB = 33, MCB_EW_MUL = 34, MCB_EW_DIV = 35, MCB_EW_MIN = 36,
+  MCB_EW_MAX = 37
+};
+#define MCB_EPILOGUE_MAX_OPS 8
+#define MCB_EPILOGUE_MAX_BOUNDARIES 4
+typedef struct mcb_epilogue_op {
+  uint32_t kind;      /* MCB_EW_* */
+  uint32_t value_pos; /* binary: 0 = v op boundary, 1 = boundary op v */
+  uint32_t boundary;  /* binary: index into `boundaries` */
+  uint32_t reserved;
+} mcb_epilogue_op;
+MCB_API mcb_status mcb_gemm_epilogue_chain_v1(const mcb_tensor *y, const mcb_tensor *x,
+                                              const mcb_tensor *w,
+                                              const mcb_tensor *boundaries,
+                                              uint32_t num_boundaries,
+                                              const mcb_epilogue_op *ops, uint32_t num_ops,
+                                              uint32_t gemm_flags,
+                                              const mcb_exec *exec) MCB_NOEXCEPT;
+
 /* ---- Family B: two-GEMM chain with elementwise glue ------------------------ */
 /* E = glue(A*B) * W where glue is a Family A epilogue (optional boundary
  * [M,N1] or row bias [N1], added or reverse-subtracted, then one activation).

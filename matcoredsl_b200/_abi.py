@@ -114,6 +114,19 @@ class PlanDesc(ctypes.Structure):
     ]
 
 
+class EpilogueOp(ctypes.Structure):
+    """mcb_epilogue_op: one link of a Family A epilogue chain."""
+    _fields_ = [("kind", ctypes.c_uint32), ("value_pos", ctypes.c_uint32),
+                ("boundary", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+
+
+# MCB_EW_* codes (unary < 32, binary >= 32).
+EW = {"relu": 1, "exp": 2, "log": 3, "tanh": 4, "sqrt": 5, "neg": 6, "abs": 7, "sin": 8,
+      "cos": 9, "rsqrt": 10, "sigmoid": 11, "gelu_tanh": 12, "gelu": 12,
+      "add": 32, "sub": 33, "mul": 34, "div": 35, "min": 36, "max": 37}
+EPILOGUE_MAX_OPS = 8
+EPILOGUE_MAX_BOUNDARIES = 4
+
 _P = ctypes.POINTER
 _T = _P(Tensor)
 _E = _P(Exec)
@@ -132,6 +145,9 @@ SIGNATURES = {
     "mcb_strict_fused_pair_f32_v1": (ctypes.c_int32, [_T, _T, _T, _T, _E]),
     "mcb_strict_fused_pair_f32_noalloc_v1": (ctypes.c_int32, [_T, _T, _T, _T, _E]),
     "mcb_gemm_epilogue_v1": (ctypes.c_int32, [_T, _T, _T, _T, _P(Epilogue), ctypes.c_uint32, _E]),
+    "mcb_gemm_epilogue_chain_v1": (ctypes.c_int32, [_T, _T, _T, _T, ctypes.c_uint32,
+                                                    _P(EpilogueOp), ctypes.c_uint32,
+                                                    ctypes.c_uint32, _E]),
     "mcb_gemm_chain_v1": (ctypes.c_int32, [_T, _T, _T, _T, _P(Epilogue), _T, _E]),
     "mcb_gemm_i8_i32_v1": (ctypes.c_int32, [_T, _T, _T, _E]),
     "mcb_gemm_i8_i32_zp_v1": (ctypes.c_int32, [_T, _T, _T, ctypes.c_int32, ctypes.c_int32, _E]),

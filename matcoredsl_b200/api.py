@@ -208,24 +208,64 @@ def strict_fused_pair(a, b, d, out=None, *, device=-1, flags=0, workspace=None):
 
 
 def gemm_epilogue(x, w, bias=None, *, bias_mode=None, bias_op="add", act="none", out=None,
-                  out_dtype=None, w_transposed=False, device=-1, flags=0):
+                  out_dtype=None, w_transposed=False, device=-1, flags=0, chain=None):
     """Y = act(X @ W (+|r-) bias) (Family A). bias [N] broadcasts over rows;
     bias [M,N] is the reference's exact-shape boundary. X and W both bf16,
     both f16 or both f32; Y (default: the inputs' type) f32 or that type."""
     if bias_mode is None:
         bias_mode = "none" if bias is None else ("full" if len(bias.shape) == 2 else "row")
     n = w.shape[0] if w_transposed else w.shape[1]
+    if chain is not None and (bias is not None or act != "none"):
+        raise ValueError("chain replaces bias/act: give the bias as a chain op")
     if out is None:
         if out_dtype is None:
             xd = str(getattr(x, "dtype", ""))
             out_dtype = ("bf16" if xd.endswith("bfloat16") else
                          "f16" if xd.endswith("float16") else "f32")
         out = _empty_like_out(x, (x.shape[0], n), out_dtype)
-    ep = _abi.make_epilogue(bias_mode, bias_op, act)
     gflags = _abi.GEMM_W_TRANSPOSED if w_transposed else 0
+    if chain is not None:
+        ops, bnd_list = _epilogue_chain(chain)
+        bnds = (_abi.Tensor * max(1, len(bnd_list)))()
+        for i, t in enumerate(bnd_list):
+            bnds[i] = _desc(t, f"boundary{i}")[0]
+        _call("mcb_gemm_epilogue_chain_v1", [("y", out), ("x", x), ("w", w)],
+              [bnds, len(bnd_list), ops, len(ops), gflags], device, flags)
+        return out
+    ep = _abi.make_epilogue(bias_mode, bias_op, act)
     _call("mcb_gemm_epilogue_v1", [("y", out), ("x", x), ("w", w), ("bias", bias)],
           [ctypes.byref(ep), gflags], device, flags)
     return out
+
+
+def _epilogue_chain(chain):
+    """ctypes ops array and boundary list for a Family A epilogue chain. Each
+    item is a unary kind ("relu", "sin", ...) or (binary kind, boundary[, side])
+    with side "left" (default: value op boundary) or "right" (boundary op
+    value); the same boundary object is passed once."""
+    if not 0 < len(chain) <= _abi.EPILOGUE_MAX_OPS:
+        raise ValueError(f"an epilogue chain has 1..{_abi.EPILOGUE_MAX_OPS} ops")
+    ops = (_abi.EpilogueOp * len(chain))()
+    bnd_list = []
+    for i, item in enumerate(chain):
+        if isinstance(item, str):
+            kind, bnd, side = item, None, "left"
+        else:
+            kind, bnd, side = (tuple(item) + ("left",))[:3]
+        code = _abi.EW[kind]
+        ops[i].kind = code
+        if code >= 32:
+            if bnd is None:
+                raise ValueError(f"binary op {kind!r} needs a boundary tensor")
+            idx = next((j for j, t in enumerate(bnd_list) if t is bnd), None)
+            if idx is None:
+                bnd_list.append(bnd)
+                idx = len(bnd_list) - 1
+            ops[i].boundary = idx
+            ops[i].value_pos = {"left": 0, "right": 1}[side]
+    if len(bnd_list) > _abi.EPILOGUE_MAX_BOUNDARIES:
+        raise ValueError(f"at most {_abi.EPILOGUE_MAX_BOUNDARIES} boundary tensors")
+    return ops, bnd_list
 
 
 def gemm_chain(a, b, w, boundary=None, *, bias_mode=None, bias_op="add", act="none", out=None,

@@ -726,9 +726,13 @@ int64_t pipeline_chunk_rows(int64_t m, const mcb_tensor *x) {
   return m >= 2 * rows ? rows : 0;
 }
 
+// `ops` (num_ops > 0): the general epilogue chain of mcb_gemm_epilogue_chain_v1
+// instead of bias + activation; `bnds` are its [M,N] boundary tensors.
 mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mcb_tensor *w,
                               const mcb_tensor *bias, const mcb_epilogue *epi,
-                              uint32_t gemm_flags, const mcb_exec *exec) {
+                              uint32_t gemm_flags, const mcb_exec *exec,
+                              const mcb_tensor *bnds = nullptr, uint32_t num_bnds = 0,
+                              const mcb_epilogue_op *ops = nullptr, uint32_t num_ops = 0) {
   mcb_status s;
   if ((s = check_tensor(x, 2, 2)) || (s = check_tensor(w, 2, 2)) || (s = check_tensor(y, 2, 2)))
     return s;
@@ -772,16 +776,51 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
     ep.bias_f16 = bias->dtype == MCB_DTYPE_F16;
     ep.ld_bias = bias->rank == 2 ? bias->strides[0] : n;
   }
+  // General chain: validate the ops and boundaries (exact [M,N] tensors, as
+  // src/fusion_emitter_family_a.cpp:186-200 requires).
+  const mcb_tensor *bt[mcb::kMaxEpiBoundaries] = {};
+  if (num_ops > 0) {
+    if (!ops || num_ops > mcb::kMaxEpiOps || num_bnds > mcb::kMaxEpiBoundaries ||
+        (num_bnds > 0 && !bnds) || ep.bias_mode != MCB_BIAS_NONE || ep.act != MCB_ACT_NONE)
+      return MCB_STATUS_INVALID_ARGUMENT;
+    for (uint32_t i = 0; i < num_bnds; ++i) {
+      const mcb_tensor *b = &bnds[i];
+      if ((s = check_tensor(b, 2, 2))) return s;
+      if (b->dtype != MCB_DTYPE_F32 && b->dtype != MCB_DTYPE_BF16 && b->dtype != MCB_DTYPE_F16)
+        return MCB_STATUS_UNSUPPORTED_DTYPE;
+      if (b->dims[0] != m || b->dims[1] != n) return MCB_STATUS_SHAPE_MISMATCH;
+      if (overlaps(y, b)) return MCB_STATUS_ALIAS_VIOLATION;
+      bt[i] = b;
+      ep.bnd_dt[i] = static_cast<uint8_t>(b->dtype);
+      ep.ld_bnd[i] = b->strides[0];
+    }
+    for (uint32_t o = 0; o < num_ops; ++o) {
+      const uint32_t kind = ops[o].kind;
+      const bool unary = kind >= MCB_EW_RELU && kind <= MCB_EW_GELU_TANH;
+      const bool binary = kind >= MCB_EW_ADD && kind <= MCB_EW_MAX;
+      if (!unary && !binary) return MCB_STATUS_INVALID_ARGUMENT;
+      if (binary && (ops[o].boundary >= num_bnds || ops[o].value_pos > 1))
+        return MCB_STATUS_INVALID_ARGUMENT;
+      ep.op_kind[o] = static_cast<uint8_t>(kind);
+      ep.op_pos[o] = static_cast<uint8_t>(binary ? ops[o].value_pos : 0);
+      ep.op_bnd[o] = static_cast<uint8_t>(binary ? ops[o].boundary : 0);
+    }
+    ep.n_ops = static_cast<int>(num_ops);
+  }
   if (overlaps(y, x) || overlaps(y, w) || (ep.bias_mode && overlaps(y, bias)))
     return MCB_STATUS_ALIAS_VIOLATION;
   bool host = false;
-  if ((s = same_space({x, w, y, ep.bias_mode ? bias : nullptr}, &host))) return s;
+  if ((s = same_space({x, w, y, ep.bias_mode ? bias : nullptr, bt[0], bt[1], bt[2], bt[3]},
+                      &host)))
+    return s;
   Call call(exec);
   if ((s = call.begin(host))) return s;
   // Host operands (untimed calls): X, a full bias and Y move in row chunks of
   // about 8 MiB of X so that uploads, GEMMs and downloads overlap (W and a
   // row bias are uploaded whole, ahead of the first chunk).
-  const int64_t chunk_rows = host && !call.timed() ? pipeline_chunk_rows(m, x) : 0;
+  // (Chain boundaries are staged whole, so such calls do not pipeline.)
+  const int64_t chunk_rows =
+      host && !call.timed() && num_bnds == 0 ? pipeline_chunk_rows(m, x) : 0;
   const bool full_bias = ep.bias_mode == MCB_BIAS_FULL;
   void *dx, *dw, *dy, *db = nullptr;
   const bool serial = chunk_rows == 0;
@@ -789,6 +828,11 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
       (s = call.device_ptr(y, false, &dy)))
     return s;
   if (ep.bias_mode && (s = call.device_ptr(bias, serial, &db))) return s;
+  for (uint32_t i = 0; i < num_bnds; ++i) {
+    void *d = nullptr;
+    if ((s = call.device_ptr(bt[i], true, &d))) return s;
+    ep.bnd[i] = d;
+  }
   ep.bias = db;
   ep.bias_aligned16 = (reinterpret_cast<uintptr_t>(db) & 15u) == 0;
   LaunchInfo info;
@@ -815,6 +859,8 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
       e.bias = static_cast<const char *>(db) + r0 * ep.ld_bias * bs;
       e.bias_aligned16 = (reinterpret_cast<uintptr_t>(e.bias) & 15u) == 0;
     }
+    for (uint32_t i = 0; i < num_bnds; ++i)
+      e.bnd[i] = static_cast<const char *>(ep.bnd[i]) + r0 * ep.ld_bnd[i] * dtype_size(bt[i]->dtype);
     if (tma_ok)
       return mcb::launch_gemm_tc_bf16(xr, dw, yr, r1 - r0, n, k, ld_x, ld_w, ld_y, wt ? 1 : 0,
                                       y_kind, e, call.ctx()->status, call.sms(), call.stream(),
@@ -1448,6 +1494,22 @@ MCB_API mcb_status mcb_gemm_epilogue_v1(const mcb_tensor *y, const mcb_tensor *x
                                         const mcb_exec *exec) noexcept {
   try {
     return gemm_epilogue_impl(y, x, w, bias, epilogue, gemm_flags, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API mcb_status mcb_gemm_epilogue_chain_v1(const mcb_tensor *y, const mcb_tensor *x,
+                                              const mcb_tensor *w,
+                                              const mcb_tensor *boundaries,
+                                              uint32_t num_boundaries,
+                                              const mcb_epilogue_op *ops, uint32_t num_ops,
+                                              uint32_t gemm_flags,
+                                              const mcb_exec *exec) noexcept {
+  try {
+    if (num_ops == 0 || !ops) return MCB_STATUS_INVALID_ARGUMENT;
+    return gemm_epilogue_impl(y, x, w, nullptr, nullptr, gemm_flags, exec, boundaries,
+                              num_boundaries, ops, num_ops);
   } catch (...) {
     return MCB_STATUS_CANDIDATE_FAILURE;
   }

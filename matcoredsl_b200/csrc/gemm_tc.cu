@@ -58,14 +58,22 @@ struct Params {
 };
 
 // Epilogue of one 32-column chunk held by one thread (one output row).
+// Rows past M (the ragged last tile) return before any load: a full [M,N]
+// bias or boundary has no row there.
+// kChain: the general op chain (its own kernel instantiation, so the
+// bias + activation kernels compile exactly as without it).
+template <bool kChain>
 __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (&r)[32],
                                                int64_t row, int64_t col0) {
+  if (row >= p.m) return;
   float v[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
   const Epilogue &e = p.epi;
   const bool full_chunk = col0 + 32 <= p.n;
-  if (e.bias_mode == 1 && e.bias_bf16 && e.bias_aligned16 && full_chunk) {
+  if constexpr (kChain) {
+    epilogue_chain_chunk(e, v, row, col0, p.n);
+  } else if (e.bias_mode == 1 && e.bias_bf16 && e.bias_aligned16 && full_chunk) {
     // Row-broadcast bf16 bias: every lane reads the same 64 bytes.
     const uint4 *bp = reinterpret_cast<const uint4 *>(
         reinterpret_cast<const __nv_bfloat16 *>(e.bias) + col0);
@@ -106,7 +114,7 @@ __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (
       }
     }
   }
-  switch (e.act) {
+  switch (kChain ? 0 : e.act) {
     case 0: break;
     case 2:
 #pragma unroll
@@ -117,7 +125,6 @@ __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (
       for (int i = 0; i < 32; ++i) v[i] = apply_act<true>(v[i], e.act);
       break;
   }
-  if (row >= p.m) return;
   if (p.y_kind == kOutF16) {
     __half *yr = reinterpret_cast<__half *>(p.y) + row * p.ld_y + col0;
     if (full_chunk) {
@@ -166,6 +173,7 @@ __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (
   }
 }
 
+template <bool kChain>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_bf16_kernel(const __grid_constant__ CUtensorMap tmap_x,
                         const __grid_constant__ CUtensorMap tmap_w, const Params p) {
@@ -307,7 +315,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (n0 + c >= p.n) break;
         uint32_t r[32];
         tmem_ld32_sync(t_row + c, r);
-        epilogue_chunk(p, r, row, n0 + c);
+        epilogue_chunk<kChain>(p, r, row, n0 + c);
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
@@ -344,6 +352,7 @@ constexpr int P_STAGES = 6;
 constexpr int P_THREADS = 320;  // producer, MMA, 8 epilogue warps (2 per TMEM lane quarter)
 constexpr size_t P_SMEM_BYTES = static_cast<size_t>(P_STAGES) * P_STAGE_BYTES + BAR_BYTES + 1024;
 
+template <bool kChain>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     gemm_tc_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
                              const __grid_constant__ CUtensorMap tmap_w, const Params p) {
@@ -489,7 +498,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         if (n0 + c >= p.n) break;
         uint32_t r[32];
         tmem_ld32_sync(t_row + c, r);
-        epilogue_chunk(p, r, row, n0 + c);
+        epilogue_chunk<kChain>(p, r, row, n0 + c);
       }
       tc_fence_before();
       mbar_arrive_cluster(acc_empty_leader + acc * 8);
@@ -518,7 +527,7 @@ int pair_clusters_resident(int device) {
   if (device < 0 || device >= 64) return 0;
   int v = cache[device].load(std::memory_order_relaxed);
   if (v != 0) return v;
-  if (cudaFuncSetAttribute(gemm_tc_bf16_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(gemm_tc_bf16_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(P_SMEM_BYTES)) != cudaSuccess) {
     (void)cudaGetLastError();
     cache[device].store(-1, std::memory_order_relaxed);
@@ -529,7 +538,8 @@ int pair_clusters_resident(int device) {
   cfg.blockDim = dim3(P_THREADS, 1, 1);
   cfg.dynamicSmemBytes = P_SMEM_BYTES;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_bf16_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_bf16_pair_kernel<false>, &cfg) != cudaSuccess ||
+      n <= 0) {
     (void)cudaGetLastError();
     n = -1;  // pair kernel unavailable on this device: use the single-SM kernel
   }
@@ -553,6 +563,7 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
                                 uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info,
                                 int in_f16) {
   if (m == 0 || n == 0) return cudaSuccess;
+  const bool chain = epi.n_ops > 0;
   // Rows of 256 go to CTA pairs (M = 256 per MMA, W tile split between the
   // two SMs); shorter problems keep one 128-row tile per SM.
   int device = 0;
@@ -560,7 +571,7 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   if (e != cudaSuccess) return e;
   const bool pair = m >= 2 * BM && pair_kernel_enabled() && pair_clusters_resident(device) > 0;
   if (pair) {
-    e = cudaFuncSetAttribute(gemm_tc_bf16_pair_kernel,
+    e = cudaFuncSetAttribute(chain ? gemm_tc_bf16_pair_kernel<true> : gemm_tc_bf16_pair_kernel<false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(P_SMEM_BYTES));
     if (e != cudaSuccess) return e;
@@ -599,14 +610,21 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
     if (clusters > sms / 2) clusters = sms / 2;
     if (clusters < 1) clusters = 1;
     grid = 2 * static_cast<int>(tiles < clusters ? tiles : clusters);
-    gemm_tc_bf16_pair_kernel<<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
+    if (chain)
+      gemm_tc_bf16_pair_kernel<true><<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
+    else
+      gemm_tc_bf16_pair_kernel<false><<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
   } else {
     // Per-device function attribute; cheap, so set on every launch.
-    e = cudaFuncSetAttribute(gemm_tc_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(chain ? gemm_tc_bf16_kernel<true> : gemm_tc_bf16_kernel<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(SMEM_BYTES));
     if (e != cudaSuccess) return e;
     grid = static_cast<int>(tiles < sms ? tiles : sms);
-    gemm_tc_bf16_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(tx, tw, p);
+    if (chain)
+      gemm_tc_bf16_kernel<true><<<grid, THREADS, SMEM_BYTES, stream>>>(tx, tw, p);
+    else
+      gemm_tc_bf16_kernel<false><<<grid, THREADS, SMEM_BYTES, stream>>>(tx, tw, p);
   }
   if (info) {
     info->launches = 1;

@@ -46,6 +46,7 @@ cudaError_t launch_strict_pair_fixed_scratch(const float *a, const float *b, con
                                              int sms, cudaStream_t stream, LaunchInfo *info);
 
 // ---- epilogue description shared by the GEMM kernels ----------------------------
+constexpr int kMaxEpiOps = 8, kMaxEpiBoundaries = 4;
 struct Epilogue {
   int bias_mode = 0;  // 0 none, 1 row-broadcast [N], 2 full [M,N]
   int bias_op = 0;    // 0 add, 1 reverse subtract
@@ -55,6 +56,19 @@ struct Epilogue {
   int bias_aligned16 = 0;  // bias base is 16-byte aligned (vector loads allowed)
   const void *bias = nullptr;
   int64_t ld_bias = 0;
+  // General chain (mcb_gemm_epilogue_chain_v1): when n_ops > 0 the fields
+  // above are unused and the ops apply in order to the f32 accumulator.
+  // Kinds are the MCB_EW_* codes (unary < 32, binary >= 32); a binary op
+  // combines the running value with boundary op_bnd[i] ([M,N], row stride
+  // ld_bnd, dtype code bnd_dt: 1 f32, 3 bf16, 6 f16), the value on the left
+  // when op_pos[i] == 0, on the right when 1.
+  int n_ops = 0;
+  uint8_t op_kind[kMaxEpiOps] = {};
+  uint8_t op_pos[kMaxEpiOps] = {};
+  uint8_t op_bnd[kMaxEpiOps] = {};
+  uint8_t bnd_dt[kMaxEpiBoundaries] = {};
+  const void *bnd[kMaxEpiBoundaries] = {};
+  int64_t ld_bnd[kMaxEpiBoundaries] = {};
 };
 
 // ---- gemm_tc.cu: tcgen05 bf16 / f16 GEMM + epilogue ------------------------------

@@ -195,6 +195,34 @@ def gemm_epilogue(x, w, bias=None, bias_mode="none", bias_op="add", act="none", 
     return y
 
 
+
+def gemm_epilogue_chain(x, w, chain):
+    """fp64 Family A epilogue chain, op by op as the reference emits them
+    (src/fusion_emitter_common.cpp:38-160; chain rules
+    src/fusion_emitter_family_a.cpp:149-220). `chain` items: a unary kind, or
+    (binary kind, boundary[, "left"|"right"]); "right" puts the running value
+    on the right of the operator."""
+    v = gemm_epilogue(x, w)
+    c0, c1 = 0.7978845608, 0.044715
+    unary = {
+        "relu": lambda a: np.maximum(a, 0.0), "exp": np.exp, "log": np.log, "tanh": np.tanh,
+        "sqrt": np.sqrt, "neg": np.negative, "abs": np.abs, "sin": np.sin, "cos": np.cos,
+        "rsqrt": lambda a: 1.0 / np.sqrt(a), "sigmoid": lambda a: 1.0 / (1.0 + np.exp(-a)),
+        "gelu_tanh": lambda a: 0.5 * a * (1.0 + np.tanh(c0 * (a + c1 * a * a * a))),
+    }
+    unary["gelu"] = unary["gelu_tanh"]
+    binary = {"add": np.add, "sub": np.subtract, "mul": np.multiply, "div": np.divide,
+              "min": np.minimum, "max": np.maximum}
+    with np.errstate(all="ignore"):
+        for item in chain:
+            if isinstance(item, str):
+                v = unary[item](v)
+                continue
+            kind, bnd, side = (tuple(item) + ("left",))[:3]
+            b = np.asarray(bnd, np.float64)
+            v = binary[kind](v, b) if side == "left" else binary[kind](b, v)
+    return v
+
 def msm(q, k, v, scale=1.0):
     """fp64 softmax(scale * q k^T) v for rank-2 q [m,d], k [n,d], v [n,dv]."""
     q, k, v = _c(q, np.float32), _c(k, np.float32), _c(v, np.float32)

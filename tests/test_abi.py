@@ -43,7 +43,8 @@ def test_abi_struct_layouts_match_c_compiler(mcb, tmp_path):
     structs = {"mcb_tensor": _abi.Tensor, "mcb_exec": _abi.Exec, "mcb_report": _abi.Report,
                "mcb_epilogue": _abi.Epilogue, "mcb_buffer": _abi.Buffer,
                "mcb_fp8_tile_config": _abi.Fp8TileConfig, "mcb_shard": _abi.Shard,
-               "mcb_plan_desc": _abi.PlanDesc, "mcb_comm_id": _abi.CommId}
+               "mcb_plan_desc": _abi.PlanDesc, "mcb_comm_id": _abi.CommId,
+               "mcb_epilogue_op": _abi.EpilogueOp}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "mcb.h"', "int main(void){"]
     for cname, py in structs.items():
         lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
