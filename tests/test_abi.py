@@ -159,3 +159,27 @@ def test_comm_arguments_checked_without_gpu(mcb):
     assert lib.mcb_comm_init_v1(None, 2, 0, 0, ctypes.byref(out)) == bad
     assert lib.mcb_allgather_v1(None, 0x1000, 0x2000, 16, None) == bad
     assert lib.mcb_comm_destroy_v1(None) == 0
+
+
+def test_epilogue_chain_encoding(mcb):
+    """Host side of mcb_gemm_epilogue_chain_v1: op codes, value side, one
+    boundary slot per distinct tensor, and the argument limits (no GPU)."""
+    from matcoredsl_b200 import _abi
+    from matcoredsl_b200.api import _epilogue_chain
+    b0, b1 = np.zeros((4, 4), np.float32), np.ones((4, 4), np.float32)
+    ops, bnds = _epilogue_chain(["relu", ("mul", b0), ("sub", b1, "right"), ("max", b0), "rsqrt"])
+    assert [o.kind for o in ops] == [1, 34, 33, 37, 10]
+    assert [o.value_pos for o in ops] == [0, 0, 1, 0, 0]
+    assert [o.boundary for o in ops[1:4]] == [0, 1, 0]
+    assert len(bnds) == 2 and bnds[0] is b0 and bnds[1] is b1
+    assert ctypes.sizeof(_abi.EpilogueOp) == 16
+    with pytest.raises(ValueError):
+        _epilogue_chain([])
+    with pytest.raises(ValueError):
+        _epilogue_chain(["relu"] * (_abi.EPILOGUE_MAX_OPS + 1))
+    with pytest.raises(ValueError):
+        _epilogue_chain([("add", None)])
+    with pytest.raises(ValueError):
+        _epilogue_chain([("add", np.zeros(1)) for _ in range(5)])
+    with pytest.raises(KeyError):
+        _epilogue_chain(["softmax"])
