@@ -314,6 +314,11 @@ def run_profile_config(cfg: int, steps: int, warmup: int):
                    for _ in range(3))
         o = torch.empty_like(q)
         fn = lambda: mcb.msm(q, k, v, 128 ** -0.5, out=o)  # noqa: E731
+    elif cfg == 9:  # MSM at head dim 64 (tensor cores), config 3's B, H, S
+        q, k, v = (torch.randn(8, 32, 4096, 64, generator=g, device=dev).to(torch.bfloat16)
+                   for _ in range(3))
+        o = torch.empty_like(q)
+        fn = lambda: mcb.msm(q, k, v, 64 ** -0.5, out=o)  # noqa: E731
     elif cfg == 4:
         t = torch.randn(16384, 16384, generator=g, device=dev)
         qa, sa = mcb.fp8_quantize_blockwise(t, 128, "e4m3")
@@ -596,7 +601,7 @@ def main():
                     help="skip the host-buffer end-to-end leg (used for short profiling runs)")
     ap.add_argument("--no-other-configs", action="store_true",
                     help="skip the configs 1/3/4/5 measurements reported beside the headline")
-    ap.add_argument("--profile-config", type=int, choices=[1, 2, 3, 4, 5, 6, 7, 8],
+    ap.add_argument("--profile-config", type=int, choices=[1, 2, 3, 4, 5, 6, 7, 8, 9],
                     help="only launch this config's operator (for ncu captures); no JSON line")
     args = ap.parse_args()
     if args.profile_config:
