@@ -54,6 +54,8 @@ struct Params {
   int w_transposed, y_kind, in_f16;  // y_kind: kOutF32 / kOutBf16 / kOutF16
   void *y;
   uint32_t *status;
+  long long spin_limit;  // clock64 cycles a pipeline wait may take before the kernel aborts
+  int stall_loads;       // self-test only: the producer issues no loads (the waits must time out)
   Epilogue epi;
 };
 
@@ -114,16 +116,21 @@ __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (
       }
     }
   }
-  switch (kChain ? 0 : e.act) {
-    case 0: break;
-    case 2:
+  // The hardware tanh / exp approximations (~2^-11 relative) are used only
+  // when the result is rounded to bf16 (8 mantissa bits) anyway; f32 and f16
+  // outputs take CUDA's accurate tanhf / expf.
+  const int act = kChain ? 0 : e.act;
+  if (act != 0 && p.y_kind == kOutBf16) {
+    if (act == 2) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = apply_act<true>(v[i], 2);
-      break;
-    default:
+    } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = apply_act<true>(v[i], e.act);
-      break;
+      for (int i = 0; i < 32; ++i) v[i] = apply_act<true>(v[i], act);
+    }
+  } else if (act != 0) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = apply_act<false>(v[i], act);
   }
   if (p.y_kind == kOutF16) {
     __half *yr = reinterpret_cast<__half *>(p.y) + row * p.ld_y + col0;
@@ -221,14 +228,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (lane == 0 && !p.stall_loads) {
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
         const int m0 = (tile / p.n_tiles) * BM;
         const int n0 = (tile % p.n_tiles) * BN;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kErrTimeoutEmpty))
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kErrTimeoutEmpty,
+                         p.spin_limit))
             goto producer_done;
           mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           tma_load_2d(sa + stage * A_BYTES, &tmap_x, &full[stage], kb * BK, m0);
@@ -257,13 +265,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.status, kErrTimeoutAccum))
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.status, kErrTimeoutAccum,
+                       p.spin_limit))
           break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         bool ok = true;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kErrTimeoutFull)) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kErrTimeoutFull, p.spin_limit)) {
             ok = false;
             break;
           }
@@ -304,7 +313,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * BM;
       const int64_t n0 = static_cast<int64_t>(tile % p.n_tiles) * BN;
-      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.status, kErrTimeoutAccum))
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.status, kErrTimeoutAccum,
+                          p.spin_limit))
         break;
       tc_fence_after();
       const int64_t row = m0 + sub * 32 + lane;
@@ -413,7 +423,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         const int m0 = (tile / p.n_tiles) * (2 * BM) + static_cast<int>(rank) * BM;
         const int n0 = (tile % p.n_tiles) * BN + static_cast<int>(rank) * P_BN_CTA;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kErrTimeoutEmpty))
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kErrTimeoutEmpty,
+                         p.spin_limit))
             goto producer_done;
           const uint32_t fbar = full_leader0 + stage * 8;
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
@@ -443,13 +454,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int tile = cluster; tile < p.num_tiles; tile += nclusters) {
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.status, kErrTimeoutAccum))
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.status, kErrTimeoutAccum,
+                       p.spin_limit))
           break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         bool ok = true;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kErrTimeoutFull)) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kErrTimeoutFull, p.spin_limit)) {
             ok = false;
             break;
           }
@@ -487,7 +499,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     for (int tile = cluster; tile < p.num_tiles; tile += nclusters) {
       const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * (2 * BM) + rank * BM;
       const int64_t n0 = static_cast<int64_t>(tile % p.n_tiles) * BN;
-      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.status, kErrTimeoutAccum))
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.status, kErrTimeoutAccum,
+                          p.spin_limit))
         break;
       tc_fence_after();
       const int64_t row = m0 + sub * 32 + lane;
@@ -603,6 +616,8 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   p.in_f16 = in_f16;
   p.y = y;
   p.status = status;
+  p.spin_limit = kSpinTimeoutCycles;
+  p.stall_loads = 0;
   p.epi = epi;
   int grid;
   if (pair) {
@@ -635,6 +650,42 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
     info->ctas = grid;
     info->set_route(in_f16 ? "tcgen05_f16_gemm_epilogue" : "tcgen05_bf16_gemm_epilogue");
   }
+  return cudaGetLastError();
+}
+
+// Self-test of the bounded waits: one single-SM GEMM tile (128x64 . 64x256)
+// whose producer issues no loads, so the MMA thread's wait for the first
+// stage must run out after `spin_limit` cycles, record kErrTimeoutFull in
+// *status and abort the CTA (the epilogue warps leave through the abort
+// flag, TMEM is freed). x must hold 128x64 and w 64x256 16-byte-aligned bf16
+// elements (they are never read), y 128x256 bf16 (never written).
+cudaError_t launch_gemm_tc_stall_selftest(const void *x, const void *w, void *y,
+                                          long long spin_limit, uint32_t *status,
+                                          cudaStream_t stream) {
+  CUtensorMap tx, tw;
+  if (!encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, BK, BM, BK * 2, BK, BM,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, BN, BK, BN * 2, 64, BK,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  Params p = {};
+  p.m = BM;
+  p.n = BN;
+  p.k = BK;
+  p.ld_y = BN;
+  p.n_tiles = 1;
+  p.num_tiles = 1;
+  p.num_kb = 1;
+  p.y_kind = kOutBf16;
+  p.y = y;
+  p.status = status;
+  p.spin_limit = spin_limit;
+  p.stall_loads = 1;
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_bf16_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(SMEM_BYTES));
+  if (e != cudaSuccess) return e;
+  gemm_tc_bf16_kernel<false><<<1, THREADS, SMEM_BYTES, stream>>>(tx, tw, p);
   return cudaGetLastError();
 }
 

@@ -85,6 +85,26 @@ def test_tcgen05_fp8_gemm(mcb, orc, shape, fmts):
     assert orc.rel_frobenius(got, full) < (6e-2 if fmts == ("e4m3", "e4m3") else 0.2)
 
 
+@pytest.mark.parametrize("shape", [(200, 264, 160), (384, 136, 4000), (130, 520, 2080)])
+@pytest.mark.parametrize("fmts", [("e4m3", "e4m3"), ("e5m2", "e5m2")])
+def test_tcgen05_fp8_gemm_ragged_k(mcb, orc, shape, fmts):
+    """K not a multiple of the 128-deep scale block (legal under the
+    reference's K % 32 == 0 rule, src/fp8_wgmma.cpp:10-24): the last K block
+    is partly zero-filled by TMA and scaled by the scales of a short block.
+    M or N is ragged as well."""
+    import torch
+    m, n, k = shape
+    a, bt, qa, sa, qb, sb = _operands(m, n, k, seed=m * 7 + n + k, fa=fmts[0], fb=fmts[1])
+    assert sa.shape[1] == (k + 127) // 128
+    c = torch.empty(m, n, dtype=torch.float32, device="cuda")
+    mcb.gemm_fp8_blockscaled(qa, sa, qb, sb, out=c)
+    assert mcb.api.last_result.route == "tcgen05_fp8_blockscaled_gemm"
+    ref = orc.gemm_fp8_blockscaled(_codes(qa), sa.cpu().numpy(), _codes(qb), sb.cpu().numpy(),
+                                   fmts[0], fmts[1])
+    assert orc.rel_frobenius(gu.from_dev(c), ref) < 1e-5
+    assert mcb.device_status(0) == 0
+
+
 def test_fp8_gemm_bf16_out_and_simt_route(mcb, orc):
     import torch
     m, n, k = 200, 136, 200  # K not a multiple of 16: CUDA-core kernel

@@ -78,6 +78,61 @@ def test_tcgen05_epilogues_bf16_out(mcb, orc, act, bias_mode, bias_op):
     assert y.dtype == torch.bfloat16
 
 
+@pytest.mark.parametrize("act", ["none", "relu", "gelu_tanh", "exp", "sigmoid", "tanh"])
+@pytest.mark.parametrize("bias_mode,bias_op", [("none", "add"), ("row", "add"), ("full", "rsub")])
+@pytest.mark.parametrize("m", [200, 512])
+def test_tcgen05_epilogues_f32_out(mcb, orc, act, bias_mode, bias_op, m):
+    """bf16 operands, f32 output: the activations must be the accurate ones
+    (the hardware tanh/exp approximations are ~2^-11 relative, far above
+    f32), so every activation and bias mode is held to 1e-5 relative
+    Frobenius error and to the reference's Family A max-abs bar of 1e-3
+    (tests/test_family_a.py). m = 200 runs the single-SM kernel, 512 the
+    CTA-pair kernel."""
+    import torch
+    k, n = 512, 384
+    x, w, b = _inputs(m, k, n, seed=11)
+    xh, xf = gu.bf16_pair(x)
+    wh, wf = gu.bf16_pair(w * 2.0)   # pre-activations ~N(0, 4): tanh/GELU saturation regions too
+    bias_np = bias_dev = None
+    if bias_mode == "row":
+        bh, bias_np = gu.bf16_pair(b)
+        bias_dev = gu.to_dev_bf16(bh)
+    elif bias_mode == "full":
+        bias_np = np.random.default_rng(12).normal(scale=0.5, size=(m, n)).astype(np.float32)
+        bias_dev = gu.to_dev_f32(bias_np)
+    y = torch.empty(m, n, dtype=torch.float32, device="cuda")
+    mcb.gemm_epilogue(gu.to_dev_bf16(xh), gu.to_dev_bf16(wh), bias_dev, bias_mode=bias_mode,
+                      bias_op=bias_op, act=act, out=y)
+    r = mcb.api.last_result
+    assert r.route == "tcgen05_bf16_gemm_epilogue"
+    assert r.tile[0] == (256 if m >= 256 else 128)
+    ref = orc.gemm_epilogue(xf, wf, bias_np, bias_mode=bias_mode, bias_op=bias_op, act=act)
+    got = gu.from_dev(y)
+    assert orc.rel_frobenius(got, ref) < REL_F32_OUT
+    assert np.max(np.abs(got - ref) / np.maximum(1.0, np.abs(ref))) < 1e-3
+
+
+@pytest.mark.parametrize("act", ["gelu_tanh", "exp", "sigmoid", "tanh"])
+def test_tcgen05_epilogues_f16_out(mcb, orc, act):
+    """f16 output (10 mantissa bits) takes the accurate activations too: the
+    error is the f16 rounding alone, under one f16 half-ulp (2^-11) relative
+    per element for normal results."""
+    import torch
+    m, k, n = 512, 512, 384
+    x, w, _ = _inputs(m, k, n, seed=13)
+    x16 = torch.from_numpy(x).half().cuda()
+    w16 = torch.from_numpy(w * 2.0).half().cuda()
+    y = torch.empty(m, n, dtype=torch.float16, device="cuda")
+    mcb.gemm_epilogue(x16, w16, act=act, out=y)
+    assert mcb.api.last_result.route.startswith("tcgen05")
+    ref = orc.gemm_epilogue(x16.float().cpu().numpy(), w16.float().cpu().numpy(), act=act)
+    got = y.float().cpu().numpy()
+    # half an f16 ulp (2^-11 relative for normal results) plus 1e-5 for the
+    # f32 accumulation error where the pre-activation cancels near zero
+    assert np.all(np.abs(got - ref) <= 2.0 ** -11 * 1.01 * np.abs(ref) + 1e-5)
+    assert orc.rel_frobenius(got, ref) < 5e-4
+
+
 # The reference's Family A GPU tests (tests/test_family_a.py:34-154): f32,
 # M=N=64, K=32, max-abs tolerance 1e-3; exp uses inputs scaled by 0.1.
 FAMILY_A = [
