@@ -81,7 +81,8 @@ constexpr size_t smem_bytes() {
 struct Params {
   int64_t heads, qblocks, nkv_tiles, units;
   int64_t o_s[3];  // output element strides [batch, head, row]
-  float c;         // scale * log2(e)
+  float c;         // |scale| * log2(e)
+  uint32_t s_neg;  // instruction-descriptor bit 13 (negate A) when scale < 0, else 0
   int o_tma;       // two-tile kernel: O leaves through shared memory and a TMA store
   int m_rows;      // query rows: rows of the last query block past it are not stored
   int n_tail;      // keys in the last key tile when N % 128 != 0, else 0
@@ -155,6 +156,17 @@ __device__ __forceinline__ void mask_key_tail(uint32_t (&s)[128], int n_tail) {
 #pragma unroll
   for (int i = 0; i < 128; ++i)
     if (i >= n_tail) s[i] = 0xff800000u;
+}
+
+// scale == 0 (c == 0): every weight is 2^0 = 1, but the -inf scores of the
+// masked tail keys would give 0 * -inf = NaN in the exponent. For that case
+// the last tile's weights are rebuilt as 1 for the n_tail real keys and 0
+// past them; returns their sum.
+__device__ __forceinline__ float zero_scale_tail_weights(uint32_t (&pk)[64], int n_tail) {
+#pragma unroll
+  for (int i = 0; i < 64; ++i)
+    pk[i] = pack_bf16x2(2 * i < n_tail ? 1.0f : 0.0f, 2 * i + 1 < n_tail ? 1.0f : 0.0f);
+  return static_cast<float>(n_tail);
 }
 
 // (batch, head, query block) of work unit u. 32-bit arithmetic (the launcher
@@ -250,7 +262,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc_s = make_idesc(1, 1, 0, 0, BQ, BKV);
+      const uint32_t idesc_s = make_idesc(1, 1, 0, 0, BQ, BKV) | p.s_neg;
       const uint32_t idesc_o = make_idesc(1, 1, 0, 1, BQ, HD);
       const uint32_t q_addr = smem_u32(sm.q), p_addr = smem_u32(sm.p);
       uint32_t st = 0, pt = 0, uc = 0;
@@ -396,6 +408,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           psum += e0 + e1;
           pk[i] = pack_bf16x2(e0, e1);
         }
+        if (kTail && t + 1 == nkv && p.c == 0.0f) psum = zero_scale_tail_weights(pk, p.n_tail);
         l += psum;
         // P buffer is free once PV of the previous tile has completed.
         if (!(ok = mbar_wait_warp(&sm.p_free, (p_cnt & 1) ^ 1, abort_flag, p.status,
@@ -581,7 +594,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc_s = make_idesc(1, 1, 0, 0, BQ, BKV);
+      const uint32_t idesc_s = make_idesc(1, 1, 0, 0, BQ, BKV) | p.s_neg;
       const uint32_t idesc_o = make_idesc(1, 1, 0, 1, BQ, HD);
       uint32_t kvc = 0, s_cnt = 0, p_cnt = 0, uc = 0;
       bool ok = true;
@@ -756,7 +769,10 @@ __global__ void __launch_bounds__(THREADS2, 1)
         {
           float a0, a1;
           f2_unpack(f2_add(f2_add(ps[0], ps[1]), f2_add(ps[2], ps[3])), a0, a1);
-          l += a0 + a1;
+          float tile_sum = a0 + a1;
+          if (kTail && t + 1 == nkv && p.c == 0.0f)
+            tile_sum = zero_scale_tail_weights(pk, p.n_tail);
+          l += tile_sum;
         }
         // P_g is free once PV_g of the previous tile has completed.
         if (!(ok = mbar_wait_warp(&sm.p_free[g], (p_cnt & 1) ^ 1, abort_flag, p.status,
@@ -901,7 +917,12 @@ cudaError_t launch_msm_tc_bf16(const void *q, const void *k, const void *v, void
   if (p.units > 0x7fffffff) return cudaErrorNotSupported;  // unit indices are 32-bit
   for (int i = 0; i < 3; ++i) p.o_s[i] = s.o_s[i];
   p.o_tma = o_tma ? 1 : 0;
-  p.c = scale * 1.4426950408889634f;
+  // softmax(scale * S) with scale < 0 equals softmax(|scale| * (-S)). The S
+  // MMA negates Q (the A operand) instead, which is exact (the negated
+  // products and their sum round symmetrically), so the softmax code always
+  // sees a non-negative factor and its row maximum is the exponent maximum.
+  p.c = fabsf(scale) * 1.4426950408889634f;
+  p.s_neg = scale < 0.0f ? kIdescNegateA : 0u;
   p.o = static_cast<__nv_bfloat16 *>(o);
   p.status = status;
   cudaError_t e;

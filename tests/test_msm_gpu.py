@@ -197,3 +197,28 @@ def test_tiled_cuda_core_msm(mcb, orc, dtype, shape):
             else:
                 assert orc.rel_frobenius(got[bi, hi], ref) < 1e-2
 
+
+
+@pytest.mark.parametrize("scale", [-0.125, -1.0, 0.0])
+@pytest.mark.parametrize("shape,route", [
+    ((1, 2, 256, 128), "tcgen05_bf16_msm"),
+    ((1, 2, 300, 64), "tcgen05_bf16_msm"),      # single-tile units, ragged M
+    ((2, 2, 1000, 128), "tcgen05_bf16_msm"),    # two-tile units, ragged M and keys
+    ((1, 3, 200, 32), "simt_tiled_online_softmax_msm"),
+    ((1, 2, 100, 96), "simt_online_softmax_msm"),
+])
+def test_non_positive_scale(mcb, orc, scale, shape, route):
+    """softmax(scale * Q K^T) for scale <= 0 on every route: a negative scale
+    turns the smallest score into the largest exponent (the tensor-core
+    kernels negate Q inside the S MMA and keep |scale|), and scale = 0 gives
+    uniform weights, i.e. the mean of V's rows."""
+    _check_msm(mcb, orc, _bf16_case(shape, 31 + sum(shape)), scale, route)
+    assert mcb.device_status(0) == 0
+
+
+def test_scale_not_finite_in_f32_rejected(mcb):
+    import torch
+    q = torch.zeros((1, 1, 128, 128), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(mcb.McbError) as ei:
+        mcb.msm(q, q, q, 1e300)
+    assert "INVALID_ARGUMENT" in str(ei.value)
