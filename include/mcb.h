@@ -7,8 +7,7 @@
  * Every entry point is extern "C", noexcept, takes plain pointers and sizes,
  * and reports failure only through its return code. Each declaration names
  * the MatcoreDSL interface (path:line in the MatcoreDSL repository) it
- * replaces; the adapters a maintainer adds on the reference side are shown in
- * INTEGRATION.md.
+ * replaces.
  *
  * Conventions
  *  - Ownership: the caller owns every buffer. Operands may live in host
@@ -155,6 +154,17 @@ MCB_API uint32_t mcb_abi_version(void) MCB_NOEXCEPT;
 MCB_API const char *mcb_status_message(mcb_status code) MCB_NOEXCEPT;
 /* Reads (and with clear != 0 resets) the device status word of `device`. */
 MCB_API mcb_status mcb_device_status(int32_t device, uint32_t *word, int32_t clear) MCB_NOEXCEPT;
+/* Self-test of the bounded device waits, the counterpart of the reference
+ * adapter's poison domain (compiler/lib/runtime/closed_cuda_candidate_v1.cpp:86-120):
+ * runs one tensor-core GEMM tile on `device` whose loads are never issued,
+ * so its pipeline wait gives up after `spin_limit_cycles` (10^4..4*10^9
+ * clock64 cycles; ordinary launches use ~2 s). Returns
+ * MCB_STATUS_DEVICE_TIMEOUT when the kernel returned and reported the stall
+ * (bit 0, "producer data never arrived", set in the device status word,
+ * which stays set until cleared with mcb_device_status). Synchronises the
+ * device; allocates 112 KiB for the call. */
+MCB_API mcb_status mcb_device_timeout_selftest_v1(int32_t device,
+                                                  uint64_t spin_limit_cycles) MCB_NOEXCEPT;
 /* Ok when `device` is an sm_100 GPU this build can run on; replaces
  * detail::cudaCandidateAvailable (compiler/lib/runtime/closed_cuda_candidate_v1.h:13). */
 MCB_API mcb_status mcb_candidate_available(int32_t device) MCB_NOEXCEPT;

@@ -140,6 +140,7 @@ SIGNATURES = {
     "mcb_abi_version": (ctypes.c_uint32, []),
     "mcb_status_message": (ctypes.c_char_p, [ctypes.c_int32]),
     "mcb_device_status": (ctypes.c_int32, [ctypes.c_int32, _P(ctypes.c_uint32), ctypes.c_int32]),
+    "mcb_device_timeout_selftest_v1": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_uint64]),
     "mcb_candidate_available": (ctypes.c_int32, [ctypes.c_int32]),
     "mcb_strict_gemm_f32_v1": (ctypes.c_int32, [_T, _T, _T, _E]),
     "mcb_strict_fused_pair_f32_v1": (ctypes.c_int32, [_T, _T, _T, _T, _E]),

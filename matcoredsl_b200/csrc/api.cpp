@@ -1104,7 +1104,9 @@ mcb_status msm_impl(const mcb_tensor *o, const mcb_tensor *q, const mcb_tensor *
   fill(v, sh.v_s);
   fill(o, sh.o_s);
   if (sh.n == 0) return MCB_STATUS_INVALID_SHAPE;  // softmax over zero keys is undefined
-  if (!std::isfinite(scale)) return MCB_STATUS_INVALID_ARGUMENT;
+  // The kernels compute in f32: a scale that is not finite there is rejected.
+  if (!std::isfinite(scale) || !std::isfinite(static_cast<float>(scale)))
+    return MCB_STATUS_INVALID_ARGUMENT;
   if (overlaps(o, q) || overlaps(o, k) || overlaps(o, v)) return MCB_STATUS_ALIAS_VIOLATION;
   bool host = false;
   if ((s = same_space({q, k, v, o}, &host))) return s;
@@ -1455,6 +1457,47 @@ MCB_API mcb_status mcb_device_status(int32_t device, uint32_t *word, int32_t cle
     return MCB_STATUS_CANDIDATE_FAILURE;
   if (clear && cudaMemset(c->status, 0, 4) != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
   return MCB_STATUS_OK;
+}
+
+MCB_API mcb_status mcb_device_timeout_selftest_v1(int32_t device,
+                                                  uint64_t spin_limit_cycles) noexcept {
+  if (spin_limit_cycles < 10000 || spin_limit_cycles > 4000000000ull)
+    return MCB_STATUS_INVALID_ARGUMENT;
+  mcb_exec ex{};
+  ex.abi_version = MCB_ABI_VERSION_V1;
+  ex.struct_size = sizeof(ex);
+  ex.device = device;
+  int dev;
+  mcb_status s = resolve_device(&ex, &dev);
+  if (s) return s;
+  DeviceGuard g(dev);
+  DeviceCtx *c;
+  if ((s = init_ctx(dev, &c))) return s;
+  // X 128x64, W 64x256 and Y 128x256 bf16 in one allocation (never read or
+  // written by the stalled kernel, but its tensor maps must be valid).
+  void *buf = nullptr;
+  const size_t xb = 128 * 64 * 2, wb = 64 * 256 * 2, yb = 128 * 256 * 2;
+  if (cudaMalloc(&buf, xb + wb + yb) != cudaSuccess) {
+    cudaGetLastError();
+    return MCB_STATUS_ALLOCATION_FAILURE;
+  }
+  uint8_t *base = static_cast<uint8_t *>(buf);
+  cudaError_t err = mcb::launch_gemm_tc_stall_selftest(base, base + xb, base + xb + wb,
+                                                       static_cast<long long>(spin_limit_cycles),
+                                                       c->status, nullptr);
+  if (err == cudaSuccess) err = cudaDeviceSynchronize();
+  cudaFree(buf);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+  uint32_t word = 0;
+  if (cudaMemcpy(&word, c->status, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  // The stalled wait must have been reported; the word stays set (sticky)
+  // until the caller clears it with mcb_device_status.
+  constexpr uint32_t kTimeoutFullBit = 1u;  // kErrTimeoutFull of the device status word
+  return (word & kTimeoutFullBit) ? MCB_STATUS_DEVICE_TIMEOUT : MCB_STATUS_CANDIDATE_FAILURE;
 }
 
 MCB_API mcb_status mcb_candidate_available(int32_t device) noexcept {

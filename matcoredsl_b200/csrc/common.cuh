@@ -58,10 +58,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity. Returns false (after recording
-// `err_bit` and raising *abort) if it does not complete in time or if another
-// role of this CTA already aborted.
+// `err_bit` and raising *abort) if it does not complete within `limit`
+// clock64 cycles or if another role of this CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
-                                          uint32_t *status, uint32_t err_bit) {
+                                          uint32_t *status, uint32_t err_bit,
+                                          long long limit = kSpinTimeoutCycles) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const long long t0 = clock64();
@@ -69,7 +70,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     if (mbar_try_wait(addr, parity)) return true;
     if ((i & 255u) == 0) {
       if (*abort) return false;
-      if (clock64() - t0 > kSpinTimeoutCycles) {
+      if (clock64() - t0 > limit) {
         if (status) atomicOr(status, err_bit);
         *abort = 1;
         return false;
@@ -82,8 +83,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
 // the warp-collective tcgen05 instructions that follow run with all 32 lanes
 // or with none (a lane that timed out never leaves the others stranded).
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort,
-                                               uint32_t *status, uint32_t err_bit) {
-  const bool ok = mbar_wait(bar, parity, abort, status, err_bit);
+                                               uint32_t *status, uint32_t err_bit,
+                                               long long limit = kSpinTimeoutCycles) {
+  const bool ok = mbar_wait(bar, parity, abort, status, err_bit, limit);
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
@@ -124,6 +126,10 @@ __device__ __forceinline__ uint64_t make_sdesc_sw128(uint32_t smem_addr, uint32_
   d |= 2ull << 61;
   return d;
 }
+
+// Instruction-descriptor bit that negates the A operand's products
+// (kind::f16 / kind::tf32 / kind::f8f6f4).
+constexpr uint32_t kIdescNegateA = 1u << 13;
 
 // Instruction descriptor for kind::f16 / kind::f8f6f4 with an f32 accumulator.
 //   a_fmt/b_fmt: kind::f16 -> 0 f16, 1 bf16; kind::f8f6f4 -> 0 e4m3, 1 e5m2.

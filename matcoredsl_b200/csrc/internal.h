@@ -39,11 +39,20 @@ cudaError_t launch_strict_pair(const float *a, const float *b, const float *d, f
 
 // The fused pair with its intermediate panel in a fixed scratch array of
 // `scratch_floats` floats (used by the allocation-free entry point).
+// *panel_too_large is set (and nothing launched) when one panel row of N
+// floats does not fit the array.
 cudaError_t launch_strict_pair_fixed_scratch(const float *a, const float *b, const float *d,
                                              float *e, float *scratch, int64_t scratch_floats,
                                              int64_t m, int64_t k, int64_t n, int64_t p,
                                              int64_t lda, int64_t ldb, int64_t ldd, int64_t lde,
-                                             int sms, cudaStream_t stream, LaunchInfo *info);
+                                             int sms, cudaStream_t stream, LaunchInfo *info,
+                                             bool *panel_too_large);
+
+// Self-test of the bounded pipeline waits (mcb_device_timeout_selftest_v1):
+// one single-SM GEMM tile whose producer issues no loads.
+cudaError_t launch_gemm_tc_stall_selftest(const void *x, const void *w, void *y,
+                                          long long spin_limit, uint32_t *status,
+                                          cudaStream_t stream);
 
 // ---- epilogue description shared by the GEMM kernels ----------------------------
 constexpr int kMaxEpiOps = 8, kMaxEpiBoundaries = 4;
