@@ -96,6 +96,10 @@ extern "C" MCB_API mcb_status mcb_strict_fused_pair_f32_noalloc_v1(
     return (e && a && b && d) ? MCB_STATUS_UNSUPPORTED_DTYPE : MCB_STATUS_INVALID_ARGUMENT;
   if (exec && (exec->abi_version != MCB_ABI_VERSION_V1 || exec->struct_size < sizeof(mcb_exec)))
     return MCB_STATUS_ABI_MISMATCH;
+  if (exec && exec->report &&
+      (exec->report->abi_version != MCB_ABI_VERSION_V1 ||
+       exec->report->struct_size < sizeof(mcb_report)))
+    return MCB_STATUS_ABI_MISMATCH;
   // Timing needs CUDA events, which this entry point does not create.
   if (exec && (exec->flags & MCB_EXEC_TIME)) return MCB_STATUS_INVALID_ARGUMENT;
   for (const mcb_tensor *t : {e, a, b, d}) {
@@ -135,15 +139,19 @@ extern "C" MCB_API mcb_status mcb_strict_fused_pair_f32_noalloc_v1(
 
   cudaStream_t stream = exec ? static_cast<cudaStream_t>(exec->stream) : nullptr;
   mcb::LaunchInfo info;
+  bool panel_too_large = false;
+  // An error left unread by the caller's earlier runtime calls must not be
+  // reported as this call's launch failure.
+  cudaGetLastError();
   cudaError_t err = mcb::launch_strict_pair_fixed_scratch(
       static_cast<const float *>(a->data), static_cast<const float *>(b->data),
       static_cast<const float *>(d->data), static_cast<float *>(e->data), s.scratch,
       kStaticScratchFloats, m, k, n, p, k ? a->strides[0] : 0, n ? b->strides[0] : 0,
-      p ? d->strides[0] : 0, e->strides[0], s.sms, stream, &info);
+      p ? d->strides[0] : 0, e->strides[0], s.sms, stream, &info, &panel_too_large);
+  if (panel_too_large) return MCB_STATUS_INSUFFICIENT_WORKSPACE;
   if (err == cudaSuccess && exec && (exec->flags & MCB_EXEC_SYNC))
     err = cudaStreamSynchronize(stream);
-  if (exec && exec->report && exec->report->abi_version == MCB_ABI_VERSION_V1 &&
-      exec->report->struct_size >= sizeof(mcb_report)) {
+  if (exec && exec->report) {
     mcb_report *r = exec->report;
     for (size_t i = 0; i < sizeof(r->route); ++i) r->route[i] = info.route[i];
     r->kernel_launches = info.launches;
@@ -156,6 +164,5 @@ extern "C" MCB_API mcb_status mcb_strict_fused_pair_f32_noalloc_v1(
     r->h2d_bytes = r->d2h_bytes = 0;
     r->device_status = 0;
   }
-  if (err == cudaErrorInvalidValue) return MCB_STATUS_INSUFFICIENT_WORKSPACE;
   return err == cudaSuccess ? MCB_STATUS_OK : MCB_STATUS_CANDIDATE_FAILURE;
 }

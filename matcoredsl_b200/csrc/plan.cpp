@@ -111,13 +111,15 @@ uint64_t workspace_for(const mcb_plan_desc &d) {
     return static_cast<uint64_t>(a.dims[0]) * ((b.dims[1] + 7) / 8 * 8) * esz;
   }
   if (d.op == MCB_PLAN_GEMM_I8) {
-    // B^T when B's rows are not 16-byte aligned, then the zero-point row and
-    // column sums (the int8 entry point's scratch layout).
+    // B^T, then the zero-point row and column sums (the int8 entry point's
+    // scratch layout). The entry point transposes B when its row stride or
+    // its base pointer is not 16-byte aligned; the base pointer of a later
+    // execute is not known at create time, so B^T is always reserved.
     const mcb_tensor &a = d.tensors[1], &b = d.tensors[2];
     auto up16 = [](uint64_t x) { return (x + 15) & ~uint64_t{15}; };
     const uint64_t m = static_cast<uint64_t>(a.dims[0]), k = static_cast<uint64_t>(a.dims[1]);
     const uint64_t n = static_cast<uint64_t>(b.dims[1]);
-    uint64_t bytes = b.strides[0] % 16 != 0 ? up16(n * k) : 0;
+    uint64_t bytes = up16(n * k);
     if (d.b_zero_point != 0) bytes += up16(m * 4);
     if (d.a_zero_point != 0) bytes += up16(n * 4);
     return bytes;

@@ -726,8 +726,10 @@ cudaError_t launch_strict_pair_fixed_scratch(const float *a, const float *b, con
                                              float *e, float *scratch, int64_t scratch_floats,
                                              int64_t m, int64_t k, int64_t n, int64_t p,
                                              int64_t lda, int64_t ldb, int64_t ldd, int64_t lde,
-                                             int sms, cudaStream_t stream, LaunchInfo *info) {
+                                             int sms, cudaStream_t stream, LaunchInfo *info,
+                                             bool *panel_too_large) {
   if (info) info->launches = 0;
+  *panel_too_large = false;
   if (m == 0 || p == 0) return cudaSuccess;
   if (n == 0) {  // empty consumer reduction: E = +0, no panel
     fill_zero_kernel<<<sms, 256, 0, stream>>>(e, m, p, lde);
@@ -739,7 +741,10 @@ cudaError_t launch_strict_pair_fixed_scratch(const float *a, const float *b, con
   }
   int R = pick_rows(m, sms);
   while (R > 1 && static_cast<int64_t>(R) * n > scratch_floats) R /= 2;
-  if (static_cast<int64_t>(R) * n > scratch_floats) return cudaErrorInvalidValue;
+  if (static_cast<int64_t>(R) * n > scratch_floats) {
+    *panel_too_large = true;  // nothing launched
+    return cudaErrorInvalidValue;
+  }
   const int64_t rows_per_launch = (scratch_floats / (static_cast<int64_t>(R) * n)) * R;
   const int threads = (n >= 256 || p >= 256) ? 256 : 128;
   int launches = 0;

@@ -109,3 +109,31 @@ def test_noalloc_rejects_host_operands(mcb):
     ex = _abi.make_exec()
     code = lib.mcb_strict_fused_pair_f32_noalloc_v1(*[ctypes.byref(z) for z in t], ctypes.byref(ex))
     assert code == _abi.STATUS_CODE["UNSUPPORTED_MEMORY_SPACE"]
+
+
+def test_noalloc_allocates_nothing(mcb):
+    """The property the entry point exists for: after a first call has done
+    the per-device set-up, repeated calls (config 1 and the multi-launch
+    shape) change neither the device's free memory nor torch's allocator
+    statistics."""
+    import torch
+    cases = []
+    for shape in [(512, 256, 384, 128), (3000, 17, 4096, 9)]:
+        m, k, n, p = shape
+        a, b, d = _inputs(m, k, n, p, seed=5 + sum(shape))
+        cases.append((torch.empty(m, p, device="cuda"), a, b, d))
+    for out, a, b, d in cases:  # first call: set-up (symbol address lookup)
+        assert _call("mcb_strict_fused_pair_f32_noalloc_v1", out, a, b, d)[0] == 0
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    stats0 = torch.cuda.memory_stats()
+    for _ in range(3):
+        for out, a, b, d in cases:
+            assert _call("mcb_strict_fused_pair_f32_noalloc_v1", out, a, b, d, sync=False)[0] == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    stats1 = torch.cuda.memory_stats()
+    assert free1 == free0
+    for key in ("allocation.all.allocated", "reserved_bytes.all.current",
+                "allocated_bytes.all.current"):
+        assert stats1.get(key, 0) == stats0.get(key, 0), key
