@@ -9,9 +9,12 @@ b [4096] bf16, Y bf16, f32 accumulation -- one call of the Family A operator
                   [--scaling weak|strong]
 
 Multi-GPU (torchrun, one process per GPU): the M rows are sharded with no
-collective on the data path. Default "weak": every rank owns 8192 rows of a
-global X of 8192*N rows (per-GPU work fixed); "strong": the 8192 rows are
-split N ways. value = FLOPs of all ranks / max-over-ranks device time.
+collective on the data path. Default "strong" ("on 8
+GPUs, M is sharded 1024 rows per GPU"): the 8192 rows are split N ways;
+"weak": every rank owns 8192 rows of a global X of 8192*N rows (per-GPU
+work fixed). value = FLOPs of all ranks / max-over-ranks device time. The
+side measurements of configs 1, 3, 4 and 5 (`other_configs`) are sharded the
+same way at N > 1.
 
 `--impl reference` times the reference's CPU arithmetic for the same workload
 (the oracle restatement, since the reference itself cannot be built here) on
@@ -71,7 +74,7 @@ class ClockSampler:
         "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.01):
+    def __init__(self, device_index: int, period_s: float = 0.001):
         self.samples, self.reasons = [], set()
         self.max_mhz = None
         self._stop = threading.Event()
@@ -200,16 +203,28 @@ def _time_steps(fn, steps, stream, flush=None):
     return statistics.mean(s.elapsed_time(e) for s, e in evs)
 
 
-def run_other_configs(dev, steps: int = 10):
-    """Configs 1, 3, 4 and 5 on this GPU (device-resident inputs, one call of
-    the public operator per step). Config 1 flushes L2 between steps; the
-    others' working sets exceed L2."""
+def run_other_configs(dev, world: int = 1, rank: int = 0, steps: int = 10):
+    """Configs 1, 3, 4 and 5 through their entry points (device-resident
+    inputs, one call of the public operator per step). Config 1 flushes L2
+    between steps; the others' working sets exceed L2.
+
+    With N > 1 ranks the sharded configs split their fixed global work
+    (strong scaling, mcb_shard_plan_v1, no collective on the data path):
+    config 3 by (batch, head) units, config 4 by rows of A, config 5 by
+    batch elements (when N divides the batch of 4). Config 1 runs as one
+    replica per GPU. Each figure is all ranks' FLOPs / the max-over-ranks
+    device time per step."""
     import torch
     import matcoredsl_b200 as mcb
     peaks = _peaks()
     stream = torch.cuda.current_stream(dev)
     g = torch.Generator(device=dev)
     out = {}
+
+    def timed(fn, n_steps, flush=None):
+        _barrier(world)
+        ms = _time_steps(fn, n_steps, stream, flush=flush)
+        return _max_over_ranks(ms, world, dev)
 
     # config 1: strict fused pair, 512x256 . 256x384 . 384x128, U(-1,1) seeds 0/1/2
     a, b, d = (torch.from_numpy(np.random.default_rng(s).uniform(-1, 1, sh).astype(np.float32))
@@ -218,75 +233,92 @@ def run_other_configs(dev, steps: int = 10):
     flush_buf = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=dev)
     for _ in range(3):
         mcb.strict_fused_pair(a, b, d, out=e)
-    ms = _time_steps(lambda: mcb.strict_fused_pair(a, b, d, out=e), 50, stream,
-                     flush=lambda: flush_buf.fill_(1))
+    ms = timed(lambda: mcb.strict_fused_pair(a, b, d, out=e), 50,
+               flush=lambda: flush_buf.fill_(1))
     fl = 2.0 * 512 * 256 * 384 + 2.0 * 512 * 384 * 128
-    out["config1_strict_pair"] = {"ms": ms, "gflops": fl / ms / 1e6,
+    out["config1_strict_pair"] = {"ms": ms, "gflops_per_gpu": fl / ms / 1e6,
                                   "route": mcb.api.last_result.route,
+                                  "parallelism": "replicas" if world > 1 else "single GPU",
                                   "note": "latency-bound; L2 flushed between steps"}
     del a, b, d, e, flush_buf
 
-    # config 3: MSM [8,32,4096,128] bf16, scale 128^-0.5, seed 20
+    # config 3: MSM [8,32,4096,128] bf16, scale 128^-0.5, seed 20; (b,h) units sharded
+    u0, nu, _, _ = mcb.shard_plan("units", 8 * 32, world, rank)
     g.manual_seed(20)
-    q, k, v = (torch.randn(8, 32, 4096, 128, generator=g, device=dev).to(torch.bfloat16)
-               for _ in range(3))
+    q, k, v = (torch.randn(8 * 32, 4096, 128, generator=g, device=dev)[u0:u0 + nu]
+               .to(torch.bfloat16).unsqueeze(0) for _ in range(3))
+    torch.cuda.empty_cache()
     o = torch.empty_like(q)
     for _ in range(2):
         mcb.msm(q, k, v, 128 ** -0.5, out=o)
-    ms = _time_steps(lambda: mcb.msm(q, k, v, 128 ** -0.5, out=o), steps, stream)
+    ms = timed(lambda: mcb.msm(q, k, v, 128 ** -0.5, out=o), steps)
     fl = 4.0 * 8 * 32 * 4096 * 4096 * 128
     out["config3_msm"] = {"ms": ms, "tflops": fl / ms / 1e9,
-                          "frac_of_bf16_peak": fl / ms / 1e9 / peaks["bf16_tflops"],
-                          "route": mcb.api.last_result.route}
+                          "tflops_per_gpu": fl / ms / 1e9 / world,
+                          "frac_of_bf16_peak": fl / ms / 1e9 / world / peaks["bf16_tflops"],
+                          "units_per_gpu": nu, "route": mcb.api.last_result.route}
     del q, k, v, o
 
-    # config 4: FP8 block-scaled 16384^3, e4m3, seed 30, bf16 out
-    g.manual_seed(30)
+    # config 4: FP8 block-scaled 16384^3, e4m3, seed 30, bf16 out; rows of A sharded
     n = 16384
+    r0, nr, _, _ = mcb.shard_plan("rows", n, world, rank, align=128)
+    g.manual_seed(30)
     x = torch.randn(n, n, generator=g, device=dev)
-    qa, sa = mcb.fp8_quantize_blockwise(x, 128, "e4m3")
+    qa, sa = mcb.fp8_quantize_blockwise(x[r0:r0 + nr], 128, "e4m3")
     x.normal_(generator=g)
     qb, sb = mcb.fp8_quantize_blockwise(x, 128, "e4m3")
     del x
-    c = torch.empty(n, n, dtype=torch.bfloat16, device=dev)
+    torch.cuda.empty_cache()
+    c = torch.empty(nr, n, dtype=torch.bfloat16, device=dev)
     for _ in range(2):
         mcb.gemm_fp8_blockscaled(qa, sa, qb, sb, out=c)
-    ms = _time_steps(lambda: mcb.gemm_fp8_blockscaled(qa, sa, qb, sb, out=c), steps, stream)
+    ms = timed(lambda: mcb.gemm_fp8_blockscaled(qa, sa, qb, sb, out=c), steps)
     fl = 2.0 * n ** 3
     route = mcb.api.last_result.route
     # Denominator: cuBLAS's fp8 GEMM on the same codes with one per-tensor
-    # scale (no block-scale promotion at all), timed here. torch offers no
-    # 128x128 block-scaled fp8 GEMM on sm_100, so this is the closest
-    # library figure; MEASURED_PEAKS.json has no fp8 entry.
+    # scale (no block-scale promotion at all), timed here on this rank's
+    # shape. torch offers no 128x128 block-scaled fp8 GEMM on sm_100, so this
+    # is the closest library figure; MEASURED_PEAKS.json has no fp8 entry.
     one = torch.ones((), dtype=torch.float32, device=dev)
-    lib = lambda: torch._scaled_mm(qa, qb.t(), one, one, out_dtype=torch.bfloat16)
+    lib = lambda: torch._scaled_mm(qa, qb.t(), one, one, out_dtype=torch.bfloat16)  # noqa
     lib()
-    ms_lib = _time_steps(lib, max(3, steps // 4), stream)
-    fp8_peak = fl / ms_lib / 1e9
+    ms_lib = timed(lib, max(3, steps // 4))
+    fp8_peak = fl / ms_lib / 1e9 / world
     out["config4_fp8_gemm"] = {"ms": ms, "tflops": fl / ms / 1e9,
-                               "frac_of_fp8_peak": fl / ms / 1e9 / fp8_peak,
+                               "tflops_per_gpu": fl / ms / 1e9 / world,
+                               "frac_of_fp8_peak": fl / ms / 1e9 / world / fp8_peak,
                                "fp8_peak": fp8_peak,
                                "fp8_peak_source": "cuBLAS fp8 GEMM (torch._scaled_mm, per-tensor "
-                                                  "scales) on the same 16384^3 e4m3 codes, timed "
-                                                  "in this run",
-                               "route": route}
+                                                  "scales) on the same e4m3 codes and per-GPU "
+                                                  "shape, timed in this run",
+                               "rows_per_gpu": nr, "route": route}
     del qa, sa, qb, sb, c
 
-    # config 5: attention-residual block, B4 S2048 D4096 H32, seed 40
-    g.manual_seed(40)
-    xb = torch.randn(4, 2048, 4096, generator=g, device=dev).to(torch.bfloat16)
-    ws = [(torch.randn(4096, 4096, generator=g, device=dev) / 64).to(torch.bfloat16)
-          for _ in range(4)]
-    yb = torch.empty_like(xb)
-    for _ in range(2):
-        mcb.attn_block(xb, *ws, 32, 1e-6, out=yb)
-    ms = _time_steps(lambda: mcb.attn_block(xb, *ws, 32, 1e-6, out=yb), steps, stream)
-    fl = 4.0 * 2 * 8192 * 4096 * 4096 + 4.0 * 4 * 32 * 2048 * 2048 * 128
-    out["config5_attn_block"] = {"ms": ms, "tflops": fl / ms / 1e9,
-                                 "frac_of_bf16_peak": fl / ms / 1e9 / peaks["bf16_tflops"],
-                                 "launches_per_step": mcb.api.last_result.kernel_launches,
-                                 "route": mcb.api.last_result.route}
-    del xb, ws, yb
+    # config 5: attention-residual block, B4 S2048 D4096 H32, seed 40; batch sharded
+    if 4 % world == 0:
+        nb = 4 // world
+        g.manual_seed(40)
+        xb = torch.randn(4, 2048, 4096, generator=g, device=dev)[rank * nb:(rank + 1) * nb] \
+            .to(torch.bfloat16)
+        ws = [(torch.randn(4096, 4096, generator=g, device=dev) / 64).to(torch.bfloat16)
+              for _ in range(4)]
+        torch.cuda.empty_cache()
+        yb = torch.empty_like(xb)
+        for _ in range(2):
+            mcb.attn_block(xb, *ws, 32, 1e-6, out=yb)
+        ms = timed(lambda: mcb.attn_block(xb, *ws, 32, 1e-6, out=yb), steps)
+        fl = 4.0 * 2 * 8192 * 4096 * 4096 + 4.0 * 4 * 32 * 2048 * 2048 * 128
+        out["config5_attn_block"] = {"ms": ms, "tflops": fl / ms / 1e9,
+                                     "tflops_per_gpu": fl / ms / 1e9 / world,
+                                     "frac_of_bf16_peak": fl / ms / 1e9 / world
+                                     / peaks["bf16_tflops"],
+                                     "batch_per_gpu": nb,
+                                     "launches_per_step": mcb.api.last_result.kernel_launches,
+                                     "route": mcb.api.last_result.route}
+        del xb, ws, yb
+    else:
+        out["config5_attn_block"] = {"skipped": f"batch 4 does not split over {world} GPUs "
+                                                "(token sharding is not measured here)"}
     torch.cuda.empty_cache()
     return out
 
@@ -497,12 +529,14 @@ def run_ours(args):
     if not args.no_e2e:
         e2e = _run_e2e(args, lib, ep, sets, descs, dev, stream, world, flops_step, m)
     others = None
-    if world == 1 and not args.no_other_configs:
+    if not args.no_other_configs:
         del sets, dsets, calls
         torch.cuda.empty_cache()
         try:  # side measurements never cost the headline line
-            others = run_other_configs(dev)
+            others = run_other_configs(dev, world, rank)
         except Exception as exc:  # noqa: BLE001
+            # a rank that fails here would leave the others in a collective:
+            # every rank takes the same steps, so all fail alike on a shape error
             others = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, working_set, route,
             clk, e2e, others, kernel)
@@ -595,7 +629,7 @@ def main():
     ap.add_argument("--steps", type=int, default=500)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="strong")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the host-buffer end-to-end leg (used for short profiling runs)")
