@@ -16,7 +16,7 @@
  *     cases of compiler/tests/generated_cpu_fused_pair/execution_test.cpp:100-135.
  *   - bf16 conversion, bf16 GEMM, int8 GEMM: pinned bit-for-bit against the
  *     reference's own compiler/lib/runtime/cpu_numeric_reference.cpp, compiled
- *     from its source into oracle/_ref by oracle/build_ref.sh.
+ *     from its source into oracle/_ref by the `ref` target of oracle/Makefile.
  *   - GELU-tanh epilogue and matmul-softmax-matmul: pinned against golden
  *     vectors produced by the reference's own numpy test oracles
  *     (tests/test_family_a.py:63, tests/test_family_c.py:27-37) via

@@ -1,6 +1,7 @@
 """Generate golden fixtures for Families A, B and C from the reference's own tests.
 
-Run in a container that has the MatcoreDSL sources (default /root/reference):
+Run in a container that has the MatcoreDSL sources (--ref, MCB_REFERENCE_DIR, or a
+`reference` directory beside this repository):
 
     python tests/golden/make_golden.py [--ref /path/to/MatcoreDSL]
 
@@ -93,7 +94,10 @@ def _eval_graph(graph, arrays):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    here = os.path.dirname(os.path.abspath(__file__))
+    ap.add_argument("--ref", default=os.environ.get(
+        "MCB_REFERENCE_DIR", os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(here))),
+                                          "reference")))
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     sys.path.insert(0, os.path.join(args.ref, "tests"))
