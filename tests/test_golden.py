@@ -1,9 +1,13 @@
-"""Golden fixtures produced by the reference's own Family A/B/C tests
-(tests/golden/make_golden.py): every stored output was accepted by the
-reference's assertion (max-abs 1e-3 / 1e-2 / 2e-3).
+"""Golden fixtures produced by the reference's own Family A/B/C and
+block_attn_res tests (tests/golden/make_golden.py): every stored output was
+accepted by the reference's assertion (max-abs 1e-3 / 1e-2 / 2e-3 / 1e-4),
+and beside it is the reference test's own numpy expectation (`expected`).
 
-CPU: the oracle reproduces every stored output.
-GPU: the CUDA path reproduces them within the reference's own tolerances.
+CPU: the oracle reproduces every stored output, and it equals the reference's
+own expectation to within 1e-6 relative to the largest value (100x tighter
+than the reference's tolerances; in practice one f32 ulp).
+GPU: the CUDA path reproduces the reference's expectation within the
+reference's own tolerances.
 """
 import json
 import os
@@ -15,15 +19,35 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 TOL = {"a": 1e-3, "b": 1e-2, "c": 2e-3}  # tests/test_family_{a,b,c}.py
 
 
-def _cases(family):
-    path = os.path.join(HERE, "golden", f"family_{family}.npz")
-    z = np.load(path)
+def _load(name, with_expected=False):
+    z = np.load(os.path.join(HERE, "golden", f"{name}.npz"))
     index = json.loads(bytes(z["index"]).decode())
     out = []
     for i, meta in enumerate(index):
         ins = [z[f"c{i}_in{j}"] for j in range(meta["inputs"])]
-        out.append((meta, ins, z[f"c{i}_out"]))
+        if with_expected:
+            out.append((meta, ins, z[f"c{i}_out"], z[f"c{i}_expected"]))
+        else:
+            out.append((meta, ins, z[f"c{i}_out"]))
     return out
+
+
+def _cases(family):
+    return _load(f"family_{family}")
+
+
+ALL_WITH_EXPECTED = [(f, c) for f in ("family_a", "family_b", "family_c", "block_attn_res")
+                     for c in _load(f, with_expected=True)]
+
+
+@pytest.mark.parametrize("fam_case", ALL_WITH_EXPECTED, ids=lambda fc: fc[1][0]["name"])
+def test_oracle_equals_reference_expectation(fam_case):
+    """The stored oracle output against the reference test's own numpy
+    expectation for the same inputs: within 1e-6 of the largest |value|."""
+    _, (meta, _ins, out, expected) = fam_case
+    assert out.shape == expected.shape
+    scale = max(1.0, float(np.max(np.abs(expected))))
+    assert np.max(np.abs(out.astype(np.float64) - expected.astype(np.float64))) <= 1e-6 * scale
 
 
 def _a_args(meta, ins):
@@ -64,9 +88,9 @@ def _qkv(meta, ins):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("case", _cases("a"), ids=lambda c: c[0]["name"])
+@pytest.mark.parametrize("case", _load("family_a", True), ids=lambda c: c[0]["name"])
 def test_cuda_family_a_matches_golden(mcb, case):
-    meta, ins, expected = case
+    meta, ins, _, expected = case
     x, w, bias = _a_args(meta, ins)
     got = mcb.gemm_epilogue(x, w, bias, bias_mode=meta["bias_mode"], bias_op=meta["bias_op"],
                             act=meta["act"])
@@ -91,9 +115,9 @@ def test_oracle_reproduces_family_b(orc, case):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("case", _cases("b"), ids=lambda c: c[0]["name"])
+@pytest.mark.parametrize("case", _load("family_b", True), ids=lambda c: c[0]["name"])
 def test_cuda_family_b_matches_golden(mcb, case):
-    meta, ins, expected = case
+    meta, ins, _, expected = case
     a, b, bnd, w = _b_args(meta, ins)
     got = mcb.gemm_chain(a, b, w, bnd, bias_mode=meta["bias_mode"], bias_op=meta["bias_op"],
                          act=meta["act"])
@@ -102,9 +126,9 @@ def test_cuda_family_b_matches_golden(mcb, case):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("case", _cases("c"), ids=lambda c: c[0]["name"])
+@pytest.mark.parametrize("case", _load("family_c", True), ids=lambda c: c[0]["name"])
 def test_cuda_family_c_matches_golden(mcb, case):
-    meta, ins, expected = case
+    meta, ins, _, expected = case
     q, k, v = _qkv(meta, ins)
     got = mcb.msm(q, k, v, 1.0)
     assert np.max(np.abs(got - expected)) < TOL["c"]
