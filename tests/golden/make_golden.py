@@ -177,6 +177,21 @@ def main():
             assert current["name"] in expectations, f"no expectation seen in {module}.{t}"
             print(f"accepted by the reference test: {module}.{t}")
 
+    # A tensor-core-sized Family C case: the reference test module's own
+    # numpy expectation (_attention_ref, tests/test_family_c.py:33-36) on
+    # bf16-representable inputs of one 256-row query block, 256 keys and head
+    # dim 128 with the 128^-0.5 scale (the stored inputs are bf16 bit patterns).
+    fc = importlib.import_module("test_family_c")
+    rng = np.random.default_rng(20261202)
+    qkv_bits = [oracle.bf16_from_f32(rng.standard_normal((256, 128)).astype(np.float32))
+                for _ in range(3)]
+    q, k, v = (oracle.bf16_to_f32(b) for b in qkv_bits)
+    tc_expected = np.asarray(fc._attention_ref(q, k, v, score_scale=128 ** -0.5), np.float32)
+    np.savez_compressed(os.path.join(HERE, "family_c_tc.npz"), q_bf16=qkv_bits[0],
+                        k_bf16=qkv_bits[1], v_bf16=qkv_bits[2], scale=np.float64(128 ** -0.5),
+                        expected=tc_expected)
+    print("family_c_tc.npz: 1 case (256x256x128, reference _attention_ref)")
+
     for family, recs in records.items():
         payload, index = {}, []
         for i, (name, arrays, result, meta) in enumerate(recs):

@@ -132,3 +132,32 @@ def test_cuda_family_c_matches_golden(mcb, case):
     q, k, v = _qkv(meta, ins)
     got = mcb.msm(q, k, v, 1.0)
     assert np.max(np.abs(got - expected)) < TOL["c"]
+
+
+def _tc_case():
+    z = np.load(os.path.join(HERE, "golden", "family_c_tc.npz"))
+    return z["q_bf16"], z["k_bf16"], z["v_bf16"], float(z["scale"]), z["expected"]
+
+
+def test_oracle_equals_reference_expectation_tensor_core_size(orc):
+    """256x256x128 with the 128^-0.5 scale: the oracle against the reference
+    test module's own _attention_ref on the same bf16-representable inputs."""
+    qb, kb, vb, scale, expected = _tc_case()
+    q, k, v = (orc.bf16_to_f32(b) for b in (qb, kb, vb))
+    got = orc.msm(q, k, v, scale)
+    assert np.max(np.abs(got - expected)) <= 1e-6
+
+
+@pytest.mark.gpu
+def test_cuda_tcgen05_msm_matches_reference_expectation(mcb, orc):
+    """The tcgen05 MSM kernel (bf16 output) against the reference's numpy
+    expectation: relative Frobenius error <= 1e-2 (the north-star bf16 bar)
+    and the reference Family C max-abs tolerance scaled for a bf16 output."""
+    from tests import gpu_util as gu
+    qb, kb, vb, scale, expected = _tc_case()
+    dev = [gu.to_dev_bf16(b.reshape(1, 1, 256, 128)) for b in (qb, kb, vb)]
+    o = mcb.msm(*dev, scale)
+    assert mcb.api.last_result.route == "tcgen05_bf16_msm"
+    got = gu.from_dev(o)[0, 0]
+    assert orc.rel_frobenius(got, expected) < 1e-2
+    assert np.max(np.abs(got - expected)) < 1e-2
