@@ -505,6 +505,54 @@ MCB_API mcb_status mcb_device_zero(mcb_buffer handle) MCB_NOEXCEPT;
 MCB_API mcb_status mcb_device_zero_raw_on_stream(void *device_ptr, uint64_t size_bytes,
                                                  void *stream) MCB_NOEXCEPT;
 
+/* ---- test support: host-side fault injection ------------------------------
+ * The counterpart of the reference's fake-driver adapter test
+ * (compiler/tests/generated_gpu/cuda_adapter_test.cpp): a table of stand-ins
+ * for the CUDA runtime calls of the host path (device discovery, staging
+ * allocations, host<->device copies, synchronisation) and for kernel
+ * launches, so that a test can fail any one of them, on a machine without a
+ * GPU. Each stand-in returns 0 for success or a CUDA runtime error code
+ * (e.g. 2 = out of memory, 999 = unknown). While a table is installed:
+ *  - kernels are not launched: `launch` stands in for each launch, and the
+ *    "device" pointers the library hands it are whatever `malloc_device`
+ *    returned;
+ *  - only the strict GEMM and strict fused pair entry points and the device
+ *    status / availability queries run; every other entry point returns
+ *    MCB_STATUS_CANDIDATE_UNAVAILABLE;
+ *  - MCB_EXEC_TIME is ignored (no events are created).
+ * Installing is refused (MCB_STATUS_INVALID_ARGUMENT) once the process has
+ * created a real device context; NULL removes the table and forgets the
+ * device state created under it. Install and remove from one thread, with
+ * no other call in flight. Not for production use. */
+typedef struct mcb_hook_launch {
+  const char *op;     /* "strict_gemm" or "strict_fused_pair" */
+  const void *in[3];  /* A, B and (pair) D */
+  void *out;          /* C, or the pair's E */
+  void *scratch;      /* the pair's intermediate C when it is in device memory, else NULL */
+  int64_t m, k, n, p; /* C = A[m,k] B[k,n]; E = C D[n,p] */
+  int64_t ld[4];      /* row strides (elements) of A, B, D and the output */
+} mcb_hook_launch;
+typedef struct mcb_runtime_hooks {
+  uint32_t abi_version; /* MCB_ABI_VERSION_V1 */
+  uint32_t struct_size; /* sizeof(mcb_runtime_hooks) */
+  int32_t (*get_device_count)(int32_t *count);
+  int32_t (*get_device)(int32_t *device);
+  int32_t (*set_device)(int32_t device);
+  int32_t (*device_info)(int32_t device, int32_t *cc_major, int32_t *cc_minor, int32_t *sms,
+                         int32_t *smem_optin_bytes);
+  int32_t (*malloc_device)(void **ptr, uint64_t bytes);
+  int32_t (*free_device)(void *ptr);
+  int32_t (*memset_device)(void *ptr, int32_t value, uint64_t bytes);
+  /* kind: 1 host->device, 2 device->host, 3 device->device */
+  int32_t (*memcpy_async)(void *dst, const void *src, uint64_t bytes, int32_t kind, void *stream);
+  int32_t (*memcpy2d_async)(void *dst, uint64_t dst_pitch, const void *src, uint64_t src_pitch,
+                            uint64_t width_bytes, uint64_t rows, int32_t kind, void *stream);
+  int32_t (*memcpy_sync)(void *dst, const void *src, uint64_t bytes, int32_t kind);
+  int32_t (*stream_synchronize)(void *stream);
+  int32_t (*launch)(const mcb_hook_launch *launch);
+} mcb_runtime_hooks;
+MCB_API mcb_status mcb_test_set_runtime_hooks_v1(const mcb_runtime_hooks *hooks) MCB_NOEXCEPT;
+
 #if defined(__cplusplus)
 }
 #endif

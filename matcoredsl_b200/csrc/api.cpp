@@ -123,17 +123,90 @@ struct DeviceCtx {
 constexpr uint64_t kPoolKeepBytes = 4ull << 30;
 DeviceCtx g_dev[kMaxDevices];
 
+// ---- host runtime calls behind a replaceable table (fault injection) ------------
+// mcb_test_set_runtime_hooks_v1 installs stand-ins for the CUDA runtime calls
+// of the host path and for kernel launches, so that tests can fail any one of
+// them on a machine without a GPU. With no table installed every rt_* helper
+// is the CUDA runtime call itself.
+mcb_runtime_hooks g_hook_table;
+std::atomic<bool> g_hooks_on{false};
+std::atomic<bool> g_real_context{false};  // a device context was created through CUDA
+const mcb_runtime_hooks *hooks() {
+  return g_hooks_on.load(std::memory_order_acquire) ? &g_hook_table : nullptr;
+}
+
+cudaError_t rt_get_device_count(int *n) {
+  if (const auto *h = hooks()) {
+    int32_t v = 0;
+    const int32_t e = h->get_device_count(&v);
+    *n = v;
+    return static_cast<cudaError_t>(e);
+  }
+  return cudaGetDeviceCount(n);
+}
+cudaError_t rt_get_device(int *d) {
+  if (const auto *h = hooks()) {
+    int32_t v = 0;
+    const int32_t e = h->get_device(&v);
+    *d = v;
+    return static_cast<cudaError_t>(e);
+  }
+  return cudaGetDevice(d);
+}
+cudaError_t rt_set_device(int d) {
+  if (const auto *h = hooks()) return static_cast<cudaError_t>(h->set_device(d));
+  return cudaSetDevice(d);
+}
+cudaError_t rt_malloc(void **p, size_t bytes) {
+  if (const auto *h = hooks()) return static_cast<cudaError_t>(h->malloc_device(p, bytes));
+  return cudaMalloc(p, bytes);
+}
+cudaError_t rt_free(void *p) {
+  if (const auto *h = hooks()) return static_cast<cudaError_t>(h->free_device(p));
+  return cudaFree(p);
+}
+cudaError_t rt_memset(void *p, int v, size_t bytes) {
+  if (const auto *h = hooks()) return static_cast<cudaError_t>(h->memset_device(p, v, bytes));
+  return cudaMemset(p, v, bytes);
+}
+cudaError_t rt_memcpy_async(void *d, const void *s, size_t bytes, cudaMemcpyKind kind,
+                            cudaStream_t st) {
+  if (const auto *h = hooks())
+    return static_cast<cudaError_t>(h->memcpy_async(d, s, bytes, static_cast<int32_t>(kind), st));
+  return cudaMemcpyAsync(d, s, bytes, kind, st);
+}
+cudaError_t rt_memcpy2d_async(void *d, size_t dp, const void *s, size_t sp, size_t w, size_t rows,
+                              cudaMemcpyKind kind, cudaStream_t st) {
+  if (const auto *h = hooks())
+    return static_cast<cudaError_t>(
+        h->memcpy2d_async(d, dp, s, sp, w, rows, static_cast<int32_t>(kind), st));
+  return cudaMemcpy2DAsync(d, dp, s, sp, w, rows, kind, st);
+}
+cudaError_t rt_memcpy(void *d, const void *s, size_t bytes, cudaMemcpyKind kind) {
+  if (const auto *h = hooks())
+    return static_cast<cudaError_t>(h->memcpy_sync(d, s, bytes, static_cast<int32_t>(kind)));
+  return cudaMemcpy(d, s, bytes, kind);
+}
+cudaError_t rt_stream_sync(cudaStream_t st) {
+  if (const auto *h = hooks()) return static_cast<cudaError_t>(h->stream_synchronize(st));
+  return cudaStreamSynchronize(st);
+}
+
 // Restores the caller's current device on scope exit.
 struct DeviceGuard {
   int prev = -1;
   bool switched = false;
+  bool ok = true;  // `dev` is current (false when the switch failed)
   explicit DeviceGuard(int dev) {
-    if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) {
-      switched = cudaSetDevice(dev) == cudaSuccess;
+    if (rt_get_device(&prev) != cudaSuccess) {
+      ok = false;  // the caller's device could not be restored afterwards
+    } else if (prev != dev) {
+      switched = rt_set_device(dev) == cudaSuccess;
+      ok = switched;
     }
   }
   ~DeviceGuard() {
-    if (switched) cudaSetDevice(prev);
+    if (switched) rt_set_device(prev);
   }
 };
 
@@ -142,15 +215,30 @@ mcb_status init_ctx(int dev, DeviceCtx **out) {
   DeviceCtx &c = g_dev[dev];
   std::lock_guard<std::mutex> lock(c.mu);
   if (!c.ready) {
-    cudaDeviceProp prop;
-    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
-    c.usable = prop.major == 10 && prop.minor == 0;
-    c.sms = prop.multiProcessorCount;
-    c.smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+    int major = 0, minor = 0;
+    if (const auto *h = hooks()) {
+      int32_t mj = 0, mn = 0, sms = 0, smem = 0;
+      if (h->device_info(dev, &mj, &mn, &sms, &smem) != 0) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
+      major = mj;
+      minor = mn;
+      c.sms = sms;
+      c.smem_optin = smem;
+    } else {
+      cudaDeviceProp prop;
+      if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
+      major = prop.major;
+      minor = prop.minor;
+      c.sms = prop.multiProcessorCount;
+      c.smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
+    }
+    c.usable = major == 10 && minor == 0 && c.sms > 0;
     if (c.usable) {
       DeviceGuard g(dev);
-      if (cudaMalloc(&c.status, sizeof(uint32_t)) != cudaSuccess) return MCB_STATUS_ALLOCATION_FAILURE;
-      if (cudaMemset(c.status, 0, sizeof(uint32_t)) != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
+      if (!g.ok) return MCB_STATUS_CANDIDATE_FAILURE;
+      if (!hooks()) g_real_context.store(true, std::memory_order_release);
+      if (!c.status && rt_malloc(reinterpret_cast<void **>(&c.status), sizeof(uint32_t)) != cudaSuccess)
+        return MCB_STATUS_ALLOCATION_FAILURE;
+      if (rt_memset(c.status, 0, sizeof(uint32_t)) != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
     }
     c.ready = true;
   }
@@ -161,12 +249,12 @@ mcb_status init_ctx(int dev, DeviceCtx **out) {
 
 mcb_status resolve_device(const mcb_exec *exec, int *dev) {
   int count = 0;
-  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
-    cudaGetLastError();
+  if (rt_get_device_count(&count) != cudaSuccess || count == 0) {
+    if (!hooks()) cudaGetLastError();
     return MCB_STATUS_CANDIDATE_UNAVAILABLE;
   }
   int d = exec ? exec->device : -1;
-  if (d < 0 && cudaGetDevice(&d) != cudaSuccess) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
+  if (d < 0 && rt_get_device(&d) != cudaSuccess) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
   if (d >= count) return MCB_STATUS_INVALID_ARGUMENT;
   *dev = d;
   return MCB_STATUS_OK;
@@ -267,7 +355,10 @@ mcb_status from_cuda(cudaError_t e) {
 // optional timing, and finishes with the synchronisation/status checks.
 class Call {
  public:
-  explicit Call(const mcb_exec *exec) : exec_(exec) {}
+  // `hookable`: the operator runs under installed runtime hooks (its kernel
+  // launches go through launch_or_hook); others refuse while hooks are on.
+  explicit Call(const mcb_exec *exec, bool hookable = false)
+      : exec_(exec), hookable_(hookable) {}
   ~Call() {
     release_pooled();
     for (auto &e : events_)
@@ -279,15 +370,17 @@ class Call {
   mcb_status begin(bool host_operands) {
     mcb_status s = check_exec(exec_);
     if (s) return s;
+    if (hooks() && !hookable_) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
     s = resolve_device(exec_, &dev_);
     if (s) return s;
     guard_ = new (std::nothrow) DeviceGuard(dev_);
     if (!guard_) return MCB_STATUS_ALLOCATION_FAILURE;
+    if (!guard_->ok) return MCB_STATUS_CANDIDATE_FAILURE;
     s = init_ctx(dev_, &ctx_);
     if (s) return s;
     stream_ = exec_ ? static_cast<cudaStream_t>(exec_->stream) : nullptr;
     host_ = host_operands;
-    timed_ = exec_ && (exec_->flags & MCB_EXEC_TIME);
+    timed_ = exec_ && (exec_->flags & MCB_EXEC_TIME) && !hooks();
     sync_ = host_ || timed_ || (exec_ && (exec_->flags & MCB_EXEC_SYNC));
     if (host_) lock_ = std::unique_lock<std::mutex>(ctx_->mu);  // staging slots are per device
     if (timed_) {
@@ -314,18 +407,23 @@ class Call {
     const int s = slot_++;
     if (ctx_->stage_cap[s] < bytes) {
       if (ctx_->stage[s]) {
-        cudaStreamSynchronize(stream_);
-        cudaFree(ctx_->stage[s]);
+        // The old buffer may still be read by queued work: a failed wait
+        // leaves it allocated (not freed under a running kernel).
+        if (rt_stream_sync(stream_) != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
+        rt_free(ctx_->stage[s]);
         ctx_->stage[s] = nullptr;
         ctx_->stage_cap[s] = 0;
       }
       const size_t cap = std::max<size_t>(bytes, 1 << 20);
-      if (cudaMalloc(&ctx_->stage[s], cap) != cudaSuccess) return MCB_STATUS_ALLOCATION_FAILURE;
+      if (rt_malloc(&ctx_->stage[s], cap) != cudaSuccess) {
+        ctx_->stage[s] = nullptr;
+        return MCB_STATUS_ALLOCATION_FAILURE;
+      }
       ctx_->stage_cap[s] = cap;
     }
     *out = ctx_->stage[s];
     if (upload) {
-      if (cudaMemcpyAsync(*out, t->data, bytes, cudaMemcpyHostToDevice, stream_) != cudaSuccess)
+      if (rt_memcpy_async(*out, t->data, bytes, cudaMemcpyHostToDevice, stream_) != cudaSuccess)
         return MCB_STATUS_CANDIDATE_FAILURE;
       h2d_bytes_ += bytes;
     }
@@ -342,7 +440,7 @@ class Call {
       *out = exec_->workspace;
       return true;
     }
-    if (n_pooled_ == kMaxPooled) return false;
+    if (n_pooled_ == kMaxPooled || hooks()) return false;
     std::call_once(ctx_->pool_once, [this] {
       cudaMemPoolProps props = {};
       props.allocType = cudaMemAllocationTypePinned;
@@ -407,7 +505,7 @@ class Call {
         d2h_bytes_ += row_bytes(out, 0, out->dims[0]);
       } else {
         const size_t bytes = span_bytes(out);
-        if (cudaMemcpyAsync(out->data, dev_out, bytes, cudaMemcpyDeviceToHost, stream_) !=
+        if (rt_memcpy_async(out->data, dev_out, bytes, cudaMemcpyDeviceToHost, stream_) !=
             cudaSuccess)
           return MCB_STATUS_CANDIDATE_FAILURE;
         d2h_bytes_ += bytes;
@@ -417,9 +515,9 @@ class Call {
     if (release_pooled() != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
     uint32_t word = 0;
     if (sync_) {
-      cudaError_t e = cudaStreamSynchronize(stream_);
+      cudaError_t e = rt_stream_sync(stream_);
       if (e != cudaSuccess) return from_cuda(e);
-      if (cudaMemcpy(&word, ctx_->status, sizeof(word), cudaMemcpyDeviceToHost) != cudaSuccess)
+      if (rt_memcpy(&word, ctx_->status, sizeof(word), cudaMemcpyDeviceToHost) != cudaSuccess)
         return MCB_STATUS_CANDIDATE_FAILURE;
     }
     if (exec_ && exec_->report) {
@@ -535,6 +633,14 @@ class Call {
   int sms() const { return ctx_->sms; }
   const mcb_exec *exec() const { return exec_; }
 
+  // A kernel launch, or under installed runtime hooks the hook standing in
+  // for it (`desc` says what the launch would compute).
+  template <typename Launch>
+  cudaError_t launch_or_hook(const mcb_hook_launch &desc, Launch &&launch) {
+    if (const auto *h = hooks()) return static_cast<cudaError_t>(h->launch(&desc));
+    return launch();
+  }
+
  private:
   // Returns this call's pool allocations to the pool, in stream order after
   // everything the call enqueued.
@@ -565,8 +671,8 @@ class Call {
     if (rows == 0 || width == 0) return cudaSuccess;
     char *d = static_cast<char *>(dst) + off;
     const char *s = static_cast<const char *>(src) + off;
-    if (pitch == width || rows == 1) return cudaMemcpyAsync(d, s, rows * width, kind, stream);
-    return cudaMemcpy2DAsync(d, pitch, s, pitch, width, rows, kind, stream);
+    if (pitch == width || rows == 1) return rt_memcpy_async(d, s, rows * width, kind, stream);
+    return rt_memcpy2d_async(d, pitch, s, pitch, width, rows, kind, stream);
   }
   // Copy streams and at least `n` events of the device's row pipeline
   // (created once; the device mutex is held for host-operand calls).
@@ -587,6 +693,7 @@ class Call {
   }
 
   const mcb_exec *exec_;
+  bool hookable_ = false;
   bool output_staged_ = false;
   int dev_ = -1;
   DeviceGuard *guard_ = nullptr;
@@ -637,7 +744,7 @@ mcb_status strict_gemm_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_
   if (overlaps(c, a) || overlaps(c, b)) return MCB_STATUS_ALIAS_VIOLATION;
   bool host = false;
   if ((s = same_space({a, b, c}, &host))) return s;
-  Call call(exec);
+  Call call(exec, /*hookable=*/true);
   if ((s = call.begin(host))) return s;
   void *da, *db, *dc;
   if ((s = call.device_ptr(a, true, &da)) || (s = call.device_ptr(b, true, &db)) ||
@@ -645,9 +752,13 @@ mcb_status strict_gemm_impl(const mcb_tensor *c, const mcb_tensor *a, const mcb_
     return s;
   LaunchInfo info;
   call.mark_compute_start();
-  cudaError_t e = mcb::launch_strict_gemm(
-      static_cast<const float *>(da), static_cast<const float *>(db), static_cast<float *>(dc), m,
-      k, n, a->strides[0], b->strides[0], c->strides[0], call.sms(), call.stream(), &info);
+  mcb_hook_launch desc{"strict_gemm", {da, db, nullptr}, dc, nullptr, m, k, n, 0,
+                       {a->strides[0], b->strides[0], 0, c->strides[0]}};
+  cudaError_t e = call.launch_or_hook(desc, [&] {
+    return mcb::launch_strict_gemm(static_cast<const float *>(da), static_cast<const float *>(db),
+                                   static_cast<float *>(dc), m, k, n, a->strides[0],
+                                   b->strides[0], c->strides[0], call.sms(), call.stream(), &info);
+  });
   call.mark_compute_end();
   return call.finish(c, dc, info, e);
 }
@@ -667,7 +778,7 @@ mcb_status strict_pair_impl(const mcb_tensor *e, const mcb_tensor *a, const mcb_
   if (overlaps(e, a) || overlaps(e, b) || overlaps(e, d)) return MCB_STATUS_ALIAS_VIOLATION;
   bool host = false;
   if ((s = same_space({a, b, d, e}, &host))) return s;
-  Call call(exec);
+  Call call(exec, /*hookable=*/true);
   if ((s = call.begin(host))) return s;
   void *da, *db, *dd, *de;
   if ((s = call.device_ptr(a, true, &da)) || (s = call.device_ptr(b, true, &db)) ||
@@ -683,11 +794,15 @@ mcb_status strict_pair_impl(const mcb_tensor *e, const mcb_tensor *a, const mcb_
     if (call.stream_scratch(cbytes, &cbuf)) {
       LaunchInfo info;
       call.mark_compute_start();
-      cudaError_t err = mcb::launch_strict_pair_two_pass(
-          static_cast<const float *>(da), static_cast<const float *>(db),
-          static_cast<const float *>(dd), static_cast<float *>(de), static_cast<float *>(cbuf),
-          m, k, n, p, k ? a->strides[0] : 0, b->strides[0], d->strides[0], e->strides[0],
-          call.sms(), call.stream(), &info);
+      mcb_hook_launch desc{"strict_fused_pair", {da, db, dd}, de, cbuf, m, k, n, p,
+                           {k ? a->strides[0] : 0, b->strides[0], d->strides[0], e->strides[0]}};
+      cudaError_t err = call.launch_or_hook(desc, [&] {
+        return mcb::launch_strict_pair_two_pass(
+            static_cast<const float *>(da), static_cast<const float *>(db),
+            static_cast<const float *>(dd), static_cast<float *>(de), static_cast<float *>(cbuf),
+            m, k, n, p, k ? a->strides[0] : 0, b->strides[0], d->strides[0], e->strides[0],
+            call.sms(), call.stream(), &info);
+      });
       call.mark_compute_end();
       return call.finish(e, de, info, err);
     }
@@ -702,11 +817,16 @@ mcb_status strict_pair_impl(const mcb_tensor *e, const mcb_tensor *a, const mcb_
     return s;
   LaunchInfo info;
   call.mark_compute_start();
-  cudaError_t err = mcb::launch_strict_pair(
-      static_cast<const float *>(da), static_cast<const float *>(db),
-      static_cast<const float *>(dd), static_cast<float *>(de), static_cast<float *>(scratch), m,
-      k, n, p, k ? a->strides[0] : 0, n ? b->strides[0] : 0, p ? d->strides[0] : 0,
-      e->strides[0], call.sms(), smem_limit, call.stream(), &info);
+  mcb_hook_launch desc{"strict_fused_pair", {da, db, dd}, de, scratch, m, k, n, p,
+                       {k ? a->strides[0] : 0, n ? b->strides[0] : 0, p ? d->strides[0] : 0,
+                        e->strides[0]}};
+  cudaError_t err = call.launch_or_hook(desc, [&] {
+    return mcb::launch_strict_pair(
+        static_cast<const float *>(da), static_cast<const float *>(db),
+        static_cast<const float *>(dd), static_cast<float *>(de), static_cast<float *>(scratch), m,
+        k, n, p, k ? a->strides[0] : 0, n ? b->strides[0] : 0, p ? d->strides[0] : 0,
+        e->strides[0], call.sms(), smem_limit, call.stream(), &info);
+  });
   call.mark_compute_end();
   return call.finish(e, de, info, err);
 }
@@ -1451,11 +1571,12 @@ MCB_API mcb_status mcb_device_status(int32_t device, uint32_t *word, int32_t cle
   mcb_status s = resolve_device(&ex, &dev);
   if (s) return s;
   DeviceGuard g(dev);
+  if (!g.ok) return MCB_STATUS_CANDIDATE_FAILURE;
   DeviceCtx *c;
   if ((s = init_ctx(dev, &c))) return s;
-  if (cudaMemcpy(word, c->status, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+  if (rt_memcpy(word, c->status, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
     return MCB_STATUS_CANDIDATE_FAILURE;
-  if (clear && cudaMemset(c->status, 0, 4) != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
+  if (clear && rt_memset(c->status, 0, 4) != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
   return MCB_STATUS_OK;
 }
 
@@ -1463,6 +1584,7 @@ MCB_API mcb_status mcb_device_timeout_selftest_v1(int32_t device,
                                                   uint64_t spin_limit_cycles) noexcept {
   if (spin_limit_cycles < 10000 || spin_limit_cycles > 4000000000ull)
     return MCB_STATUS_INVALID_ARGUMENT;
+  if (hooks()) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
   mcb_exec ex{};
   ex.abi_version = MCB_ABI_VERSION_V1;
   ex.struct_size = sizeof(ex);
@@ -1471,6 +1593,7 @@ MCB_API mcb_status mcb_device_timeout_selftest_v1(int32_t device,
   mcb_status s = resolve_device(&ex, &dev);
   if (s) return s;
   DeviceGuard g(dev);
+  if (!g.ok) return MCB_STATUS_CANDIDATE_FAILURE;
   DeviceCtx *c;
   if ((s = init_ctx(dev, &c))) return s;
   // X 128x64, W 64x256 and Y 128x256 bf16 in one allocation (never read or
@@ -1498,6 +1621,35 @@ MCB_API mcb_status mcb_device_timeout_selftest_v1(int32_t device,
   // until the caller clears it with mcb_device_status.
   constexpr uint32_t kTimeoutFullBit = 1u;  // kErrTimeoutFull of the device status word
   return (word & kTimeoutFullBit) ? MCB_STATUS_DEVICE_TIMEOUT : MCB_STATUS_CANDIDATE_FAILURE;
+}
+
+MCB_API mcb_status mcb_test_set_runtime_hooks_v1(const mcb_runtime_hooks *h) noexcept {
+  if (!h) {
+    if (g_hooks_on.exchange(false, std::memory_order_acq_rel)) {
+      // Forget the device state created under the table (its pointers came
+      // from the stand-ins; nothing is freed through CUDA).
+      for (DeviceCtx &c : g_dev) {
+        std::lock_guard<std::mutex> lock(c.mu);
+        c.ready = c.usable = false;
+        c.status = nullptr;
+        for (int i = 0; i < kStageSlots; ++i) {
+          c.stage[i] = nullptr;
+          c.stage_cap[i] = 0;
+        }
+      }
+    }
+    return MCB_STATUS_OK;
+  }
+  if (h->abi_version != MCB_ABI_VERSION_V1 || h->struct_size < sizeof(mcb_runtime_hooks))
+    return MCB_STATUS_ABI_MISMATCH;
+  if (!h->get_device_count || !h->get_device || !h->set_device || !h->device_info ||
+      !h->malloc_device || !h->free_device || !h->memset_device || !h->memcpy_async ||
+      !h->memcpy2d_async || !h->memcpy_sync || !h->stream_synchronize || !h->launch)
+    return MCB_STATUS_INVALID_ARGUMENT;
+  if (g_real_context.load(std::memory_order_acquire) || g_hooks_on.load()) return MCB_STATUS_INVALID_ARGUMENT;
+  g_hook_table = *h;
+  g_hooks_on.store(true, std::memory_order_release);
+  return MCB_STATUS_OK;
 }
 
 MCB_API mcb_status mcb_candidate_available(int32_t device) noexcept {
@@ -1744,6 +1896,7 @@ MCB_API mcb_status mcb_device_alloc(int32_t device, uint64_t size_bytes, mcb_buf
   mcb_status s = resolve_device(&ex, &dev);
   if (s) return s;
   DeviceGuard g(dev);
+  if (!g.ok) return MCB_STATUS_CANDIDATE_FAILURE;
   void *p = nullptr;
   if (cudaMalloc(&p, size_bytes ? size_bytes : 1) != cudaSuccess) {
     cudaGetLastError();
@@ -1850,3 +2003,7 @@ MCB_API mcb_status mcb_device_zero_raw_on_stream(void *device_ptr, uint64_t size
 }
 
 }  // extern "C"
+
+namespace mcb {
+bool runtime_hooks_installed() { return hooks() != nullptr; }
+}  // namespace mcb

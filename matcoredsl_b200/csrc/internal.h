@@ -54,6 +54,10 @@ cudaError_t launch_gemm_tc_stall_selftest(const void *x, const void *w, void *y,
                                           long long spin_limit, uint32_t *status,
                                           cudaStream_t stream);
 
+// True while test runtime hooks (mcb_test_set_runtime_hooks_v1) are installed:
+// entry points that launch kernels outside the hookable path refuse to run.
+bool runtime_hooks_installed();
+
 // ---- epilogue description shared by the GEMM kernels ----------------------------
 constexpr int kMaxEpiOps = 8, kMaxEpiBoundaries = 4;
 struct Epilogue {

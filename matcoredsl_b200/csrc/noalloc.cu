@@ -112,6 +112,7 @@ extern "C" MCB_API mcb_status mcb_strict_fused_pair_f32_noalloc_v1(
   if (overlap(e, a) || overlap(e, b) || overlap(e, d)) return MCB_STATUS_ALIAS_VIOLATION;
   // One panel row of N floats must fit in the fixed array.
   if (m > 0 && p > 0 && n > kStaticScratchFloats) return MCB_STATUS_INSUFFICIENT_WORKSPACE;
+  if (mcb::runtime_hooks_installed()) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
 
   int count = 0;
   if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
