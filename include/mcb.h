@@ -29,7 +29,10 @@
  *    too long records a bit in the per-device status word and exits, and a
  *    synchronous call then returns MCB_STATUS_DEVICE_TIMEOUT.
  *  - Threading: calls on distinct streams are independent; the only global
- *    state is a lazily created per-device context guarded by a mutex.
+ *    state is a lazily created per-device context guarded by a mutex. One
+ *    exception: GEMM launches that take the stream-K route share a per-device
+ *    workspace, so the library orders each such launch after the previous
+ *    one on that device (an event wait when they are on different streams).
  */
 #ifndef MCB_H
 #define MCB_H
@@ -129,8 +132,11 @@ typedef struct mcb_report {
   float h2d_ms, d2h_ms;    /* staging copies (MCB_EXEC_TIME, host operands) */
   uint64_t h2d_bytes, d2h_bytes;
   uint32_t device_status;  /* device status word after a synchronous call */
-  uint32_t reserved0;
+  uint32_t route_flags;    /* MCB_ROUTE_* bits describing how the route ran */
 } mcb_report;
+/* report->route_flags: the CTA-pair GEMM split the K-block ranges of some
+ * tiles over several clusters (stream-K) to fill every SM. */
+enum { MCB_ROUTE_STREAM_K = 1u << 0 };
 
 /* Execution context: device, stream and options for one call. */
 enum {
@@ -400,7 +406,9 @@ enum {
   MCB_PLAN_MSM = 5,           /* o, q, k, v */
   MCB_PLAN_FP8_GEMM = 6,      /* c, a, sa, bt, sbt */
   MCB_PLAN_ATTN_BLOCK = 7,    /* y, x, wq, wk, wv, wo */
-  MCB_PLAN_GEMM_I8 = 8        /* c, a, b (zero points from the descriptor) */
+  MCB_PLAN_GEMM_I8 = 8,       /* c, a, b (zero points from the descriptor) */
+  MCB_PLAN_GEMM_EPILOGUE_CHAIN = 9 /* y, x, w, boundaries[num_boundaries] (ops from the
+                                      descriptor's chain extension) */
 };
 #define MCB_PLAN_MAX_TENSORS 8
 typedef struct mcb_plan_desc {
@@ -422,7 +430,16 @@ typedef struct mcb_plan_desc {
   int32_t a_zero_point;  /* GEMM_I8 */
   int32_t b_zero_point;  /* GEMM_I8 */
   uint64_t reserved;
+  /* Chain extension (GEMM_EPILOGUE_CHAIN; read only when struct_size covers
+   * it, so descriptors built against the smaller first layout stay valid):
+   * the op list of mcb_gemm_epilogue_chain_v1, copied into the plan, and the
+   * number of boundary tensors, which follow y, x, w in `tensors`. */
+  uint32_t num_ops;
+  uint32_t num_boundaries;
+  mcb_epilogue_op ops[MCB_EPILOGUE_MAX_OPS];
 } mcb_plan_desc;
+/* struct_size of a descriptor without the chain extension. */
+#define MCB_PLAN_DESC_BASE_SIZE ((uint32_t)offsetof(mcb_plan_desc, num_ops))
 typedef struct mcb_plan mcb_plan;
 MCB_API mcb_status mcb_plan_create_v1(const mcb_plan_desc *desc, mcb_plan **out) MCB_NOEXCEPT;
 /* Runs the plan on `stream` (cudaStream_t, NULL = legacy default stream);

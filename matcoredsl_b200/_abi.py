@@ -53,7 +53,7 @@ class Report(ctypes.Structure):
         ("stages", ctypes.c_int32), ("ctas", ctypes.c_int32),
         ("kernel_ms", ctypes.c_float), ("h2d_ms", ctypes.c_float), ("d2h_ms", ctypes.c_float),
         ("h2d_bytes", ctypes.c_uint64), ("d2h_bytes", ctypes.c_uint64),
-        ("device_status", ctypes.c_uint32), ("reserved0", ctypes.c_uint32),
+        ("device_status", ctypes.c_uint32), ("route_flags", ctypes.c_uint32),
     ]
 
 
@@ -98,7 +98,13 @@ class Fp8TileConfig(ctypes.Structure):
 
 PLAN_MAX_TENSORS = 8
 PLAN_OPS = {"strict_pair": 1, "strict_gemm": 2, "gemm_epilogue": 3, "gemm_chain": 4, "msm": 5,
-            "fp8_gemm": 6, "attn_block": 7, "gemm_i8_i32": 8}
+            "fp8_gemm": 6, "attn_block": 7, "gemm_i8_i32": 8, "gemm_epilogue_chain": 9}
+
+
+class EpilogueOp(ctypes.Structure):
+    """mcb_epilogue_op: one link of a Family A epilogue chain."""
+    _fields_ = [("kind", ctypes.c_uint32), ("value_pos", ctypes.c_uint32),
+                ("boundary", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
 
 
 class PlanDesc(ctypes.Structure):
@@ -111,13 +117,10 @@ class PlanDesc(ctypes.Structure):
         ("eps", ctypes.c_float), ("reserved1", ctypes.c_uint32),
         ("a_zero_point", ctypes.c_int32), ("b_zero_point", ctypes.c_int32),
         ("reserved", ctypes.c_uint64),
+        # chain extension (MCB_PLAN_GEMM_EPILOGUE_CHAIN)
+        ("num_ops", ctypes.c_uint32), ("num_boundaries", ctypes.c_uint32),
+        ("ops", EpilogueOp * 8),
     ]
-
-
-class EpilogueOp(ctypes.Structure):
-    """mcb_epilogue_op: one link of a Family A epilogue chain."""
-    _fields_ = [("kind", ctypes.c_uint32), ("value_pos", ctypes.c_uint32),
-                ("boundary", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
 
 
 # MCB_EW_* codes (unary < 32, binary >= 32).

@@ -122,6 +122,7 @@ class Result:
         self.h2d_ms, self.d2h_ms = rep.h2d_ms, rep.d2h_ms
         self.h2d_bytes, self.d2h_bytes = rep.h2d_bytes, rep.d2h_bytes
         self.device_status = rep.device_status
+        self.stream_k = bool(rep.route_flags & 1)  # MCB_ROUTE_STREAM_K
 
 
 last_result: Result | None = None
@@ -369,12 +370,23 @@ class Plan:
     """Shape-locked operator call with optional CUDA-graph replay (the
     reference's create_plan / execute_plan). Tensors are passed in the entry
     point's argument order (outputs first); None marks an absent optional
-    bias/boundary slot."""
+    bias/boundary slot.
+
+    op "gemm_epilogue_chain": templates are (y, x, w) and `chain` is the op
+    list of gemm_epilogue(chain=...), whose binary items name boundary
+    template tensors; the boundaries become slots 3.. in order of first use,
+    and execute takes (y, x, w, *boundaries) in that order."""
 
     def __init__(self, op, *templates, graph=False, device=-1, bias_mode="none", bias_op="add",
                  act="none", w_transposed=False, scale=1.0, block=128, heads=0, eps=1e-6,
-                 a_zero_point=0, b_zero_point=0):
+                 a_zero_point=0, b_zero_point=0, chain=None):
         lib = _abi.load()
+        chain_ops = None
+        if op == "gemm_epilogue_chain":
+            if chain is None or len(templates) != 3:
+                raise ValueError("gemm_epilogue_chain plans take (y, x, w) and chain=[...]")
+            chain_ops, bnd_list = _epilogue_chain(chain)
+            templates = tuple(templates) + tuple(bnd_list)
         d = _abi.PlanDesc()
         d.abi_version = _abi.ABI_VERSION
         d.struct_size = ctypes.sizeof(_abi.PlanDesc)
@@ -395,6 +407,11 @@ class Plan:
         d.gemm_flags = _abi.GEMM_W_TRANSPOSED if w_transposed else 0
         d.scale, d.block, d.heads, d.eps = float(scale), int(block), int(heads), float(eps)
         d.a_zero_point, d.b_zero_point = _zero_point(a_zero_point), _zero_point(b_zero_point)
+        if chain_ops is not None:
+            d.num_ops = len(chain_ops)
+            d.num_boundaries = len(templates) - 3
+            for i, o in enumerate(chain_ops):
+                d.ops[i] = o
         self._zero_points = (d.a_zero_point, d.b_zero_point)
         self._handle = ctypes.c_void_p()
         _abi.check(lib.mcb_plan_create_v1(ctypes.byref(d), ctypes.byref(self._handle)),

@@ -117,6 +117,15 @@ struct DeviceCtx {
   // touches no other allocator in the process. Created on first use.
   std::once_flag pool_once;
   cudaMemPool_t pool = nullptr;
+  // Stream-K workspace of the CTA-pair GEMM (created on first use): the
+  // counters and partial slots are shared by every launch on the device, so
+  // each stream-K launch is ordered after the previous one (sk_done).
+  std::mutex sk_mu;
+  bool sk_tried = false;
+  mcb::GemmStreamK sk;
+  cudaEvent_t sk_done = nullptr;
+  cudaStream_t sk_stream = nullptr;
+  bool sk_pending = false;
 };
 // Bytes the scratch pool keeps reserved across synchronisations, so repeated
 // calls reuse mapped memory instead of mapping it again.
@@ -532,6 +541,7 @@ class Call {
       r->h2d_bytes = h2d_bytes_;
       r->d2h_bytes = d2h_bytes_;
       r->device_status = word;
+      r->route_flags = info.stream_k ? MCB_ROUTE_STREAM_K : 0u;
       r->kernel_ms = r->h2d_ms = r->d2h_ms = 0.0f;
       if (timed_) {
         cudaEventElapsedTime(&r->h2d_ms, events_[0], events_[1]);
@@ -632,6 +642,52 @@ class Call {
   cudaStream_t stream() const { return stream_; }
   int sms() const { return ctx_->sms; }
   const mcb_exec *exec() const { return exec_; }
+
+  // Runs `launch(sk)` with the device's stream-K workspace (nullptr when it
+  // cannot be used: runtime hooks installed, the stream is being captured,
+  // or the workspace could not be created), ordered after the previous
+  // stream-K launch on this device when that was on another stream.
+  // `launch` reports through `info->stream_k` whether it used the workspace.
+  template <typename Launch>
+  cudaError_t with_stream_k(LaunchInfo *info, Launch &&launch) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (hooks() || cudaStreamIsCapturing(stream_, &cs) != cudaSuccess ||
+        cs != cudaStreamCaptureStatusNone) {
+      (void)cudaGetLastError();
+      return launch(static_cast<const mcb::GemmStreamK *>(nullptr));
+    }
+    std::lock_guard<std::mutex> lock(ctx_->sk_mu);
+    if (!ctx_->sk_tried) {
+      ctx_->sk_tried = true;
+      mcb::GemmStreamK w;
+      w.clusters = std::max(1, ctx_->sms / 2);
+      w.max_tiles = 2 * w.clusters;
+      const size_t part_bytes = static_cast<size_t>(w.clusters) * 4 *
+                                static_cast<size_t>(mcb::kGemmStreamKSlotFloats) * sizeof(float);
+      const size_t ctr_bytes = static_cast<size_t>(w.max_tiles) * 2 * sizeof(int);
+      if (cudaMalloc(reinterpret_cast<void **>(&w.part), part_bytes) == cudaSuccess &&
+          cudaMalloc(reinterpret_cast<void **>(&w.ctr), ctr_bytes) == cudaSuccess &&
+          cudaMemset(w.ctr, 0, ctr_bytes) == cudaSuccess &&
+          cudaEventCreateWithFlags(&ctx_->sk_done, cudaEventDisableTiming) == cudaSuccess) {
+        ctx_->sk = w;
+      } else {
+        (void)cudaGetLastError();
+        if (w.part) cudaFree(w.part);
+        if (w.ctr) cudaFree(w.ctr);
+      }
+    }
+    if (!ctx_->sk.ctr) return launch(static_cast<const mcb::GemmStreamK *>(nullptr));
+    if (ctx_->sk_pending && ctx_->sk_stream != stream_ &&
+        cudaStreamWaitEvent(stream_, ctx_->sk_done, 0) != cudaSuccess)
+      return cudaErrorUnknown;
+    const cudaError_t err = launch(static_cast<const mcb::GemmStreamK *>(&ctx_->sk));
+    if (err == cudaSuccess && info->stream_k) {
+      if (cudaEventRecord(ctx_->sk_done, stream_) != cudaSuccess) return cudaErrorUnknown;
+      ctx_->sk_stream = stream_;
+      ctx_->sk_pending = true;
+    }
+    return err;
+  }
 
   // A kernel launch, or under installed runtime hooks the hook standing in
   // for it (`desc` says what the launch would compute).
@@ -1003,6 +1059,12 @@ mcb_status gemm_epilogue_impl(const mcb_tensor *y, const mcb_tensor *x, const mc
         &err);
     if (s) return s;
     info.launches = launches;
+  } else if (tma_ok) {
+    err = call.with_stream_k(&info, [&](const mcb::GemmStreamK *sk) {
+      return mcb::launch_gemm_tc_bf16(dx, dw, dy, m, n, k, ld_x, ld_w, ld_y, wt ? 1 : 0, y_kind,
+                                      ep, call.ctx()->status, call.sms(), call.stream(), &info,
+                                      in_f16 ? 1 : 0, sk);
+    });
   } else {
     err = launch_rows(0, m);
   }
@@ -1577,6 +1639,13 @@ MCB_API mcb_status mcb_device_status(int32_t device, uint32_t *word, int32_t cle
   if (rt_memcpy(word, c->status, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
     return MCB_STATUS_CANDIDATE_FAILURE;
   if (clear && rt_memset(c->status, 0, 4) != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
+  if (clear && *word != 0 && !hooks()) {
+    // A stream-K launch that aborted may have left arrival counts behind.
+    std::lock_guard<std::mutex> lock(c->sk_mu);
+    if (c->sk.ctr && cudaMemset(c->sk.ctr, 0, static_cast<size_t>(c->sk.max_tiles) * 2 *
+                                                  sizeof(int)) != cudaSuccess)
+      return MCB_STATUS_CANDIDATE_FAILURE;
+  }
   return MCB_STATUS_OK;
 }
 

@@ -265,6 +265,36 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// ---- named barriers ------------------------------------------------------------------
+// Barrier `id` among `n` threads (a multiple of 32) of this CTA.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+// Barrier `id` among `n` threads that also returns the OR of `pred` over them,
+// so every participant takes the same branch afterwards.
+__device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t n, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred q, r;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred r, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, r;\n\t}"
+      : "=r"(out)
+      : "r"(pred ? 1u : 0u), "r"(id), "r"(n)
+      : "memory");
+  return out != 0;
+}
+
+// GPU-scope atomic add with acquire-release semantics: releases everything
+// this thread has observed (e.g. the CTA's stores ordered before it by a CTA
+// barrier) and acquires what earlier releasers of the same counter published.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int *p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
 // ---- CTA pairs (clusters of 2, tcgen05 cta_group::2) ------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

@@ -56,6 +56,13 @@ struct Params {
   uint32_t *status;
   long long spin_limit;  // clock64 cycles a pipeline wait may take before the kernel aborts
   int stall_loads;       // self-test only: the producer issues no loads (the waits must time out)
+  // Stream-K (CTA-pair kernel): tiles [0, sk_first_tile) run whole, one per
+  // cluster in turn; the K-block iterations of tiles [sk_first_tile,
+  // num_tiles) (sk_iters of them) are split evenly over the clusters.
+  int sk_first_tile;
+  int64_t sk_iters;
+  int *sk_ctr;    // arrivals per (stream-K tile, CTA rank); 0 between launches
+  float *sk_part; // partial accumulators: per (cluster, slot 0/1, CTA rank) 128x256 f32
   Epilogue epi;
 };
 
@@ -362,7 +369,64 @@ constexpr int P_STAGES = 6;
 constexpr int P_THREADS = 320;  // producer, MMA, 8 epilogue warps (2 per TMEM lane quarter)
 constexpr size_t P_SMEM_BYTES = static_cast<size_t>(P_STAGES) * P_STAGE_BYTES + BAR_BYTES + 1024;
 
-template <bool kChain>
+// ---- stream-K work split ----------------------------------------------------------
+// A unit of a cluster's work: tile `tile`, K blocks [kb0, kb1). `sk_tile`
+// >= 0 marks a partial tile (other clusters hold the rest of its K range):
+// its accumulator is combined through the partial slots and the arrival
+// counter; `slot` is 0 for the cluster's first stream-K unit, else 1.
+struct Unit {
+  int tile, kb0, kb1, sk_tile, slot;
+};
+constexpr int64_t kSlotFloats = 2 * BM * BN / 2;  // 128 rows x 256 columns per CTA
+
+__device__ __forceinline__ int64_t sk_begin(const Params &p, int64_t c, int64_t g) {
+  return c * p.sk_iters / g;
+}
+// The cluster whose stream-K range holds iteration `it`.
+__device__ __forceinline__ int sk_cluster_of(const Params &p, int64_t it, int64_t g) {
+  int64_t c = it * g / p.sk_iters;
+  while (c + 1 < g && sk_begin(p, c + 1, g) <= it) ++c;
+  return static_cast<int>(c);
+}
+
+// Units of one cluster in order: whole tiles cluster, cluster + G, ... below
+// sk_first_tile, then its contiguous share of the stream-K iterations
+// (tile-major, K blocks innermost). Producer, MMA and epilogue walk the same
+// sequence.
+struct UnitIter {
+  int tile;
+  int64_t it, begin, end;
+  __device__ UnitIter(const Params &p, int cluster, int g) : tile(cluster) {
+    begin = it = sk_begin(p, cluster, g);
+    end = sk_begin(p, cluster + 1, g);
+  }
+  __device__ bool next(const Params &p, int g, Unit &u) {
+    if (tile < p.sk_first_tile) {
+      u = {tile, 0, p.num_kb, -1, 0};
+      tile += g;
+      return true;
+    }
+    if (it >= end) return false;
+    const int t = static_cast<int>(it / p.num_kb);
+    const int kb0 = static_cast<int>(it - static_cast<int64_t>(t) * p.num_kb);
+    const int64_t left = end - it;
+    const int kb1 = left < p.num_kb - kb0 ? kb0 + static_cast<int>(left) : p.num_kb;
+    u.tile = p.sk_first_tile + t;
+    u.kb0 = kb0;
+    u.kb1 = kb1;
+    u.sk_tile = (kb0 == 0 && kb1 == p.num_kb) ? -1 : t;
+    u.slot = it == begin ? 0 : 1;
+    it += kb1 - kb0;
+    return true;
+  }
+};
+
+// kSK: the stream-K instantiation. Its epilogue warps agree on every
+// pipeline wait through a CTA barrier (all leave together on a timeout) and
+// combine partial tiles: each holder of a part writes its accumulator to its
+// slot and counts itself in; the last to arrive adds the other parts to its
+// own and runs the epilogue. Nothing ever waits for another CTA.
+template <bool kChain, bool kSK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     gemm_tc_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
                              const __grid_constant__ CUtensorMap tmap_w, const Params p) {
@@ -379,6 +443,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
   uint64_t *drain = acc_empty + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  volatile int *sk_last = reinterpret_cast<volatile int *>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -398,6 +463,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
+    *sk_last = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -419,10 +485,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = cluster; tile < p.num_tiles; tile += nclusters) {
-        const int m0 = (tile / p.n_tiles) * (2 * BM) + static_cast<int>(rank) * BM;
-        const int n0 = (tile % p.n_tiles) * BN + static_cast<int>(rank) * P_BN_CTA;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+      UnitIter units(p, cluster, nclusters);
+      Unit u;
+      while (units.next(p, nclusters, u)) {
+        const int m0 = (u.tile / p.n_tiles) * (2 * BM) + static_cast<int>(rank) * BM;
+        const int n0 = (u.tile % p.n_tiles) * BN + static_cast<int>(rank) * P_BN_CTA;
+        for (int kb = u.kb0; kb < u.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kErrTimeoutEmpty,
                          p.spin_limit))
             goto producer_done;
@@ -453,14 +521,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = cluster; tile < p.num_tiles; tile += nclusters) {
+      UnitIter units(p, cluster, nclusters);
+      Unit u;
+      while (units.next(p, nclusters, u)) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.status, kErrTimeoutAccum,
                        p.spin_limit))
           break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         bool ok = true;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = u.kb0; kb < u.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status, kErrTimeoutFull, p.spin_limit)) {
             ok = false;
             break;
@@ -474,7 +544,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
             const uint64_t bdesc = p.w_transposed
                                        ? make_sdesc_sw128(b_addr + kk * 32, 16, 1024)
                                        : make_sdesc_sw128(b_addr + kk * 2048, 64 * BK * 2, 1024);
-            mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            mma_f16_ss_pair(d_tmem, adesc, bdesc, idesc, (kb != u.kb0 || kk != 0) ? 1u : 0u);
           }
           mma_commit_pair(&empty[stage], 0x3);
           if (++stage == P_STAGES) {
@@ -496,22 +566,91 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = cluster; tile < p.num_tiles; tile += nclusters) {
-      const int64_t m0 = static_cast<int64_t>(tile / p.n_tiles) * (2 * BM) + rank * BM;
-      const int64_t n0 = static_cast<int64_t>(tile % p.n_tiles) * BN;
-      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.status, kErrTimeoutAccum,
-                          p.spin_limit))
-        break;
+    UnitIter units(p, cluster, nclusters);
+    Unit u;
+    while (units.next(p, nclusters, u)) {
+      const int64_t m0 = static_cast<int64_t>(u.tile / p.n_tiles) * (2 * BM) + rank * BM;
+      const int64_t n0 = static_cast<int64_t>(u.tile % p.n_tiles) * BN;
+      const bool ok = mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.status,
+                                     kErrTimeoutAccum, p.spin_limit);
+      if constexpr (kSK) {
+        if (named_bar_or(1, 256, !ok)) break;  // every epilogue warp leaves together
+      } else {
+        if (!ok) break;
+      }
       tc_fence_after();
       const int64_t row = m0 + sub * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
+      if (!kSK || u.sk_tile < 0) {
 #pragma unroll 1
-      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
-        if (n0 + c >= p.n) break;
-        uint32_t r[32];
-        tmem_ld32_sync(t_row + c, r);
-        epilogue_chunk<kChain>(p, r, row, n0 + c);
+        for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+          if (n0 + c >= p.n) break;
+          uint32_t r[32];
+          tmem_ld32_sync(t_row + c, r);
+          epilogue_chunk<kChain>(p, r, row, n0 + c);
+        }
+      } else {
+        // Partial tile. Slot layout: float4 q of chunk (32 columns) c for
+        // row r at ((c * 8 + q) * 128 + r) * 4 floats, so one warp-wide
+        // float4 store (32 rows) covers 512 contiguous bytes.
+        const int64_t g = nclusters;
+        const int r_local = sub * 32 + lane;
+        float4 *mine = reinterpret_cast<float4 *>(
+            p.sk_part + ((static_cast<int64_t>(cluster) * 2 + u.slot) * 2 + rank) * kSlotFloats);
+#pragma unroll 1
+        for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+          uint32_t r[32];
+          tmem_ld32_sync(t_row + c, r);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            mine[((c >> 5) * 8 + q) * BM + r_local] =
+                make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                            __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+        }
+        // The CTA barrier orders every thread's stores before the counting
+        // thread's release (acq_rel atomic at GPU scope); the last arriver's
+        // acquire plus the second barrier make the other parts visible to all
+        // of its threads.
+        named_bar_sync(1, 256);
+        const int64_t t0 = static_cast<int64_t>(u.sk_tile) * p.num_kb;
+        const int c_first = sk_cluster_of(p, t0, g);
+        const int c_last = sk_cluster_of(p, t0 + p.num_kb - 1, g);
+        if (warp == 2 && lane == 0) {
+          const int old = atomic_add_acq_rel_gpu(p.sk_ctr + u.sk_tile * 2 + rank, 1);
+          *sk_last = old == c_last - c_first ? 1 : 0;
+        }
+        named_bar_sync(1, 256);
+        if (*sk_last) {
+#pragma unroll 1
+          for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+            if (n0 + c >= p.n) break;
+            uint32_t r[32];
+            tmem_ld32_sync(t_row + c, r);
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            for (int c2 = c_first; c2 <= c_last; ++c2) {
+              if (c2 == cluster) continue;
+              // A part that starts inside this tile is its holder's first unit.
+              const int slot2 = sk_begin(p, c2, g) >= t0 ? 0 : 1;
+              const float4 *src = reinterpret_cast<const float4 *>(
+                  p.sk_part + ((static_cast<int64_t>(c2) * 2 + slot2) * 2 + rank) * kSlotFloats);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 f = __ldcg(src + ((c >> 5) * 8 + q) * BM + r_local);
+                v[4 * q] += f.x;
+                v[4 * q + 1] += f.y;
+                v[4 * q + 2] += f.z;
+                v[4 * q + 3] += f.w;
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
+            epilogue_chunk<kChain>(p, r, row, n0 + c);
+          }
+          if (warp == 2 && lane == 0) p.sk_ctr[u.sk_tile * 2 + rank] = 0;  // ready for the next launch
+        }
       }
       tc_fence_before();
       mbar_arrive_cluster(acc_empty_leader + acc * 8);
@@ -540,7 +679,7 @@ int pair_clusters_resident(int device) {
   if (device < 0 || device >= 64) return 0;
   int v = cache[device].load(std::memory_order_relaxed);
   if (v != 0) return v;
-  if (cudaFuncSetAttribute(gemm_tc_bf16_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  if (cudaFuncSetAttribute(gemm_tc_bf16_pair_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(P_SMEM_BYTES)) != cudaSuccess) {
     (void)cudaGetLastError();
     cache[device].store(-1, std::memory_order_relaxed);
@@ -551,7 +690,7 @@ int pair_clusters_resident(int device) {
   cfg.blockDim = dim3(P_THREADS, 1, 1);
   cfg.dynamicSmemBytes = P_SMEM_BYTES;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_bf16_pair_kernel<false>, &cfg) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_tc_bf16_pair_kernel<false, false>, &cfg) != cudaSuccess ||
       n <= 0) {
     (void)cudaGetLastError();
     n = -1;  // pair kernel unavailable on this device: use the single-SM kernel
@@ -568,13 +707,22 @@ bool pair_kernel_enabled() {
   return on;
 }
 
+// MCB_GEMM_STREAM_K=0 in the environment keeps whole tiles (A/B measurement).
+bool stream_k_enabled() {
+  static const bool on = [] {
+    const char *e = getenv("MCB_GEMM_STREAM_K");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 }  // namespace
 
 cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m, int64_t n,
                                 int64_t k, int64_t ld_x, int64_t ld_w, int64_t ld_y,
                                 int w_transposed, int y_kind, const Epilogue &epi,
                                 uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info,
-                                int in_f16) {
+                                int in_f16, const GemmStreamK *sk) {
   if (m == 0 || n == 0) return cudaSuccess;
   const bool chain = epi.n_ops > 0;
   // Rows of 256 go to CTA pairs (M = 256 per MMA, W tile split between the
@@ -584,10 +732,12 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   if (e != cudaSuccess) return e;
   const bool pair = m >= 2 * BM && pair_kernel_enabled() && pair_clusters_resident(device) > 0;
   if (pair) {
-    e = cudaFuncSetAttribute(chain ? gemm_tc_bf16_pair_kernel<true> : gemm_tc_bf16_pair_kernel<false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(P_SMEM_BYTES));
-    if (e != cudaSuccess) return e;
+    for (auto *kernel : {gemm_tc_bf16_pair_kernel<true, false>, gemm_tc_bf16_pair_kernel<false, false>,
+                         gemm_tc_bf16_pair_kernel<false, true>}) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(P_SMEM_BYTES));
+      if (e != cudaSuccess) return e;
+    }
   }
   const int w_rows = pair ? P_BN_CTA : BN;  // W^T box height per CTA
   CUtensorMap tx, tw;
@@ -618,17 +768,43 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   p.status = status;
   p.spin_limit = kSpinTimeoutCycles;
   p.stall_loads = 0;
+  p.sk_first_tile = p.num_tiles;  // whole tiles only unless stream-K applies below
+  p.sk_iters = 0;
+  p.sk_ctr = nullptr;
+  p.sk_part = nullptr;
   p.epi = epi;
   int grid;
+  bool use_sk = false;
   if (pair) {
     int clusters = pair_clusters_resident(device);
     if (clusters > sms / 2) clusters = sms / 2;
     if (clusters < 1) clusters = 1;
-    grid = 2 * static_cast<int>(tiles < clusters ? tiles : clusters);
+    // Stream-K when whole tiles would leave more than 5% of the last wave's
+    // clusters idle (e.g. 1024 rows: 64 tiles on 74 clusters). All but one
+    // full wave stays whole-tile; the remaining tiles' K-block iterations are
+    // split evenly over every cluster.
+    if (sk && !chain && sk->ctr && sk->part && clusters <= sk->clusters && stream_k_enabled()) {
+      const int64_t g = clusters;
+      const int64_t waves = (tiles + g - 1) / g;
+      const int64_t full = tiles / g;
+      const int64_t dp = full >= 2 ? (full - 1) * g : 0;
+      const int64_t sk_tiles = tiles - dp;
+      const int64_t iters = sk_tiles * p.num_kb;
+      if (tiles * 100 < waves * g * 95 && iters >= 4 * g && sk_tiles <= sk->max_tiles) {
+        use_sk = true;
+        p.sk_first_tile = static_cast<int>(dp);
+        p.sk_iters = iters;
+        p.sk_ctr = sk->ctr;
+        p.sk_part = sk->part;
+      }
+    }
+    grid = 2 * static_cast<int>(use_sk ? clusters : (tiles < clusters ? tiles : clusters));
     if (chain)
-      gemm_tc_bf16_pair_kernel<true><<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
+      gemm_tc_bf16_pair_kernel<true, false><<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
+    else if (use_sk)
+      gemm_tc_bf16_pair_kernel<false, true><<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
     else
-      gemm_tc_bf16_pair_kernel<false><<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
+      gemm_tc_bf16_pair_kernel<false, false><<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
   } else {
     // Per-device function attribute; cheap, so set on every launch.
     e = cudaFuncSetAttribute(chain ? gemm_tc_bf16_kernel<true> : gemm_tc_bf16_kernel<false>,
@@ -648,6 +824,7 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
     info->tile_k = BK;
     info->stages = pair ? P_STAGES : STAGES;
     info->ctas = grid;
+    info->stream_k = use_sk;
     info->set_route(in_f16 ? "tcgen05_f16_gemm_epilogue" : "tcgen05_bf16_gemm_epilogue");
   }
   return cudaGetLastError();

@@ -12,6 +12,7 @@ namespace mcb {
 struct LaunchInfo {
   int launches = 0;
   int tile_m = 0, tile_n = 0, tile_k = 0, stages = 0, ctas = 0;
+  bool stream_k = false;  // the GEMM split K-block ranges of tiles over clusters
   char route[48] = {0};
   void set_route(const char *r) {
     strncpy(route, r, sizeof(route) - 1);
@@ -90,11 +91,23 @@ struct Epilogue {
 // K, N, ld_x, ld_w multiples of 8 and 16-byte aligned bases (TMA); the caller
 // checks.
 enum : int { kOutF32 = 0, kOutBf16 = 1, kOutF16 = 2 };
+// Device workspace of the stream-K route of the CTA-pair GEMM: arrival
+// counters (2 per stream-K tile, zero between launches; every launch leaves
+// them zero unless it aborted) and partial-accumulator slots (128x256 f32 per
+// cluster, slot 0/1 and CTA rank). Launches that share one workspace must not
+// overlap on the GPU.
+struct GemmStreamK {
+  int *ctr = nullptr;
+  float *part = nullptr;
+  int clusters = 0;   // clusters the slots cover
+  int max_tiles = 0;  // stream-K tiles the counters cover
+};
+constexpr int64_t kGemmStreamKSlotFloats = 128 * 256;
 cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m, int64_t n,
                                 int64_t k, int64_t ld_x, int64_t ld_w, int64_t ld_y,
                                 int w_transposed, int y_kind, const Epilogue &epi,
                                 uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info,
-                                int in_f16 = 0);
+                                int in_f16 = 0, const GemmStreamK *sk = nullptr);
 
 // ---- simt.cu: CUDA-core fallbacks for shapes/dtypes the tensor-core kernels do not take
 // dtype codes: 1 f32, 3 bf16, 6 f16 (as in mcb.h)

@@ -39,8 +39,8 @@ bool is_optional_slot(uint32_t op, uint32_t i) {
   return (op == MCB_PLAN_GEMM_EPILOGUE && i == 3) || (op == MCB_PLAN_GEMM_CHAIN && i == 3);
 }
 
-uint32_t slots_for(uint32_t op) {
-  switch (op) {
+uint32_t slots_for(const mcb_plan_desc &d) {
+  switch (d.op) {
     case MCB_PLAN_STRICT_PAIR: return 4;
     case MCB_PLAN_STRICT_GEMM: return 3;
     case MCB_PLAN_GEMM_EPILOGUE: return 4;
@@ -49,6 +49,8 @@ uint32_t slots_for(uint32_t op) {
     case MCB_PLAN_FP8_GEMM: return 5;
     case MCB_PLAN_ATTN_BLOCK: return 6;
     case MCB_PLAN_GEMM_I8: return 3;
+    case MCB_PLAN_GEMM_EPILOGUE_CHAIN:
+      return d.num_boundaries <= MCB_EPILOGUE_MAX_BOUNDARIES ? 3 + d.num_boundaries : 0;
     default: return 0;
   }
 }
@@ -95,6 +97,11 @@ mcb_status run_op(const mcb_plan &p, const mcb_tensor *t, cudaStream_t stream) {
     case MCB_PLAN_GEMM_I8:
       return mcb_gemm_i8_i32_zp_v1(&t[0], &t[1], &t[2], p.desc.a_zero_point,
                                    p.desc.b_zero_point, &ex);
+    case MCB_PLAN_GEMM_EPILOGUE_CHAIN:
+      return mcb_gemm_epilogue_chain_v1(&t[0], &t[1], &t[2],
+                                        p.desc.num_boundaries ? &t[3] : nullptr,
+                                        p.desc.num_boundaries, p.desc.ops, p.desc.num_ops,
+                                        p.desc.gemm_flags, &ex);
     default:
       return MCB_STATUS_INVALID_ARGUMENT;
   }
@@ -160,19 +167,28 @@ extern "C" {
 MCB_API mcb_status mcb_plan_create_v1(const mcb_plan_desc *desc, mcb_plan **out) noexcept {
   if (!desc || !out) return MCB_STATUS_INVALID_ARGUMENT;
   *out = nullptr;
-  if (desc->abi_version != MCB_ABI_VERSION_V1 || desc->struct_size < sizeof(mcb_plan_desc))
+  if (desc->abi_version != MCB_ABI_VERSION_V1 || desc->struct_size < MCB_PLAN_DESC_BASE_SIZE)
     return MCB_STATUS_ABI_MISMATCH;
-  const uint32_t n = slots_for(desc->op);
-  if (n == 0 || desc->num_tensors != n) return MCB_STATUS_INVALID_ARGUMENT;
+  // The plan keeps its own copy; fields past the caller's struct_size (the
+  // chain extension of a descriptor built with the first layout) read as 0.
+  mcb_plan_desc d;
+  std::memset(&d, 0, sizeof(d));
+  std::memcpy(&d, desc, desc->struct_size < sizeof(d) ? desc->struct_size : sizeof(d));
+  if (d.op == MCB_PLAN_GEMM_EPILOGUE_CHAIN) {
+    if (desc->struct_size < sizeof(mcb_plan_desc)) return MCB_STATUS_ABI_MISMATCH;
+    if (d.num_ops == 0 || d.num_ops > MCB_EPILOGUE_MAX_OPS) return MCB_STATUS_INVALID_ARGUMENT;
+  }
+  const uint32_t n = slots_for(d);
+  if (n == 0 || d.num_tensors != n) return MCB_STATUS_INVALID_ARGUMENT;
   for (uint32_t i = 0; i < n; ++i) {
-    const mcb_tensor &t = desc->tensors[i];
-    if (is_optional_slot(desc->op, i) && t.dtype == MCB_DTYPE_INVALID) continue;
+    const mcb_tensor &t = d.tensors[i];
+    if (is_optional_slot(d.op, i) && t.dtype == MCB_DTYPE_INVALID) continue;
     if (t.abi_version != MCB_ABI_VERSION_V1 || t.struct_size < sizeof(mcb_tensor))
       return MCB_STATUS_ABI_MISMATCH;
-    if (desc->graph_mode && t.memory_space != MCB_MEMORY_CUDA_DEVICE)
+    if (d.graph_mode && t.memory_space != MCB_MEMORY_CUDA_DEVICE)
       return MCB_STATUS_UNSUPPORTED_MEMORY_SPACE;
   }
-  int dev = desc->device;
+  int dev = d.device;
   int count = 0;
   if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
     cudaGetLastError();
@@ -183,16 +199,16 @@ MCB_API mcb_status mcb_plan_create_v1(const mcb_plan_desc *desc, mcb_plan **out)
   if (s != MCB_STATUS_OK) return s;
   mcb_plan *p = new (std::nothrow) mcb_plan;
   if (!p) return MCB_STATUS_ALLOCATION_FAILURE;
-  p->desc = *desc;
+  p->desc = d;
   p->device = dev;
   p->generation = g_next_generation.fetch_add(1);
   int prev = -1;
   cudaGetDevice(&prev);
   if (prev != dev) cudaSetDevice(dev);
   cudaError_t e = cudaSuccess;
-  p->workspace_bytes = workspace_for(*desc);
+  p->workspace_bytes = workspace_for(d);
   if (p->workspace_bytes) e = cudaMalloc(&p->workspace, p->workspace_bytes);
-  if (e == cudaSuccess && desc->graph_mode) {
+  if (e == cudaSuccess && d.graph_mode) {
     e = cudaStreamCreateWithFlags(&p->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->ev_in, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->ev_out, cudaEventDisableTiming);
@@ -210,7 +226,7 @@ MCB_API mcb_status mcb_plan_create_v1(const mcb_plan_desc *desc, mcb_plan **out)
 MCB_API mcb_status mcb_plan_execute_v1(mcb_plan *p, const mcb_tensor *tensors,
                                        uint32_t num_tensors, void *stream_v) noexcept {
   if (!p || !tensors) return MCB_STATUS_INVALID_ARGUMENT;
-  const uint32_t n = slots_for(p->desc.op);
+  const uint32_t n = slots_for(p->desc);
   if (num_tensors != n) return MCB_STATUS_SHAPE_MISMATCH;
   for (uint32_t i = 0; i < n; ++i)
     if (!same_meta(tensors[i], p->desc.tensors[i])) return MCB_STATUS_SHAPE_MISMATCH;

@@ -183,3 +183,35 @@ def test_epilogue_chain_encoding(mcb):
         _epilogue_chain([("add", np.zeros(1)) for _ in range(5)])
     with pytest.raises(KeyError):
         _epilogue_chain(["softmax"])
+
+
+def test_plan_descriptor_base_size_and_chain_extension(mcb):
+    """A descriptor built with the first layout (struct_size up to `reserved`)
+    is still accepted; the chain op needs the extension and 1..8 ops. No GPU
+    here, so accepted descriptors end at CANDIDATE_UNAVAILABLE."""
+    from matcoredsl_b200 import _abi
+    lib = mcb.load()
+    base = _abi.PlanDesc.num_ops.offset
+
+    def desc(op, size, n_tensors, num_ops=0, num_bnd=0):
+        d = _abi.PlanDesc()
+        d.abi_version, d.struct_size, d.op = _abi.ABI_VERSION, size, op
+        d.num_tensors, d.num_ops, d.num_boundaries = n_tensors, num_ops, num_bnd
+        for i in range(n_tensors):
+            d.tensors[i].abi_version = _abi.ABI_VERSION
+            d.tensors[i].struct_size = ctypes.sizeof(_abi.Tensor)
+            d.tensors[i].dtype = 1
+        return d
+
+    h = ctypes.c_void_p()
+    code = lambda d: lib.mcb_plan_create_v1(ctypes.byref(d), ctypes.byref(h))  # noqa: E731
+    unavailable = _abi.STATUS_CODE["CANDIDATE_UNAVAILABLE"]
+    full = ctypes.sizeof(_abi.PlanDesc)
+    assert code(desc(_abi.PLAN_OPS["strict_gemm"], base, 3)) == unavailable
+    assert code(desc(_abi.PLAN_OPS["strict_gemm"], base - 8, 3)) == _abi.STATUS_CODE["ABI_MISMATCH"]
+    chain = _abi.PLAN_OPS["gemm_epilogue_chain"]
+    assert code(desc(chain, base, 5, 2, 2)) == _abi.STATUS_CODE["ABI_MISMATCH"]
+    assert code(desc(chain, full, 5, 0, 2)) == _abi.STATUS_CODE["INVALID_ARGUMENT"]
+    assert code(desc(chain, full, 5, 9, 2)) == _abi.STATUS_CODE["INVALID_ARGUMENT"]
+    assert code(desc(chain, full, 4, 2, 2)) == _abi.STATUS_CODE["INVALID_ARGUMENT"]  # 3 + 2 slots
+    assert code(desc(chain, full, 5, 2, 2)) == unavailable

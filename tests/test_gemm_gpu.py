@@ -261,3 +261,82 @@ def test_family_b_chain_tcgen05(mcb, orc, act, bias_mode, bias_op):
     ref = orc.gemm_epilogue(mid.astype(np.float32), wf)
     assert orc.rel_frobenius(gu.from_dev(e), ref) < REL_BF16
     assert e.dtype == torch.float32
+
+
+# ---- stream-K route of the CTA-pair kernel ----------------------------------------
+# Shapes whose whole tiles would leave clusters idle split the K-block ranges
+# of tiles over all clusters; a tile's parts are summed in f32 by whichever
+# CTA arrives last. Checked at the f32-output bar (1e-5) against the fp64
+# oracle, twice in a row (the arrival counters must be back at zero).
+@pytest.mark.parametrize("shape,w_transposed", [
+    ((1024, 4096, 4096), False),   # config 2 rows per GPU at 8 GPUs: 64 tiles
+    ((2048, 4096, 4096), False),   # 4 GPUs: 128 tiles, all stream-K
+    ((4096, 2048, 4096), False),   # 2 GPUs: whole-tile waves, then stream-K
+    ((1000, 4096, 1032), True),    # ragged M and N, 3-4 parts per tile
+    ((512, 8192, 768), False),     # long K: many parts per tile
+])
+def test_stream_k_f32_out(mcb, orc, shape, w_transposed):
+    import torch
+    m, k, n = shape
+    x, w, b = _inputs(m, k, n, seed=m + n)
+    xh, xf = gu.bf16_pair(x)
+    wh, wf = gu.bf16_pair(w)
+    tx = gu.to_dev_bf16(xh)
+    tw = gu.to_dev_bf16(np.ascontiguousarray(wh.T) if w_transposed else wh)
+    bh, bf = gu.bf16_pair(b)
+    rows = gu.sample_rows(m, seed=3)
+    ref = orc.gemm_epilogue(xf[rows], wf, bf, bias_mode="row", act="gelu_tanh")
+    for _ in range(2):
+        y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+        mcb.gemm_epilogue(tx, tw, gu.to_dev_bf16(bh), bias_mode="row", act="gelu_tanh", out=y,
+                          w_transposed=w_transposed)
+        r = mcb.api.last_result
+        assert r.route == "tcgen05_bf16_gemm_epilogue" and r.stream_k
+        got = gu.from_dev(y)
+        assert not np.isnan(got).any()
+        assert orc.rel_frobenius(got[rows], ref) < REL_F32_OUT
+    assert mcb.device_status(0) == 0
+
+
+def test_stream_k_bf16_out_matches_whole_tile_run(mcb, orc):
+    """bf16 output at config 2's 1024-row shard: stream-K against the oracle
+    at the bf16 bar, and the headline 8192-row shape keeps whole tiles."""
+    import torch
+    m, k, n = 1024, 4096, 4096
+    x, w, b = _inputs(m, k, n, seed=10)
+    xh, xf = gu.bf16_pair(x)
+    wh, wf = gu.bf16_pair(w)
+    bh, bf = gu.bf16_pair(b)
+    y = mcb.gemm_epilogue(gu.to_dev_bf16(xh), gu.to_dev_bf16(wh), gu.to_dev_bf16(bh),
+                          bias_mode="row", act="gelu_tanh")
+    assert mcb.api.last_result.stream_k
+    ref = orc.gemm_epilogue(xf, wf, bf, bias_mode="row", act="gelu_tanh")
+    assert orc.rel_frobenius(gu.from_dev(y), ref) < REL_BF16
+    big = torch.zeros(8192, 4096, dtype=torch.bfloat16, device="cuda")
+    mcb.gemm_epilogue(big, gu.to_dev_bf16(wh), gu.to_dev_bf16(bh), bias_mode="row",
+                      act="gelu_tanh")
+    assert not mcb.api.last_result.stream_k  # 512 tiles: 6.9 waves, whole tiles
+
+
+def test_stream_k_on_two_streams(mcb, orc):
+    """Stream-K launches from two streams share the device workspace: the
+    library orders them, so interleaved calls stay exact."""
+    import torch
+    m, k, n = 1024, 2048, 4096
+    cases = []
+    for seed in (21, 22):
+        x, w, _ = _inputs(m, k, n, seed=seed)
+        xh, xf = gu.bf16_pair(x)
+        wh, wf = gu.bf16_pair(w)
+        cases.append((gu.to_dev_bf16(xh), gu.to_dev_bf16(wh), orc.gemm_epilogue(xf[:64], wf)))
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = [torch.empty(m, n, dtype=torch.float32, device="cuda") for _ in range(2)]
+    torch.cuda.synchronize()
+    for _ in range(5):
+        for i in (0, 1):
+            with torch.cuda.stream(streams[i]):
+                mcb.gemm_epilogue(cases[i][0], cases[i][1], out=outs[i])
+                assert mcb.api.last_result.stream_k
+    torch.cuda.synchronize()
+    for i in (0, 1):
+        assert orc.rel_frobenius(gu.from_dev(outs[i])[:64], cases[i][2]) < REL_F32_OUT

@@ -90,3 +90,40 @@ def test_graph_plans_for_msm_chain_and_region(mcb, orc):
     torch.cuda.synchronize()
     assert torch.equal(yb, ref)
     assert mcb.device_status(0) == 0
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_epilogue_chain_plan(mcb, orc, graph):
+    """A Family A chain with two boundaries (MatcorePlan freezes any accepted
+    Family A graph, src/jit_runner.cpp:881-1125): the plan replays the direct
+    call bit for bit; a graph plan rejects a moved boundary and a new shape."""
+    import torch
+    m, k, n = 256, 512, 384
+    x, w, _, _ = _gemm_inputs(m, k, n, seed=5)
+    rng = np.random.default_rng(6)
+    b0 = torch.from_numpy(rng.standard_normal((m, n), dtype=np.float32)).cuda()
+    b1 = gu.to_dev_bf16(gu.bf16_pair(rng.standard_normal((m, n), dtype=np.float32))[0])
+    chain = [("add", b0), "gelu_tanh", ("mul", b1, "right"), "tanh"]
+    ref = mcb.gemm_epilogue(x, w, chain=chain, out_dtype="f32")
+    y = torch.empty(m, n, dtype=torch.float32, device="cuda")
+    plan = mcb.Plan("gemm_epilogue_chain", y, x, w, graph=graph, chain=chain)
+    for _ in range(3):
+        y.fill_(float("nan"))
+        plan.execute(y, x, w, b0, b1)
+        torch.cuda.synchronize()
+        assert torch.equal(y, ref)
+    # and the result is the chain itself (fp64 oracle of the same ops)
+    xf = x.float().cpu().numpy()
+    wf = w.float().cpu().numpy()
+    acc = xf.astype(np.float64) @ wf.astype(np.float64) + b0.cpu().numpy()
+    acc = 0.5 * acc * (1 + np.tanh(0.7978845608 * (acc + 0.044715 * acc ** 3)))
+    expect = np.tanh(b1.float().cpu().numpy() * acc)
+    assert orc.rel_frobenius(gu.from_dev(y), expect) < 1e-5
+    if graph:
+        with pytest.raises(mcb.McbError) as e:
+            plan.execute(y, x, w, b0.clone(), b1)
+        assert e.value.name == "INVALID_ARGUMENT"
+    with pytest.raises(mcb.McbError) as e:
+        plan.execute(y[:128], x[:128], w, b0[:128], b1[:128])
+    assert e.value.name == "SHAPE_MISMATCH"
+    plan.close()
