@@ -31,6 +31,11 @@
 
 #include <atomic>
 #include <cstdlib>
+#include <type_traits>
+
+#ifndef MCB_PAIR_EPI_WARPS
+#define MCB_PAIR_EPI_WARPS 8
+#endif
 
 #include "common.cuh"
 #include "epilogue.cuh"
@@ -71,9 +76,12 @@ struct Params {
 // bias or boundary has no row there.
 // kChain: the general op chain (its own kernel instantiation, so the
 // bias + activation kernels compile exactly as without it).
+// `bias_smem` (optional): the chunk's 32 row-bias bf16 values already staged
+// in shared memory (read as 4 broadcast 16-byte loads instead of global ones).
 template <bool kChain>
 __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (&r)[32],
-                                               int64_t row, int64_t col0) {
+                                               int64_t row, int64_t col0,
+                                               const uint4 *bias_smem = nullptr) {
   if (row >= p.m) return;
   float v[32];
 #pragma unroll
@@ -88,7 +96,7 @@ __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (
         reinterpret_cast<const __nv_bfloat16 *>(e.bias) + col0);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const uint4 w4 = __ldg(bp + q);
+      const uint4 w4 = bias_smem ? bias_smem[q] : __ldg(bp + q);
       const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
@@ -366,8 +374,15 @@ constexpr int P_A_BYTES = BM * BK * 2;        // 16 KiB
 constexpr int P_B_BYTES = P_BN_CTA * BK * 2;  // 16 KiB
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
 constexpr int P_STAGES = 6;
-constexpr int P_THREADS = 320;  // producer, MMA, 8 epilogue warps (2 per TMEM lane quarter)
-constexpr size_t P_SMEM_BYTES = static_cast<size_t>(P_STAGES) * P_STAGE_BYTES + BAR_BYTES + 1024;
+// Epilogue warps: P_EPI_WARPS / 4 per TMEM lane quarter, each owning
+// P_COLS_PER_WARP consecutive columns of the 256-column tile.
+constexpr int P_EPI_WARPS = MCB_PAIR_EPI_WARPS;
+constexpr int P_EPI_THREADS = P_EPI_WARPS * 32;
+constexpr int P_COLS_PER_WARP = BN * 4 / P_EPI_WARPS;
+constexpr int P_THREADS = 64 + P_EPI_THREADS;  // producer, MMA, epilogue warps
+constexpr int P_BIAS_BYTES = P_EPI_WARPS * P_COLS_PER_WARP * 2;  // per warp: its bf16 bias slice
+constexpr size_t P_SMEM_BYTES =
+    static_cast<size_t>(P_STAGES) * P_STAGE_BYTES + BAR_BYTES + P_BIAS_BYTES + 1024;
 
 // ---- stream-K work split ----------------------------------------------------------
 // A unit of a cluster's work: tile `tile`, K blocks [kb0, kb1). `sk_tile`
@@ -459,7 +474,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 512);  // 256 epilogue threads of each CTA (leader's copy)
+      mbar_init(&acc_empty[a], 2 * P_EPI_THREADS);  // epilogue threads of both CTAs (leader's copy)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -562,8 +577,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     }
   } else {
     const int sub = warp & 3;
-    const int half = (warp - 2) >> 2;  // 128-column half of the tile
+    const int cbeg = ((warp - 2) >> 2) * P_COLS_PER_WARP;  // this warp's columns of the tile
     const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    uint8_t *bias_slice = smem + P_STAGES * P_STAGE_BYTES + BAR_BYTES + (warp - 2) * P_COLS_PER_WARP * 2;
     int acc = 0;
     uint32_t acc_phase = 0;
     UnitIter units(p, cluster, nclusters);
@@ -571,10 +587,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     while (units.next(p, nclusters, u)) {
       const int64_t m0 = static_cast<int64_t>(u.tile / p.n_tiles) * (2 * BM) + rank * BM;
       const int64_t n0 = static_cast<int64_t>(u.tile % p.n_tiles) * BN;
+      // Stage this warp's 128-column slice of a row-broadcast bf16 bias in
+      // shared memory while the tile's MMAs still run (lane l: 4 columns).
+      const uint4 *bias_sm = nullptr;
+      if constexpr (!kChain) {
+        const Epilogue &e = p.epi;
+        if (e.bias_mode == 1 && e.bias_bf16 && e.bias_aligned16 &&
+            n0 + cbeg + P_COLS_PER_WARP <= p.n) {
+          // lane l stages bytes [l * B, l * B + B) of the slice, B = 2 * cols / 32
+          using Piece = typename std::conditional<P_COLS_PER_WARP == 128, uint2, uint32_t>::type;
+          const Piece bv = __ldg(reinterpret_cast<const Piece *>(
+                                     reinterpret_cast<const __nv_bfloat16 *>(e.bias) + n0 + cbeg) +
+                                 lane);
+          __syncwarp();  // the previous tile's reads of the slice are done
+          reinterpret_cast<Piece *>(bias_slice)[lane] = bv;
+          __syncwarp();
+          bias_sm = reinterpret_cast<const uint4 *>(bias_slice);
+        }
+      }
       const bool ok = mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.status,
                                      kErrTimeoutAccum, p.spin_limit);
       if constexpr (kSK) {
-        if (named_bar_or(1, 256, !ok)) break;  // every epilogue warp leaves together
+        if (named_bar_or(1, P_EPI_THREADS, !ok)) break;  // every epilogue warp leaves together
       } else {
         if (!ok) break;
       }
@@ -584,11 +618,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                              static_cast<uint32_t>(acc * BN);
       if (!kSK || u.sk_tile < 0) {
 #pragma unroll 1
-        for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+        for (int c = cbeg; c < cbeg + P_COLS_PER_WARP; c += 32) {
           if (n0 + c >= p.n) break;
           uint32_t r[32];
           tmem_ld32_sync(t_row + c, r);
-          epilogue_chunk<kChain>(p, r, row, n0 + c);
+          epilogue_chunk<kChain>(p, r, row, n0 + c, bias_sm ? bias_sm + ((c - cbeg) >> 3) : nullptr);
         }
       } else {
         // Partial tile. Slot layout: float4 q of chunk (32 columns) c for
@@ -599,7 +633,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         float4 *mine = reinterpret_cast<float4 *>(
             p.sk_part + ((static_cast<int64_t>(cluster) * 2 + u.slot) * 2 + rank) * kSlotFloats);
 #pragma unroll 1
-        for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+        for (int c = cbeg; c < cbeg + P_COLS_PER_WARP; c += 32) {
           uint32_t r[32];
           tmem_ld32_sync(t_row + c, r);
 #pragma unroll
@@ -612,7 +646,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         // thread's release (acq_rel atomic at GPU scope); the last arriver's
         // acquire plus the second barrier make the other parts visible to all
         // of its threads.
-        named_bar_sync(1, 256);
+        named_bar_sync(1, P_EPI_THREADS);
         const int64_t t0 = static_cast<int64_t>(u.sk_tile) * p.num_kb;
         const int c_first = sk_cluster_of(p, t0, g);
         const int c_last = sk_cluster_of(p, t0 + p.num_kb - 1, g);
@@ -620,10 +654,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           const int old = atomic_add_acq_rel_gpu(p.sk_ctr + u.sk_tile * 2 + rank, 1);
           *sk_last = old == c_last - c_first ? 1 : 0;
         }
-        named_bar_sync(1, 256);
+        named_bar_sync(1, P_EPI_THREADS);
         if (*sk_last) {
 #pragma unroll 1
-          for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+          for (int c = cbeg; c < cbeg + P_COLS_PER_WARP; c += 32) {
             if (n0 + c >= p.n) break;
             uint32_t r[32];
             tmem_ld32_sync(t_row + c, r);
@@ -707,13 +741,12 @@ bool pair_kernel_enabled() {
   return on;
 }
 
-// MCB_GEMM_STREAM_K=0 in the environment keeps whole tiles (A/B measurement).
+// Stream-K is opt-in (MCB_GEMM_STREAM_K=1, read at every launch): on B200 at
+// config 2's per-GPU shapes its partial-tile traffic and fixup cost more than
+// the idle clusters of the last wave.
 bool stream_k_enabled() {
-  static const bool on = [] {
-    const char *e = getenv("MCB_GEMM_STREAM_K");
-    return !(e && e[0] == '0');
-  }();
-  return on;
+  const char *e = getenv("MCB_GEMM_STREAM_K");
+  return e && e[0] == '1';
 }
 
 }  // namespace

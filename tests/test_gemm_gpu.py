@@ -263,11 +263,15 @@ def test_family_b_chain_tcgen05(mcb, orc, act, bias_mode, bias_op):
     assert e.dtype == torch.float32
 
 
-# ---- stream-K route of the CTA-pair kernel ----------------------------------------
+# ---- stream-K route of the CTA-pair kernel (opt-in: MCB_GEMM_STREAM_K=1) --------
 # Shapes whose whole tiles would leave clusters idle split the K-block ranges
 # of tiles over all clusters; a tile's parts are summed in f32 by whichever
 # CTA arrives last. Checked at the f32-output bar (1e-5) against the fp64
 # oracle, twice in a row (the arrival counters must be back at zero).
+@pytest.fixture
+def stream_k(monkeypatch):
+    monkeypatch.setenv("MCB_GEMM_STREAM_K", "1")  # read by the library at every launch
+
 @pytest.mark.parametrize("shape,w_transposed", [
     ((1024, 4096, 4096), False),   # config 2 rows per GPU at 8 GPUs: 64 tiles
     ((2048, 4096, 4096), False),   # 4 GPUs: 128 tiles, all stream-K
@@ -275,7 +279,7 @@ def test_family_b_chain_tcgen05(mcb, orc, act, bias_mode, bias_op):
     ((1000, 4096, 1032), True),    # ragged M and N, 3-4 parts per tile
     ((512, 8192, 768), False),     # long K: many parts per tile
 ])
-def test_stream_k_f32_out(mcb, orc, shape, w_transposed):
+def test_stream_k_f32_out(mcb, orc, stream_k, shape, w_transposed):
     import torch
     m, k, n = shape
     x, w, b = _inputs(m, k, n, seed=m + n)
@@ -298,7 +302,7 @@ def test_stream_k_f32_out(mcb, orc, shape, w_transposed):
     assert mcb.device_status(0) == 0
 
 
-def test_stream_k_bf16_out_matches_whole_tile_run(mcb, orc):
+def test_stream_k_bf16_out_matches_whole_tile_run(mcb, orc, stream_k):
     """bf16 output at config 2's 1024-row shard: stream-K against the oracle
     at the bf16 bar, and the headline 8192-row shape keeps whole tiles."""
     import torch
@@ -318,7 +322,7 @@ def test_stream_k_bf16_out_matches_whole_tile_run(mcb, orc):
     assert not mcb.api.last_result.stream_k  # 512 tiles: 6.9 waves, whole tiles
 
 
-def test_stream_k_on_two_streams(mcb, orc):
+def test_stream_k_on_two_streams(mcb, orc, stream_k):
     """Stream-K launches from two streams share the device workspace: the
     library orders them, so interleaved calls stay exact."""
     import torch
@@ -340,3 +344,14 @@ def test_stream_k_on_two_streams(mcb, orc):
     torch.cuda.synchronize()
     for i in (0, 1):
         assert orc.rel_frobenius(gu.from_dev(outs[i])[:64], cases[i][2]) < REL_F32_OUT
+
+
+def test_whole_tiles_by_default(mcb):
+    """Without the opt-in, a 1024-row shard keeps whole 256x256 tiles."""
+    import os
+    import torch
+    assert os.environ.get("MCB_GEMM_STREAM_K") != "1"
+    x = torch.zeros(1024, 4096, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(4096, 4096, dtype=torch.bfloat16, device="cuda")
+    mcb.gemm_epilogue(x, w)
+    assert not mcb.api.last_result.stream_k
