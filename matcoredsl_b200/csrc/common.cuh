@@ -93,6 +93,14 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, v
 __device__ __forceinline__ void tma_prefetch_desc(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
+// Prefetch of one 2D box into L2 (no shared memory, no completion signal; a
+// hint that cannot return stale data). Same coordinate rules as a load.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void *tmap, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y)
+               : "memory");
+}
 // 2D tiled load of one box into shared memory; completion is signalled on
 // `bar` as transaction bytes. (x is the innermost coordinate.)
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *tmap, uint64_t *bar,
@@ -265,6 +273,20 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// ---- programmatic dependent launch ------------------------------------------------
+// Waits until the grid this launch depends on (the previous kernel in the
+// stream, when launched with programmatic stream serialization) has completed
+// and its memory operations are visible; returns at once otherwise.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Lets the next kernel in the stream (if launched programmatically) be
+// scheduled onto SMs this grid frees; it still waits in grid_dependency_wait
+// for this grid to complete.
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- named barriers ------------------------------------------------------------------
 // Barrier `id` among `n` threads (a multiple of 32) of this CTA.
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t n) {
@@ -379,6 +401,11 @@ __device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 __device__ __forceinline__ float fmax3(float a, float b, float c) {

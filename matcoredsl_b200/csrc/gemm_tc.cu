@@ -103,8 +103,12 @@ __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (
         const float b0 = __uint_as_float(ws[h] << 16);
         const float b1 = __uint_as_float(ws[h] & 0xffff0000u);
         float &x0 = v[q * 8 + h * 2], &x1 = v[q * 8 + h * 2 + 1];
-        x0 = e.bias_op == 1 ? b0 - x0 : x0 + b0;
-        x1 = e.bias_op == 1 ? b1 - x1 : x1 + b1;
+        if (e.bias_op == 1) {
+          x0 = b0 - x0;
+          x1 = b1 - x1;
+        } else {  // two adds in one packed f32x2 instruction
+          f2_unpack(f2_add(f2_pack(x0, x1), f2_pack(b0, b1)), x0, x1);
+        }
       }
     }
   } else if (e.bias_mode == 1 && e.bias_f16 && e.bias_aligned16 && full_chunk) {
@@ -137,8 +141,20 @@ __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (
   const int act = kChain ? 0 : e.act;
   if (act != 0 && p.y_kind == kOutBf16) {
     if (act == 2) {
+      // GELU-tanh on pairs: 0.5 x (1 + tanh(c0 x (1 + c1 x^2))) with packed
+      // f32x2 multiplies/FMAs (half the FMA-pipe instructions) and the
+      // hardware tanh.
+      const uint64_t c0 = f2_pack(kGeluC0, kGeluC0), c1 = f2_pack(kGeluC1, kGeluC1);
+      const uint64_t one = f2_pack(1.0f, 1.0f), half = f2_pack(0.5f, 0.5f);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = apply_act<true>(v[i], 2);
+      for (int i = 0; i < 16; ++i) {
+        const uint64_t x = f2_pack(v[2 * i], v[2 * i + 1]);
+        const uint64_t u = f2_mul(f2_mul(x, c0), f2_fma(f2_mul(x, x), c1, one));
+        float u0, u1;
+        f2_unpack(u, u0, u1);
+        const uint64_t hx = f2_mul(x, half);
+        f2_unpack(f2_fma(f2_pack(tanh_fast(u0), tanh_fast(u1)), hx, hx), v[2 * i], v[2 * i + 1]);
+      }
     } else {
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = apply_act<true>(v[i], act);
@@ -494,6 +510,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
   cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Set-up above overlaps the previous kernel's tail when this launch is
+  // programmatic. Before the dependency wait only L2 prefetches are issued
+  // (hints: they read nothing into the SM and cannot return stale data):
+  // the first P_STAGES K blocks of this CTA's first tile, so the first loads
+  // after the wait hit L2 instead of HBM.
+  if (warp == 0 && lane == 0 && cluster < p.sk_first_tile) {
+    const int m0 = (cluster / p.n_tiles) * (2 * BM) + static_cast<int>(rank) * BM;
+    const int n0 = (cluster % p.n_tiles) * BN + static_cast<int>(rank) * P_BN_CTA;
+    for (int kb = 0; kb < P_STAGES && kb < p.num_kb; ++kb) {
+      tma_prefetch_l2_2d(&tmap_x, kb * BK, m0);
+      if (p.w_transposed) {
+        tma_prefetch_l2_2d(&tmap_w, kb * BK, n0);
+      } else {
+#pragma unroll
+        for (int j = 0; j < P_BN_CTA / 64; ++j) tma_prefetch_l2_2d(&tmap_w, n0 + j * 64, kb * BK);
+      }
+    }
+  }
+  grid_dependency_wait();
+  grid_launch_dependents();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -741,6 +777,16 @@ bool pair_kernel_enabled() {
   return on;
 }
 
+// Programmatic dependent launch of the CTA-pair kernel; MCB_GEMM_PDL=0 turns
+// it off (A/B measurement).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *e = getenv("MCB_GEMM_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 // Stream-K is opt-in (MCB_GEMM_STREAM_K=1, read at every launch): on B200 at
 // config 2's per-GPU shapes its partial-tile traffic and fixup cost more than
 // the idle clusters of the last wave.
@@ -832,12 +878,26 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
       }
     }
     grid = 2 * static_cast<int>(use_sk ? clusters : (tiles < clusters ? tiles : clusters));
+    // Programmatic stream serialization: the kernel's set-up (barriers, TMEM
+    // allocation, L2 prefetches) may start while the previous kernel in the
+    // stream drains; the kernel waits for it before its first load or store.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(P_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if (chain)
-      gemm_tc_bf16_pair_kernel<true, false><<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
+      e = cudaLaunchKernelEx(&cfg, gemm_tc_bf16_pair_kernel<true, false>, tx, tw, p);
     else if (use_sk)
-      gemm_tc_bf16_pair_kernel<false, true><<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
+      e = cudaLaunchKernelEx(&cfg, gemm_tc_bf16_pair_kernel<false, true>, tx, tw, p);
     else
-      gemm_tc_bf16_pair_kernel<false, false><<<grid, P_THREADS, P_SMEM_BYTES, stream>>>(tx, tw, p);
+      e = cudaLaunchKernelEx(&cfg, gemm_tc_bf16_pair_kernel<false, false>, tx, tw, p);
+    if (e != cudaSuccess) return e;
   } else {
     // Per-device function attribute; cheap, so set on every launch.
     e = cudaFuncSetAttribute(chain ? gemm_tc_bf16_kernel<true> : gemm_tc_bf16_kernel<false>,
