@@ -36,6 +36,7 @@ SOURCES = {
     "simt.cu": [],
     "noalloc.cu": [],
     "msm_tc.cu": [],
+    "chain_tc.cu": [],
     "fp8.cu": [],
     "region.cu": [],
     "plan.cpp": [],

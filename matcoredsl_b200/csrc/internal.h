@@ -109,6 +109,24 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
                                 uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info,
                                 int in_f16 = 0, const GemmStreamK *sk = nullptr);
 
+// Family B chain E = glue(A B) W fused on tcgen05 (chain_tc.cu): bf16 A [M,K],
+// B [K,N1], W [N1,N2] (row-major, 16-byte aligned bases and row strides,
+// K, N1, N2 multiples of 8), E f32 or bf16 (e_kind); `glue` is a bias +
+// activation epilogue over the intermediate (no op chain). The intermediate
+// stays in TMEM / shared memory. cudaErrorNotSupported: nothing launched.
+cudaError_t launch_chain_tc_bf16(const void *a, const void *b, const void *w, void *e, int64_t m,
+                                 int64_t k, int64_t n1, int64_t n2, int64_t lda, int64_t ldb,
+                                 int64_t ldw, int64_t lde, int e_kind, const Epilogue &glue,
+                                 uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info);
+
+// Small Family B chains on CUDA cores in one launch, the intermediate in
+// shared memory in f32 (16 rows per CTA, N1 <= 1536). dt: operand dtype (1 f32,
+// 3 bf16); e_dt: output dtype. cudaErrorNotSupported: nothing launched.
+cudaError_t launch_chain_simt_small(const void *a, const void *b, const void *w, void *e, int dt,
+                                    int e_dt, int64_t m, int64_t k, int64_t n1, int64_t n2,
+                                    int64_t lda, int64_t ldb, int64_t ldw, int64_t lde,
+                                    const Epilogue &glue, cudaStream_t stream, LaunchInfo *info);
+
 // ---- simt.cu: CUDA-core fallbacks for shapes/dtypes the tensor-core kernels do not take
 // dtype codes: 1 f32, 3 bf16, 6 f16 (as in mcb.h)
 cudaError_t launch_gemm_simt(const void *x, int x_dtype, const void *w, int w_dtype, void *y,

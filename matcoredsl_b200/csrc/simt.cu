@@ -481,4 +481,62 @@ cudaError_t launch_msm_simt(const void *q, const void *k, const void *v, void *o
   return cudaGetLastError();
 }
 
+
+namespace {
+// Family B chain on CUDA cores for small problems, with the intermediate
+// kept in shared memory in f32 (the reference's Family B intermediate,
+// src/fusion_emitter_family_b.cpp:231-383): one CTA per CHAIN_RB rows of A
+// computes glue(A B) for its rows into shared memory, then E = C W.
+constexpr int CHAIN_RB = 16;
+__global__ void __launch_bounds__(256) chain_simt_kernel(const void *a, const void *b,
+                                                         const void *w, void *e, int dt,
+                                                         int e_dt, int64_t m, int64_t k,
+                                                         int64_t n1, int64_t n2, int64_t lda,
+                                                         int64_t ldb, int64_t ldw, int64_t lde,
+                                                         Epilogue glue) {
+  extern __shared__ float c_sm[];  // [CHAIN_RB][n1]
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * CHAIN_RB;
+  const int64_t rows = m - r0 < CHAIN_RB ? m - r0 : CHAIN_RB;
+  for (int64_t i = threadIdx.x; i < rows * n1; i += blockDim.x) {
+    const int64_t r = i / n1, c = i % n1;
+    float acc = 0.0f;
+    for (int64_t kk = 0; kk < k; ++kk)
+      acc = fmaf(load_elem(a, dt, (r0 + r) * lda + kk), load_elem(b, dt, kk * ldb + c), acc);
+    c_sm[r * n1 + c] = apply_epilogue<false>(glue, acc, r0 + r, c);
+  }
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < rows * n2; i += blockDim.x) {
+    const int64_t r = i / n2, c = i % n2;
+    float acc = 0.0f;
+    for (int64_t j = 0; j < n1; ++j) acc = fmaf(c_sm[r * n1 + j], load_elem(w, dt, j * ldw + c), acc);
+    store_elem(e, e_dt, (r0 + r) * lde + c, acc);
+  }
+}
+}  // namespace
+
+cudaError_t launch_chain_simt_small(const void *a, const void *b, const void *w, void *e, int dt,
+                                    int e_dt, int64_t m, int64_t k, int64_t n1, int64_t n2,
+                                    int64_t lda, int64_t ldb, int64_t ldw, int64_t lde,
+                                    const Epilogue &glue, cudaStream_t stream, LaunchInfo *info) {
+  if (m == 0 || n2 == 0) return cudaSuccess;
+  const size_t smem = static_cast<size_t>(CHAIN_RB) * static_cast<size_t>(n1) * sizeof(float);
+  if (n1 <= 0 || smem > 96 * 1024 || glue.n_ops != 0) return cudaErrorNotSupported;
+  cudaError_t err = cudaFuncSetAttribute(chain_simt_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+  if (err != cudaSuccess) return err;
+  const int64_t blocks = (m + CHAIN_RB - 1) / CHAIN_RB;
+  if (blocks > 0x7fffffff) return cudaErrorNotSupported;
+  chain_simt_kernel<<<static_cast<unsigned>(blocks), 256, smem, stream>>>(
+      a, b, w, e, dt, e_dt, m, k, n1, n2, lda, ldb, ldw, lde, glue);
+  if (info) {
+    info->launches = 1;
+    info->tile_m = CHAIN_RB;
+    info->tile_n = static_cast<int>(n2);
+    info->ctas = static_cast<int>(blocks);
+    info->set_route("simt_chain_fused");
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace mcb

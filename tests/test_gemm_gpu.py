@@ -238,7 +238,9 @@ def test_config2_full_size_sampled(mcb, orc):
                                                    ("gelu_tanh", "full", "rsub"),
                                                    ("relu", "row", "add")])
 def test_family_b_chain_tcgen05(mcb, orc, act, bias_mode, bias_op):
-    """E = glue(A B) W on tensor cores (two tcgen05 launches, bf16 intermediate)."""
+    """E = glue(A B) W in one tcgen05 kernel: the intermediate stays in TMEM
+    (f32) and shared memory (bf16 operand of the second GEMM), never in HBM;
+    N2 = 320 takes two 256-column tiles of E."""
     import torch
     m, k, n1, n2 = 384, 512, 256, 320
     rng = np.random.default_rng(21)
@@ -256,11 +258,82 @@ def test_family_b_chain_tcgen05(mcb, orc, act, bias_mode, bias_op):
     e = mcb.gemm_chain(gu.to_dev_bf16(ah), gu.to_dev_bf16(bh), gu.to_dev_bf16(wh), bnd_dev,
                        bias_mode=bias_mode, bias_op=bias_op, act=act, out_dtype="f32")
     r = mcb.api.last_result
-    assert r.route == "chain:tcgen05_bf16_gemm_epilogue" and r.kernel_launches == 2
+    assert r.route == "tcgen05_bf16_chain_fused" and r.kernel_launches == 1
     mid = orc.gemm_epilogue(af, bf, bnd_np, bias_mode=bias_mode, bias_op=bias_op, act=act)
     ref = orc.gemm_epilogue(mid.astype(np.float32), wf)
     assert orc.rel_frobenius(gu.from_dev(e), ref) < REL_BF16
     assert e.dtype == torch.float32
+
+
+@pytest.mark.parametrize("shape,out_dtype,act,bias_mode", [
+    ((200, 72, 200, 24), "f32", "gelu_tanh", "row"),     # ragged M, K, N1; N2 < 64
+    ((130, 520, 264, 136), "bf16", "exp", "none"),        # N1 chunks 128+128+8
+    ((1024, 1024, 1024, 256), "bf16", "relu", "full"),    # 8 units, 8 chunks each
+    ((256, 4096, 512, 64), "f32", "sigmoid", "none"),     # long K
+    ((640, 256, 384, 512), "f32", "tanh", "row"),         # two E tiles of 256
+])
+def test_family_b_fused_shapes(mcb, orc, shape, out_dtype, act, bias_mode):
+    """The fused chain kernel at ragged and larger shapes: values past N1 and M
+    are masked to 0 before the second GEMM, so they contribute nothing."""
+    import torch
+    m, k, n1, n2 = shape
+    rng = np.random.default_rng(m + k + n1 + n2)
+    a = rng.standard_normal((m, k), dtype=np.float32) * np.float32(0.5)
+    b = rng.standard_normal((k, n1), dtype=np.float32) / np.float32(np.sqrt(k))
+    w = rng.standard_normal((n1, n2), dtype=np.float32) / np.float32(np.sqrt(n1))
+    if act == "exp":
+        b *= np.float32(0.5)
+    (ah, af), (bh, bf), (wh, wf) = gu.bf16_pair(a), gu.bf16_pair(b), gu.bf16_pair(w)
+    bnd_np = bnd_dev = None
+    if bias_mode == "full":
+        bnd_np = rng.standard_normal((m, n1), dtype=np.float32) * np.float32(0.3)
+        bnd_dev = gu.to_dev_bf16(gu.bf16_pair(bnd_np)[0])
+        bnd_np = gu.bf16_pair(bnd_np)[1]
+    elif bias_mode == "row":
+        bnd_np = rng.standard_normal(n1, dtype=np.float32) * np.float32(0.3)
+        bnd_dev = gu.to_dev_f32(bnd_np)
+    for _ in range(2):
+        e = mcb.gemm_chain(gu.to_dev_bf16(ah), gu.to_dev_bf16(bh), gu.to_dev_bf16(wh), bnd_dev,
+                           bias_mode=bias_mode, act=act, out_dtype=out_dtype)
+        r = mcb.api.last_result
+        assert r.route == "tcgen05_bf16_chain_fused" and r.kernel_launches == 1
+    mid = orc.gemm_epilogue(af, bf, bnd_np, bias_mode=bias_mode, act=act)
+    ref = orc.gemm_epilogue(mid.astype(np.float32), wf)
+    assert orc.rel_frobenius(gu.from_dev(e), ref) < REL_BF16
+    assert e.dtype == (torch.bfloat16 if out_dtype == "bf16" else torch.float32)
+    assert mcb.device_status(0) == 0
+
+
+def test_family_b_large_takes_two_launches(mcb, orc):
+    """A above 2^22 elements: two tcgen05 GEMMs through scratch (faster than
+    the fused kernel, which re-reads A for every 128 intermediate columns)."""
+    m, k, n1, n2 = 4096, 2048, 256, 64
+    rng = np.random.default_rng(6)
+    a = rng.standard_normal((m, k), dtype=np.float32) * np.float32(0.5)
+    b = rng.standard_normal((k, n1), dtype=np.float32) / np.float32(np.sqrt(k))
+    w = rng.standard_normal((n1, n2), dtype=np.float32) / np.float32(np.sqrt(n1))
+    (ah, af), (bh, bf), (wh, wf) = gu.bf16_pair(a), gu.bf16_pair(b), gu.bf16_pair(w)
+    e = mcb.gemm_chain(gu.to_dev_bf16(ah), gu.to_dev_bf16(bh), gu.to_dev_bf16(wh), act="relu",
+                       out_dtype="f32")
+    r = mcb.api.last_result
+    assert r.route == "chain:tcgen05_bf16_gemm_epilogue" and r.kernel_launches == 2
+    rows = gu.sample_rows(m, seed=2)
+    ref = orc.gemm_epilogue(orc.gemm_epilogue(af[rows], bf, act="relu").astype(np.float32), wf)
+    assert orc.rel_frobenius(gu.from_dev(e)[rows], ref) < REL_BF16
+
+
+def test_family_b_unaligned_takes_two_launches(mcb, orc):
+    """K not a multiple of 8 (no TMA rows): the two-GEMM route through scratch."""
+    m, k, n1, n2 = 256, 60, 128, 64
+    rng = np.random.default_rng(5)
+    a, b, w = (rng.standard_normal(sh, dtype=np.float32) * np.float32(0.2)
+               for sh in ((m, k), (k, n1), (n1, n2)))
+    (ah, af), (bh, bf), (wh, wf) = gu.bf16_pair(a), gu.bf16_pair(b), gu.bf16_pair(w)
+    e = mcb.gemm_chain(gu.to_dev_bf16(ah), gu.to_dev_bf16(bh), gu.to_dev_bf16(wh), act="relu",
+                       out_dtype="f32")
+    assert mcb.api.last_result.kernel_launches == 2
+    ref = orc.gemm_epilogue(orc.gemm_epilogue(af, bf, act="relu").astype(np.float32), wf)
+    assert orc.rel_frobenius(gu.from_dev(e), ref) < REL_BF16
 
 
 # ---- stream-K route of the CTA-pair kernel (opt-in: MCB_GEMM_STREAM_K=1) --------
