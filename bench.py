@@ -294,6 +294,35 @@ def run_other_configs(dev, world: int = 1, rank: int = 0, steps: int = 10):
                                "rows_per_gpu": nr, "route": route}
     del qa, sa, qb, sb, c
 
+    # Family B chain E = GELU(A B + b) W at a thin shape (K = 256, N1 = 4096,
+    # N2 = 64, 16384 rows): the fused kernel keeps the 16384x4096
+    # intermediate on chip; the two-GEMM route (MCB_CHAIN_FUSED=0) writes and
+    # reads it through HBM. Replicas at N > 1 (not one of BASELINE's configs).
+    cm, ck, cn1, cn2 = 16384, 256, 4096, 64
+    g.manual_seed(50)
+    ca = torch.randn(cm, ck, generator=g, device=dev).to(torch.bfloat16)
+    cb = (torch.randn(ck, cn1, generator=g, device=dev) / 16).to(torch.bfloat16)
+    cw = (torch.randn(cn1, cn2, generator=g, device=dev) / 64).to(torch.bfloat16)
+    cbias = (torch.randn(cn1, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    ce = torch.empty(cm, cn2, dtype=torch.bfloat16, device=dev)
+    chain = lambda: mcb.gemm_chain(ca, cb, cw, cbias, bias_mode="row", act="gelu_tanh",  # noqa
+                                   out=ce)
+    fl = 2.0 * cm * ck * cn1 + 2.0 * cm * cn1 * cn2
+    times = {}
+    for mode in ("1", "0"):
+        os.environ["MCB_CHAIN_FUSED"] = mode
+        for _ in range(3):
+            chain()
+        times[mode] = (timed(chain, steps), mcb.api.last_result.route)
+    os.environ.pop("MCB_CHAIN_FUSED", None)
+    out["family_b_chain"] = {
+        "shape": [cm, ck, cn1, cn2], "ms": times["1"][0], "route": times["1"][1],
+        "tflops_per_gpu": fl / times["1"][0] / 1e9,
+        "two_gemm_ms": times["0"][0], "two_gemm_route": times["0"][1],
+        "intermediate_hbm_bytes_avoided": 2 * cm * cn1 * 2,
+        "parallelism": "replicas" if world > 1 else "single GPU"}
+    del ca, cb, cw, cbias, ce
+
     # config 5: attention-residual block, B4 S2048 D4096 H32, seed 40; batch sharded
     if 4 % world == 0:
         nb = 4 // world

@@ -1230,20 +1230,24 @@ mcb_status chain_impl(const mcb_tensor *e, const mcb_tensor *a, const mcb_tensor
   if (ep.bias_mode && (s = call.device_ptr(boundary, true, &dbnd))) return s;
   ep.bias = dbnd;
   ep.bias_aligned16 = (reinterpret_cast<uintptr_t>(dbnd) & 15u) == 0;
-  // bf16 operands with TMA-compatible rows and a small problem: one fused
-  // tensor-core kernel, the intermediate kept on chip (TMEM and shared
-  // memory), no scratch. The fused kernel re-reads A once per 128 columns of
-  // the intermediate and runs one unit per 128 rows, so for larger problems
-  // (A or the intermediate above 2^22 elements, or E wider than 512) the two
-  // GEMMs below are faster: measured 908 vs 401 us at 16384x4096x4096x256.
-  const bool small_chain = m * k <= (int64_t{1} << 22) && m * n1 <= (int64_t{1} << 22) &&
-                           n2 <= 512;
+  // bf16 operands with TMA-compatible rows: one fused tensor-core kernel, the
+  // intermediate kept on chip (TMEM and shared memory), no scratch, where it
+  // is the faster route (measured, back to back, B200):
+  //  - tiny problems (M*K*N1 <= 2^25), where the second launch and the
+  //    intermediate's round trip dominate (256x512x256x64: 23.7 vs 30.1 us);
+  //  - K <= 256 with at least 8192 rows and E at most 256 wide, where the
+  //    intermediate outweighs A (16384x256x4096x64: 103.8 vs 114.0 us).
+  // The fused kernel re-reads A once per 128 intermediate columns and runs
+  // one unit per 128 rows, so elsewhere the two GEMMs below win
+  // (16384x4096x4096x256: 927 vs 424 us; 1024x1024x1024x256: 92 vs 29 us).
+  const bool small_chain = m * k * n1 <= (int64_t{1} << 25) && n2 <= 512;
+  const bool thin_chain = k <= 256 && m >= 8192 && n2 <= 256;
   auto al16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
-  static const bool fused_on = [] {
-    const char *v = getenv("MCB_CHAIN_FUSED");  // =0: two-GEMM route (A/B measurement)
-    return !(v && v[0] == '0');
-  }();
-  if (fused_on && small_chain && dt == MCB_DTYPE_BF16 && k > 0 && n1 > 0 && k % 8 == 0 &&
+  // MCB_CHAIN_FUSED (read per call): 0 = always two GEMMs, 2 = fused at any
+  // size (A/B measurement); unset = the rule above.
+  const char *fused_env = getenv("MCB_CHAIN_FUSED");
+  const int fused_mode = fused_env ? atoi(fused_env) : 1;
+  if (fused_mode != 0 && (small_chain || thin_chain || fused_mode == 2) && dt == MCB_DTYPE_BF16 && k > 0 && n1 > 0 && k % 8 == 0 &&
       n1 % 8 == 0 && n2 % 8 == 0 &&
       a->strides[0] % 8 == 0 && b->strides[0] % 8 == 0 && w->strides[0] % 8 == 0 && al16(da) &&
       al16(db) && al16(dw)) {

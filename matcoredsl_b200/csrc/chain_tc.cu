@@ -7,20 +7,20 @@
 // f32 accumulation, E bf16 or f32.
 //
 // One work unit = 128 rows of A and one tile of up to 256 columns of E.
-// Persistent CTAs (one per SM, 224 threads) loop over units:
+// Persistent CTAs (one per SM, 352 threads) loop over units:
 //   warp 0      TMA producer of GEMM 1: for every 128-column chunk j of the
 //               intermediate, K blocks of A (128x64, K-major) and B (64x128,
 //               consumed MN-major from the row-major [K,N1] matrix) into a
 //               3-stage ring.
-//   warp 6      TMA producer of W: rows [128j, 128j+128) x the unit's E
+//   warp 10     TMA producer of W: rows [128j, 128j+128) x the unit's E
 //               columns, as 64-column chunks (MN-major B operand of GEMM 2).
 //   warp 1      TMEM owner (S0 | S1 | E) and the single MMA issuer:
 //               S_j = A B_j (M=128, N=128) into S[j%2]; after S_j, the
 //               GEMM 2 step E += P_{j-1} W_{j-1} (M=128, N=E columns, K=128)
 //               for the previous chunk, so the glue of chunk j-1 overlaps the
 //               MMAs of chunk j.
-//   warps 2-5   glue: thread r owns row r (its TMEM lane). It reads its 128
-//               intermediate values of S_j, applies the glue in f32 (values
+//   warps 2-9   glue: two threads own row r (its TMEM lane), 64 columns
+//               each. They read their intermediate values of S_j, applies the glue in f32 (values
 //               past N1 or M become 0), writes them as bf16 P_j in the
 //               128-byte-swizzled K-major layout GEMM 2 reads, and signals
 //               the MMA warp. At the end of a unit the same threads read E
@@ -52,7 +52,8 @@ constexpr int W_CHUNK_BYTES = CN1 * 64 * 2;  // 16 KiB: 128 rows x 64 columns of
 constexpr int W_BYTES = MAX_N2T / 64 * W_CHUNK_BYTES;
 constexpr int P_CHUNK_BYTES = CM * 64 * 2;   // 16 KiB: 128 rows x 64 intermediate columns
 constexpr int P_BYTES = 2 * P_CHUNK_BYTES;
-constexpr int THREADS = 224;
+constexpr int GLUE_THREADS = 256;  // 8 glue warps: two per TMEM lane quarter, 64 columns each
+constexpr int THREADS = 64 + GLUE_THREADS + 32;  // + producer, MMA, W producer
 constexpr uint32_t S_COL = 0, E_COL = 256;
 constexpr int TMEM_COLS = 512;
 
@@ -99,14 +100,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.s_free[s], 128);
+      mbar_init(&sm.s_free[s], GLUE_THREADS);
     }
-    mbar_init(&sm.p_full, 128);
+    mbar_init(&sm.p_full, GLUE_THREADS);
     mbar_init(&sm.p_free, 1);
     mbar_init(&sm.w_full, 1);
     mbar_init(&sm.w_empty, 1);
     mbar_init(&sm.e_full, 1);
-    mbar_init(&sm.e_empty, 128);
+    mbar_init(&sm.e_empty, GLUE_THREADS);
     mbar_init(&sm.drain, 1);
     sm.abort_flag = 0;
     fence_mbar_init();
@@ -148,7 +149,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
     }
-  } else if (warp == 6) {
+  } else if (warp == 2 + GLUE_THREADS / 32) {
     // ---------------- W producer ----------------
     if (lane == 0) {
       uint32_t wt = 0;
@@ -231,8 +232,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!mbar_wait(&sm.drain, 0, nullptr, p.status, kErrTimeoutDrain)) *abort_flag = 1;
     }
   } else {
-    // ---------------- glue (warps 2-5) and output ----------------
+    // ---------------- glue (warps 2-9) and output ----------------
     const int sub = warp & 3;
+    const int half = (warp - 2) >> 2;  // this warp's 64 columns of each chunk
     const int r_local = sub * 32 + lane;
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(sub * 32) << 16);
     uint8_t *p_row = sm.p + r_local * 128;
@@ -264,8 +266,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (g.bias_mode == 1) {
           // Row bias: thread r stages column col0 + r of this chunk; the four
           // glue warps then read the staged chunk (broadcast).
-          sm.bias[sb][r_local] = col0 + r_local < p.n1 ? load_bias(g, 0, col0 + r_local) : 0.0f;
-          named_bar_sync(1, 128);
+          if (half == 0)
+            sm.bias[sb][r_local] = col0 + r_local < p.n1 ? load_bias(g, 0, col0 + r_local) : 0.0f;
+          named_bar_sync(1, GLUE_THREADS);
         }
         const bool row_ok = row < p.m;
         const int64_t bbase = row * g.ld_bias + col0;
@@ -278,7 +281,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                                   kErrTimeoutAccum)))
           break;
 #pragma unroll 1
-        for (int grp = 0; grp < 4; ++grp) {
+        for (int grp = 2 * half; grp < 2 * half + 2; ++grp) {
           uint32_t r[32];
           tmem_ld32_sync(s_addr + grp * 32, r);
           float v[32];
@@ -384,7 +387,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       tc_fence_after();
 #pragma unroll 1
-      for (int c0 = 0; c0 < p.n2t; c0 += 32) {
+      for (int c0 = half * (p.n2t / 2); c0 < (half + 1) * (p.n2t / 2); c0 += 32) {
         uint32_t r[32];
         tmem_ld32_sync(lane_base + E_COL + c0, r);
         if (row >= p.m) continue;
