@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&pfull[b], 1);
-      mbar_init(&pempty[b], 32 * PROMO_WARPS);
+      mbar_init(&pempty[b], PROMO_WARPS);  // one elected arrival per promotion warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -198,8 +198,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             acc2[c * 8 + i] = f2_fma(s2, f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])),
                                      acc2[c * 8 + i]);
         }
+        // One arrival per warp, after every lane's loads have completed
+        // (per-thread arrivals: config 4 1690 instead of 1955 TFLOP/s).
         tc_fence_before();
-        mbar_arrive(&pempty[buf]);
+        mbar_arrive_warp(&pempty[buf]);
       }
       if (!ok) break;
       float acc[COLS_PER_WARP];

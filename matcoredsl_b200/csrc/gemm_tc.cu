@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
+      mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         epilogue_chunk<kChain>(p, r, row, n0 + c);
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
+      mbar_arrive_warp(&acc_empty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
@@ -490,7 +490,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 2 * P_EPI_THREADS);  // epilogue threads of both CTAs (leader's copy)
+      mbar_init(&acc_empty[a], 2 * P_EPI_WARPS);  // epilogue warps of both CTAs (leader's copy)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -723,7 +723,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive_cluster(acc_empty_leader + acc * 8);
+      mbar_arrive_cluster_warp(acc_empty_leader + acc * 8);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }

@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
+      mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         store_chunk(p, r, row, n0 + c);
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
+      mbar_arrive_warp(&acc_empty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
@@ -298,7 +298,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 512);  // 256 epilogue threads of each CTA (leader's copy)
+      mbar_init(&acc_empty[a], 16);  // 8 epilogue warps of each CTA (leader's copy)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -404,7 +404,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
         store_chunk(p, r, row, n0 + c);
       }
       tc_fence_before();
-      mbar_arrive_cluster(acc_empty_leader + acc * 8);
+      mbar_arrive_cluster_warp(acc_empty_leader + acc * 8);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
