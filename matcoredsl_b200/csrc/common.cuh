@@ -282,6 +282,34 @@ __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// ---- TMA stores ------------------------------------------------------------------
+// Makes this thread's generic-proxy shared-memory writes visible to the async
+// proxy (a TMA store issued afterwards reads them).
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// 2D TMA store of one box from shared memory into the bulk group of the
+// issuing thread; rows and columns outside the tensor map are not written.
+__device__ __forceinline__ void tma_store_2d(const void *tmap, const void *src, int32_t x,
+                                             int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(smem_u32(src)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until the issuing thread's bulk groups have finished reading shared
+// memory, or (bulk_wait_all) have fully completed.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // ---- programmatic dependent launch ------------------------------------------------
 // Waits until the grid this launch depends on (the previous kernel in the
 // stream, when launched with programmatic stream serialization) has completed

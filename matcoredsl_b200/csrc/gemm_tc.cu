@@ -31,6 +31,7 @@
 
 #include <atomic>
 #include <cstdlib>
+#include <cstring>
 #include <type_traits>
 
 #ifndef MCB_PAIR_EPI_WARPS
@@ -57,6 +58,7 @@ struct Params {
   int64_t m, n, k, ld_y;
   int n_tiles, num_tiles, num_kb;
   int w_transposed, y_kind, in_f16;  // y_kind: kOutF32 / kOutBf16 / kOutF16
+  int y_tma;  // CTA-pair kernel: 0, or y_kind (16-bit) when whole tiles are stored by TMA
   void *y;
   uint32_t *status;
   long long spin_limit;  // clock64 cycles a pipeline wait may take before the kernel aborts
@@ -71,19 +73,20 @@ struct Params {
   Epilogue epi;
 };
 
-// Epilogue of one 32-column chunk held by one thread (one output row).
-// Rows past M (the ragged last tile) return before any load: a full [M,N]
-// bias or boundary has no row there.
+// Epilogue of one 32-column chunk held by one thread (one output row):
+// epilogue_values applies the bias / boundary and the activation (row < M
+// only: a full [M,N] bias or boundary has no row past M); epilogue_chunk
+// adds the row guard and stores the row's 32 values itself;
+// epilogue_chunk_tma (CTA-pair kernel, 16-bit outputs) stages the warp's 32
+// rows in shared memory and stores them with one TMA copy.
 // kChain: the general op chain (its own kernel instantiation, so the
 // bias + activation kernels compile exactly as without it).
 // `bias_smem` (optional): the chunk's 32 row-bias bf16 values already staged
 // in shared memory (read as 4 broadcast 16-byte loads instead of global ones).
 template <bool kChain>
-__device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (&r)[32],
-                                               int64_t row, int64_t col0,
-                                               const uint4 *bias_smem = nullptr) {
-  if (row >= p.m) return;
-  float v[32];
+__device__ __forceinline__ void epilogue_values(const Params &p, const uint32_t (&r)[32],
+                                                int64_t row, int64_t col0,
+                                                const uint4 *bias_smem, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
   const Epilogue &e = p.epi;
@@ -163,6 +166,16 @@ __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = apply_act<false>(v[i], act);
   }
+}
+
+template <bool kChain>
+__device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (&r)[32],
+                                               int64_t row, int64_t col0,
+                                               const uint4 *bias_smem = nullptr) {
+  if (row >= p.m) return;
+  float v[32];
+  epilogue_values<kChain>(p, r, row, col0, bias_smem, v);
+  const bool full_chunk = col0 + 32 <= p.n;
   if (p.y_kind == kOutF16) {
     __half *yr = reinterpret_cast<__half *>(p.y) + row * p.ld_y + col0;
     if (full_chunk) {
@@ -208,6 +221,51 @@ __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (
       for (int i = 0; i < 32; ++i)
         if (col0 + i < p.n) yr[i] = v[i];
     }
+  }
+}
+
+// One warp's 32 rows x 32 columns through shared memory: `stage` is the
+// warp's 2 KiB buffer (512-byte aligned), written in the 64-byte-swizzled
+// layout of the TMA box (16-byte piece q of row r at r * 64 + ((q ^ (r >> 1
+// & 3)) << 4): four wavefronts per warp-wide 16-byte store), then lane 0
+// issues the store of box (col0, row0). Rows past M and columns past N fall
+// outside the tensor map and are not written. Per-row 16-byte global stores
+// instead cost the load/store unit one L2 transaction per row and piece.
+template <int kYKind>
+__device__ __forceinline__ void epilogue_chunk_tma(const Params &p, const uint32_t (&r)[32],
+                                                   int64_t row, int64_t col0, int64_t row0,
+                                                   const uint4 *bias_smem, uint8_t *stage,
+                                                   const CUtensorMap *tmap_y, int lane) {
+  float v[32];
+  const bool live = row < p.m;
+  if (live) epilogue_values<false>(p, r, row, col0, bias_smem, v);
+  if (lane == 0) bulk_wait_read_all();  // the previous chunk's store has read the buffer
+  __syncwarp();
+  if (live) {
+    uint8_t *dst = stage + lane * 64;
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 o;
+      if constexpr (kYKind == kOutF16) {
+        o.x = pack_f16x2(v[q * 8 + 0], v[q * 8 + 1]);
+        o.y = pack_f16x2(v[q * 8 + 2], v[q * 8 + 3]);
+        o.z = pack_f16x2(v[q * 8 + 4], v[q * 8 + 5]);
+        o.w = pack_f16x2(v[q * 8 + 6], v[q * 8 + 7]);
+      } else {
+        o.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+        o.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+        o.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+        o.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+      }
+      *reinterpret_cast<uint4 *>(dst + ((q ^ sw) << 4)) = o;
+    }
+  }
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tmap_y, stage, static_cast<int32_t>(col0), static_cast<int32_t>(row0));
+    bulk_commit();
   }
 }
 
@@ -397,8 +455,11 @@ constexpr int P_EPI_THREADS = P_EPI_WARPS * 32;
 constexpr int P_COLS_PER_WARP = BN * 4 / P_EPI_WARPS;
 constexpr int P_THREADS = 64 + P_EPI_THREADS;  // producer, MMA, epilogue warps
 constexpr int P_BIAS_BYTES = P_EPI_WARPS * P_COLS_PER_WARP * 2;  // per warp: its bf16 bias slice
+constexpr int P_YST_BYTES = P_EPI_WARPS * 2048;  // per warp: 32 rows x 32 16-bit outputs
+constexpr int P_YST_OFF = P_STAGES * P_STAGE_BYTES;  // 1024-aligned
+constexpr int P_BAR_OFF = P_YST_OFF + P_YST_BYTES;
 constexpr size_t P_SMEM_BYTES =
-    static_cast<size_t>(P_STAGES) * P_STAGE_BYTES + BAR_BYTES + P_BIAS_BYTES + 1024;
+    static_cast<size_t>(P_BAR_OFF) + BAR_BYTES + P_BIAS_BYTES + 1024;
 
 // ---- stream-K work split ----------------------------------------------------------
 // A unit of a cluster's work: tile `tile`, K blocks [kb0, kb1). `sk_tile`
@@ -460,13 +521,14 @@ struct UnitIter {
 template <bool kChain, bool kSK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     gemm_tc_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
-                             const __grid_constant__ CUtensorMap tmap_w, const Params p) {
+                             const __grid_constant__ CUtensorMap tmap_w,
+                             const __grid_constant__ CUtensorMap tmap_y, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *sa = smem;
   uint8_t *sb = smem + P_STAGES * P_A_BYTES;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_STAGES * P_STAGE_BYTES);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + P_BAR_OFF);
   uint64_t *full = bars;
   uint64_t *empty = bars + P_STAGES;
   uint64_t *acc_full = bars + 2 * P_STAGES;
@@ -615,7 +677,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     const int sub = warp & 3;
     const int cbeg = ((warp - 2) >> 2) * P_COLS_PER_WARP;  // this warp's columns of the tile
     const uint32_t acc_empty_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
-    uint8_t *bias_slice = smem + P_STAGES * P_STAGE_BYTES + BAR_BYTES + (warp - 2) * P_COLS_PER_WARP * 2;
+    uint8_t *bias_slice = smem + P_BAR_OFF + BAR_BYTES + (warp - 2) * P_COLS_PER_WARP * 2;
+    uint8_t *y_stage = smem + P_YST_OFF + (warp - 2) * 2048;
     int acc = 0;
     uint32_t acc_phase = 0;
     UnitIter units(p, cluster, nclusters);
@@ -658,7 +721,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           if (n0 + c >= p.n) break;
           uint32_t r[32];
           tmem_ld32_sync(t_row + c, r);
-          epilogue_chunk<kChain>(p, r, row, n0 + c, bias_sm ? bias_sm + ((c - cbeg) >> 3) : nullptr);
+          const uint4 *bias_c = bias_sm ? bias_sm + ((c - cbeg) >> 3) : nullptr;
+          if (!kChain && p.y_tma == kOutBf16)
+            epilogue_chunk_tma<kOutBf16>(p, r, row, n0 + c, m0 + sub * 32, bias_c, y_stage,
+                                         &tmap_y, lane);
+          else if (!kChain && p.y_tma == kOutF16)
+            epilogue_chunk_tma<kOutF16>(p, r, row, n0 + c, m0 + sub * 32, bias_c, y_stage,
+                                        &tmap_y, lane);
+          else
+            epilogue_chunk<kChain>(p, r, row, n0 + c, bias_c);
         }
       } else {
         // Partial tile. Slot layout: float4 q of chunk (32 columns) c for
@@ -727,6 +798,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
     }
+    // The TMA stores must finish reading shared memory (and land) before
+    // the block exits.
+    if (p.y_tma && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -795,6 +869,14 @@ bool stream_k_enabled() {
   return e && e[0] == '1';
 }
 
+// TMA-staged output stores in the CTA-pair kernel (16-bit outputs with
+// 16-byte aligned rows); MCB_GEMM_Y_TMA=0 (read at every launch) turns them
+// off, for measurement.
+bool y_tma_enabled() {
+  const char *e = getenv("MCB_GEMM_Y_TMA");
+  return !(e && e[0] == '0');
+}
+
 }  // namespace
 
 cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m, int64_t n,
@@ -829,6 +911,17 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
           ? encode_tmap_2d(&tw, dt, w, k, n, ld_w * 2, BK, w_rows, CU_TENSOR_MAP_SWIZZLE_128B)
           : encode_tmap_2d(&tw, dt, w, n, k, ld_w * 2, 64, BK, CU_TENSOR_MAP_SWIZZLE_128B);
   if (!ok_w) return cudaErrorInvalidValue;
+  CUtensorMap ty;
+  memset(&ty, 0, sizeof(ty));
+  int y_tma = 0;
+  if (pair && !chain && (y_kind == kOutBf16 || y_kind == kOutF16) &&
+      reinterpret_cast<uintptr_t>(y) % 16 == 0 && (ld_y * 2) % 16 == 0 && y_tma_enabled()) {
+    if (!encode_tmap_2d(&ty, y_kind == kOutF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                        y, n, m, ld_y * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return cudaErrorInvalidValue;
+    y_tma = y_kind;
+  }
   Params p;
   p.m = m;
   p.n = n;
@@ -847,6 +940,7 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   p.status = status;
   p.spin_limit = kSpinTimeoutCycles;
   p.stall_loads = 0;
+  p.y_tma = y_tma;
   p.sk_first_tile = p.num_tiles;  // whole tiles only unless stream-K applies below
   p.sk_iters = 0;
   p.sk_ctr = nullptr;
@@ -892,11 +986,11 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     if (chain)
-      e = cudaLaunchKernelEx(&cfg, gemm_tc_bf16_pair_kernel<true, false>, tx, tw, p);
+      e = cudaLaunchKernelEx(&cfg, gemm_tc_bf16_pair_kernel<true, false>, tx, tw, ty, p);
     else if (use_sk)
-      e = cudaLaunchKernelEx(&cfg, gemm_tc_bf16_pair_kernel<false, true>, tx, tw, p);
+      e = cudaLaunchKernelEx(&cfg, gemm_tc_bf16_pair_kernel<false, true>, tx, tw, ty, p);
     else
-      e = cudaLaunchKernelEx(&cfg, gemm_tc_bf16_pair_kernel<false, false>, tx, tw, p);
+      e = cudaLaunchKernelEx(&cfg, gemm_tc_bf16_pair_kernel<false, false>, tx, tw, ty, p);
     if (e != cudaSuccess) return e;
   } else {
     // Per-device function attribute; cheap, so set on every launch.

@@ -96,13 +96,8 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void fence_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // TMA store of one 64-column x 128-row box from shared memory (bulk group of
-// the issuing thread), and the waits on that thread's bulk groups: until
-// their shared-memory reads are done, or until they have fully completed.
+// the issuing thread; commit and waits in common.cuh).
 __device__ __forceinline__ void tma_store_4d(const void *tmap, const void *src, int32_t x,
                                              int32_t y, int32_t z, int32_t w) {
   asm volatile(
@@ -110,15 +105,6 @@ __device__ __forceinline__ void tma_store_4d(const void *tmap, const void *src, 
           reinterpret_cast<uint64_t>(tmap)),
       "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
-}
-__device__ __forceinline__ void bulk_commit() {
-  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_wait_read_all() {
-  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_wait_all() {
-  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // K-major SW128 descriptor for the K=16 slice `kk` (0..7) of a 128x128 bf16
