@@ -21,6 +21,7 @@ enum : uint32_t {
   kErrTimeoutAccum = 1u << 2,     // accumulator handoff stalled
   kErrTimeoutDrain = 1u << 3,     // final tensor-core drain stalled
   kErrBadLaunch = 1u << 4,        // kernel saw an impossible configuration
+  kErrTimeoutPeer = 1u << 5,      // another CTA's stream-K partial never arrived
 };
 
 constexpr long long kSpinTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz

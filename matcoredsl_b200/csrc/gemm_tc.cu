@@ -29,6 +29,7 @@
 // bf16 dense tensor peak; ideal HBM traffic X + W + Y = 160 MiB.
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
@@ -64,12 +65,12 @@ struct Params {
   long long spin_limit;  // clock64 cycles a pipeline wait may take before the kernel aborts
   int stall_loads;       // self-test only: the producer issues no loads (the waits must time out)
   // Stream-K (CTA-pair kernel): tiles [0, sk_first_tile) run whole, one per
-  // cluster in turn; the K-block iterations of tiles [sk_first_tile,
-  // num_tiles) (sk_iters of them) are split evenly over the clusters.
+  // cluster in turn; tiles [sk_first_tile, num_tiles) are split in chains
+  // (see the stream-K work split below).
   int sk_first_tile;
-  int64_t sk_iters;
-  int *sk_ctr;    // arrivals per (stream-K tile, CTA rank); 0 between launches
-  float *sk_part; // partial accumulators: per (cluster, slot 0/1, CTA rank) 128x256 f32
+  int sk_tiles, sk_chains, sk_w;  // split tiles, chains, last-share reduction (K blocks)
+  int *sk_flag;    // per (split tile, CTA rank): 1 once the tail's partial is written; 0 between launches
+  float *sk_part;  // tail partial accumulators: per (cluster, CTA rank) 128x256 f32
   Epilogue epi;
 };
 
@@ -462,62 +463,119 @@ constexpr size_t P_SMEM_BYTES =
     static_cast<size_t>(P_BAR_OFF) + BAR_BYTES + P_BIAS_BYTES + 1024;
 
 // ---- stream-K work split ----------------------------------------------------------
-// A unit of a cluster's work: tile `tile`, K blocks [kb0, kb1). `sk_tile`
-// >= 0 marks a partial tile (other clusters hold the rest of its K range):
-// its accumulator is combined through the partial slots and the arrival
-// counter; `slot` is 0 for the cluster's first stream-K unit, else 1.
+// Tiles [0, sk_first_tile) run whole, cluster c taking c, c + G, ... The last
+// sk_tiles tiles (fewer than the G clusters) are split in chains: chain i
+// holds k consecutive tiles and k + 1 consecutive clusters, and its k * KB
+// K-block iterations are cut at k boundaries b_1 < ... < b_k, one strictly
+// inside each tile (b_j in tile j - 1). Cluster j of the chain computes the
+// tail of tile j - 1 (from b_j) first and the head of tile j (up to b_{j+1})
+// last; every split tile thus has exactly two parts, its tail finished early
+// by the next cluster and its head finished last by its owner. The owner's
+// producer fetches the tail's partial accumulator into the freed stages of
+// its ring while its last MMAs run, and its epilogue adds it in. The last
+// cluster of a chain holds only a tail that is also computed last, so its
+// share is `sk_w` K blocks x k/(k+1) shorter (the time its partial takes to
+// write), the other clusters' shares 1/k of that longer.
+enum : int { kUnitWhole = 0, kUnitTail = 1, kUnitHead = 2 };
 struct Unit {
-  int tile, kb0, kb1, sk_tile, slot;
+  int tile, kb0, kb1, role, sk_tile;  // sk_tile: index among the split tiles
 };
 constexpr int64_t kSlotFloats = 2 * BM * BN / 2;  // 128 rows x 256 columns per CTA
 
-__device__ __forceinline__ int64_t sk_begin(const Params &p, int64_t c, int64_t g) {
-  return c * p.sk_iters / g;
+struct ChainPos {
+  int t0, k, j;  // chain's first split tile, tiles in the chain, cluster within it
+};
+// Chain position of stream-K cluster c (false: c takes no stream-K work).
+__host__ __device__ inline bool sk_chain_pos(int sk_tiles, int chains, int c, ChainPos &cp) {
+  if (chains <= 0 || c >= sk_tiles + chains) return false;
+  const int kq = sk_tiles / chains, kr = sk_tiles % chains;
+  const int big = kr * (kq + 2);  // clusters of the kr chains of kq + 1 tiles
+  int i;
+  if (c < big) {
+    i = c / (kq + 2);
+    cp.j = c % (kq + 2);
+    cp.k = kq + 1;
+  } else {
+    i = kr + (c - big) / (kq + 1);
+    cp.j = (c - big) % (kq + 1);
+    cp.k = kq;
+  }
+  cp.t0 = i * kq + (i < kr ? i : kr);
+  return true;
 }
-// The cluster whose stream-K range holds iteration `it`.
-__device__ __forceinline__ int sk_cluster_of(const Params &p, int64_t it, int64_t g) {
-  int64_t c = it * g / p.sk_iters;
-  while (c + 1 < g && sk_begin(p, c + 1, g) <= it) ++c;
-  return static_cast<int>(c);
+// Boundary b_jj (1 <= jj <= k) of a chain of k tiles of kb K blocks each.
+__host__ __device__ inline int sk_boundary(int k, int kb, int w, int jj) {
+  const int delta = (w * k + k) / (k + 1);  // ceil(w * k / (k + 1))
+  const int last = k * kb / (k + 1) - delta;  // the last cluster's share
+  return static_cast<int>(static_cast<int64_t>(jj) * (k * kb - last) / k);
 }
 
-// Units of one cluster in order: whole tiles cluster, cluster + G, ... below
-// sk_first_tile, then its contiguous share of the stream-K iterations
-// (tile-major, K blocks innermost). Producer, MMA and epilogue walk the same
-// sequence.
+// Units of one cluster in order: its whole tiles, then its tail and head
+// parts. Producer, MMA and epilogue walk the same sequence.
 struct UnitIter {
-  int tile;
-  int64_t it, begin, end;
-  __device__ UnitIter(const Params &p, int cluster, int g) : tile(cluster) {
-    begin = it = sk_begin(p, cluster, g);
-    end = sk_begin(p, cluster + 1, g);
+  int tile, phase;  // phase: 0 whole tiles, 1 tail, 2 head, 3 done
+  ChainPos cp;
+  bool in_sk;
+  __device__ UnitIter(const Params &p, int cluster, int g) : tile(cluster), phase(0) {
+    in_sk = sk_chain_pos(p.sk_tiles, p.sk_chains, cluster, cp);
   }
   __device__ bool next(const Params &p, int g, Unit &u) {
-    if (tile < p.sk_first_tile) {
-      u = {tile, 0, p.num_kb, -1, 0};
-      tile += g;
-      return true;
+    if (phase == 0) {
+      if (tile < p.sk_first_tile) {
+        u = {tile, 0, p.num_kb, kUnitWhole, -1};
+        tile += g;
+        return true;
+      }
+      phase = in_sk ? 1 : 3;
     }
-    if (it >= end) return false;
-    const int t = static_cast<int>(it / p.num_kb);
-    const int kb0 = static_cast<int>(it - static_cast<int64_t>(t) * p.num_kb);
-    const int64_t left = end - it;
-    const int kb1 = left < p.num_kb - kb0 ? kb0 + static_cast<int>(left) : p.num_kb;
-    u.tile = p.sk_first_tile + t;
-    u.kb0 = kb0;
-    u.kb1 = kb1;
-    u.sk_tile = (kb0 == 0 && kb1 == p.num_kb) ? -1 : t;
-    u.slot = it == begin ? 0 : 1;
-    it += kb1 - kb0;
-    return true;
+    if (phase == 1) {
+      phase = 2;
+      if (cp.j > 0) {  // tail of split tile t0 + j - 1
+        const int t = cp.t0 + cp.j - 1;
+        const int b = sk_boundary(cp.k, p.num_kb, p.sk_w, cp.j) - (cp.j - 1) * p.num_kb;
+        u = {p.sk_first_tile + t, b, p.num_kb, kUnitTail, t};
+        return true;
+      }
+    }
+    if (phase == 2) {
+      phase = 3;
+      if (cp.j < cp.k) {  // head of split tile t0 + j (owner)
+        const int t = cp.t0 + cp.j;
+        const int b = sk_boundary(cp.k, p.num_kb, p.sk_w, cp.j + 1) - cp.j * p.num_kb;
+        u = {p.sk_first_tile + t, 0, b, kUnitHead, t};
+        return true;
+      }
+    }
+    return false;
   }
 };
 
+// Global flag of one split tile's tail part (per CTA rank): written with
+// release semantics at GPU scope once the partial is in memory, read with
+// acquire by the owner's producer.
+__device__ __forceinline__ void flag_release_gpu(int *f, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+__device__ __forceinline__ int flag_acquire_gpu(const int *f) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+// 16 KiB piece of a partial slot into shared memory, counted on `bar`.
+__device__ __forceinline__ void bulk_load_g2s(void *smem_dst, const void *src, uint32_t bytes,
+                                              uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(smem_dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // kSK: the stream-K instantiation. Its epilogue warps agree on every
-// pipeline wait through a CTA barrier (all leave together on a timeout) and
-// combine partial tiles: each holder of a part writes its accumulator to its
-// slot and counts itself in; the last to arrive adds the other parts to its
-// own and runs the epilogue. Nothing ever waits for another CTA.
+// pipeline wait through a CTA barrier (all leave together on a timeout).
+// The one wait on another cluster is an owner's producer waiting (bounded by
+// spin_limit) for the flag of its tile's tail part, which the next cluster
+// computes as its first unit and never waits for anything itself.
 template <bool kChain, bool kSK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     gemm_tc_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmap_x,
@@ -534,9 +592,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
   uint64_t *acc_full = bars + 2 * P_STAGES;
   uint64_t *acc_empty = acc_full + 2;
   uint64_t *drain = acc_empty + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  uint64_t *part_full = drain + 1;  // stream-K: the tail's partial is in the ring
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(part_full + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-  volatile int *sk_last = reinterpret_cast<volatile int *>(tmem_slot + 2);
+  volatile int *part_stage = reinterpret_cast<volatile int *>(tmem_slot + 2);  // 4 ring stages
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -555,8 +614,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       mbar_init(&acc_empty[a], 2 * P_EPI_WARPS);  // epilogue warps of both CTAs (leader's copy)
     }
     mbar_init(drain, 1);
+    mbar_init(part_full, 1);
     *abort_flag = 0;
-    *sk_last = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -577,10 +636,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
   // (hints: they read nothing into the SM and cannot return stale data):
   // the first P_STAGES K blocks of this CTA's first tile, so the first loads
   // after the wait hit L2 instead of HBM.
-  if (warp == 0 && lane == 0 && cluster < p.sk_first_tile) {
-    const int m0 = (cluster / p.n_tiles) * (2 * BM) + static_cast<int>(rank) * BM;
-    const int n0 = (cluster % p.n_tiles) * BN + static_cast<int>(rank) * P_BN_CTA;
-    for (int kb = 0; kb < P_STAGES && kb < p.num_kb; ++kb) {
+  if (warp == 0 && lane == 0) {
+    UnitIter first(p, cluster, nclusters);
+    Unit u0;
+    if (!first.next(p, nclusters, u0)) u0 = {0, 0, 0, kUnitWhole, -1};
+    const int m0 = (u0.tile / p.n_tiles) * (2 * BM) + static_cast<int>(rank) * BM;
+    const int n0 = (u0.tile % p.n_tiles) * BN + static_cast<int>(rank) * P_BN_CTA;
+    for (int kb = u0.kb0; kb < u0.kb0 + P_STAGES && kb < u0.kb1; ++kb) {
       tma_prefetch_l2_2d(&tmap_x, kb * BK, m0);
       if (p.w_transposed) {
         tma_prefetch_l2_2d(&tmap_w, kb * BK, n0);
@@ -621,6 +683,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           if (++stage == P_STAGES) {
             stage = 0;
             phase ^= 1;
+          }
+        }
+        if constexpr (kSK) {
+          if (u.role == kUnitHead) {
+            // The owner's last unit: once the tail's flag is up, fetch its
+            // partial (this CTA's 128 rows, 128 KiB) into the next four ring
+            // stages as the MMAs free them. The stages are fixed first, then
+            // published by the expect-tx arrival the epilogue acquires.
+            const int *flag = p.sk_flag + u.sk_tile * 2 + rank;
+            const long long t0 = clock64();
+            while (flag_acquire_gpu(flag) != 1) {
+              if (*abort_flag) goto producer_done;
+              if (clock64() - t0 > p.spin_limit) {
+                atomicOr(p.status, kErrTimeoutPeer);
+                *abort_flag = 1;
+                goto producer_done;
+              }
+            }
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            const float *slot = p.sk_part + (static_cast<int64_t>(cluster + 1) * 2 + rank) * kSlotFloats;
+            for (int i = 0; i < 4; ++i) part_stage[i] = (stage + i) % P_STAGES;
+            mbar_arrive_expect_tx(part_full, 4 * P_STAGE_BYTES);
+            for (int i = 0; i < 4; ++i) {
+              if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status, kErrTimeoutEmpty,
+                             p.spin_limit))
+                goto producer_done;
+              bulk_load_g2s(sa + stage * P_A_BYTES, slot + (2 * i) * (P_A_BYTES / 4), P_A_BYTES,
+                            part_full);
+              bulk_load_g2s(sb + stage * P_B_BYTES, slot + (2 * i + 1) * (P_B_BYTES / 4),
+                            P_B_BYTES, part_full);
+              if (++stage == P_STAGES) {
+                stage = 0;
+                phase ^= 1;
+              }
+            }
+            // The copies must have landed before the block can exit.
+            mbar_wait(part_full, 0, abort_flag, p.status, kErrTimeoutPeer, p.spin_limit);
           }
         }
       }
@@ -715,12 +814,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
       const int64_t row = m0 + sub * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
-      if (!kSK || u.sk_tile < 0) {
+      if (!kSK || u.role != kUnitTail) {
+        bool have_part = false;  // stream-K owner: the tail's partial sits in the ring
+        if constexpr (kSK) {
+          if (u.role == kUnitHead) {
+            const bool okp = mbar_wait_warp(part_full, 0, abort_flag, p.status, kErrTimeoutPeer,
+                                            p.spin_limit);
+            if (named_bar_or(1, P_EPI_THREADS, !okp)) break;
+            have_part = true;
+          }
+        }
 #pragma unroll 1
         for (int c = cbeg; c < cbeg + P_COLS_PER_WARP; c += 32) {
           if (n0 + c >= p.n) break;
           uint32_t r[32];
           tmem_ld32_sync(t_row + c, r);
+          if constexpr (kSK) {
+            if (have_part) {
+              // Chunk c / 32 of the slot is one 16 KiB piece: ring stage
+              // part_stage[piece / 2], its A half for even pieces, B for odd.
+              const int piece = c >> 5;
+              const int st = part_stage[piece >> 1];
+              const float4 *src =
+                  reinterpret_cast<const float4 *>(piece & 1 ? sb + st * P_B_BYTES
+                                                             : sa + st * P_A_BYTES) +
+                  sub * 32 + lane;
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 f = src[q * BM];
+                r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + f.x);
+                r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + f.y);
+                r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + f.z);
+                r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + f.w);
+              }
+            }
+          }
           const uint4 *bias_c = bias_sm ? bias_sm + ((c - cbeg) >> 3) : nullptr;
           if (!kChain && p.y_tma == kOutBf16)
             epilogue_chunk_tma<kOutBf16>(p, r, row, n0 + c, m0 + sub * 32, bias_c, y_stage,
@@ -731,14 +859,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
           else
             epilogue_chunk<kChain>(p, r, row, n0 + c, bias_c);
         }
+        // The copies have read the slot (part_full completed): the flag is
+        // ready for the next launch.
+        if (have_part && warp == 2 && lane == 0) p.sk_flag[u.sk_tile * 2 + rank] = 0;
       } else {
-        // Partial tile. Slot layout: float4 q of chunk (32 columns) c for
-        // row r at ((c * 8 + q) * 128 + r) * 4 floats, so one warp-wide
-        // float4 store (32 rows) covers 512 contiguous bytes.
-        const int64_t g = nclusters;
+        // Tail part: its accumulator goes to this cluster's slot. Layout:
+        // float4 q of chunk (32 columns) c for row r at (c * 8 + q) * 128 + r,
+        // so a warp-wide float4 store covers 512 contiguous bytes and chunk c
+        // is 16 KiB at c * 16 KiB. The CTA barrier orders every thread's
+        // stores before the flag's release at GPU scope.
         const int r_local = sub * 32 + lane;
         float4 *mine = reinterpret_cast<float4 *>(
-            p.sk_part + ((static_cast<int64_t>(cluster) * 2 + u.slot) * 2 + rank) * kSlotFloats);
+            p.sk_part + (static_cast<int64_t>(cluster) * 2 + rank) * kSlotFloats);
 #pragma unroll 1
         for (int c = cbeg; c < cbeg + P_COLS_PER_WARP; c += 32) {
           uint32_t r[32];
@@ -749,49 +881,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                 make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
                             __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
         }
-        // The CTA barrier orders every thread's stores before the counting
-        // thread's release (acq_rel atomic at GPU scope); the last arriver's
-        // acquire plus the second barrier make the other parts visible to all
-        // of its threads.
         named_bar_sync(1, P_EPI_THREADS);
-        const int64_t t0 = static_cast<int64_t>(u.sk_tile) * p.num_kb;
-        const int c_first = sk_cluster_of(p, t0, g);
-        const int c_last = sk_cluster_of(p, t0 + p.num_kb - 1, g);
-        if (warp == 2 && lane == 0) {
-          const int old = atomic_add_acq_rel_gpu(p.sk_ctr + u.sk_tile * 2 + rank, 1);
-          *sk_last = old == c_last - c_first ? 1 : 0;
-        }
-        named_bar_sync(1, P_EPI_THREADS);
-        if (*sk_last) {
-#pragma unroll 1
-          for (int c = cbeg; c < cbeg + P_COLS_PER_WARP; c += 32) {
-            if (n0 + c >= p.n) break;
-            uint32_t r[32];
-            tmem_ld32_sync(t_row + c, r);
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-            for (int c2 = c_first; c2 <= c_last; ++c2) {
-              if (c2 == cluster) continue;
-              // A part that starts inside this tile is its holder's first unit.
-              const int slot2 = sk_begin(p, c2, g) >= t0 ? 0 : 1;
-              const float4 *src = reinterpret_cast<const float4 *>(
-                  p.sk_part + ((static_cast<int64_t>(c2) * 2 + slot2) * 2 + rank) * kSlotFloats);
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                const float4 f = __ldcg(src + ((c >> 5) * 8 + q) * BM + r_local);
-                v[4 * q] += f.x;
-                v[4 * q + 1] += f.y;
-                v[4 * q + 2] += f.z;
-                v[4 * q + 3] += f.w;
-              }
-            }
-#pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
-            epilogue_chunk<kChain>(p, r, row, n0 + c);
-          }
-          if (warp == 2 && lane == 0) p.sk_ctr[u.sk_tile * 2 + rank] = 0;  // ready for the next launch
-        }
+        if (warp == 2 && lane == 0) flag_release_gpu(p.sk_flag + u.sk_tile * 2 + rank, 1);
       }
       tc_fence_before();
       mbar_arrive_cluster_warp(acc_empty_leader + acc * 8);
@@ -861,12 +952,46 @@ bool pdl_enabled() {
   return on;
 }
 
-// Stream-K is opt-in (MCB_GEMM_STREAM_K=1, read at every launch): on B200 at
-// config 2's per-GPU shapes its partial-tile traffic and fixup cost more than
-// the idle clusters of the last wave.
-bool stream_k_enabled() {
+// Stream-K mode, read at every launch: MCB_GEMM_STREAM_K=0 never, =1
+// whenever it cuts the busiest cluster's K blocks by 5% (tests and
+// measurement), unset: only when the last wave fills at most 70% of the
+// clusters. Measured on B200 (back to back, bias + GELU, K = N = 4096, 74
+// clusters; rows: tiles in the last wave, stream-K vs whole tiles): 256: 4,
+// 24.2 vs 29.0 us; 768: 48, 28.2 vs 31.2; 3072: 44, 80.0 vs 83.0; 4096: 34,
+// 112.4 vs 118.7; 6144: 14, 166.1 vs 173.0; but 2048: 54, 53.7 vs 53.1 and
+// 1024: 64, 32.5 vs 30.8. A nearly full last wave already runs at the
+// power-capped clock the whole GPU's tensor throughput sets, so its few idle
+// clusters cost little.
+int stream_k_mode() {
   const char *e = getenv("MCB_GEMM_STREAM_K");
-  return e && e[0] == '1';
+  if (!e || !e[0]) return 2;
+  return e[0] == '1' ? 1 : 0;
+}
+
+// K blocks the last cluster of a stream-K chain gives up so that its
+// partial (written last) is in memory when its owner needs it: ~2.5 us of
+// partial write at ~0.38 us per 256x256x64 pair K block.
+constexpr int kSkW = 7;
+
+// The largest K-block load of any stream-K cluster (its share of the split
+// tiles), or -1 when a chain would have an empty part (every boundary must
+// lie strictly inside its tile).
+int sk_max_share(int sk_tiles, int chains, int kb, int w) {
+  const int kq = sk_tiles / chains;
+  int worst = 0;
+  for (int k : {kq, kq + 1}) {
+    if (k < 1 || (k == kq + 1 && sk_tiles % chains == 0)) continue;
+    int prev = 0;
+    for (int jj = 1; jj <= k; ++jj) {
+      const int b = sk_boundary(k, kb, w, jj);
+      if (b <= (jj - 1) * kb || b >= jj * kb) return -1;
+      worst = std::max(worst, b - prev);
+      prev = b;
+    }
+    if (k * kb - prev < 1) return -1;
+    worst = std::max(worst, k * kb - prev);
+  }
+  return worst;
 }
 
 // TMA-staged output stores in the CTA-pair kernel (16-bit outputs with
@@ -942,8 +1067,10 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   p.stall_loads = 0;
   p.y_tma = y_tma;
   p.sk_first_tile = p.num_tiles;  // whole tiles only unless stream-K applies below
-  p.sk_iters = 0;
-  p.sk_ctr = nullptr;
+  p.sk_tiles = 0;
+  p.sk_chains = 0;
+  p.sk_w = kSkW;
+  p.sk_flag = nullptr;
   p.sk_part = nullptr;
   p.epi = epi;
   int grid;
@@ -952,22 +1079,29 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
     int clusters = pair_clusters_resident(device);
     if (clusters > sms / 2) clusters = sms / 2;
     if (clusters < 1) clusters = 1;
-    // Stream-K when whole tiles would leave more than 5% of the last wave's
-    // clusters idle (e.g. 1024 rows: 64 tiles on 74 clusters). All but one
-    // full wave stays whole-tile; the remaining tiles' K-block iterations are
-    // split evenly over every cluster.
-    if (sk && !chain && sk->ctr && sk->part && clusters <= sk->clusters && stream_k_enabled()) {
+    // Stream-K when the last wave leaves clusters idle (4096 rows: 34 tiles
+    // on 74 clusters): every full wave stays whole-tile and the last wave's
+    // tiles are split in chains.
+    const int sk_mode = stream_k_mode();
+    if (sk && !chain && sk->ctr && sk->part && clusters <= sk->clusters && sk_mode != 0) {
       const int64_t g = clusters;
       const int64_t waves = (tiles + g - 1) / g;
-      const int64_t full = tiles / g;
-      const int64_t dp = full >= 2 ? (full - 1) * g : 0;
-      const int64_t sk_tiles = tiles - dp;
-      const int64_t iters = sk_tiles * p.num_kb;
-      if (tiles * 100 < waves * g * 95 && iters >= 4 * g && sk_tiles <= sk->max_tiles) {
+      const int64_t dp = (waves - 1) * g;
+      const int64_t skt = tiles - dp;  // 1..g
+      const int64_t chains = std::min(g - skt, skt);
+      const int share = chains >= 1 ? sk_max_share(static_cast<int>(skt), static_cast<int>(chains),
+                                                   p.num_kb, kSkW)
+                                    : -1;
+      // Worth it when the busiest cluster's K blocks drop by 5% or more
+      // (and, by default, when the last wave is at most 70% full).
+      if (share > 0 && skt <= sk->max_tiles &&
+          ((waves - 1) * p.num_kb + share) * 100 <= waves * p.num_kb * 95 &&
+          (sk_mode == 1 || 10 * skt <= 7 * g)) {
         use_sk = true;
         p.sk_first_tile = static_cast<int>(dp);
-        p.sk_iters = iters;
-        p.sk_ctr = sk->ctr;
+        p.sk_tiles = static_cast<int>(skt);
+        p.sk_chains = static_cast<int>(chains);
+        p.sk_flag = sk->ctr;
         p.sk_part = sk->part;
       }
     }

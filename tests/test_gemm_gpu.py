@@ -355,8 +355,10 @@ def stream_k(monkeypatch):
     ((1024, 4096, 4096), False),   # config 2 rows per GPU at 8 GPUs: 64 tiles
     ((2048, 4096, 4096), False),   # 4 GPUs: 128 tiles, all stream-K
     ((4096, 2048, 4096), False),   # 2 GPUs: whole-tile waves, then stream-K
-    ((1000, 4096, 1032), True),    # ragged M and N, 3-4 parts per tile
-    ((512, 8192, 768), False),     # long K: many parts per tile
+    ((1000, 4096, 1032), True),    # ragged M and N: 20 tiles in chains of one
+    ((512, 8192, 768), False),     # long K: 6 tiles, 12 clusters
+    ((256, 4096, 256), False),     # one tile, split over two clusters
+    ((4096, 1000, 4096), False),   # K not a multiple of 64: the last K block is ragged
 ])
 def test_stream_k_f32_out(mcb, orc, stream_k, shape, w_transposed):
     import torch
@@ -425,12 +427,23 @@ def test_stream_k_on_two_streams(mcb, orc, stream_k):
         assert orc.rel_frobenius(gu.from_dev(outs[i])[:64], cases[i][2]) < REL_F32_OUT
 
 
-def test_whole_tiles_by_default(mcb):
-    """Without the opt-in, a 1024-row shard keeps whole 256x256 tiles."""
-    import os
+def test_stream_k_default_policy(mcb, orc, monkeypatch):
+    """By default stream-K splits only a last wave that fills at most 70% of
+    the 74 clusters: 1024, 2048 and 8192 rows (64, 54 and 68 tiles in the
+    last wave) keep whole tiles, 4096 rows (34) splits them, and the result
+    matches the whole-tile run (MCB_GEMM_STREAM_K=0) to f32 rounding."""
     import torch
-    assert os.environ.get("MCB_GEMM_STREAM_K") != "1"
-    x = torch.zeros(1024, 4096, dtype=torch.bfloat16, device="cuda")
+    monkeypatch.delenv("MCB_GEMM_STREAM_K", raising=False)
     w = torch.zeros(4096, 4096, dtype=torch.bfloat16, device="cuda")
-    mcb.gemm_epilogue(x, w)
+    for rows in (1024, 2048, 8192):
+        mcb.gemm_epilogue(torch.zeros(rows, 4096, dtype=torch.bfloat16, device="cuda"), w)
+        assert not mcb.api.last_result.stream_k
+    x, wn, _ = _inputs(4096, 4096, 4096, seed=77)
+    tx, tw = gu.to_dev_bf16(gu.bf16_pair(x)[0]), gu.to_dev_bf16(gu.bf16_pair(wn)[0])
+    y = mcb.gemm_epilogue(tx, tw, out=torch.empty(4096, 4096, device="cuda"))
+    assert mcb.api.last_result.stream_k
+    monkeypatch.setenv("MCB_GEMM_STREAM_K", "0")
+    y0 = mcb.gemm_epilogue(tx, tw, out=torch.empty(4096, 4096, device="cuda"))
     assert not mcb.api.last_result.stream_k
+    assert orc.rel_frobenius(gu.from_dev(y), gu.from_dev(y0).astype(np.float64)) < 1e-6
+    assert mcb.device_status(0) == 0

@@ -40,12 +40,19 @@ def test_bf16_full_bias_padded_output(mcb, orc):
     assert np.all(big[:, n:] == -7.0), "padding of the host output was overwritten"
     ref = orc.gemm_epilogue(xf, wf, bias, bias_mode="full", bias_op="rsub", act="tanh")
     assert orc.rel_frobenius(out, ref) < 1e-5
-    # The serial staging path (timed calls) gives the same bytes.
+    # The serial staging path (timed calls, one launch) agrees to f32
+    # rounding: its 22 tiles and the chunks' 8 each are split differently by
+    # stream-K, so the two sum the K blocks of some tiles in a different
+    # order. The same call twice gives the same bytes.
     serial = np.empty((m, n), np.float32)
     mcb.gemm_epilogue(_bf16_host(xh), _bf16_host(wh), bias, bias_mode="full", bias_op="rsub",
                       act="tanh", out=serial, flags=_abi.EXEC_TIME)
     assert mcb.api.last_result.kernel_launches == 1
-    np.testing.assert_array_equal(out, serial)
+    assert orc.rel_frobenius(serial, out.astype(np.float64)) < 1e-5
+    again = np.empty((m, n), np.float32)
+    mcb.gemm_epilogue(_bf16_host(xh), _bf16_host(wh), bias, bias_mode="full", bias_op="rsub",
+                      act="tanh", out=again)
+    np.testing.assert_array_equal(out, again)
 
 
 def test_bf16_row_bias_bf16_output_many_chunks(mcb, orc):
