@@ -13,6 +13,8 @@
 // threads stride over output columns so global loads of B/D are coalesced
 // and every thread carries R independent reduction chains to hide the
 // dependent-add latency.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -321,6 +323,11 @@ __global__ void __launch_bounds__(TX *TY) strict_tiled_kernel(
     cp_async_commit();
   };
 
+  // When launched programmatically (the second GEMM of a two-pass pair):
+  // wait for the previous grid, whose output this one reads, and let the
+  // next launch start its own set-up. No-ops otherwise.
+  grid_dependency_wait();
+  grid_launch_dependents();
   float acc[MR][NR];
 #pragma unroll
   for (int r = 0; r < MR; ++r)
@@ -519,17 +526,26 @@ __global__ void __launch_bounds__(256, 2) strict_big_kernel(
 template <int MR, int NR>
 cudaError_t launch_tiled_variant(const float *a, const float *b, float *c, int64_t m, int64_t k,
                                  int64_t n, int64_t lda, int64_t ldb, int64_t ldc, bool vec,
-                                 cudaStream_t stream, LaunchInfo *info) {
+                                 bool pdl, cudaStream_t stream, LaunchInfo *info) {
   constexpr int TX = 16, TY = 8, TM = TY * MR, TN = TX * NR;
   const int64_t gy = (m + TM - 1) / TM, gx = (n + TN - 1) / TN;
   if (gy > 65535 || gx > 0x7fffffff) return cudaErrorInvalidConfiguration;
   const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy));
-  if (vec)
-    strict_tiled_kernel<MR, NR, TX, TY, true><<<grid, TX * TY, 0, stream>>>(a, b, c, m, k, n, lda,
-                                                                          ldb, ldc);
-  else
-    strict_tiled_kernel<MR, NR, TX, TY, false><<<grid, TX * TY, 0, stream>>>(a, b, c, m, k, n,
-                                                                           lda, ldb, ldc);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(TX * TY, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e =
+      vec ? cudaLaunchKernelEx(&cfg, strict_tiled_kernel<MR, NR, TX, TY, true>, a, b, c, m, k, n,
+                               lda, ldb, ldc)
+          : cudaLaunchKernelEx(&cfg, strict_tiled_kernel<MR, NR, TX, TY, false>, a, b, c, m, k, n,
+                               lda, ldb, ldc);
+  if (e != cudaSuccess) return e;
   if (info) {
     info->launches += 1;
     info->tile_m = TM;
@@ -548,7 +564,7 @@ cudaError_t launch_tiled_variant(const float *a, const float *b, float *c, int64
 // when every row allows them.
 cudaError_t launch_tiled(const float *a, const float *b, float *c, int64_t m, int64_t k, int64_t n,
                          int64_t lda, int64_t ldb, int64_t ldc, int sms, cudaStream_t stream,
-                         LaunchInfo *info) {
+                         LaunchInfo *info, bool pdl = false) {
   const auto al16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
   const bool vec = k % 4 == 0 && n % 4 == 0 && lda % 4 == 0 && ldb % 4 == 0 &&
                    (k == 0 || (al16(a) && al16(b)));
@@ -569,10 +585,10 @@ cudaError_t launch_tiled(const float *a, const float *b, float *c, int64_t m, in
     return cudaGetLastError();
   }
   if (outputs / 8 >= 4 * warp_slots && n >= 64)
-    return launch_tiled_variant<2, 4>(a, b, c, m, k, n, lda, ldb, ldc, vec, stream, info);
+    return launch_tiled_variant<2, 4>(a, b, c, m, k, n, lda, ldb, ldc, vec, pdl, stream, info);
   if (outputs / 4 >= warp_slots && n >= 32)
-    return launch_tiled_variant<2, 2>(a, b, c, m, k, n, lda, ldb, ldc, vec, stream, info);
-  return launch_tiled_variant<1, 2>(a, b, c, m, k, n, lda, ldb, ldc, vec, stream, info);
+    return launch_tiled_variant<2, 2>(a, b, c, m, k, n, lda, ldb, ldc, vec, pdl, stream, info);
+  return launch_tiled_variant<1, 2>(a, b, c, m, k, n, lda, ldb, ldc, vec, pdl, stream, info);
 }
 
 }  // namespace
@@ -599,8 +615,16 @@ cudaError_t launch_strict_pair_two_pass(const float *a, const float *b, const fl
     info->ctas = 0;
   }
   if (m == 0 || p == 0) return cudaSuccess;
+  // The second GEMM is launched programmatically: its CTAs are scheduled as
+  // the first one's finish and wait in-kernel for the whole first grid
+  // (MCB_STRICT_PDL=0 turns this off, for measurement).
+  static const bool pdl = [] {
+    const char *v = getenv("MCB_STRICT_PDL");
+    return !(v && v[0] == '0');
+  }();
   cudaError_t err = launch_tiled(a, b, c_buf, m, k, n, lda, ldb, n, sms, stream, info);
-  if (err == cudaSuccess) err = launch_tiled(c_buf, d, e, m, n, p, n, ldd, lde, sms, stream, info);
+  if (err == cudaSuccess)
+    err = launch_tiled(c_buf, d, e, m, n, p, n, ldd, lde, sms, stream, info, pdl);
   if (info) info->set_route("strict_f32_simt_pair_two_pass");
   return err;
 }
