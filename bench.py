@@ -405,6 +405,14 @@ def run_profile_config(cfg: int, steps: int, warmup: int):
         out = torch.empty_like(partial)
         fn = lambda: mcb.block_attn_res(blocks, partial, query, block_count=16,  # noqa: E731
                                         has_partial=True, eps=1e-6, out=out)
+    elif cfg == 11:  # Family B chain at the bench's side-line shape (fused tcgen05 kernel)
+        a = torch.randn(16384, 256, generator=g, device=dev).to(torch.bfloat16)
+        b = (torch.randn(256, 4096, generator=g, device=dev) / 16).to(torch.bfloat16)
+        w = (torch.randn(4096, 64, generator=g, device=dev) / 64).to(torch.bfloat16)
+        bias = (torch.randn(4096, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        e = torch.empty(16384, 64, dtype=torch.bfloat16, device=dev)
+        fn = lambda: mcb.gemm_chain(a, b, w, bias, bias_mode="row", act="gelu_tanh",  # noqa
+                                    out=e)
     elif cfg == 7:  # int8 x int8 -> int32 on tcgen05, 4096^3
         a = torch.randint(-128, 128, (4096, 4096), generator=g, device=dev, dtype=torch.int8)
         b = torch.randint(-128, 128, (4096, 4096), generator=g, device=dev, dtype=torch.int8)
@@ -668,7 +676,7 @@ def main():
                     help="skip the host-buffer end-to-end leg (used for short profiling runs)")
     ap.add_argument("--no-other-configs", action="store_true",
                     help="skip the configs 1/3/4/5 measurements reported beside the headline")
-    ap.add_argument("--profile-config", type=int, choices=[1, 2, 3, 4, 5, 6, 7, 8, 9, 10],
+    ap.add_argument("--profile-config", type=int, choices=list(range(1, 12)),
                     help="only launch this config's operator (for ncu captures); no JSON line")
     args = ap.parse_args()
     if args.profile_config:
