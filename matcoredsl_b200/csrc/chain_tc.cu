@@ -70,7 +70,9 @@ struct Smem {
   uint32_t tmem_slot;
   int abort_flag;
   float bias[2][CN1];  // a chunk's row bias in f32 (two buffers, alternating chunks)
+  alignas(16) float bias_row[4096];  // the whole row bias when N1 <= 4096, staged once
 };
+constexpr int kBiasRowMax = 4096;
 constexpr size_t SMEM_BYTES = sizeof(Smem) + 1024;
 
 struct Params {
@@ -241,6 +243,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int rsw = r_local & 7;
     uint32_t sc = 0, pc = 0, uc = 0;
     bool ok = true;
+    // A row bias of at most kBiasRowMax columns is the same for every unit:
+    // staged once, so no chunk waits for a global load and a barrier.
+    const bool bias_whole = p.glue.bias_mode == 1 && p.n1 <= kBiasRowMax;
+    if (bias_whole) {
+      for (int64_t i = threadIdx.x - 64; i < p.n1; i += GLUE_THREADS)
+        sm.bias_row[i] = load_bias(p.glue, 0, i);
+      named_bar_sync(1, GLUE_THREADS);
+    }
     for (int64_t u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++uc) {
       const int64_t row = (u / p.n2_tiles) * CM + r_local;
       const int64_t n0 = (u % p.n2_tiles) * p.n2t;
@@ -262,8 +272,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         // Consecutive chunks (also across units) alternate bias buffers, so
         // the barrier of chunk c+1 orders chunk c's reads before chunk c+2's
         // writes into the same buffer.
-        const float *bs = sm.bias[sb];
-        if (g.bias_mode == 1) {
+        const float *bs = bias_whole ? sm.bias_row + col0 : sm.bias[sb];
+        if (g.bias_mode == 1 && !bias_whole) {
           // Row bias: thread r stages column col0 + r of this chunk; the four
           // glue warps then read the staged chunk (broadcast).
           if (half == 0)
@@ -276,10 +286,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                               ((reinterpret_cast<uintptr_t>(g.bias) +
                                 bbase * (g.bias_bf16 ? 2 : 4)) & 15u) == 0;
         const uint32_t s_addr = lane_base + S_COL + sb * CN1;
-        // P is free once GEMM 2 of the previous chunk has read it.
-        if (!(ok = mbar_wait_warp(&sm.p_free, (pc & 1) ^ 1, abort_flag, p.status,
-                                  kErrTimeoutAccum)))
-          break;
+        bool p_ready = false;
 #pragma unroll 1
         for (int grp = 2 * half; grp < 2 * half + 2; ++grp) {
           uint32_t r[32];
@@ -363,6 +370,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int i = 0; i < 32; ++i)
               if (cg + i >= p.n1) v[i] = 0.0f;
           }
+          // P is free once GEMM 2 of the previous chunk has read it: waited
+          // for only now, so the first group's loads and math overlap it.
+          if (!p_ready) {
+            if (!(ok = mbar_wait_warp(&sm.p_free, (pc & 1) ^ 1, abort_flag, p.status,
+                                      kErrTimeoutAccum)))
+              break;
+            p_ready = true;
+          }
           // 32 columns = 4 granules of 16 bytes of this row of P.
           uint8_t *pc_base = p_row + (grp >> 1) * P_CHUNK_BYTES;
 #pragma unroll
@@ -374,6 +389,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                            pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
           }
         }
+        if (!ok) break;
         tc_fence_before();
         mbar_arrive(&sm.s_free[sb]);
         ++sc;
