@@ -171,6 +171,15 @@ MCB_API mcb_status mcb_device_status(int32_t device, uint32_t *word, int32_t cle
  * device; allocates 112 KiB for the call. */
 MCB_API mcb_status mcb_device_timeout_selftest_v1(int32_t device,
                                                   uint64_t spin_limit_cycles) MCB_NOEXCEPT;
+/* The same for the one wait on another CTA cluster: a stream-K GEMM (two
+ * 256x256 tiles, K = 4096, each split over two clusters) whose tail parts
+ * never raise their ready flags, so each owner's wait gives up after
+ * `spin_limit_cycles` (same range). Returns MCB_STATUS_DEVICE_TIMEOUT when
+ * the kernel returned and reported it (bit 5, "another CTA's stream-K partial
+ * never arrived", sticky like bit 0). Synchronises the device; allocates
+ * about 8.3 MiB for the call. */
+MCB_API mcb_status mcb_device_peer_timeout_selftest_v1(int32_t device,
+                                                       uint64_t spin_limit_cycles) MCB_NOEXCEPT;
 /* Ok when `device` is an sm_100 GPU this build can run on; replaces
  * detail::cudaCandidateAvailable (compiler/lib/runtime/closed_cuda_candidate_v1.h:13). */
 MCB_API mcb_status mcb_candidate_available(int32_t device) MCB_NOEXCEPT;

@@ -144,6 +144,7 @@ SIGNATURES = {
     "mcb_status_message": (ctypes.c_char_p, [ctypes.c_int32]),
     "mcb_device_status": (ctypes.c_int32, [ctypes.c_int32, _P(ctypes.c_uint32), ctypes.c_int32]),
     "mcb_device_timeout_selftest_v1": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_uint64]),
+    "mcb_device_peer_timeout_selftest_v1": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_uint64]),
     # test support (host-side fault injection); exercised from C in tests/adapter/
     "mcb_test_set_runtime_hooks_v1": (ctypes.c_int32, [ctypes.c_void_p]),
     "mcb_candidate_available": (ctypes.c_int32, [ctypes.c_int32]),

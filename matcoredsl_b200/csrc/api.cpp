@@ -1738,6 +1738,53 @@ MCB_API mcb_status mcb_device_timeout_selftest_v1(int32_t device,
   return (word & kTimeoutFullBit) ? MCB_STATUS_DEVICE_TIMEOUT : MCB_STATUS_CANDIDATE_FAILURE;
 }
 
+MCB_API mcb_status mcb_device_peer_timeout_selftest_v1(int32_t device,
+                                                       uint64_t spin_limit_cycles) noexcept {
+  if (spin_limit_cycles < 10000 || spin_limit_cycles > 4000000000ull)
+    return MCB_STATUS_INVALID_ARGUMENT;
+  if (hooks()) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
+  mcb_exec ex{};
+  ex.abi_version = MCB_ABI_VERSION_V1;
+  ex.struct_size = sizeof(ex);
+  ex.device = device;
+  int dev;
+  mcb_status s = resolve_device(&ex, &dev);
+  if (s) return s;
+  DeviceGuard g(dev);
+  if (!g.ok) return MCB_STATUS_CANDIDATE_FAILURE;
+  DeviceCtx *c;
+  if ((s = init_ctx(dev, &c))) return s;
+  // X 256x4096, W 4096x512, Y 256x512 bf16, the partial slots of four
+  // clusters (two CTAs each) and four zeroed flags in one allocation.
+  void *buf = nullptr;
+  const size_t xb = 256 * 4096 * 2, wb = 4096 * 512 * 2, yb = 256 * 512 * 2;
+  const size_t pb = 4 * 2 * static_cast<size_t>(mcb::kGemmStreamKSlotFloats) * 4, fb = 256;
+  if (cudaMalloc(&buf, xb + wb + yb + pb + fb) != cudaSuccess) {
+    cudaGetLastError();
+    return MCB_STATUS_ALLOCATION_FAILURE;
+  }
+  uint8_t *base = static_cast<uint8_t *>(buf);
+  int *flags = reinterpret_cast<int *>(base + xb + wb + yb + pb);
+  cudaError_t err = cudaMemset(flags, 0, fb);
+  if (err == cudaSuccess)
+    err = mcb::launch_gemm_tc_peer_stall_selftest(
+        base, base + xb, base + xb + wb, reinterpret_cast<float *>(base + xb + wb + yb), flags,
+        static_cast<long long>(spin_limit_cycles), c->status, nullptr);
+  if (err == cudaSuccess) err = cudaDeviceSynchronize();
+  cudaFree(buf);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+  uint32_t word = 0;
+  if (cudaMemcpy(&word, c->status, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  // The stalled wait must have been reported; the word stays set (sticky)
+  // until the caller clears it with mcb_device_status.
+  constexpr uint32_t kTimeoutPeerBit = 1u << 5;  // kErrTimeoutPeer of the device status word
+  return (word & kTimeoutPeerBit) ? MCB_STATUS_DEVICE_TIMEOUT : MCB_STATUS_CANDIDATE_FAILURE;
+}
+
 MCB_API mcb_status mcb_test_set_runtime_hooks_v1(const mcb_runtime_hooks *h) noexcept {
   if (!h) {
     if (g_hooks_on.exchange(false, std::memory_order_acq_rel)) {

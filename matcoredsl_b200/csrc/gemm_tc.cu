@@ -71,6 +71,7 @@ struct Params {
   int sk_tiles, sk_chains, sk_w;  // split tiles, chains, last-share reduction (K blocks)
   int *sk_flag;    // per (split tile, CTA rank): 1 once the tail's partial is written; 0 between launches
   float *sk_part;  // tail partial accumulators: per (cluster, CTA rank) 128x256 f32
+  int sk_test_no_release;  // self-test only: tails never raise their flag (owners' waits run out)
   Epilogue epi;
 };
 
@@ -882,7 +883,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
                             __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
         }
         named_bar_sync(1, P_EPI_THREADS);
-        if (warp == 2 && lane == 0) flag_release_gpu(p.sk_flag + u.sk_tile * 2 + rank, 1);
+        if (warp == 2 && lane == 0 && !p.sk_test_no_release)
+          flag_release_gpu(p.sk_flag + u.sk_tile * 2 + rank, 1);
       }
       tc_fence_before();
       mbar_arrive_cluster_warp(acc_empty_leader + acc * 8);
@@ -1072,6 +1074,7 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   p.sk_w = kSkW;
   p.sk_flag = nullptr;
   p.sk_part = nullptr;
+  p.sk_test_no_release = 0;
   p.epi = epi;
   int grid;
   bool use_sk = false;
@@ -1184,6 +1187,55 @@ cudaError_t launch_gemm_tc_stall_selftest(const void *x, const void *w, void *y,
                                        static_cast<int>(SMEM_BYTES));
   if (e != cudaSuccess) return e;
   gemm_tc_bf16_kernel<false><<<1, THREADS, SMEM_BYTES, stream>>>(tx, tw, p);
+  return cudaGetLastError();
+}
+
+// Self-test of the one wait on another cluster: a stream-K launch of two
+// 256x256 tiles (K = 4096: chains of one tile over two clusters) whose tails
+// never raise their flags, so each owner's producer gives up after
+// `spin_limit` cycles, records kErrTimeoutPeer and aborts its CTA; the
+// owner's epilogue leaves through its own bounded wait, the tails finish
+// normally. x: 256x4096, w: 4096x512 bf16 (16-byte aligned, never needed
+// valid), y: 256x512 bf16; `part` 4 clusters x 2 ranks x 128 KiB, `flags`
+// 4 ints, zero.
+cudaError_t launch_gemm_tc_peer_stall_selftest(const void *x, const void *w, void *y, float *part,
+                                               int *flags, long long spin_limit, uint32_t *status,
+                                               cudaStream_t stream) {
+  constexpr int kM = 256, kN = 512, kK = 4096;
+  CUtensorMap tx, tw, ty;
+  memset(&ty, 0, sizeof(ty));
+  if (!encode_tmap_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, kK, kM, kK * 2, BK, BM,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, kN, kK, kN * 2, 64, BK,
+                      CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  Params p = {};
+  p.m = kM;
+  p.n = kN;
+  p.k = kK;
+  p.ld_y = kN;
+  p.n_tiles = kN / BN;
+  p.num_tiles = p.n_tiles;
+  p.num_kb = kK / BK;
+  p.y_kind = kOutBf16;
+  p.y = y;
+  p.status = status;
+  p.spin_limit = spin_limit;
+  p.sk_first_tile = 0;
+  p.sk_tiles = p.num_tiles;
+  p.sk_chains = p.num_tiles;
+  p.sk_w = kSkW;
+  p.sk_flag = flags;
+  p.sk_part = part;
+  p.sk_test_no_release = 1;
+  if (sk_max_share(p.sk_tiles, p.sk_chains, p.num_kb, kSkW) <= 0) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_bf16_pair_kernel<false, true>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(P_SMEM_BYTES));
+  if (e != cudaSuccess) return e;
+  const int clusters = p.sk_tiles + p.sk_chains;  // chains of one tile: two clusters each
+  gemm_tc_bf16_pair_kernel<false, true><<<2 * clusters, P_THREADS, P_SMEM_BYTES, stream>>>(
+      tx, tw, ty, p);
   return cudaGetLastError();
 }
 

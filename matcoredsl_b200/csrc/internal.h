@@ -49,6 +49,11 @@ cudaError_t launch_strict_pair_fixed_scratch(const float *a, const float *b, con
                                              int sms, cudaStream_t stream, LaunchInfo *info,
                                              bool *panel_too_large);
 
+// Self-test of the bounded wait of a stream-K owner for another cluster's
+// partial (mcb_device_peer_timeout_selftest_v1); see gemm_tc.cu.
+cudaError_t launch_gemm_tc_peer_stall_selftest(const void *x, const void *w, void *y, float *part,
+                                               int *flags, long long spin_limit, uint32_t *status,
+                                               cudaStream_t stream);
 // Self-test of the bounded pipeline waits (mcb_device_timeout_selftest_v1):
 // one single-SM GEMM tile whose producer issues no loads.
 cudaError_t launch_gemm_tc_stall_selftest(const void *x, const void *w, void *y,

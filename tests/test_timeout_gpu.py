@@ -19,6 +19,7 @@ from tests import gpu_util as gu
 pytestmark = pytest.mark.gpu
 
 TIMEOUT_FULL = 1 << 0
+TIMEOUT_PEER = 1 << 5
 
 
 def test_stalled_pipeline_returns_timeout_and_context_survives(mcb, orc):
@@ -48,3 +49,32 @@ def test_selftest_rejects_out_of_range_limits(mcb):
     lib = _abi.load()
     assert lib.mcb_device_timeout_selftest_v1(0, 10) == _abi.STATUS_CODE["INVALID_ARGUMENT"]
     assert lib.mcb_device_timeout_selftest_v1(0, 10 ** 10) == _abi.STATUS_CODE["INVALID_ARGUMENT"]
+
+
+def test_stream_k_owner_wait_for_a_flag_nothing_sets_returns_timeout(mcb, orc):
+    """The one wait on another CTA cluster: a stream-K owner's producer waits
+    for the flag of its tile's tail part. In the self-test the tails never
+    raise it, so every owner's wait must run out (10^6 cycles), the kernel
+    must return with the "stream-K partial never arrived" bit set, and a
+    stream-K call afterwards must be correct."""
+    import torch
+    lib = _abi.load()
+    mcb.device_status(0, clear=True)
+    for _ in range(2):
+        code = lib.mcb_device_peer_timeout_selftest_v1(0, 1_000_000)
+        assert code == _abi.STATUS_CODE["DEVICE_TIMEOUT"], _abi.STATUS.get(code, code)
+        word = mcb.device_status(0, clear=True)
+        assert word & TIMEOUT_PEER
+        assert mcb.device_status(0) == 0
+    assert lib.mcb_device_peer_timeout_selftest_v1(0, 10) == _abi.STATUS_CODE["INVALID_ARGUMENT"]
+    # a real stream-K launch (two tiles over four clusters) on the same device
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((256, 4096)).astype(np.float32)
+    w = (rng.standard_normal((4096, 512)) / 64).astype(np.float32)
+    xh, xf = gu.bf16_pair(x)
+    wh, wf = gu.bf16_pair(w)
+    y = torch.empty(256, 512, dtype=torch.float32, device="cuda")
+    mcb.gemm_epilogue(gu.to_dev_bf16(xh), gu.to_dev_bf16(wh), out=y)
+    assert mcb.api.last_result.stream_k
+    assert orc.rel_frobenius(gu.from_dev(y), orc.gemm_epilogue(xf, wf)) < 1e-5
+    assert mcb.device_status(0) == 0
