@@ -188,8 +188,11 @@ def cpu_baseline(target_seconds: float = 10.0, rows: int = 256):
 
 
 def _time_steps(fn, steps, stream, flush=None):
-    """Mean device ms of `fn` over `steps` launches (CUDA events on `stream`);
-    `flush` (if given) runs between steps, outside the timed events."""
+    """Median device ms of `fn` over `steps` launches (CUDA events on `stream`);
+    `flush` (if given) runs between steps, outside the timed events. The
+    median, not the mean: a step whose first kernel the host enqueues after
+    the GPU has already passed the start event (config 1's ~23 us of work is
+    shorter than a Python call) would count host time as device time."""
     import torch
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(steps)]
@@ -200,7 +203,7 @@ def _time_steps(fn, steps, stream, flush=None):
         fn()
         evs[i][1].record(stream)
     torch.cuda.synchronize()
-    return statistics.mean(s.elapsed_time(e) for s, e in evs)
+    return statistics.median(s.elapsed_time(e) for s, e in evs)
 
 
 def run_other_configs(dev, world: int = 1, rank: int = 0, steps: int = 10):
