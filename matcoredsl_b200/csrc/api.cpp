@@ -663,7 +663,8 @@ class Call {
       mcb::GemmStreamK w;
       w.clusters = std::max(1, ctx_->sms / 2);
       w.max_tiles = 2 * w.clusters;
-      const size_t part_bytes = static_cast<size_t>(w.clusters) * 4 *
+      // One tail partial per CTA: two 128x256 f32 slots per cluster.
+      const size_t part_bytes = static_cast<size_t>(w.clusters) * 2 *
                                 static_cast<size_t>(mcb::kGemmStreamKSlotFloats) * sizeof(float);
       const size_t ctr_bytes = static_cast<size_t>(w.max_tiles) * 2 * sizeof(int);
       if (cudaMalloc(reinterpret_cast<void **>(&w.part), part_bytes) == cudaSuccess &&
