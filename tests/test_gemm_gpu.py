@@ -447,3 +447,33 @@ def test_stream_k_default_policy(mcb, orc, monkeypatch):
     assert not mcb.api.last_result.stream_k
     assert orc.rel_frobenius(gu.from_dev(y), gu.from_dev(y0).astype(np.float64)) < 1e-6
     assert mcb.device_status(0) == 0
+
+
+@pytest.mark.parametrize("out_dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("rows", [1000, 4096])  # whole tiles; a stream-K last wave
+def test_tma_stored_output_into_a_strided_view(mcb, orc, out_dtype, rows):
+    """16-bit outputs of the CTA-pair kernel go out through shared memory and
+    TMA stores whose tensor map has the view's row stride: a column slice of
+    a wider buffer gets exactly its own columns (ragged N and M included),
+    and the padding columns keep their bytes."""
+    import torch
+    m, k, n, pad = rows, 512, 1000, 24
+    x, w, b = _inputs(m, k, n, seed=rows + len(out_dtype))
+    xh, xf = gu.bf16_pair(x)
+    wh, wf = gu.bf16_pair(w)
+    bh, bf = gu.bf16_pair(b)
+    tdt = torch.bfloat16 if out_dtype == "bf16" else torch.float16
+    big = torch.full((m, n + pad), -3.0, dtype=tdt, device="cuda")
+    view = big[:, :n]
+    assert view.stride(0) == n + pad
+    xd = gu.to_dev_bf16(xh)
+    if out_dtype == "f16":
+        xd, wd, bd = (torch.from_numpy(v).cuda().to(torch.float16) for v in (xf, wf, bf))
+    else:
+        wd, bd = gu.to_dev_bf16(wh), gu.to_dev_bf16(bh)
+    mcb.gemm_epilogue(xd, wd, bd, bias_mode="row", act="gelu_tanh", out=view)
+    assert mcb.api.last_result.route == f"tcgen05_{out_dtype}_gemm_epilogue"
+    ref = orc.gemm_epilogue(xf, wf, bf, bias_mode="row", act="gelu_tanh")
+    assert orc.rel_frobenius(view.float().cpu().numpy(), ref) < REL_BF16
+    assert torch.all(big[:, n:] == -3.0)
+    assert mcb.device_status(0) == 0
