@@ -119,7 +119,7 @@ struct DeviceCtx {
   std::once_flag pool_once;
   cudaMemPool_t pool = nullptr;
   // Stream-K workspace of the CTA-pair GEMM (created on first use): the
-  // counters and partial slots are shared by every launch on the device, so
+  // ready flags and partial slots are shared by every launch on the device, so
   // each stream-K launch is ordered after the previous one (sk_done).
   std::mutex sk_mu;
   bool sk_tried = false;
@@ -666,19 +666,19 @@ class Call {
       // One tail partial per CTA: two 128x256 f32 slots per cluster.
       const size_t part_bytes = static_cast<size_t>(w.clusters) * 2 *
                                 static_cast<size_t>(mcb::kGemmStreamKSlotFloats) * sizeof(float);
-      const size_t ctr_bytes = static_cast<size_t>(w.max_tiles) * 2 * sizeof(int);
+      const size_t flag_bytes = static_cast<size_t>(w.max_tiles) * 2 * sizeof(int);
       if (cudaMalloc(reinterpret_cast<void **>(&w.part), part_bytes) == cudaSuccess &&
-          cudaMalloc(reinterpret_cast<void **>(&w.ctr), ctr_bytes) == cudaSuccess &&
-          cudaMemset(w.ctr, 0, ctr_bytes) == cudaSuccess &&
+          cudaMalloc(reinterpret_cast<void **>(&w.flags), flag_bytes) == cudaSuccess &&
+          cudaMemset(w.flags, 0, flag_bytes) == cudaSuccess &&
           cudaEventCreateWithFlags(&ctx_->sk_done, cudaEventDisableTiming) == cudaSuccess) {
         ctx_->sk = w;
       } else {
         (void)cudaGetLastError();
         if (w.part) cudaFree(w.part);
-        if (w.ctr) cudaFree(w.ctr);
+        if (w.flags) cudaFree(w.flags);
       }
     }
-    if (!ctx_->sk.ctr) return launch(static_cast<const mcb::GemmStreamK *>(nullptr));
+    if (!ctx_->sk.flags) return launch(static_cast<const mcb::GemmStreamK *>(nullptr));
     if (ctx_->sk_pending && ctx_->sk_stream != stream_ &&
         cudaStreamWaitEvent(stream_, ctx_->sk_done, 0) != cudaSuccess)
       return cudaErrorUnknown;
@@ -1687,9 +1687,9 @@ MCB_API mcb_status mcb_device_status(int32_t device, uint32_t *word, int32_t cle
     return MCB_STATUS_CANDIDATE_FAILURE;
   if (clear && rt_memset(c->status, 0, 4) != cudaSuccess) return MCB_STATUS_CANDIDATE_FAILURE;
   if (clear && *word != 0 && !hooks()) {
-    // A stream-K launch that aborted may have left arrival counts behind.
+    // A stream-K launch that aborted may have left ready flags raised.
     std::lock_guard<std::mutex> lock(c->sk_mu);
-    if (c->sk.ctr && cudaMemset(c->sk.ctr, 0, static_cast<size_t>(c->sk.max_tiles) * 2 *
+    if (c->sk.flags && cudaMemset(c->sk.flags, 0, static_cast<size_t>(c->sk.max_tiles) * 2 *
                                                   sizeof(int)) != cudaSuccess)
       return MCB_STATUS_CANDIDATE_FAILURE;
   }

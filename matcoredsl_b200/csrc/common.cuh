@@ -345,16 +345,6 @@ __device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t n, bool pred)
   return out != 0;
 }
 
-// GPU-scope atomic add with acquire-release semantics: releases everything
-// this thread has observed (e.g. the CTA's stores ordered before it by a CTA
-// barrier) and acquires what earlier releasers of the same counter published.
-__device__ __forceinline__ int atomic_add_acq_rel_gpu(int *p, int v) {
-  int old;
-  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
-               : "memory");
-  return old;
-}
-
 // ---- CTA pairs (clusters of 2, tcgen05 cta_group::2) ------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

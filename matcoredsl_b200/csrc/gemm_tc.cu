@@ -1086,7 +1086,7 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
     // on 74 clusters): every full wave stays whole-tile and the last wave's
     // tiles are split in chains.
     const int sk_mode = stream_k_mode();
-    if (sk && !chain && sk->ctr && sk->part && clusters <= sk->clusters && sk_mode != 0) {
+    if (sk && !chain && sk->flags && sk->part && clusters <= sk->clusters && sk_mode != 0) {
       const int64_t g = clusters;
       const int64_t waves = (tiles + g - 1) / g;
       const int64_t dp = (waves - 1) * g;
@@ -1104,7 +1104,7 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
         p.sk_first_tile = static_cast<int>(dp);
         p.sk_tiles = static_cast<int>(skt);
         p.sk_chains = static_cast<int>(chains);
-        p.sk_flag = sk->ctr;
+        p.sk_flag = sk->flags;
         p.sk_part = sk->part;
       }
     }

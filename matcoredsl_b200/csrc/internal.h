@@ -102,10 +102,10 @@ enum : int { kOutF32 = 0, kOutBf16 = 1, kOutF16 = 2 };
 // cluster, slot 0/1 and CTA rank). Launches that share one workspace must not
 // overlap on the GPU.
 struct GemmStreamK {
-  int *ctr = nullptr;
-  float *part = nullptr;
-  int clusters = 0;   // clusters the slots cover
-  int max_tiles = 0;  // stream-K tiles the counters cover
+  int *flags = nullptr;  // ready flag per (split tile, CTA rank); 0 between launches
+  float *part = nullptr; // tail partials: one 128x256 f32 slot per (cluster, CTA rank)
+  int clusters = 0;      // clusters the slots cover
+  int max_tiles = 0;     // split tiles the flags cover
 };
 constexpr int64_t kGemmStreamKSlotFloats = 128 * 256;
 cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m, int64_t n,
