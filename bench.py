@@ -25,6 +25,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import math
 import os
 import re
 import statistics
@@ -206,7 +207,25 @@ def _time_steps(fn, steps, stream, flush=None):
     return statistics.median(s.elapsed_time(e) for s, e in evs)
 
 
-def run_other_configs(dev, world: int = 1, rank: int = 0, steps: int = 10):
+def _attn_head_groups(world: int, attn_shard: str) -> int:
+    """Head groups per batch element for config 5: 1 (batch sharding) when
+    N divides the batch of 4, else the smallest split of the 32 heads that
+    makes batch groups x head groups = N (N = 8: 4 x 2). attn_shard "heads"
+    asks for head sharding at any N > 1 (measurement of that path at N = 2)."""
+    if world == 1:
+        return 1
+    if attn_shard == "heads":
+        bg = 1
+    else:
+        if 4 % world == 0:
+            return 1
+        bg = math.gcd(world, 4)
+    hg = world // bg
+    return hg if 32 % hg == 0 and (4 // bg) * 2048 % hg == 0 else 0
+
+
+def run_other_configs(dev, world: int = 1, rank: int = 0, steps: int = 10,
+                      attn_shard: str = "auto"):
     """Configs 1, 3, 4 and 5 through their entry points (device-resident
     inputs, one call of the public operator per step). Config 1 flushes L2
     between steps; the others' working sets exceed L2.
@@ -214,8 +233,10 @@ def run_other_configs(dev, world: int = 1, rank: int = 0, steps: int = 10):
     With N > 1 ranks the sharded configs split their fixed global work
     (strong scaling, mcb_shard_plan_v1, no collective on the data path):
     config 3 by (batch, head) units, config 4 by rows of A, config 5 by
-    batch elements (when N divides the batch of 4). Config 1 runs as one
-    replica per GPU. Each figure is all ranks' FLOPs / the max-over-ranks
+    batch elements when N divides the batch of 4, else by batch elements and
+    head groups (N = 8: 4 x 2), whose partial output projections one NCCL
+    reduce-scatter per batch group sums. Config 1 runs as one replica per
+    GPU. Each figure is all ranks' FLOPs / the max-over-ranks
     device time per step."""
     import torch
     import matcoredsl_b200 as mcb
@@ -329,8 +350,12 @@ def run_other_configs(dev, world: int = 1, rank: int = 0, steps: int = 10):
         "parallelism": "replicas" if world > 1 else "single GPU"}
     del ca, cb, cw, cbias, ce
 
-    # config 5: attention-residual block, B4 S2048 D4096 H32, seed 40; batch sharded
-    if 4 % world == 0:
+    # config 5: attention-residual block, B4 S2048 D4096 H32, seed 40; batch sharded,
+    # or batch x heads sharded when N does not divide the batch
+    hg = _attn_head_groups(world, attn_shard)
+    if hg > 1:
+        out["config5_attn_block"] = _config5_heads(dev, world, rank, hg, steps, timed, peaks)
+    elif hg == 1 and 4 % world == 0:
         nb = 4 // world
         g.manual_seed(40)
         xb = torch.randn(4, 2048, 4096, generator=g, device=dev)[rank * nb:(rank + 1) * nb] \
@@ -352,8 +377,7 @@ def run_other_configs(dev, world: int = 1, rank: int = 0, steps: int = 10):
                                      "route": mcb.api.last_result.route}
         del xb, ws, yb
     else:
-        out["config5_attn_block"] = {"skipped": f"batch 4 does not split over {world} GPUs "
-                                                "(token sharding is not measured here)"}
+        out["config5_attn_block"] = {"skipped": f"batch 4 x 32 heads do not split over {world} GPUs"}
     torch.cuda.empty_cache()
     return out
 
@@ -577,13 +601,70 @@ def run_ours(args):
         del sets, dsets, calls
         torch.cuda.empty_cache()
         try:  # side measurements never cost the headline line
-            others = run_other_configs(dev, world, rank)
+            others = run_other_configs(dev, world, rank, attn_shard=args.attn_shard)
         except Exception as exc:  # noqa: BLE001
             # a rank that fails here would leave the others in a collective:
             # every rank takes the same steps, so all fail alike on a shape error
             others = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, working_set, route,
             clk, e2e, others, kernel)
+
+
+def _config5_heads(dev, world, rank, hg, steps, timed, peaks):
+    """Config 5 split by batch elements and head groups: rank r holds batch
+    group r // hg and head group r % hg. Each step: the group's partial output
+    projection (mcb_attn_block_heads_v1), one NCCL reduce-scatter over the
+    batch group's hg ranks (mcb_reduce_scatter_v1: the sum of the partials,
+    this rank's rows of it), and residual + RMSNorm of those rows."""
+    import torch
+    import torch.distributed as dist
+    import matcoredsl_b200 as mcb
+    bg = world // hg
+    nb = 4 // bg
+    bi, gi = rank // hg, rank % hg
+    g = torch.Generator(device=dev)
+    g.manual_seed(40)
+    xb = torch.randn(4, 2048, 4096, generator=g, device=dev)[bi * nb:(bi + 1) * nb] \
+        .to(torch.bfloat16)
+    ws = [(torch.randn(4096, 4096, generator=g, device=dev) / 64).to(torch.bfloat16)
+          for _ in range(4)]
+    dh = 4096 // hg
+    cols = slice(gi * dh, (gi + 1) * dh)
+    wq, wk, wv = (w[:, cols].contiguous() for w in ws[:3])
+    wo = ws[3][cols, :].contiguous()
+    del ws
+    torch.cuda.empty_cache()
+    # every rank makes an id and all take part in the exchange; each batch
+    # group uses its first rank's
+    uids = [None] * world
+    dist.all_gather_object(uids, mcb.Comm.unique_id())
+    comm = mcb.Comm(uids[bi * hg], hg, gi, torch.cuda.current_device())
+    rows = nb * 2048 // hg
+    p = torch.empty_like(xb)
+    mine = torch.empty(rows, 4096, dtype=torch.bfloat16, device=dev)
+    x_rows = xb.view(-1, 4096)[gi * rows:(gi + 1) * rows]
+    yb = torch.empty_like(mine)
+
+    def step():
+        mcb.attn_block_heads(xb, wq, wk, wv, wo, 32 // hg, out=p)
+        comm.reduce_scatter(p.view(-1), mine.view(-1))
+        mcb.residual_rmsnorm(x_rows, mine, 1e-6, out=yb)
+
+    try:
+        for _ in range(2):
+            step()
+        ms = timed(step, steps)
+    finally:
+        torch.cuda.synchronize()
+        comm.close()
+    fl = 4.0 * 2 * 8192 * 4096 * 4096 + 4.0 * 4 * 32 * 2048 * 2048 * 128
+    return {"ms": ms, "tflops": fl / ms / 1e9, "tflops_per_gpu": fl / ms / 1e9 / world,
+            "frac_of_bf16_peak": fl / ms / 1e9 / world / peaks["bf16_tflops"],
+            "batch_per_gpu": nb, "head_groups": hg, "heads_per_gpu": 32 // hg,
+            "collective": "one NCCL reduce-scatter per step over each batch group's "
+                          f"{hg} ranks ({nb * 2048 * 4096 * 2} B of partial output projection "
+                          "per rank)",
+            "route": "attn_block_heads + reduce_scatter + residual_rmsnorm"}
 
 
 def _run_e2e(args, lib, ep, sets, descs, dev, stream, world, flops_step, m):
@@ -679,6 +760,9 @@ def main():
                     help="skip the host-buffer end-to-end leg (used for short profiling runs)")
     ap.add_argument("--no-other-configs", action="store_true",
                     help="skip the configs 1/3/4/5 measurements reported beside the headline")
+    ap.add_argument("--attn-shard", choices=["auto", "heads"], default="auto",
+                    help="config 5 at N > 1: batch sharding where N divides the batch (auto), "
+                         "or batch x heads sharding with a reduce-scatter (heads)")
     ap.add_argument("--profile-config", type=int, choices=list(range(1, 12)),
                     help="only launch this config's operator (for ncu captures); no JSON line")
     args = ap.parse_args()

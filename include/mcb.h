@@ -395,6 +395,28 @@ MCB_API mcb_status mcb_attn_block_region_v1(const mcb_tensor *y, const mcb_tenso
                                             int64_t heads, float eps,
                                             const mcb_exec *exec) MCB_NOEXCEPT;
 
+/* Head-sharded form of the region, for a batch too small to split over the
+ * GPUs (batch x heads sharding; no counterpart in the single-GPU reference).
+ * mcb_attn_block_heads_v1 computes one head group's share of the output
+ * projection, P = MSM(X Wq_g, X Wk_g, X Wv_g) Wo_g: X [B,S,D] and P [B,S,D]
+ * dense bf16; Wq_g, Wk_g, Wv_g [D,Dh] the group's column slices of Wq, Wk,
+ * Wv and Wo_g [Dh,D] the matching row slice of Wo, all dense bf16; `heads`
+ * heads of Dh/heads, softmax scale (Dh/heads)^-0.5 (the region's, since the
+ * head width is the same). Scratch: mcb_attn_block_heads_workspace_bytes_v1.
+ * Summing P over the head groups (mcb_reduce_scatter_v1 across GPUs) gives
+ * the region's Wo * MSM(...); mcb_residual_rmsnorm_v1 then writes
+ * Y = RMSNorm(X + sum P) for any dense [.., D] bf16 rows (D <= 8192), the
+ * region's last step. */
+MCB_API uint64_t mcb_attn_block_heads_workspace_bytes_v1(int64_t batch, int64_t seq,
+                                                         int64_t d_heads) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_attn_block_heads_v1(const mcb_tensor *p, const mcb_tensor *x,
+                                           const mcb_tensor *wq, const mcb_tensor *wk,
+                                           const mcb_tensor *wv, const mcb_tensor *wo,
+                                           int64_t heads, const mcb_exec *exec) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_residual_rmsnorm_v1(const mcb_tensor *y, const mcb_tensor *x,
+                                           const mcb_tensor *p, float eps,
+                                           const mcb_exec *exec) MCB_NOEXCEPT;
+
 /* ---- execution plans (shape-locked, optional CUDA-graph replay) ------------ */
 /* Mirrors MatcorePlan::create / execute (include/matcore/plan.h:37-107): a
  * plan freezes the operator and the metadata (dtype, rank, dims, strides,
@@ -498,6 +520,14 @@ MCB_API mcb_status mcb_comm_init_v1(const mcb_comm_id *id, int32_t world, int32_
                                     int32_t device, mcb_comm **out) MCB_NOEXCEPT;
 MCB_API mcb_status mcb_allgather_v1(mcb_comm *comm, const void *send, void *recv,
                                     uint64_t bytes_per_rank, void *stream) MCB_NOEXCEPT;
+/* mcb_reduce_scatter_v1 queues on `stream` the element-wise sum over all
+ * ranks of `send` (world * count_per_rank elements of dtype MCB_DTYPE_F32 or
+ * MCB_DTYPE_BF16), leaving in `recv` this rank's slot of the sum (elements
+ * [rank * count_per_rank, (rank + 1) * count_per_rank)); `recv` may be this
+ * rank's slot of `send`. The exchange step of the head-sharded region. */
+MCB_API mcb_status mcb_reduce_scatter_v1(mcb_comm *comm, const void *send, void *recv,
+                                         uint64_t count_per_rank, int32_t dtype,
+                                         void *stream) MCB_NOEXCEPT;
 MCB_API mcb_status mcb_comm_destroy_v1(mcb_comm *comm) MCB_NOEXCEPT;
 
 /* ---- device buffers ------------------------------------------------------- */

@@ -8,14 +8,15 @@ is missing -- there is no CPU fallback.
 """
 from . import _abi
 from ._abi import McbError, load
-from .api import (Comm, Plan, attn_block, block_attn_res, device_status, fp8_quantize_blockwise,
-                  gemm_bf16_f32_fma,
-                  gemm_chain, gemm_epilogue, gemm_fp8_blockscaled, gemm_i8_i32, msm, shard_plan,
-                  strict_fused_pair, strict_gemm)
+from .api import (Comm, Plan, attn_block, attn_block_heads, block_attn_res, device_status,
+                  fp8_quantize_blockwise, gemm_bf16_f32_fma,
+                  gemm_chain, gemm_epilogue, gemm_fp8_blockscaled, gemm_i8_i32, msm,
+                  residual_rmsnorm, shard_plan, strict_fused_pair, strict_gemm)
 
 __all__ = ["McbError", "load", "strict_gemm", "strict_fused_pair", "gemm_epilogue", "gemm_chain",
            "msm",
-           "fp8_quantize_blockwise", "gemm_fp8_blockscaled", "attn_block", "shard_plan",
+           "fp8_quantize_blockwise", "gemm_fp8_blockscaled", "attn_block", "attn_block_heads",
+           "residual_rmsnorm", "shard_plan",
            "device_status", "Comm"]
 
 load()

@@ -169,6 +169,9 @@ SIGNATURES = {
     "mcb_attn_block_workspace_bytes_v1": (ctypes.c_uint64, [ctypes.c_int64] * 3),
     "mcb_attn_block_region_v1": (ctypes.c_int32, [_T, _T, _T, _T, _T, _T, ctypes.c_int64,
                                                   ctypes.c_float, _E]),
+    "mcb_attn_block_heads_workspace_bytes_v1": (ctypes.c_uint64, [ctypes.c_int64] * 3),
+    "mcb_attn_block_heads_v1": (ctypes.c_int32, [_T, _T, _T, _T, _T, _T, ctypes.c_int64, _E]),
+    "mcb_residual_rmsnorm_v1": (ctypes.c_int32, [_T, _T, _T, ctypes.c_float, _E]),
     "mcb_plan_create_v1": (ctypes.c_int32, [_P(PlanDesc), _P(ctypes.c_void_p)]),
     "mcb_plan_execute_v1": (ctypes.c_int32, [ctypes.c_void_p, _T, ctypes.c_uint32,
                                              ctypes.c_void_p]),
@@ -191,6 +194,8 @@ SIGNATURES = {
                                           ctypes.c_int32, _P(ctypes.c_void_p)]),
     "mcb_allgather_v1": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                           ctypes.c_uint64, ctypes.c_void_p]),
+    "mcb_reduce_scatter_v1": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                               ctypes.c_uint64, ctypes.c_int32, ctypes.c_void_p]),
     "mcb_comm_destroy_v1": (ctypes.c_int32, [ctypes.c_void_p]),
     "mcb_device_zero": (ctypes.c_int32, [Buffer]),
     "mcb_device_zero_raw_on_stream": (ctypes.c_int32, [ctypes.c_void_p, ctypes.c_uint64,

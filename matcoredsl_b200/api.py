@@ -366,6 +366,30 @@ def attn_block(x, wq, wk, wv, wo, heads, eps=1e-6, out=None, *, device=-1, flags
     return out
 
 
+def attn_block_heads(x, wq, wk, wv, wo, heads, out=None, *, device=-1, flags=0, workspace=None):
+    """One head group's share of the attention block's output projection,
+    P = MSM(X Wq_g, X Wk_g, X Wv_g) Wo_g: X [B, S, D] bf16, Wq_g/Wk_g/Wv_g
+    [D, Dh] (the group's columns of Wq/Wk/Wv), Wo_g [Dh, D] (the matching rows
+    of Wo), `heads` heads of Dh/heads. Summing P over all head groups and
+    calling residual_rmsnorm(x, sum) gives attn_block(x, ...)."""
+    if out is None:
+        out = _empty_like_out(x, tuple(x.shape), "bf16")
+    _call("mcb_attn_block_heads_v1",
+          [("p", out), ("x", x), ("wq", wq), ("wk", wk), ("wv", wv), ("wo", wo)],
+          [int(heads)], device, flags, workspace)
+    return out
+
+
+def residual_rmsnorm(x, p, eps=1e-6, out=None, *, device=-1, flags=0):
+    """Y = RMSNorm(X + P) over the last dimension (unit gain); X, P, Y dense
+    bf16 of one shape (rank 2 or 3)."""
+    if out is None:
+        out = _empty_like_out(x, tuple(x.shape), "bf16")
+    _call("mcb_residual_rmsnorm_v1", [("y", out), ("x", x), ("p", p)], [float(eps)], device,
+          flags)
+    return out
+
+
 class Plan:
     """Shape-locked operator call with optional CUDA-graph replay (the
     reference's create_plan / execute_plan). Tensors are passed in the entry
@@ -467,8 +491,8 @@ def shard_plan(kind, total, world, rank, *, group=0, align=1):
 
 
 class Comm:
-    """NCCL communicator for the optional all-gather of output shards
-    (mcb_comm_*_v1). Rank 0 calls Comm.unique_id() and passes the bytes to the
+    """NCCL communicator for the optional all-gather of output shards and
+    the reduce-scatter of the head-sharded attention block (mcb_comm_*_v1). Rank 0 calls Comm.unique_id() and passes the bytes to the
     other ranks out of band; every rank then constructs Comm(uid, world, rank,
     device) (collective)."""
 
@@ -499,6 +523,24 @@ class Comm:
         stream = _exec(True, self.device, 0, None).stream
         _abi.check(_abi.load().mcb_allgather_v1(self._h, send.data_ptr(), recv.data_ptr(), nbytes,
                                                 stream), "mcb_allgather_v1")
+        return recv
+
+    def reduce_scatter(self, send, recv):
+        """Sums `send` (a CUDA tensor of world x recv's elements, f32 or bf16)
+        over all ranks and leaves this rank's slot of the sum in `recv`, on
+        torch's current stream."""
+        names = _torch_dtype_names()
+        dt = names.get(send.dtype)
+        if dt not in ("f32", "bf16") or recv.dtype != send.dtype:
+            raise TypeError("reduce_scatter: send and recv must both be f32 or both bf16")
+        if send.numel() != recv.numel() * self.world:
+            raise ValueError("reduce_scatter: send must hold world x recv elements")
+        if not (send.is_contiguous() and recv.is_contiguous()):
+            raise ValueError("reduce_scatter: send and recv must be contiguous")
+        stream = _exec(True, self.device, 0, None).stream
+        _abi.check(_abi.load().mcb_reduce_scatter_v1(self._h, send.data_ptr(), recv.data_ptr(),
+                                                     recv.numel(), _abi.DTYPE[dt], stream),
+                   "mcb_reduce_scatter_v1")
         return recv
 
     def close(self):

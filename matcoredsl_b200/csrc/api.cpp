@@ -1625,6 +1625,162 @@ mcb_status attn_block_impl(const mcb_tensor *y, const mcb_tensor *x, const mcb_t
   return call.finish(y, dy, info, err);
 }
 
+// ---- head-sharded attention block (the region split over GPUs by heads) --------------------
+// One head group's share of the region's output projection,
+//   P = MSM(X Wq_g, X Wk_g, X Wv_g) Wo_g,
+// with Wq_g / Wk_g / Wv_g the group's [D, Dh] column slices and Wo_g the
+// matching [Dh, D] row slice. The sum of P over all head groups is the
+// region's Wo * MSM(...); residual_rmsnorm_impl then finishes the block.
+uint64_t attn_heads_workspace_bytes(int64_t rows, int64_t dh) {
+  // Q, K, V and O of the group: four [rows, Dh] bf16 buffers.
+  const uint64_t one = static_cast<uint64_t>(rows) * dh * 2;
+  return 4 * ((one + 255) / 256 * 256);
+}
+
+mcb_status attn_heads_impl(const mcb_tensor *p, const mcb_tensor *x, const mcb_tensor *wq,
+                           const mcb_tensor *wk, const mcb_tensor *wv, const mcb_tensor *wo,
+                           int64_t heads, const mcb_exec *exec) {
+  mcb_status s;
+  if ((s = check_tensor(x, 3, 3)) || (s = check_tensor(p, 3, 3)) || (s = check_tensor(wq, 2, 2)) ||
+      (s = check_tensor(wk, 2, 2)) || (s = check_tensor(wv, 2, 2)) || (s = check_tensor(wo, 2, 2)))
+    return s;
+  for (const mcb_tensor *t : {x, p, wq, wk, wv, wo})
+    if (t->dtype != MCB_DTYPE_BF16) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  const int64_t B = x->dims[0], S = x->dims[1], D = x->dims[2], Dh = wq->dims[1];
+  if (heads <= 0 || Dh <= 0 || Dh % heads != 0) return MCB_STATUS_INVALID_ARGUMENT;
+  const int64_t hd = Dh / heads, M = B * S;
+  auto dense3 = [&](const mcb_tensor *t) {
+    return t->dims[0] == B && t->dims[1] == S && t->dims[2] == D && t->strides[2] == 1 &&
+           (S <= 1 || t->strides[1] == D) && (B <= 1 || t->strides[0] == S * D);
+  };
+  if (!dense3(x) || !dense3(p)) return MCB_STATUS_SHAPE_MISMATCH;
+  for (const mcb_tensor *w : {wq, wk, wv})
+    if (!dense2(w, D, Dh)) return MCB_STATUS_SHAPE_MISMATCH;
+  if (!dense2(wo, Dh, D)) return MCB_STATUS_SHAPE_MISMATCH;
+  if (S == 0) return MCB_STATUS_INVALID_SHAPE;
+  for (const mcb_tensor *t : {x, wq, wk, wv, wo})
+    if (overlaps(p, t)) return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({x, p, wq, wk, wv, wo}, &host))) return s;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  void *dx, *dq, *dk, *dv, *dwo, *dp;
+  if ((s = call.device_ptr(x, true, &dx)) || (s = call.device_ptr(wq, true, &dq)) ||
+      (s = call.device_ptr(wk, true, &dk)) || (s = call.device_ptr(wv, true, &dv)) ||
+      (s = call.device_ptr(wo, true, &dwo)) || (s = call.device_ptr(p, false, &dp)))
+    return s;
+  void *ws = nullptr;
+  const uint64_t ws_bytes = attn_heads_workspace_bytes(M, Dh);
+  if ((s = call.scratch(ws_bytes, &ws))) return s;
+  const uint64_t one = ws_bytes / 4;
+  uint8_t *base = static_cast<uint8_t *>(ws);
+  void *Q = base, *K = base + one, *V = base + 2 * one, *O = base + 3 * one;
+
+  LaunchInfo info, step;
+  cudaError_t err = cudaSuccess;
+  mcb::Epilogue none;
+  // [M, k] x [k, n] -> [M, n], all dense bf16 rows.
+  auto gemm = [&](const void *a, const void *w, void *out, int64_t n, int64_t k) {
+    const bool tc = k % 8 == 0 && n % 8 == 0 &&
+                    ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w) |
+                      reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
+    if (tc)
+      return mcb::launch_gemm_tc_bf16(a, w, out, M, n, k, k, n, n, 0, 1, none, call.ctx()->status,
+                                      call.sms(), call.stream(), &step);
+    return mcb::launch_gemm_simt(a, MCB_DTYPE_BF16, w, MCB_DTYPE_BF16, out, MCB_DTYPE_BF16, M, n,
+                                 k, k, n, n, 0, none, call.stream(), &step);
+  };
+  call.mark_compute_start();
+  int launches = 0;
+  for (auto [w, out] : {std::pair<void *, void *>{dq, Q}, {dk, K}, {dv, V}}) {
+    step.launches = 0;
+    if ((err = gemm(dx, w, out, Dh, D)) != cudaSuccess) break;
+    launches += step.launches;
+  }
+  if (err == cudaSuccess) {
+    // Q/K/V/O are [B, S, Dh] = [B, S, heads, hd], read as [B, heads, S, hd].
+    mcb::MsmShape sh;
+    sh.batch = B;
+    sh.heads = heads;
+    sh.m = sh.n = S;
+    sh.dqk = sh.dv = hd;
+    const int64_t st[3] = {S * Dh, hd, Dh};
+    for (int i = 0; i < 3; ++i) sh.q_s[i] = sh.k_s[i] = sh.v_s[i] = sh.o_s[i] = st[i];
+    const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+    step.launches = 0;
+    err = cudaErrorNotSupported;
+    if ((hd == 64 || hd == 128) && Dh % 8 == 0)
+      err = mcb::launch_msm_tc_bf16(Q, K, V, O, sh, scale, call.ctx()->status, call.sms(),
+                                    call.stream(), &step);
+    if (err == cudaErrorNotSupported)
+      err = hd <= 256 ? mcb::launch_msm_simt(Q, K, V, O, MCB_DTYPE_BF16, sh, scale, call.stream(),
+                                             &step)
+                      : cudaErrorNotSupported;
+    launches += step.launches;
+  }
+  if (err == cudaSuccess) {
+    step.launches = 0;
+    err = gemm(O, dwo, dp, D, Dh);
+    launches += step.launches;
+  }
+  call.mark_compute_end();
+  if (err == cudaErrorNotSupported) return MCB_STATUS_UNAVAILABLE_VARIANT;
+  info.launches = launches;
+  info.tile_m = 128;
+  info.tile_n = 256;
+  info.ctas = call.sms();
+  info.set_route("attn_block_heads");
+  return call.finish(p, dp, info, err);
+}
+
+// Y = RMSNorm(X + P) over the last dimension (unit gain), the region's last
+// step, for X / P / Y of the same dense bf16 shape (rank 2 or 3).
+mcb_status residual_rmsnorm_impl(const mcb_tensor *y, const mcb_tensor *x, const mcb_tensor *pp,
+                                 float eps, const mcb_exec *exec) {
+  mcb_status s;
+  if ((s = check_tensor(x, 2, 3)) || (s = check_tensor(y, 2, 3)) || (s = check_tensor(pp, 2, 3)))
+    return s;
+  for (const mcb_tensor *t : {x, y, pp})
+    if (t->dtype != MCB_DTYPE_BF16) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  if (!(eps >= 0.0f)) return MCB_STATUS_INVALID_ARGUMENT;
+  const int r = x->rank;
+  const int64_t D = x->dims[r - 1];
+  int64_t rows = 1;
+  for (int i = 0; i < r - 1; ++i) rows *= x->dims[i];
+  auto dense_like_x = [&](const mcb_tensor *t) {
+    if (t->rank != r) return false;
+    int64_t stride = 1;
+    for (int i = r - 1; i >= 0; --i) {
+      if (t->dims[i] != x->dims[i]) return false;
+      if (t->dims[i] > 1 && t->strides[i] != stride) return false;
+      stride *= t->dims[i];
+    }
+    return true;
+  };
+  if (!dense_like_x(x) || !dense_like_x(y) || !dense_like_x(pp)) return MCB_STATUS_SHAPE_MISMATCH;
+  if (rows == 0 || D == 0) return MCB_STATUS_OK;
+  for (const mcb_tensor *t : {x, pp})
+    if (overlaps(y, t)) return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({x, y, pp}, &host))) return s;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  void *dx, *dp, *dy;
+  if ((s = call.device_ptr(x, true, &dx)) || (s = call.device_ptr(pp, true, &dp)) ||
+      (s = call.device_ptr(y, false, &dy)))
+    return s;
+  LaunchInfo info;
+  call.mark_compute_start();
+  cudaError_t err = mcb::launch_residual_rmsnorm(dx, dp, dy, rows, D, eps, call.stream(), &info);
+  call.mark_compute_end();
+  if (err == cudaErrorNotSupported) return MCB_STATUS_UNAVAILABLE_VARIANT;
+  info.tile_m = 1;
+  info.tile_n = 256;
+  info.ctas = static_cast<int>(std::min<int64_t>(rows, 0x7fffffff));
+  info.set_route("residual_rmsnorm");
+  return call.finish(y, dy, info, err);
+}
+
 // ---- device buffers ------------------------------------------------------------------------
 std::mutex g_buf_mu;
 std::unordered_map<uint64_t, mcb_buffer> g_bufs;  // ptr -> live handle
@@ -1997,6 +2153,33 @@ MCB_API mcb_status mcb_attn_block_region_v1(const mcb_tensor *y, const mcb_tenso
                                             const mcb_exec *exec) noexcept {
   try {
     return attn_block_impl(y, x, wq, wk, wv, wo, heads, eps, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API uint64_t mcb_attn_block_heads_workspace_bytes_v1(int64_t batch, int64_t seq,
+                                                         int64_t d_heads) noexcept {
+  if (batch < 0 || seq < 0 || d_heads < 0) return 0;
+  return attn_heads_workspace_bytes(batch * seq, d_heads);
+}
+
+MCB_API mcb_status mcb_attn_block_heads_v1(const mcb_tensor *p, const mcb_tensor *x,
+                                           const mcb_tensor *wq, const mcb_tensor *wk,
+                                           const mcb_tensor *wv, const mcb_tensor *wo,
+                                           int64_t heads, const mcb_exec *exec) noexcept {
+  try {
+    return attn_heads_impl(p, x, wq, wk, wv, wo, heads, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API mcb_status mcb_residual_rmsnorm_v1(const mcb_tensor *y, const mcb_tensor *x,
+                                           const mcb_tensor *p, float eps,
+                                           const mcb_exec *exec) noexcept {
+  try {
+    return residual_rmsnorm_impl(y, x, p, eps, exec);
   } catch (...) {
     return MCB_STATUS_CANDIDATE_FAILURE;
   }

@@ -1,10 +1,15 @@
-// Optional output all-gather for sharded runs (mcb_comm_*_v1, mcb_allgather_v1).
+// NCCL collectives for sharded runs (mcb_comm_*_v1, mcb_allgather_v1,
+// mcb_reduce_scatter_v1).
 //
-// The path shards with no collective on its data path: each rank computes
-// its own rows / units / tokens (mcb_shard_plan_v1). A caller that wants the
-// whole output on every rank gathers the shards afterwards with one NCCL
-// all-gather per output, over NVLink / NVSwitch. The reference is
-// single-GPU, so this has no counterpart there.
+// Row, unit and batch shards need no collective on their data path: each
+// rank computes its own rows / units / tokens (mcb_shard_plan_v1). A caller
+// that wants the whole output on every rank gathers the shards afterwards
+// with one NCCL all-gather per output, over NVLink / NVSwitch. The one real
+// exchange is the head-sharded attention block: each rank's
+// mcb_attn_block_heads_v1 partial holds its heads' share of the output
+// projection, and one reduce-scatter sums the partials of a batch group and
+// leaves each rank its rows. The reference is single-GPU, so none of this
+// has a counterpart there.
 //
 // NCCL is resolved at run time: the copy already loaded in the process (for
 // example by PyTorch) is reused, else libnccl.so.2 is opened privately, so a
@@ -33,6 +38,7 @@ struct NcclApi {
   decltype(&ncclCommInitRank) comm_init_rank = nullptr;
   decltype(&ncclCommDestroy) comm_destroy = nullptr;
   decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclReduceScatter) reduce_scatter = nullptr;
   bool ok = false;
 };
 
@@ -48,7 +54,10 @@ const NcclApi &nccl_api() {
         reinterpret_cast<decltype(&ncclCommInitRank)>(dlsym(h, "ncclCommInitRank"));
     api.comm_destroy = reinterpret_cast<decltype(&ncclCommDestroy)>(dlsym(h, "ncclCommDestroy"));
     api.all_gather = reinterpret_cast<decltype(&ncclAllGather)>(dlsym(h, "ncclAllGather"));
-    api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_gather;
+    api.reduce_scatter =
+        reinterpret_cast<decltype(&ncclReduceScatter)>(dlsym(h, "ncclReduceScatter"));
+    api.ok = api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_gather &&
+             api.reduce_scatter;
   });
   return api;
 }
@@ -126,6 +135,37 @@ MCB_API mcb_status mcb_allgather_v1(mcb_comm *comm, const void *send, void *recv
   DeviceScope scope(comm->device);
   return api.all_gather(send, recv, bytes_per_rank, ncclUint8, comm->nccl,
                         static_cast<cudaStream_t>(stream)) == ncclSuccess
+             ? MCB_STATUS_OK
+             : MCB_STATUS_CANDIDATE_FAILURE;
+}
+
+MCB_API mcb_status mcb_reduce_scatter_v1(mcb_comm *comm, const void *send, void *recv,
+                                         uint64_t count_per_rank, int32_t dtype,
+                                         void *stream) noexcept {
+  if (!comm) return MCB_STATUS_INVALID_ARGUMENT;
+  ncclDataType_t nt;
+  uint64_t elem;
+  switch (dtype) {
+    case MCB_DTYPE_F32: nt = ncclFloat32; elem = 4; break;
+    case MCB_DTYPE_BF16: nt = ncclBfloat16; elem = 2; break;
+    default: return MCB_STATUS_UNSUPPORTED_DTYPE;
+  }
+  if (count_per_rank == 0) return MCB_STATUS_OK;
+  if (!send || !recv) return MCB_STATUS_INVALID_ARGUMENT;
+  const uint64_t world = static_cast<uint64_t>(comm->world);
+  const uint64_t recv_bytes = count_per_rank * elem;
+  if (recv_bytes / elem != count_per_rank || (recv_bytes * world) / world != recv_bytes)
+    return MCB_STATUS_ARITHMETIC_OVERFLOW;
+  const uint64_t send_bytes = recv_bytes * world;
+  const uintptr_t s0 = reinterpret_cast<uintptr_t>(send), r0 = reinterpret_cast<uintptr_t>(recv);
+  // In place only as NCCL defines it: recv is this rank's slot of send.
+  const uintptr_t own = s0 + recv_bytes * static_cast<uint64_t>(comm->rank);
+  if (r0 != own && r0 < s0 + send_bytes && s0 < r0 + recv_bytes) return MCB_STATUS_ALIAS_VIOLATION;
+  const NcclApi &api = nccl_api();
+  if (!api.ok) return MCB_STATUS_CANDIDATE_UNAVAILABLE;
+  DeviceScope scope(comm->device);
+  return api.reduce_scatter(send, recv, count_per_rank, nt, ncclSum, comm->nccl,
+                            static_cast<cudaStream_t>(stream)) == ncclSuccess
              ? MCB_STATUS_OK
              : MCB_STATUS_CANDIDATE_FAILURE;
 }

@@ -158,7 +158,39 @@ def test_comm_arguments_checked_without_gpu(mcb):
     assert lib.mcb_comm_init_v1(ctypes.byref(cid), 2, 0, -1, ctypes.byref(out)) == bad  # device
     assert lib.mcb_comm_init_v1(None, 2, 0, 0, ctypes.byref(out)) == bad
     assert lib.mcb_allgather_v1(None, 0x1000, 0x2000, 16, None) == bad
+    assert lib.mcb_reduce_scatter_v1(None, 0x1000, 0x2000, 16, _abi.DTYPE["bf16"], None) == bad
     assert lib.mcb_comm_destroy_v1(None) == 0
+
+
+def test_attn_heads_arguments_checked_without_gpu(mcb):
+    """The head-sharded block and residual + RMSNorm reject bad shapes and
+    arguments before touching a device."""
+    from matcoredsl_b200 import _abi
+    lib = mcb.load()
+    b, s, d, dh = 1, 8, 16, 8
+    x = np.zeros((b, s, d), np.uint16)
+    w = np.zeros((d, dh), np.uint16)
+    wo = np.zeros((dh, d), np.uint16)
+    p = np.zeros((b, s, d), np.uint16)
+    t = lambda a, st: _abi.make_tensor(a.ctypes.data, "bf16", a.shape, st, False)  # noqa: E731
+    tx, tw, two, tp = t(x, [s * d, d, 1]), t(w, [dh, 1]), t(wo, [d, 1]), t(p, [s * d, d, 1])
+    ex = _abi.make_exec()
+    call = lambda heads, wq=tw, wout=two: lib.mcb_attn_block_heads_v1(  # noqa: E731
+        ctypes.byref(tp), ctypes.byref(tx), ctypes.byref(wq), ctypes.byref(tw), ctypes.byref(tw),
+        ctypes.byref(wout), heads, ctypes.byref(ex))
+    assert call(3) == _abi.STATUS_CODE["INVALID_ARGUMENT"]      # Dh % heads != 0
+    assert call(0) == _abi.STATUS_CODE["INVALID_ARGUMENT"]
+    assert call(2, wout=tw) == _abi.STATUS_CODE["SHAPE_MISMATCH"]  # Wo not [Dh, D]
+    assert lib.mcb_attn_block_heads_workspace_bytes_v1(1, 8, 8) == 4 * 256
+    y = np.zeros((b, s, d), np.uint16)
+    ty = t(y, [s * d, d, 1])
+    assert lib.mcb_residual_rmsnorm_v1(ctypes.byref(ty), ctypes.byref(tx), ctypes.byref(tp),
+                                       -1.0, ctypes.byref(ex)) == _abi.STATUS_CODE["INVALID_ARGUMENT"]
+    assert lib.mcb_residual_rmsnorm_v1(ctypes.byref(ty), ctypes.byref(tx), ctypes.byref(tw),
+                                       1e-6, ctypes.byref(ex)) in (
+        _abi.STATUS_CODE["SHAPE_MISMATCH"], _abi.STATUS_CODE["INVALID_SHAPE"])
+    assert lib.mcb_residual_rmsnorm_v1(ctypes.byref(tx), ctypes.byref(tx), ctypes.byref(tp),
+                                       1e-6, ctypes.byref(ex)) == _abi.STATUS_CODE["ALIAS_VIOLATION"]
 
 
 def test_epilogue_chain_encoding(mcb):

@@ -78,3 +78,47 @@ def test_config5_full_size_sampled(mcb, orc):
         ref = orc.attn_block(f[0], f[1], f[2], f[3], f[4], heads, 1e-6, batch=bi, tokens=tok)
         assert orc.rel_frobenius(got[bi][tok], ref) < 1e-2
     assert mcb.device_status(0) == 0
+
+
+# Head-sharded form (batch x heads sharding over GPUs, emulated here on one
+# GPU): each head group's partial P_g = MSM(X Wq_g, X Wk_g, X Wv_g) Wo_g,
+# summed in bf16 as the reduce-scatter sums them, then residual + RMSNorm.
+@pytest.mark.parametrize("shape,groups", [(((1, 256, 512, 4)), 2), (((2, 300, 512, 8)), 4),
+                                          (((1, 256, 1024, 8)), 2)])
+def test_block_heads_partials_sum_to_region(mcb, orc, shape, groups):
+    import torch
+    b, s, d, heads = shape
+    pairs = _inputs(b, s, d, seed=sum(shape) + groups)
+    x, wq, wk, wv, wo = [gu.to_dev_bf16(h) for h, _ in pairs]
+    dh = d // groups
+    total = torch.zeros(b, s, d, device="cuda")
+    for g in range(groups):
+        cols = slice(g * dh, (g + 1) * dh)
+        p = mcb.attn_block_heads(x, wq[:, cols].contiguous(), wk[:, cols].contiguous(),
+                                 wv[:, cols].contiguous(), wo[cols, :].contiguous(),
+                                 heads // groups)
+        assert mcb.api.last_result.route == "attn_block_heads"
+        total += p.float()
+    y = mcb.residual_rmsnorm(x, total.to(torch.bfloat16), 1e-6)
+    assert mcb.api.last_result.route == "residual_rmsnorm"
+    got = gu.from_dev(y)
+    whole = gu.from_dev(mcb.attn_block(x, wq, wk, wv, wo, heads, 1e-6))
+    f = [fp for _, fp in pairs]
+    for bi in range(b):
+        ref = orc.attn_block(f[0], f[1], f[2], f[3], f[4], heads, 1e-6, batch=bi)
+        assert orc.rel_frobenius(got[bi], ref) < 1e-2
+        assert orc.rel_frobenius(got[bi], whole[bi]) < 1e-2
+
+
+@pytest.mark.parametrize("shape", [(3, 5, 4096), (7, 1000), (2, 4, 8192), (1, 3, 96)])
+def test_residual_rmsnorm_matches_fp32(mcb, shape):
+    import torch
+    g = torch.Generator(device="cuda")
+    g.manual_seed(len(shape) * 1000 + shape[-1])
+    x = torch.randn(*shape, device="cuda", generator=g).to(torch.bfloat16)
+    p = torch.randn(*shape, device="cuda", generator=g).to(torch.bfloat16)
+    y = mcb.residual_rmsnorm(x, p, 1e-6)
+    sm = x.float() + p.float()
+    ref = sm * torch.rsqrt(sm.pow(2).mean(-1, keepdim=True) + 1e-6)
+    err = (y.float() - ref).norm() / ref.norm()
+    assert err.item() < 5e-3, err.item()
