@@ -57,12 +57,16 @@ def _peaks():
             "source": "fallback"}
 
 
-def _profiled_traffic(kernel_key: str):
-    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+def _profiled_traffic(kernel_key: str, rows: int = M_FULL):
+    """DRAM bytes per launch of `rows` rows from the committed ncu summary,
+    when it holds a capture of that launch size (config 2's 8192 rows, the
+    8-GPU shard's 1024); None otherwise, since the traffic does not scale
+    with the rows (all of W is read at any size)."""
     p = os.path.join(ROOT, "profiles", "gemm_tc_bf16_config2.md")
     if not os.path.exists(p):
         return None
-    m = re.search(rf"{kernel_key}_dram_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
+    tag = "" if rows == M_FULL else f"_{rows}rows"
+    m = re.search(rf"{kernel_key}{tag}_dram_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
     return float(m.group(1)) if m else None
 
 
@@ -711,6 +715,14 @@ def _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, wo
             clk, e2e, others=None, kernel="gemm_tc_bf16_kernel"):
     peaks = _peaks()
     achieved = flops_step / (launch_ms_max / 1e3) / 1e12
+    # ranks that ran a non-empty shard (every rank takes this collective)
+    gpus_active = world
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([1 if m > 0 else 0], dtype=torch.int64, device=torch.cuda.current_device())
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        gpus_active = int(t.item())
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -719,7 +731,8 @@ def _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, wo
             cpu = {"value": None, "error": f"{type(exc).__name__}: {exc}"[:300]}
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "gpus_active": gpus_active,
+            "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": t_ms_max / args.steps,
             "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
@@ -732,7 +745,7 @@ def _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, wo
             "pct_of_peak": value / world / peaks["bf16_tflops"],
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
                          "unit": UNIT, "frac": achieved / peaks["bf16_tflops"],
-                         "traffic": _profiled_traffic(kernel),
+                         "traffic": _profiled_traffic(kernel, m),
                          "peak_source": f"{peaks['source']} bf16 burst (cuBLAS)",
                          "kernel": kernel,
                          "algorithmic_flops_per_launch": flops_step},
