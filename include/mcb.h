@@ -417,6 +417,41 @@ MCB_API mcb_status mcb_residual_rmsnorm_v1(const mcb_tensor *y, const mcb_tensor
                                            const mcb_tensor *p, float eps,
                                            const mcb_exec *exec) MCB_NOEXCEPT;
 
+/* Two head groups on two GPUs with the exchange fused into the output
+ * projection (no counterpart in the reference). Each GPU of the pair creates
+ * its side with mcb_peer_exchange_create_v1 (a device allocation for
+ * `recv_bytes` of received rows plus two step counters) and gets an IPC
+ * handle, which the caller passes to the other process out of band; each
+ * then calls mcb_peer_exchange_connect_v1 with the other's handle.
+ * mcb_attn_block_heads_pair_v1 then computes, on GPU `group` (0 or 1), the
+ * group's Q/K/V projections and MSM, and the output projection in two row
+ * halves: the other GPU's rows are stored straight into that GPU's receive
+ * buffer by the GEMM's epilogue (NVLink stores that overlap the math), the
+ * own rows locally; after the other GPU's counter says its share has arrived
+ * it writes Y = RMSNorm(X_own + P_own + P_received) for its half of the rows.
+ * X [B,S,D] (the pair's batch elements), W* as in mcb_attn_block_heads_v1,
+ * Y [B*S/2, D] (rows [group*B*S/2, (group+1)*B*S/2) of X), all dense bf16 in
+ * device memory; recv_bytes >= B*S/2 * D * 2. Both GPUs must make the same
+ * calls in the same order; waits on the other GPU give up after ~2 s with
+ * MCB_STATUS_DEVICE_TIMEOUT (the pair must then be destroyed and recreated).
+ * Destroy only after both GPUs have finished their calls. */
+typedef struct mcb_peer_exchange mcb_peer_exchange;
+typedef struct mcb_ipc_handle {
+  char internal[64];
+} mcb_ipc_handle;
+MCB_API mcb_status mcb_peer_exchange_create_v1(int32_t device, uint64_t recv_bytes,
+                                               mcb_peer_exchange **out,
+                                               mcb_ipc_handle *handle) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_peer_exchange_connect_v1(mcb_peer_exchange *x,
+                                                const mcb_ipc_handle *peer) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_peer_exchange_destroy_v1(mcb_peer_exchange *x) MCB_NOEXCEPT;
+MCB_API mcb_status mcb_attn_block_heads_pair_v1(const mcb_tensor *y, const mcb_tensor *x,
+                                                const mcb_tensor *wq, const mcb_tensor *wk,
+                                                const mcb_tensor *wv, const mcb_tensor *wo,
+                                                int64_t heads, float eps, int32_t group,
+                                                mcb_peer_exchange *exchange,
+                                                const mcb_exec *exec) MCB_NOEXCEPT;
+
 /* ---- execution plans (shape-locked, optional CUDA-graph replay) ------------ */
 /* Mirrors MatcorePlan::create / execute (include/matcore/plan.h:37-107): a
  * plan freezes the operator and the metadata (dtype, rank, dims, strides,

@@ -8,7 +8,8 @@ is missing -- there is no CPU fallback.
 """
 from . import _abi
 from ._abi import McbError, load
-from .api import (Comm, Plan, attn_block, attn_block_heads, block_attn_res, device_status,
+from .api import (Comm, PeerExchange, Plan, attn_block, attn_block_heads, attn_block_heads_pair,
+                  block_attn_res, device_status,
                   fp8_quantize_blockwise, gemm_bf16_f32_fma,
                   gemm_chain, gemm_epilogue, gemm_fp8_blockscaled, gemm_i8_i32, msm,
                   residual_rmsnorm, shard_plan, strict_fused_pair, strict_gemm)
@@ -16,7 +17,7 @@ from .api import (Comm, Plan, attn_block, attn_block_heads, block_attn_res, devi
 __all__ = ["McbError", "load", "strict_gemm", "strict_fused_pair", "gemm_epilogue", "gemm_chain",
            "msm",
            "fp8_quantize_blockwise", "gemm_fp8_blockscaled", "attn_block", "attn_block_heads",
-           "residual_rmsnorm", "shard_plan",
+           "attn_block_heads_pair", "PeerExchange", "residual_rmsnorm", "shard_plan",
            "device_status", "Comm"]
 
 load()

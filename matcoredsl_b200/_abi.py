@@ -139,6 +139,11 @@ class CommId(ctypes.Structure):
     _fields_ = [("internal", ctypes.c_uint8 * 128)]  # raw bytes (c_char would stop at NUL)
 
 
+class IpcHandle(ctypes.Structure):
+    """mcb_ipc_handle: a CUDA IPC memory handle (64 opaque bytes)."""
+    _fields_ = [("internal", ctypes.c_uint8 * 64)]
+
+
 SIGNATURES = {
     "mcb_abi_version": (ctypes.c_uint32, []),
     "mcb_status_message": (ctypes.c_char_p, [ctypes.c_int32]),
@@ -172,6 +177,13 @@ SIGNATURES = {
     "mcb_attn_block_heads_workspace_bytes_v1": (ctypes.c_uint64, [ctypes.c_int64] * 3),
     "mcb_attn_block_heads_v1": (ctypes.c_int32, [_T, _T, _T, _T, _T, _T, ctypes.c_int64, _E]),
     "mcb_residual_rmsnorm_v1": (ctypes.c_int32, [_T, _T, _T, ctypes.c_float, _E]),
+    "mcb_peer_exchange_create_v1": (ctypes.c_int32, [ctypes.c_int32, ctypes.c_uint64,
+                                                     _P(ctypes.c_void_p), _P(IpcHandle)]),
+    "mcb_peer_exchange_connect_v1": (ctypes.c_int32, [ctypes.c_void_p, _P(IpcHandle)]),
+    "mcb_peer_exchange_destroy_v1": (ctypes.c_int32, [ctypes.c_void_p]),
+    "mcb_attn_block_heads_pair_v1": (ctypes.c_int32, [_T, _T, _T, _T, _T, _T, ctypes.c_int64,
+                                                      ctypes.c_float, ctypes.c_int32,
+                                                      ctypes.c_void_p, _E]),
     "mcb_plan_create_v1": (ctypes.c_int32, [_P(PlanDesc), _P(ctypes.c_void_p)]),
     "mcb_plan_execute_v1": (ctypes.c_int32, [ctypes.c_void_p, _T, ctypes.c_uint32,
                                              ctypes.c_void_p]),

@@ -380,6 +380,52 @@ def attn_block_heads(x, wq, wk, wv, wo, heads, out=None, *, device=-1, flags=0, 
     return out
 
 
+class PeerExchange:
+    """This GPU's side of a two-GPU head-sharded attention block
+    (mcb_peer_exchange_*_v1): create it on each GPU with the bytes of the
+    rows it receives, pass `handle` (64 bytes) to the other process out of
+    band, then `connect(other_handle)`. Close it only after both GPUs have
+    finished their calls."""
+
+    def __init__(self, device: int, recv_bytes: int):
+        self._h = ctypes.c_void_p()
+        h = _abi.IpcHandle()
+        _abi.check(_abi.load().mcb_peer_exchange_create_v1(device, recv_bytes,
+                                                           ctypes.byref(self._h), ctypes.byref(h)),
+                   "mcb_peer_exchange_create_v1")
+        self.device = device
+        self.handle = ctypes.string_at(ctypes.addressof(h), ctypes.sizeof(h))
+
+    def connect(self, other: bytes):
+        h = _abi.IpcHandle()
+        if len(other) != ctypes.sizeof(h):
+            raise ValueError("PeerExchange.connect: the handle must be 64 bytes")
+        ctypes.memmove(ctypes.addressof(h), other, ctypes.sizeof(h))
+        _abi.check(_abi.load().mcb_peer_exchange_connect_v1(self._h, ctypes.byref(h)),
+                   "mcb_peer_exchange_connect_v1")
+
+    def close(self):
+        if self._h:
+            _abi.check(_abi.load().mcb_peer_exchange_destroy_v1(self._h),
+                       "mcb_peer_exchange_destroy_v1")
+            self._h = ctypes.c_void_p()
+
+
+def attn_block_heads_pair(x, wq, wk, wv, wo, heads, eps, group, exchange, out=None, *, device=-1,
+                          flags=0, workspace=None):
+    """GPU `group` (0 or 1) of a two-GPU head-sharded attention block: its
+    head group's partial output projection, the other GPU's rows sent into
+    that GPU's receive buffer by the GEMM itself, and Y = RMSNorm(X + sum of
+    both partials) for this GPU's half of the rows (returned, [B*S/2, D])."""
+    if out is None:
+        rows = x.shape[0] * x.shape[1] // 2
+        out = _empty_like_out(x, (rows, x.shape[2]), "bf16")
+    _call("mcb_attn_block_heads_pair_v1",
+          [("y", out), ("x", x), ("wq", wq), ("wk", wk), ("wv", wv), ("wo", wo)],
+          [int(heads), float(eps), int(group), exchange._h], device, flags, workspace)
+    return out
+
+
 def residual_rmsnorm(x, p, eps=1e-6, out=None, *, device=-1, flags=0):
     """Y = RMSNorm(X + P) over the last dimension (unit gain); X, P, Y dense
     bf16 of one shape (rank 2 or 3)."""

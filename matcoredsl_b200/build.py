@@ -42,6 +42,7 @@ SOURCES = {
     "plan.cpp": [],
     "typed.cu": [],
     "comm.cpp": [],
+    "peer.cu": [],
 }
 HEADERS = ["common.cuh", "internal.h", "epilogue.cuh"]
 

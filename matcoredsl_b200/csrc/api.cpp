@@ -1781,6 +1781,157 @@ mcb_status residual_rmsnorm_impl(const mcb_tensor *y, const mcb_tensor *x, const
   return call.finish(y, dy, info, err);
 }
 
+// Two head groups on two GPUs, the exchange fused into the output projection
+// (peer.cu holds the exchange object and the counter kernels). Step s of GPU
+// g (both GPUs run the same steps):
+//   projections and MSM of the group (local);
+//   wait until the peer has consumed what this GPU wrote at step s-1;
+//   GEMM of the peer's rows of O_g Wo_g, stored into the peer's receive
+//   buffer by the epilogue (plain stores: no TMA touches the peer);
+//   raise the peer's "data" counter to s;
+//   GEMM of the own rows into scratch;
+//   wait for this GPU's "data" counter to reach s;
+//   Y = RMSNorm(X_own + P_own + P_received);
+//   raise the peer's "consumed" counter to s.
+// The waits on the other GPU's counters give up after ~2 s (clock64 cycles
+// at ~1.9 GHz), as the pipeline waits of the GEMM kernels do.
+constexpr long long kSpinTimeoutCyclesHost = 4000000000LL;
+
+mcb_status attn_heads_pair_impl(const mcb_tensor *y, const mcb_tensor *x, const mcb_tensor *wq,
+                                const mcb_tensor *wk, const mcb_tensor *wv, const mcb_tensor *wo,
+                                int64_t heads, float eps, int32_t group, mcb_peer_exchange *xch,
+                                const mcb_exec *exec) {
+  mcb_status s;
+  if ((s = check_tensor(x, 3, 3)) || (s = check_tensor(y, 2, 2)) || (s = check_tensor(wq, 2, 2)) ||
+      (s = check_tensor(wk, 2, 2)) || (s = check_tensor(wv, 2, 2)) || (s = check_tensor(wo, 2, 2)))
+    return s;
+  for (const mcb_tensor *t : {x, y, wq, wk, wv, wo})
+    if (t->dtype != MCB_DTYPE_BF16) return MCB_STATUS_UNSUPPORTED_DTYPE;
+  if (!xch || !xch->local || !xch->remote || (group != 0 && group != 1))
+    return MCB_STATUS_INVALID_ARGUMENT;
+  if (!(eps >= 0.0f)) return MCB_STATUS_INVALID_ARGUMENT;
+  const int64_t B = x->dims[0], S = x->dims[1], D = x->dims[2], Dh = wq->dims[1];
+  if (heads <= 0 || Dh <= 0 || Dh % heads != 0) return MCB_STATUS_INVALID_ARGUMENT;
+  const int64_t hd = Dh / heads, M = B * S;
+  if (S == 0 || M % 2 != 0) return MCB_STATUS_INVALID_SHAPE;
+  const int64_t R = M / 2;
+  if (!(x->dims[0] == B && x->strides[2] == 1 && (S <= 1 || x->strides[1] == D) &&
+        (B <= 1 || x->strides[0] == S * D)))
+    return MCB_STATUS_SHAPE_MISMATCH;
+  if (!dense2(y, R, D)) return MCB_STATUS_SHAPE_MISMATCH;
+  for (const mcb_tensor *w : {wq, wk, wv})
+    if (!dense2(w, D, Dh)) return MCB_STATUS_SHAPE_MISMATCH;
+  if (!dense2(wo, Dh, D)) return MCB_STATUS_SHAPE_MISMATCH;
+  if (static_cast<uint64_t>(R) * static_cast<uint64_t>(D) * 2 > xch->recv_bytes)
+    return MCB_STATUS_INSUFFICIENT_WORKSPACE;
+  for (const mcb_tensor *t : {x, wq, wk, wv, wo})
+    if (overlaps(y, t)) return MCB_STATUS_ALIAS_VIOLATION;
+  bool host = false;
+  if ((s = same_space({x, y, wq, wk, wv, wo}, &host))) return s;
+  if (host) return MCB_STATUS_UNSUPPORTED_MEMORY_SPACE;
+  Call call(exec);
+  if ((s = call.begin(host))) return s;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != xch->device) return MCB_STATUS_INVALID_ARGUMENT;
+  void *dx, *dq, *dk, *dv, *dwo, *dy;
+  if ((s = call.device_ptr(x, true, &dx)) || (s = call.device_ptr(wq, true, &dq)) ||
+      (s = call.device_ptr(wk, true, &dk)) || (s = call.device_ptr(wv, true, &dv)) ||
+      (s = call.device_ptr(wo, true, &dwo)) || (s = call.device_ptr(y, false, &dy)))
+    return s;
+  void *ws = nullptr;
+  const uint64_t qkvo = attn_heads_workspace_bytes(M, Dh);
+  const uint64_t pown = (static_cast<uint64_t>(R) * D * 2 + 255) / 256 * 256;
+  if ((s = call.scratch(qkvo + pown, &ws))) return s;
+  const uint64_t one = qkvo / 4;
+  uint8_t *base = static_cast<uint8_t *>(ws);
+  void *Q = base, *K = base + one, *V = base + 2 * one, *O = base + 3 * one, *P = base + qkvo;
+  uint8_t *loc = static_cast<uint8_t *>(xch->local), *rem = static_cast<uint8_t *>(xch->remote);
+  uint32_t *data_local = reinterpret_cast<uint32_t *>(loc);
+  uint32_t *consumed_local = reinterpret_cast<uint32_t *>(loc + 128);
+  uint32_t *data_remote = reinterpret_cast<uint32_t *>(rem);
+  uint32_t *consumed_remote = reinterpret_cast<uint32_t *>(rem + 128);
+  void *recv_local = loc + mcb_peer_exchange::kHeaderBytes;
+  void *recv_remote = rem + mcb_peer_exchange::kHeaderBytes;
+
+  LaunchInfo info, step;
+  cudaError_t err = cudaSuccess;
+  mcb::Epilogue none;
+  auto gemm = [&](const void *a, const void *w, void *out, int64_t m, int64_t n, int64_t k,
+                  int no_tma_store) {
+    const bool tc = k % 8 == 0 && n % 8 == 0 &&
+                    ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(w) |
+                      reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
+    if (tc)
+      return mcb::launch_gemm_tc_bf16(a, w, out, m, n, k, k, n, n, 0, 1, none, call.ctx()->status,
+                                      call.sms(), call.stream(), &step, 0, nullptr, no_tma_store);
+    return mcb::launch_gemm_simt(a, MCB_DTYPE_BF16, w, MCB_DTYPE_BF16, out, MCB_DTYPE_BF16, m, n,
+                                 k, k, n, n, 0, none, call.stream(), &step);
+  };
+  const uint32_t st = ++xch->step;
+  uint32_t *status = call.ctx()->status;
+  call.mark_compute_start();
+  int launches = 0;
+  for (auto [w, out] : {std::pair<void *, void *>{dq, Q}, {dk, K}, {dv, V}}) {
+    step.launches = 0;
+    if ((err = gemm(dx, w, out, M, Dh, D, 0)) != cudaSuccess) break;
+    launches += step.launches;
+  }
+  if (err == cudaSuccess) {
+    mcb::MsmShape sh;
+    sh.batch = B;
+    sh.heads = heads;
+    sh.m = sh.n = S;
+    sh.dqk = sh.dv = hd;
+    const int64_t stv[3] = {S * Dh, hd, Dh};
+    for (int i = 0; i < 3; ++i) sh.q_s[i] = sh.k_s[i] = sh.v_s[i] = sh.o_s[i] = stv[i];
+    const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+    step.launches = 0;
+    err = cudaErrorNotSupported;
+    if ((hd == 64 || hd == 128) && Dh % 8 == 0)
+      err = mcb::launch_msm_tc_bf16(Q, K, V, O, sh, scale, status, call.sms(), call.stream(), &step);
+    if (err == cudaErrorNotSupported)
+      err = hd <= 256 ? mcb::launch_msm_simt(Q, K, V, O, MCB_DTYPE_BF16, sh, scale, call.stream(),
+                                             &step)
+                      : cudaErrorNotSupported;
+    launches += step.launches;
+  }
+  const int peer = 1 - group;
+  const uint8_t *o_rows = static_cast<const uint8_t *>(O);
+  if (err == cudaSuccess)
+    err = mcb::launch_peer_wait(consumed_local, st - 1, kSpinTimeoutCyclesHost, status,
+                                call.stream());
+  if (err == cudaSuccess) {
+    step.launches = 0;
+    err = gemm(o_rows + static_cast<uint64_t>(peer) * R * Dh * 2, dwo, recv_remote, R, D, Dh, 1);
+    launches += step.launches;
+  }
+  if (err == cudaSuccess) err = mcb::launch_peer_signal(data_remote, st, call.stream());
+  if (err == cudaSuccess) {
+    step.launches = 0;
+    err = gemm(o_rows + static_cast<uint64_t>(group) * R * Dh * 2, dwo, P, R, D, Dh, 0);
+    launches += step.launches;
+  }
+  if (err == cudaSuccess)
+    err = mcb::launch_peer_wait(data_local, st, kSpinTimeoutCyclesHost, status, call.stream());
+  if (err == cudaSuccess) {
+    step.launches = 0;
+    err = mcb::launch_residual_rmsnorm(static_cast<const uint8_t *>(dx) +
+                                           static_cast<uint64_t>(group) * R * D * 2,
+                                       P, dy, R, D, eps, call.stream(), &step, recv_local);
+    launches += step.launches;
+  }
+  if (err == cudaSuccess) err = mcb::launch_peer_signal(consumed_remote, st, call.stream());
+  launches += 4;  // the two waits and two signals
+  call.mark_compute_end();
+  if (err == cudaErrorNotSupported) return MCB_STATUS_UNAVAILABLE_VARIANT;
+  info.launches = launches;
+  info.tile_m = 128;
+  info.tile_n = 256;
+  info.ctas = call.sms();
+  info.set_route("attn_block_heads_pair_p2p");
+  return call.finish(y, dy, info, err);
+}
+
 // ---- device buffers ------------------------------------------------------------------------
 std::mutex g_buf_mu;
 std::unordered_map<uint64_t, mcb_buffer> g_bufs;  // ptr -> live handle
@@ -2180,6 +2331,19 @@ MCB_API mcb_status mcb_residual_rmsnorm_v1(const mcb_tensor *y, const mcb_tensor
                                            const mcb_exec *exec) noexcept {
   try {
     return residual_rmsnorm_impl(y, x, p, eps, exec);
+  } catch (...) {
+    return MCB_STATUS_CANDIDATE_FAILURE;
+  }
+}
+
+MCB_API mcb_status mcb_attn_block_heads_pair_v1(const mcb_tensor *y, const mcb_tensor *x,
+                                                const mcb_tensor *wq, const mcb_tensor *wk,
+                                                const mcb_tensor *wv, const mcb_tensor *wo,
+                                                int64_t heads, float eps, int32_t group,
+                                                mcb_peer_exchange *exchange,
+                                                const mcb_exec *exec) noexcept {
+  try {
+    return attn_heads_pair_impl(y, x, wq, wk, wv, wo, heads, eps, group, exchange, exec);
   } catch (...) {
     return MCB_STATUS_CANDIDATE_FAILURE;
   }

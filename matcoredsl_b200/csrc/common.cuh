@@ -22,6 +22,7 @@ enum : uint32_t {
   kErrTimeoutDrain = 1u << 3,     // final tensor-core drain stalled
   kErrBadLaunch = 1u << 4,        // kernel saw an impossible configuration
   kErrTimeoutPeer = 1u << 5,      // another CTA's stream-K partial never arrived
+  kErrTimeoutRemote = 1u << 6,    // the other GPU of a head-sharded pair never raised its flag
 };
 
 constexpr long long kSpinTimeoutCycles = 4000000000LL;  // ~2 s at 1.9 GHz

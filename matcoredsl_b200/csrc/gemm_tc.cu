@@ -59,7 +59,8 @@ struct Params {
   int64_t m, n, k, ld_y;
   int n_tiles, num_tiles, num_kb;
   int w_transposed, y_kind, in_f16;  // y_kind: kOutF32 / kOutBf16 / kOutF16
-  int y_tma;  // CTA-pair kernel: 0, or y_kind (16-bit) when whole tiles are stored by TMA
+  int y_tma;  // CTA-pair kernel: 0, or y_kind (16-bit) when whole tiles are staged per warp
+  int y_lsu;  // staged chunks leave shared memory by coalesced st.global (1) or a TMA store (0)
   void *y;
   uint32_t *status;
   long long spin_limit;  // clock64 cycles a pipeline wait may take before the kernel aborts
@@ -233,6 +234,10 @@ __device__ __forceinline__ void epilogue_chunk(const Params &p, const uint32_t (
 // issues the store of box (col0, row0). Rows past M and columns past N fall
 // outside the tensor map and are not written. Per-row 16-byte global stores
 // instead cost the load/store unit one L2 transaction per row and piece.
+// With p.y_lsu (an output in another GPU's memory, which no tensor map may
+// cover) the warp instead reads the buffer back transposed, lane l taking
+// piece l & 3 of rows l / 4 + 8 i, so each st.global.v4 writes 8 rows x 64
+// contiguous bytes; rows past M and columns past N are skipped.
 template <int kYKind>
 __device__ __forceinline__ void epilogue_chunk_tma(const Params &p, const uint32_t (&r)[32],
                                                    int64_t row, int64_t col0, int64_t row0,
@@ -241,7 +246,7 @@ __device__ __forceinline__ void epilogue_chunk_tma(const Params &p, const uint32
   float v[32];
   const bool live = row < p.m;
   if (live) epilogue_values<false>(p, r, row, col0, bias_smem, v);
-  if (lane == 0) bulk_wait_read_all();  // the previous chunk's store has read the buffer
+  if (lane == 0 && !p.y_lsu) bulk_wait_read_all();  // the previous chunk's store has read the buffer
   __syncwarp();
   if (live) {
     uint8_t *dst = stage + lane * 64;
@@ -262,6 +267,33 @@ __device__ __forceinline__ void epilogue_chunk_tma(const Params &p, const uint32
       }
       *reinterpret_cast<uint4 *>(dst + ((q ^ sw) << 4)) = o;
     }
+  }
+  if (p.y_lsu) {
+    __syncwarp();
+    const int q = lane & 3;
+    uint16_t *y = reinterpret_cast<uint16_t *>(p.y);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = (lane >> 2) + 8 * i;
+      const int64_t grow = row0 + rr;
+      const int64_t gcol = col0 + q * 8;
+      if (grow < p.m && gcol < p.n) {
+        const uint4 o =
+            *reinterpret_cast<const uint4 *>(stage + rr * 64 + ((q ^ ((rr >> 1) & 3)) << 4));
+        uint16_t *dst = y + grow * p.ld_y + gcol;
+        if (gcol + 8 <= p.n) {
+          *reinterpret_cast<uint4 *>(dst) = o;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t w = e < 2 ? o.x : e < 4 ? o.y : e < 6 ? o.z : o.w;
+            if (gcol + e < p.n) dst[e] = static_cast<uint16_t>(w >> ((e & 1) * 16));
+          }
+        }
+      }
+    }
+    __syncwarp();  // every lane has read the buffer before the next chunk writes it
+    return;
   }
   fence_async_smem();
   __syncwarp();
@@ -893,7 +925,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(P_THREADS, 1)
     }
     // The TMA stores must finish reading shared memory (and land) before
     // the block exits.
-    if (p.y_tma && lane == 0) bulk_wait_all();
+    if (p.y_tma && !p.y_lsu && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -1010,7 +1042,7 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
                                 int64_t k, int64_t ld_x, int64_t ld_w, int64_t ld_y,
                                 int w_transposed, int y_kind, const Epilogue &epi,
                                 uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info,
-                                int in_f16, const GemmStreamK *sk) {
+                                int in_f16, const GemmStreamK *sk, int no_tma_store) {
   if (m == 0 || n == 0) return cudaSuccess;
   const bool chain = epi.n_ops > 0;
   // Rows of 256 go to CTA pairs (M = 256 per MMA, W tile split between the
@@ -1043,8 +1075,11 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   int y_tma = 0;
   if (pair && !chain && (y_kind == kOutBf16 || y_kind == kOutF16) &&
       reinterpret_cast<uintptr_t>(y) % 16 == 0 && (ld_y * 2) % 16 == 0 && y_tma_enabled()) {
-    if (!encode_tmap_2d(&ty, y_kind == kOutF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+    // no_tma_store (y in another GPU's memory): staged chunks, coalesced
+    // st.global, no tensor map over y.
+    if (!no_tma_store &&
+        !encode_tmap_2d(&ty, y_kind == kOutF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                         y, n, m, ld_y * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
       return cudaErrorInvalidValue;
     y_tma = y_kind;
@@ -1068,6 +1103,7 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
   p.spin_limit = kSpinTimeoutCycles;
   p.stall_loads = 0;
   p.y_tma = y_tma;
+  p.y_lsu = y_tma && no_tma_store ? 1 : 0;
   p.sk_first_tile = p.num_tiles;  // whole tiles only unless stream-K applies below
   p.sk_tiles = 0;
   p.sk_chains = 0;

@@ -7,6 +7,23 @@
 #include <stdint.h>
 #include <string.h>
 
+#include "mcb.h"
+
+// This GPU's side of a head-sharded pair's exchange (peer.cu): one device
+// allocation of a header (two step counters: "data" at byte 0, raised by the
+// peer once its share of this GPU's rows is in the receive buffer;
+// "consumed" at byte 128, raised by the peer once it has read the data this
+// GPU wrote into its buffer) and the receive buffer at kHeaderBytes; `remote`
+// is the peer's allocation opened through its IPC handle.
+struct mcb_peer_exchange {
+  static constexpr uint64_t kHeaderBytes = 256;
+  int32_t device = -1;
+  uint64_t recv_bytes = 0;
+  void *local = nullptr;
+  void *remote = nullptr;
+  uint32_t step = 0;  // calls made so far (both GPUs of the pair call in lockstep)
+};
+
 namespace mcb {
 
 struct LaunchInfo {
@@ -112,7 +129,8 @@ cudaError_t launch_gemm_tc_bf16(const void *x, const void *w, void *y, int64_t m
                                 int64_t k, int64_t ld_x, int64_t ld_w, int64_t ld_y,
                                 int w_transposed, int y_kind, const Epilogue &epi,
                                 uint32_t *status, int sms, cudaStream_t stream, LaunchInfo *info,
-                                int in_f16 = 0, const GemmStreamK *sk = nullptr);
+                                int in_f16 = 0, const GemmStreamK *sk = nullptr,
+                                int no_tma_store = 0);
 
 // Family B chain E = glue(A B) W fused on tcgen05 (chain_tc.cu): bf16 A [M,K],
 // B [K,N1], W [N1,N2] (row-major, 16-byte aligned bases and row strides,
@@ -213,9 +231,21 @@ cudaError_t launch_block_attn_res(const float *blocks, const float *partial, con
                                   cudaStream_t stream, LaunchInfo *info);
 
 // ---- rmsnorm (attention block) -------------------------------------------------------------
+// attn_proj2 (optional): a second bf16 partial of the projection, added after attn_proj.
 cudaError_t launch_residual_rmsnorm(const void *x, const void *attn_proj, void *y, int64_t rows,
                                     int64_t cols, float eps, cudaStream_t stream,
-                                    LaunchInfo *info);
+                                    LaunchInfo *info, const void *attn_proj2 = nullptr);
+
+// ---- peer.cu: flags between the two GPUs of a head-sharded pair -----------------------------
+// One thread spins (bounded by `limit` clock64 cycles, nanosleep between
+// polls) until the 32-bit step counter at `flag` (this GPU's memory, written
+// by the peer) reaches `target`; on timeout it sets kErrTimeoutRemote in
+// *status and returns.
+cudaError_t launch_peer_wait(const uint32_t *flag, uint32_t target, long long limit,
+                             uint32_t *status, cudaStream_t stream);
+// One thread makes every earlier write of this stream visible system-wide,
+// then stores `value` to `flag` (the peer's memory) with release semantics.
+cudaError_t launch_peer_signal(uint32_t *flag, uint32_t value, cudaStream_t stream);
 
 // Tensor-map encoder (driver entry point fetched once through the runtime).
 bool encode_tmap_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base,

@@ -15,13 +15,18 @@ namespace {
 constexpr int THREADS = 256;
 constexpr int MAX_PER_THREAD = 32;
 
+// kTwo: the projection is the sum of two bf16 partials (proj + proj2), added
+// in that order after x (the head-sharded block's own and received halves).
+template <bool kTwo>
 __global__ void __launch_bounds__(THREADS) residual_rmsnorm_kernel(
     const __nv_bfloat16 *__restrict__ x, const __nv_bfloat16 *__restrict__ proj,
-    __nv_bfloat16 *__restrict__ y, int64_t cols, float eps, int aligned16) {
+    const __nv_bfloat16 *__restrict__ proj2, __nv_bfloat16 *__restrict__ y, int64_t cols,
+    float eps, int aligned16) {
   __shared__ float red[THREADS / 32];
   const int64_t row = blockIdx.x;
   const __nv_bfloat16 *xr = x + row * cols;
   const __nv_bfloat16 *pr = proj + row * cols;
+  const __nv_bfloat16 *qr = kTwo ? proj2 + row * cols : nullptr;
   __nv_bfloat16 *yr = y + row * cols;
   float s[MAX_PER_THREAD];
   float ss = 0.0f;
@@ -36,10 +41,17 @@ __global__ void __launch_bounds__(THREADS) residual_rmsnorm_kernel(
       const uint4 a = *reinterpret_cast<const uint4 *>(xr + off);
       const uint4 b = *reinterpret_cast<const uint4 *>(pr + off);
       const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+      uint4 c = make_uint4(0u, 0u, 0u, 0u);
+      if constexpr (kTwo) c = *reinterpret_cast<const uint4 *>(qr + off);
+      const uint32_t cw4[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
-        const float s0 = __uint_as_float(aw[h] << 16) + __uint_as_float(bw[h] << 16);
-        const float s1 = __uint_as_float(aw[h] & 0xffff0000u) + __uint_as_float(bw[h] & 0xffff0000u);
+        float s0 = __uint_as_float(aw[h] << 16) + __uint_as_float(bw[h] << 16);
+        float s1 = __uint_as_float(aw[h] & 0xffff0000u) + __uint_as_float(bw[h] & 0xffff0000u);
+        if constexpr (kTwo) {
+          s0 += __uint_as_float(cw4[h] << 16);
+          s1 += __uint_as_float(cw4[h] & 0xffff0000u);
+        }
         s[v * 8 + h * 2] = s0;
         s[v * 8 + h * 2 + 1] = s1;
         ss = fmaf(s0, s0, fmaf(s1, s1, ss));
@@ -49,7 +61,8 @@ __global__ void __launch_bounds__(THREADS) residual_rmsnorm_kernel(
     for (int i = 0; i < MAX_PER_THREAD; ++i) {
       const int64_t c = static_cast<int64_t>(i) * THREADS + threadIdx.x;
       if (c >= cols) break;
-      const float v = __bfloat162float(xr[c]) + __bfloat162float(pr[c]);
+      float v = __bfloat162float(xr[c]) + __bfloat162float(pr[c]);
+      if constexpr (kTwo) v += __bfloat162float(qr[c]);
       s[i] = v;
       ss = fmaf(v, v, ss);
     }
@@ -362,15 +375,22 @@ cudaError_t launch_block_attn_res(const float *blocks, const float *partial, con
 
 cudaError_t launch_residual_rmsnorm(const void *x, const void *attn_proj, void *y, int64_t rows,
                                     int64_t cols, float eps, cudaStream_t stream,
-                                    LaunchInfo *info) {
+                                    LaunchInfo *info, const void *attn_proj2) {
   if (rows == 0 || cols == 0) return cudaSuccess;
   if (cols > static_cast<int64_t>(THREADS) * MAX_PER_THREAD) return cudaErrorNotSupported;
   if (rows > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  residual_rmsnorm_kernel<<<static_cast<unsigned>(rows), THREADS, 0, stream>>>(
-      static_cast<const __nv_bfloat16 *>(x), static_cast<const __nv_bfloat16 *>(attn_proj),
-      static_cast<__nv_bfloat16 *>(y), cols, eps,
-      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(attn_proj) |
-        reinterpret_cast<uintptr_t>(y)) & 15u) == 0);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(attn_proj) |
+                         reinterpret_cast<uintptr_t>(attn_proj2) | reinterpret_cast<uintptr_t>(y)) &
+                        15u) == 0;
+  if (attn_proj2)
+    residual_rmsnorm_kernel<true><<<static_cast<unsigned>(rows), THREADS, 0, stream>>>(
+        static_cast<const __nv_bfloat16 *>(x), static_cast<const __nv_bfloat16 *>(attn_proj),
+        static_cast<const __nv_bfloat16 *>(attn_proj2), static_cast<__nv_bfloat16 *>(y), cols,
+        eps, aligned);
+  else
+    residual_rmsnorm_kernel<false><<<static_cast<unsigned>(rows), THREADS, 0, stream>>>(
+        static_cast<const __nv_bfloat16 *>(x), static_cast<const __nv_bfloat16 *>(attn_proj),
+        nullptr, static_cast<__nv_bfloat16 *>(y), cols, eps, aligned);
   if (info) {
     info->launches += 1;
     info->set_route("attn_block_region");

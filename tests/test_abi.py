@@ -162,6 +162,30 @@ def test_comm_arguments_checked_without_gpu(mcb):
     assert lib.mcb_comm_destroy_v1(None) == 0
 
 
+def test_peer_exchange_arguments_checked_without_gpu(mcb):
+    """The two-GPU exchange entry points validate their arguments first."""
+    from matcoredsl_b200 import _abi
+    lib = mcb.load()
+    bad = _abi.STATUS_CODE["INVALID_ARGUMENT"]
+    out = ctypes.c_void_p()
+    h = _abi.IpcHandle()
+    assert lib.mcb_peer_exchange_create_v1(-1, 16, ctypes.byref(out), ctypes.byref(h)) == bad
+    assert lib.mcb_peer_exchange_create_v1(0, 0, ctypes.byref(out), ctypes.byref(h)) == bad
+    assert lib.mcb_peer_exchange_create_v1(0, 16, None, ctypes.byref(h)) == bad
+    assert lib.mcb_peer_exchange_connect_v1(None, ctypes.byref(h)) == bad
+    assert lib.mcb_peer_exchange_destroy_v1(None) == 0
+    a = np.zeros((1, 2, 8), np.uint16)
+    t = _abi.make_tensor(a.ctypes.data, "bf16", a.shape, [16, 8, 1], False)
+    w = np.zeros((8, 8), np.uint16)
+    tw = _abi.make_tensor(w.ctypes.data, "bf16", w.shape, [8, 1], False)
+    y = np.zeros((1, 8), np.uint16)
+    ty = _abi.make_tensor(y.ctypes.data, "bf16", y.shape, [8, 1], False)
+    ex = _abi.make_exec()
+    assert lib.mcb_attn_block_heads_pair_v1(ctypes.byref(ty), ctypes.byref(t), ctypes.byref(tw),
+                                            ctypes.byref(tw), ctypes.byref(tw), ctypes.byref(tw),
+                                            1, 1e-6, 0, None, ctypes.byref(ex)) == bad
+
+
 def test_attn_heads_arguments_checked_without_gpu(mcb):
     """The head-sharded block and residual + RMSNorm reject bad shapes and
     arguments before touching a device."""

@@ -7,7 +7,10 @@ each rank's partial output projection, mcb_reduce_scatter_v1 sums the two
 partials and leaves each rank half of the rows, and mcb_residual_rmsnorm_v1
 finishes those rows. The result must match the one-GPU region within the
 bf16 bar (1e-2 relative Frobenius error); the reduce-scatter alone must sum
-f32 exactly. Child processes with bounded waits; skipped on a box with fewer
+f32 exactly. The same block then runs three times with the exchange fused
+into the output projection (mcb_attn_block_heads_pair_v1: each GPU's GEMM
+stores the other GPU's rows into that GPU's receive buffer and raises a
+counter there) and must match as well. Child processes with bounded waits; skipped on a box with fewer
 than two GPUs."""
 import os
 import subprocess
@@ -63,7 +66,35 @@ CHILD = textwrap.dedent(r'''
     comm.close()
     err = ((y.float() - ref.float()).norm() / ref.float().norm()).item()
     assert err < 1e-2, err
-    print("rank", rank, "ok", err)
+
+    # the same block with the exchange fused into the output projection:
+    # this GPU's GEMM stores the other GPU's rows into its receive buffer
+    def swap(tag, data):
+        mine_f = f"{id_file}.{tag}{rank}"
+        with open(mine_f + ".tmp", "wb") as f:
+            f.write(data)
+        os.replace(mine_f + ".tmp", mine_f)
+        other = f"{id_file}.{tag}{1 - rank}"
+        t0 = time.time()
+        while not os.path.exists(other):
+            assert time.time() - t0 < 60, "no " + tag + " from the other rank"
+            time.sleep(0.02)
+        return open(other, "rb").read()
+    xch = mcb.PeerExchange(rank, rows * D * 2)
+    xch.connect(swap("h", xch.handle))
+    for it in range(3):  # three steps: the counters and the buffer are reused
+        y2 = mcb.attn_block_heads_pair(x, *[w[:, cols].contiguous() for w in ws[:3]],
+                                       ws[3][cols, :].contiguous(), H // world, 1e-6, rank, xch)
+        assert mcb.api.last_result.route == "attn_block_heads_pair_p2p"
+        torch.cuda.synchronize()
+        err2 = ((y2.float() - ref.reshape(rows, D).float()).norm() / ref.float().norm()).item()
+        assert err2 < 1e-2, (it, err2)
+        diff = ((y2.float() - y.reshape(rows, D).float()).norm() / ref.float().norm()).item()
+        assert diff < 1e-2, (it, diff)
+    assert mcb.device_status(rank) == 0
+    swap("done", b"1")  # neither side frees its buffer while the other may still write it
+    xch.close()
+    print("rank", rank, "ok", err, err2)
 ''')
 
 
