@@ -44,7 +44,7 @@ def test_abi_struct_layouts_match_c_compiler(mcb, tmp_path):
                "mcb_epilogue": _abi.Epilogue, "mcb_buffer": _abi.Buffer,
                "mcb_fp8_tile_config": _abi.Fp8TileConfig, "mcb_shard": _abi.Shard,
                "mcb_plan_desc": _abi.PlanDesc, "mcb_comm_id": _abi.CommId,
-               "mcb_epilogue_op": _abi.EpilogueOp}
+               "mcb_epilogue_op": _abi.EpilogueOp, "mcb_ipc_handle": _abi.IpcHandle}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "mcb.h"', "int main(void){"]
     for cname, py in structs.items():
         lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
