@@ -602,6 +602,9 @@ def run_ours(args):
     launch_ms = t_ms / args.steps
     t_ms_max = _max_over_ranks(t_ms, world, dev)
     launch_ms_max = _max_over_ranks(launch_ms, world, dev)
+    # fastest rank too (every rank takes this collective): the spread over
+    # GPUs of one step's time, reported beside the max the value is built on
+    t_ms_min = -_max_over_ranks(-t_ms, world, dev)
     value = world * flops_step * args.steps / (t_ms_max / 1e3) / 1e12
 
     # ---- end to end through the public API with host buffers -------------------------
@@ -618,6 +621,7 @@ def run_ours(args):
             # a rank that fails here would leave the others in a collective:
             # every rank takes the same steps, so all fail alike on a shape error
             others = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+    args.rank_ms_per_step = [t_ms_min / args.steps, t_ms_max / args.steps]
     _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, working_set, route,
             clk, e2e, others, kernel)
 
@@ -797,6 +801,8 @@ def _finish(args, world, rank, m, flops_step, t_ms_max, launch_ms_max, value, wo
             "clocks": clk.summary(),
             "e2e": e2e,
             "gpu_launches": args.steps,
+            "rank_ms_per_step": {"min": args.rank_ms_per_step[0],
+                                 "max": args.rank_ms_per_step[1]},
             "cpu_baseline": cpu,
             "other_configs": others,
         }
